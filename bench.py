@@ -1,0 +1,383 @@
+"""Benchmark: fused geo-biased station attention, forward + backward, on 1..8 B200 (one process per GPU).
+
+Workload (the scaling configuration): 256 issue dates sharded over the ranks, 16 heads, 512 stations,
+head dim 128, bf16; per-head alpha/beta/gamma; geo prior from synthetic station coordinates
+(lat ~ U(35,49), lon ~ U(-124,-104), elevation ~ U(500,3500) m). One step = forward + backward of the attention
+on this rank's issue dates followed by an NCCL all-reduce of the bias-parameter gradients (N > 1).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Prints ONE JSON line on rank 0. ``value`` is whole-job algorithmic TFLOP/s, 12*B*H*N^2*D per fwd+bwd (recompute not
+counted), over the max-over-ranks device time of K steps. ``e2e`` is the same metric through the public API with
+the step's inputs copied from pinned host memory and the bias gradients read back, every step. ``roofline``
+describes the dominant kernel timed live with CUDA events on its launching stream. ``--impl reference`` times the
+reference's operator on the host CPU cores (the oracle's restatement of the eager PyTorch op, all threads) on a
+bounded sample of the same workload.
+"""
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+import torch
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+METRIC = "geo-attn fwd+bwd TFLOPS & % tensor peak at 1/2/4/8 B200 vs eager; ms/step"
+UNIT = "TFLOP/s"
+B_TOTAL, H, N, D = 256, 16, 512, 128
+
+
+def flops(b):
+    return 12.0 * b * H * N * N * D
+
+
+def config(world):
+    return {"workload": "geo-attn fwd+bwd, %d issue dates sharded over %d GPU(s), H=%d heads, N=%d stations, "
+                        "D=%d, bf16, per-head alpha/beta/gamma, prior from station coordinates" % (B_TOTAL, world, H, N, D),
+            "global_batch": B_TOTAL, "per_gpu_batch": B_TOTAL // world, "heads": H, "stations": N, "head_dim": D,
+            "parallelism": "dp%d over issue dates; NCCL all-reduce of d(alpha,beta,gamma)" % world,
+            "l2": "inputs larger than L2: q,k,v,dO = %.0f MB per rank vs 126 MB L2" % (4 * B_TOTAL // world * H * N * D * 2 / 1e6)}
+
+
+def stations(seed=0):
+    rng = np.random.default_rng(seed)
+    lat = rng.uniform(35.0, 49.0, N)
+    lon = rng.uniform(-124.0, -104.0, N)
+    elev_ft = rng.uniform(500.0, 3500.0, N) / 0.3048
+    return lat, lon, elev_ft
+
+
+def inputs(b, seed, device):
+    g = torch.Generator().manual_seed(seed)
+    s = D ** -0.25
+    q, k, v = (torch.randn(b, H, N, D, generator=g) * s for _ in range(3))
+    do = torch.randn(b, H, N, D, generator=g)
+    gp = torch.Generator().manual_seed(7)
+    a = torch.rand(H, generator=gp) * 0.9 + 0.1
+    bb = torch.randn(H, generator=gp) * 0.5
+    c = torch.randn(H, generator=gp) * 0.5
+    t = [x.to(torch.bfloat16) for x in (q, k, v, do)]
+    return t, [x.to(device) for x in (a, bb, c)]
+
+
+def peaks():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            m = json.load(f)
+        return m.get("bf16_tflops_sustained", 1381.7), "measured (MEASURED_PEAKS.json bf16_tflops_sustained)"
+    return 1400.0, "fallback (sustained bf16 1.4 PFLOP/s)"
+
+
+def traffic_per_launch(kernel):
+    """DRAM bytes per launch of `kernel` for this workload from the committed ncu summary, else None."""
+    p = os.path.join(REPO, "profiles", "traffic_c5_bf16_d128.txt")
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        if line.startswith(kernel + " "):
+            try:
+                return float(line.split()[1])
+            except (IndexError, ValueError):
+                return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpus):
+        self.gpus = set(gpus)
+        self.proc = None
+        self.path = os.path.join("/tmp", "geoattn_clocks_%d.csv" % os.getpid())
+
+    def start(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", "--query-gpu=" + self.Q, "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        self.proc.wait()
+        self.f.close()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9 or not f[0].isdigit() or int(f[0]) not in self.gpus:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, val in zip(names, f[5:9]):
+                if val.lower() == "active":
+                    reasons.add(n)
+        os.unlink(self.path)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_reference(seconds, threads):
+    """The reference operator on the host CPU (the oracle's restatement of the eager PyTorch op, fp32), fwd+bwd on
+    one issue date (H heads x N stations x D) repeated for about `seconds`; returns TFLOP/s and the sample."""
+    from oracle import geo_attention as oga
+    from oracle import geometry as ogeo
+    torch.set_num_threads(threads)
+    lat, lon, el = stations(0)
+    dist, ang = (torch.from_numpy(x).float() for x in ogeo.distance_and_angularity(lat, lon, el))
+    (q, k, v, do), (a, b, c) = inputs(1, 1000, "cpu")
+    q, k, v, do = (t.float() for t in (q, k, v, do))
+    oga.grads(q, k, v, dist, ang, a, b, c, do, dtype=torch.float32)  # warm-up
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        oga.grads(q, k, v, dist, ang, a, b, c, do, dtype=torch.float32)
+        reps += 1
+        el_s = time.perf_counter() - t0
+        if el_s >= seconds or reps >= 200:
+            break
+    return flops(1) * reps / el_s / 1e12, reps, el_s
+
+
+def gpu_eager_ms(q, k, v, do, dist, ang, a, b, c, steps):
+    """Eager PyTorch on the same GPU and inputs (bf16 storage; the reference's op written with torch ops)."""
+    def op(q, k, v):
+        s = torch.matmul(q, k.transpose(-2, -1)) / math.sqrt(D)
+        p1 = torch.softmax(s, dim=-1)
+        z = a.view(1, -1, 1, 1) * p1 + b.view(1, -1, 1, 1) * (1 / (1 + dist)) + c.view(1, -1, 1, 1) * (1 / (1 + ang))
+        return torch.matmul(torch.softmax(z, dim=-1).to(v.dtype), v)
+    x = [t.detach().requires_grad_(True) for t in (q, k, v)]
+    try:
+        for _ in range(2):
+            op(*x).backward(do)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            for t in x:
+                t.grad = None
+            op(*x).backward(do)
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / steps
+    except torch.OutOfMemoryError:
+        return None
+    finally:
+        del x
+        torch.cuda.empty_cache()
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    threads = os.cpu_count() or 1
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
+    samples = []
+    for _ in range(args.warmup):
+        cpu_reference(1.0, threads)
+    for _ in range(args.steps):
+        samples.append(cpu_reference(args.cpu_seconds / max(1, args.steps), threads))
+    value = statistics.median(s[0] for s in samples)
+    reps = sum(s[1] for s in samples)
+    el = sum(s[2] for s in samples)
+    sample = "fwd+bwd of 1 issue date (H=%d, N=%d, D=%d) fp32 eager on the CPU, %d repetitions in %.1f s" % (
+        H, N, D, reps, el)
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": flops(B_TOTAL) / (value * 1e12) * 1e3,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
+            "config": config(world),
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-eager", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import foreswe_gpu_optimization_b200 as g
+    from foreswe_gpu_optimization_b200 import geo_attention_v2 as gv2
+
+    rank, world = int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist_on = world > 1
+    if dist_on:
+        import datetime
+        import torch.distributed as tdist
+        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    if B_TOTAL % world:
+        raise SystemExit("world size must divide %d" % B_TOTAL)
+    b = B_TOTAL // world
+    lat, lon, el = stations(0)
+    geom = g.StationGeometry(lat, lon, el, device=dev)
+    geom.prior(torch.bfloat16)
+    (qh, kh, vh, doh), (a0, b0, c0) = inputs(b, 1000 + rank, "cpu")
+    q, k, v, do = (t.to(dev) for t in (qh, kh, vh, doh))
+    params = [t.clone().requires_grad_(True) for t in (a0, b0, c0)]
+    x = [t.detach().requires_grad_(True) for t in (q, k, v)]
+
+    def allreduce_bias_grads():
+        if dist_on:
+            flat = torch.cat([p.grad for p in params])
+            tdist.all_reduce(flat)
+            for i, p in enumerate(params):
+                p.grad.copy_(flat[i * H:(i + 1) * H])
+
+    def step(qq, kk, vv, dd):
+        for t in x + params:
+            t.grad = None
+        o = g.geo_attention(qq, kk, vv, geom, *params)
+        o.backward(dd)
+        allreduce_bias_grads()
+
+    # warm-up
+    for _ in range(args.warmup):
+        step(x[0], x[1], x[2], do)
+    torch.cuda.synchronize()
+
+    # per-kernel timing events (one set per step), recorded by the library on the launching stream
+    def mk(n):
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(n)]
+        for e in evs:
+            e.record()
+        return evs
+    ev_sets = [(mk(2), mk(3)) for _ in range(args.steps)]
+    torch.cuda.synchronize()
+
+    clocks = ClockSampler(range(world) if world > 1 else [local])
+    if rank == 0:
+        clocks.start()
+    if dist_on:
+        tdist.barrier()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for i in range(args.steps):
+        gv2.TIMING_EVENTS["fwd"], gv2.TIMING_EVENTS["bwd"] = ev_sets[i]
+        step(x[0], x[1], x[2], do)
+    t1.record()
+    torch.cuda.synchronize()
+    gv2.TIMING_EVENTS["fwd"] = gv2.TIMING_EVENTS["bwd"] = None
+    if dist_on:
+        tdist.barrier()
+    clk = clocks.stop() if rank == 0 else None
+    ms = t0.elapsed_time(t1) / args.steps
+    kt = {"geoattn_fwd_kernel": statistics.mean(f[0].elapsed_time(f[1]) for f, _ in ev_sets),
+          "geoattn_bwd_rows_kernel": statistics.mean(bw[0].elapsed_time(bw[1]) for _, bw in ev_sets),
+          "geoattn_bwd_cols_kernel": statistics.mean(bw[1].elapsed_time(bw[2]) for _, bw in ev_sets)}
+    if dist_on:
+        tt = torch.tensor([ms] + list(kt.values()), device=dev, dtype=torch.float64)
+        tdist.all_reduce(tt, op=tdist.ReduceOp.MAX)
+        ms = tt[0].item()
+        kt = dict(zip(kt.keys(), tt[1:].tolist()))
+    value = flops(B_TOTAL) / (ms * 1e-3) / 1e12
+
+    # end to end through the public API: pinned host inputs copied in every step, bias gradients read back
+    e2e = None
+    if not args.no_e2e:
+        hq, hk, hv, hd = (t.pin_memory() for t in (qh, kh, vh, doh))
+        dq_, dk_, dv_, dd_ = (torch.empty_like(t) for t in (q, k, v, do))
+        out = torch.empty(3 * H, dtype=torch.float32).pin_memory()
+
+        def e2e_step():
+            for dst, src in ((dq_, hq), (dk_, hk), (dv_, hv), (dd_, hd)):
+                dst.copy_(src, non_blocking=True)
+            xs = [t.requires_grad_(True) for t in (dq_, dk_, dv_)]
+            for t in params:
+                t.grad = None
+            o = g.geo_attention(xs[0], xs[1], xs[2], geom, *params)
+            o.backward(dd_)
+            allreduce_bias_grads()
+            out.copy_(torch.cat([p.grad for p in params]), non_blocking=True)
+            for t in xs:
+                t.grad = None
+                t.requires_grad_(False)
+        for _ in range(args.warmup):
+            e2e_step()
+        torch.cuda.synchronize()
+        if dist_on:
+            tdist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            e2e_step()
+        e1.record()
+        torch.cuda.synchronize()
+        ems = e0.elapsed_time(e1) / args.steps
+        if dist_on:
+            tt = torch.tensor([ems], device=dev, dtype=torch.float64)
+            tdist.all_reduce(tt, op=tdist.ReduceOp.MAX)
+            ems = tt.item()
+        e2e = {"value": flops(B_TOTAL) / (ems * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": ems,
+               "h2d_bytes_per_step": 4 * q.numel() * 2, "d2h_bytes_per_step": 3 * H * 4}
+        del hq, hk, hv, hd, dq_, dk_, dv_, dd_
+
+    eager = None
+    if not args.no_eager and rank == 0:
+        dmat, amat = geom.distance_and_angularity()
+        e_ms = gpu_eager_ms(q, k, v, do, dmat, amat, *[p.detach() for p in params], steps=3)
+        if e_ms is not None:
+            eager = {"ms_per_step": e_ms, "value": flops(b) / (e_ms * 1e-3) / 1e12, "unit": UNIT,
+                     "what": "eager PyTorch (bf16 storage, cuBLAS + elementwise kernels) on this GPU, same shard"}
+
+    cpu = None
+    if rank == 0 and world == 1:
+        threads = os.cpu_count() or 1
+        val, reps, el_s = cpu_reference(args.cpu_seconds, threads)
+        cpu = {"value": val, "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": "fwd+bwd of 1 issue date (H=%d, N=%d, D=%d) fp32 eager on the CPU, %d repetitions in %.1f s"
+                         % (H, N, D, reps, el_s)}
+
+    if rank == 0:
+        dom = max(kt, key=kt.get)
+        per_launch = 4.0 * b * H * N * N * D        # each kernel carries one third of the algorithmic flops
+        ach = per_launch / (kt[dom] * 1e-3) / 1e12
+        pk, pk_src = peaks()
+        roof = {"bound": "tensor", "kernel": dom, "achieved": ach, "peak": pk, "unit": "TFLOP/s", "frac": ach / pk,
+                "peak_source": pk_src, "traffic": traffic_per_launch(dom),
+                "kernel_ms": kt, "flops_per_launch": per_launch}
+        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+                "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": config(world),
+                "tensor_peak_frac": value / world / pk, "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
+                "gpu_eager": eager, "gpu_launches": 4 * args.steps, "clocks": clk}
+        print(json.dumps(line), flush=True)
+    if dist_on:
+        tdist.barrier()
+        tdist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,542 @@
+// libgeoattn.so: host launchers behind the C ABI in include/geoattn.h, plus the small auxiliary kernels
+// (geometry prologue, TF32 operand split, deterministic bias-gradient reduction).
+#include <cuda_fp16.h>
+
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+
+#include "../../include/geoattn.h"
+#include "geoattn_kernels.cuh"
+#include "tma_host.h"
+
+namespace geoattn {
+
+// ---------------------------------------------------------------------------------------------------------------
+// Geometry prologue
+// ---------------------------------------------------------------------------------------------------------------
+template <bool F16>
+struct PairT;
+template <>
+struct PairT<true> {
+  using type = __half2;
+  __device__ static type make(float a, float b) { return __floats2half2_rn(a, b); }
+};
+template <>
+struct PairT<false> {
+  using type = float2;
+  __device__ static type make(float a, float b) { return make_float2(a, b); }
+};
+
+// Reciprocal prior exactly as the reference's fp32 elementwise ops: 1 / (1 + x), both correctly rounded.
+__device__ __forceinline__ float recip1p(float x) { return __frcp_rn(__fadd_rn(1.0f, x)); }
+
+template <bool F16>
+__global__ void prior_dense_kernel(const float* __restrict__ dist, long long ldd, const float* __restrict__ ang,
+                                   long long lda, int N, int np, void* prior, void* priorT) {
+  using P = PairT<F16>;
+  using V = typename P::type;
+  __shared__ V tile[32][33];
+  const int i0 = blockIdx.y * 32, j0 = blockIdx.x * 32, tx = threadIdx.x;
+  V* pr = reinterpret_cast<V*>(prior);
+  V* pt = reinterpret_cast<V*>(priorT);
+  for (int k = threadIdx.y; k < 32; k += 8) {
+    const int i = i0 + k, j = j0 + tx;
+    float a = 0.f, b = 0.f;
+    if (i < N && j < N) {
+      a = recip1p(dist[(long long)i * ldd + j]);
+      b = recip1p(ang[(long long)i * lda + j]);
+    }
+    const V v = P::make(a, b);
+    pr[(size_t)i * np + j] = v;
+    tile[k][tx] = v;
+  }
+  __syncthreads();
+  for (int k = threadIdx.y; k < 32; k += 8) pt[(size_t)(j0 + k) * np + (i0 + tx)] = tile[tx][k];
+}
+
+// float64 station geometry, operation order of the reference's numpy code (no FMA contraction):
+//   haversine: 2*asin(sqrt(sin^2((lat_i-lat_j)/2) + cos(lat_i)cos(lat_j) sin^2((lon_i-lon_j)/2))) * 6371
+//   vectors:   R = 6371 + elev_ft*0.3048; x = R cos(lat) cos(lon); y = R cos(lat) sin(lon); v = (x, y, x)
+//   angle:     2*atan2(|n_i v_j - n_j v_i|, |n_i v_j + n_j v_i|) in degrees
+__device__ __forceinline__ void station_vec(double lat, double lon, double elev_ft, double& x, double& y, double& n) {
+  const double d2r = 0.017453292519943295;  // pi / 180
+  const double r = __dadd_rn(6371.0, __dmul_rn(elev_ft, 0.3048));
+  const double cl = cos(__dmul_rn(lat, d2r));
+  x = __dmul_rn(__dmul_rn(r, cl), cos(__dmul_rn(lon, d2r)));
+  y = __dmul_rn(__dmul_rn(r, cl), sin(__dmul_rn(lon, d2r)));
+  n = sqrt(__dadd_rn(__dadd_rn(__dmul_rn(x, x), __dmul_rn(y, y)), __dmul_rn(x, x)));
+}
+
+__device__ __forceinline__ void pair_geometry(const double* lat, const double* lon, const double* elev, int i, int j,
+                                              float& dist_km, float& ang_deg) {
+  const double d2r = 0.017453292519943295;
+  const double li = __dmul_rn(lat[i], d2r), lj = __dmul_rn(lat[j], d2r);
+  const double oi = __dmul_rn(lon[i], d2r), oj = __dmul_rn(lon[j], d2r);
+  const double s1 = sin(__dmul_rn(0.5, __dsub_rn(li, lj)));
+  const double s2 = sin(__dmul_rn(0.5, __dsub_rn(oi, oj)));
+  const double h = __dadd_rn(__dmul_rn(s1, s1), __dmul_rn(__dmul_rn(__dmul_rn(cos(li), cos(lj)), s2), s2));
+  dist_km = (float)__dmul_rn(__dmul_rn(2.0, asin(sqrt(h))), 6371.0);
+  double xi, yi, ni, xj, yj, nj;
+  station_vec(lat[i], lon[i], elev[i], xi, yi, ni);
+  station_vec(lat[j], lon[j], elev[j], xj, yj, nj);
+  // u_norm_v = n_i * v_j, v_norm_u = n_j * v_i (components x, y, x)
+  const double ax = __dsub_rn(__dmul_rn(ni, xj), __dmul_rn(nj, xi));
+  const double ay = __dsub_rn(__dmul_rn(ni, yj), __dmul_rn(nj, yi));
+  const double sx = __dadd_rn(__dmul_rn(ni, xj), __dmul_rn(nj, xi));
+  const double sy = __dadd_rn(__dmul_rn(ni, yj), __dmul_rn(nj, yi));
+  const double na = sqrt(__dadd_rn(__dadd_rn(__dmul_rn(ax, ax), __dmul_rn(ay, ay)), __dmul_rn(ax, ax)));
+  const double ns = sqrt(__dadd_rn(__dadd_rn(__dmul_rn(sx, sx), __dmul_rn(sy, sy)), __dmul_rn(sx, sx)));
+  ang_deg = (float)__dmul_rn(__dmul_rn(2.0, atan2(na, ns)), 57.29577951308232);  // 180 / pi
+}
+
+template <bool F16>
+__global__ void prior_coords_kernel(const double* __restrict__ lat, const double* __restrict__ lon,
+                                    const double* __restrict__ elev, int N, int np, void* prior, void* priorT,
+                                    float* dist_out, float* ang_out) {
+  using P = PairT<F16>;
+  using V = typename P::type;
+  __shared__ V tile[32][33];
+  const int i0 = blockIdx.y * 32, j0 = blockIdx.x * 32, tx = threadIdx.x;
+  V* pr = reinterpret_cast<V*>(prior);
+  V* pt = reinterpret_cast<V*>(priorT);
+  for (int k = threadIdx.y; k < 32; k += 8) {
+    const int i = i0 + k, j = j0 + tx;
+    float a = 0.f, b = 0.f;
+    if (i < N && j < N) {
+      float dk, ad;
+      pair_geometry(lat, lon, elev, i, j, dk, ad);
+      if (dist_out) dist_out[(size_t)i * N + j] = dk;
+      if (ang_out) ang_out[(size_t)i * N + j] = ad;
+      a = recip1p(dk);
+      b = recip1p(ad);
+    }
+    const V v = P::make(a, b);
+    if (pr) pr[(size_t)i * np + j] = v;
+    tile[k][tx] = v;
+  }
+  __syncthreads();
+  if (pt)
+    for (int k = threadIdx.y; k < 32; k += 8) pt[(size_t)(j0 + k) * np + (i0 + tx)] = tile[tx][k];
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// TF32 operand split: x = hi + lo, hi = tf32_rn(x), lo = tf32_rn(x - hi).
+//   natural planes: [2][B][H][N][DP] (hi then lo), transposed hi plane: [B][H][DP][NP]; zero padded.
+// ---------------------------------------------------------------------------------------------------------------
+__global__ void split_tf32_kernel(const float* __restrict__ x, long long s0, long long s1, long long s2, long long s3,
+                                  int B, int H, int N, int D, int DP, int NP, float* nat, float* tr) {
+  __shared__ float tile[32][33];
+  const int bh = blockIdx.z, b = bh / H, h = bh % H;
+  const int n0 = blockIdx.x * 32, d0 = blockIdx.y * 32, tx = threadIdx.x;
+  const size_t plane = (size_t)B * H * N * DP;
+  for (int k = threadIdx.y; k < 32; k += 8) {
+    const int n = n0 + k, d = d0 + tx;
+    float v = 0.f;
+    if (n < N && d < D) v = x[b * s0 + h * s1 + (long long)n * s2 + (long long)d * s3];
+    const float hi = round_tf32(v);
+    const float lo = round_tf32(v - hi);
+    if (nat && n < N) {
+      const size_t o = ((size_t)bh * N + n) * DP + d;
+      nat[o] = hi;
+      nat[plane + o] = lo;
+    }
+    tile[k][tx] = hi;
+  }
+  if (!tr) return;
+  __syncthreads();
+  for (int k = threadIdx.y; k < 32; k += 8) tr[((size_t)bh * DP + d0 + k) * NP + n0 + tx] = tile[tx][k];
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// d(alpha), d(beta), d(gamma): fixed-order float64 sum of the per-(b*h, row block) partials.
+// ---------------------------------------------------------------------------------------------------------------
+__global__ void finalize_abg_kernel(const double* __restrict__ part, int B, int H, int nrb, int per_head, float* dabg) {
+  __shared__ double red[256];
+  const int k = blockIdx.x, hh = blockIdx.y, nabg = per_head ? H : 1;
+  const int count = per_head ? B * nrb : B * H * nrb;
+  double acc = 0.0;
+  for (int idx = threadIdx.x; idx < count; idx += blockDim.x) {
+    int bh, rb;
+    if (per_head) {
+      bh = (idx / nrb) * H + hh;
+      rb = idx % nrb;
+    } else {
+      bh = idx / nrb;
+      rb = idx % nrb;
+    }
+    acc += part[((size_t)bh * nrb + rb) * 3 + k];
+  }
+  red[threadIdx.x] = acc;
+  __syncthreads();
+  for (int s = 128; s > 0; s >>= 1) {
+    if (threadIdx.x < s) red[threadIdx.x] += red[threadIdx.x + s];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) dabg[k * nabg + hh] = (float)red[0];
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Host helpers
+// ---------------------------------------------------------------------------------------------------------------
+namespace {
+
+constexpr size_t kAlign = 256;
+inline size_t align_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
+
+struct Dims {
+  int B, H, N, D, DP, nrb, np;
+  bool bf16;
+  int nabg;
+};
+
+int check_shape(const GeoAttnShape* s, Dims& d) {
+  if (!s || s->batch <= 0 || s->heads <= 0 || s->n <= 0 || s->head_dim <= 0) return GEOATTN_ERR_INVALID;
+  if (s->dtype != GEOATTN_DTYPE_BF16 && s->dtype != GEOATTN_DTYPE_FP32) return GEOATTN_ERR_INVALID;
+  d.B = s->batch;
+  d.H = s->heads;
+  d.N = s->n;
+  d.D = s->head_dim;
+  d.bf16 = s->dtype == GEOATTN_DTYPE_BF16;
+  d.nrb = (d.N + kBM - 1) / kBM;
+  d.np = d.nrb * kBM;
+  d.nabg = s->per_head ? d.H : 1;
+  if (d.bf16) {
+    if (d.D > 192) return GEOATTN_ERR_UNSUPPORTED;
+    d.DP = d.D <= 64 ? 64 : d.D <= 128 ? 128 : 192;
+  } else {
+    if (d.D > 64) return GEOATTN_ERR_UNSUPPORTED;
+    d.DP = 64;
+  }
+  if ((long long)d.B * d.H > 65535) return GEOATTN_ERR_UNSUPPORTED;  // grid.y
+  return GEOATTN_OK;
+}
+
+size_t prior_table_bytes(const Dims& d) { return (size_t)d.np * d.np * (d.bf16 ? 4 : 8); }
+
+// workspace segments
+struct FwdWs {
+  int* status;
+  float *qn, *kn, *vt;
+};
+size_t fwd_ws(const Dims& d, uint8_t* base, FwdWs* w) {
+  size_t off = 0;
+  auto take = [&](size_t bytes) -> uint8_t* {
+    uint8_t* p = base ? base + off : nullptr;
+    off += align_up(bytes);
+    return p;
+  };
+  FwdWs t{};
+  t.status = reinterpret_cast<int*>(take(sizeof(int)));
+  if (!d.bf16) {
+    const size_t nat = (size_t)2 * d.B * d.H * d.N * d.DP * 4, trn = (size_t)d.B * d.H * d.DP * d.np * 4;
+    t.qn = reinterpret_cast<float*>(take(nat));
+    t.kn = reinterpret_cast<float*>(take(nat));
+    t.vt = reinterpret_cast<float*>(take(trn));
+  }
+  if (w) *w = t;
+  return off;
+}
+
+struct BwdWs {
+  int* status;
+  float* rowrec;
+  double* part;
+  float *qn, *kn, *vn, *don, *kt, *qt, *dot;
+};
+size_t bwd_ws(const Dims& d, uint8_t* base, BwdWs* w) {
+  size_t off = 0;
+  auto take = [&](size_t bytes) -> uint8_t* {
+    uint8_t* p = base ? base + off : nullptr;
+    off += align_up(bytes);
+    return p;
+  };
+  BwdWs t{};
+  t.status = reinterpret_cast<int*>(take(sizeof(int)));
+  t.rowrec = reinterpret_cast<float*>(take((size_t)d.B * d.H * d.N * 8 * 4));
+  t.part = reinterpret_cast<double*>(take((size_t)d.B * d.H * d.nrb * 3 * 8));
+  if (!d.bf16) {
+    const size_t nat = (size_t)2 * d.B * d.H * d.N * d.DP * 4, trn = (size_t)d.B * d.H * d.DP * d.np * 4;
+    t.qn = reinterpret_cast<float*>(take(nat));
+    t.kn = reinterpret_cast<float*>(take(nat));
+    t.vn = reinterpret_cast<float*>(take(nat));
+    t.don = reinterpret_cast<float*>(take(nat));
+    t.kt = reinterpret_cast<float*>(take(trn));
+    t.qt = reinterpret_cast<float*>(take(trn));
+    t.dot = reinterpret_cast<float*>(take(trn));
+  }
+  if (w) *w = t;
+  return off;
+}
+
+// TMA map over a user bf16 tensor [B, H, N, D] (box: 64 x rows).
+int map_user_bf16(CUtensorMap* m, const GeoAttnTensor& t, const Dims& d, int rows) {
+  if (!t.data) return GEOATTN_ERR_INVALID;
+  if (t.stride[3] != 1) return GEOATTN_ERR_ALIGNMENT;
+  if ((reinterpret_cast<uintptr_t>(t.data) & 15) != 0) return GEOATTN_ERR_ALIGNMENT;
+  for (int i = 0; i < 3; ++i)
+    if (t.stride[i] <= 0 || ((t.stride[i] * 2) & 15) != 0) return GEOATTN_ERR_ALIGNMENT;
+  const uint64_t dims[4] = {(uint64_t)d.D, (uint64_t)d.N, (uint64_t)d.H, (uint64_t)d.B};
+  const uint64_t str[3] = {(uint64_t)t.stride[2] * 2, (uint64_t)t.stride[1] * 2, (uint64_t)t.stride[0] * 2};
+  const uint32_t box[4] = {64, (uint32_t)rows, 1, 1};
+  return make_tmap(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, t.data, dims, str, box) ? GEOATTN_OK : GEOATTN_ERR_TMA;
+}
+
+// TMA map over natural fp32 planes [2][B][H][N][DP] viewed as 4-D (DP, N, H, 2B) (box: 32 x rows).
+int map_planes(CUtensorMap* m, const float* base, const Dims& d, int rows) {
+  const uint64_t dims[4] = {(uint64_t)d.DP, (uint64_t)d.N, (uint64_t)d.H, (uint64_t)(2 * d.B)};
+  const uint64_t str[3] = {(uint64_t)d.DP * 4, (uint64_t)d.N * d.DP * 4, (uint64_t)d.H * d.N * d.DP * 4};
+  const uint32_t box[4] = {32, (uint32_t)rows, 1, 1};
+  return make_tmap(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base, dims, str, box) ? GEOATTN_OK : GEOATTN_ERR_TMA;
+}
+
+// TMA map over a transposed fp32 plane [B][H][DP][NP] viewed as 4-D (NP, DP, H, B) (box: 32 x DP).
+int map_transposed(CUtensorMap* m, const float* base, const Dims& d) {
+  const uint64_t dims[4] = {(uint64_t)d.np, (uint64_t)d.DP, (uint64_t)d.H, (uint64_t)d.B};
+  const uint64_t str[3] = {(uint64_t)d.np * 4, (uint64_t)d.DP * d.np * 4, (uint64_t)d.H * d.DP * d.np * 4};
+  const uint32_t box[4] = {32, (uint32_t)d.DP, 1, 1};
+  return make_tmap(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base, dims, str, box) ? GEOATTN_OK : GEOATTN_ERR_TMA;
+}
+
+int split(const GeoAttnTensor& t, const Dims& d, float* nat, float* tr, cudaStream_t st) {
+  if (!t.data) return GEOATTN_ERR_INVALID;
+  dim3 grid((d.np + 31) / 32, d.DP / 32, d.B * d.H), block(32, 8);
+  split_tf32_kernel<<<grid, block, 0, st>>>(reinterpret_cast<const float*>(t.data), t.stride[0], t.stride[1],
+                                            t.stride[2], t.stride[3], d.B, d.H, d.N, d.D, d.DP, d.np, nat, tr);
+  return cudaGetLastError() == cudaSuccess ? GEOATTN_OK : GEOATTN_ERR_LAUNCH;
+}
+
+KParams base_params(const Dims& d, const float* abg, int per_head, const void* prior) {
+  KParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.B = d.B;
+  p.H = d.H;
+  p.N = d.N;
+  p.D = d.D;
+  p.nrb = d.nrb;
+  p.np = d.np;
+  p.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)d.D));
+  p.inv_sqrt_d = (float)(1.0 / std::sqrt((double)d.D));
+  p.abg = abg;
+  p.per_head = per_head;
+  p.prior = prior;
+  p.priorT = reinterpret_cast<const uint8_t*>(prior) + prior_table_bytes(d);
+  return p;
+}
+
+template <class K>
+int launch(K kernel, int smem, dim3 grid, cudaStream_t st, const TileMaps& maps, const KParams& p) {
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+    return GEOATTN_ERR_LAUNCH;
+  kernel<<<grid, kThreads, smem, st>>>(maps, p);
+  return cudaGetLastError() == cudaSuccess ? GEOATTN_OK : GEOATTN_ERR_LAUNCH;
+}
+
+inline void record(void* const* ev, int i, cudaStream_t st) {
+  if (ev && ev[i]) cudaEventRecord(reinterpret_cast<cudaEvent_t>(ev[i]), st);
+}
+
+template <bool BF16, int DP>
+int run_fwd(const TileMaps& maps, const KParams& p, const Dims& d, cudaStream_t st, void* const* ev) {
+  record(ev, 0, st);
+  int rc = launch(geoattn_fwd_kernel<BF16, DP>, FwdCfg<BF16, DP>::SMEM, dim3(d.nrb, d.B * d.H), st, maps, p);
+  record(ev, 1, st);
+  return rc;
+}
+template <bool BF16, int DP>
+int run_bwd(const TileMaps& rmaps, const TileMaps& cmaps, const KParams& p, const Dims& d, cudaStream_t st,
+            void* const* ev) {
+  record(ev, 0, st);
+  int rc = launch(geoattn_bwd_rows_kernel<BF16, DP>, RowsCfg<BF16, DP>::SMEM, dim3(d.nrb, d.B * d.H), st, rmaps, p);
+  if (rc) return rc;
+  record(ev, 1, st);
+  rc = launch(geoattn_bwd_cols_kernel<BF16, DP>, ColsCfg<BF16, DP>::SMEM, dim3(d.nrb, d.B * d.H), st, cmaps, p);
+  record(ev, 2, st);
+  return rc;
+}
+
+}  // namespace
+}  // namespace geoattn
+
+using namespace geoattn;
+
+extern "C" {
+
+int geoattn_version(void) { return GEOATTN_VERSION; }
+
+const char* geoattn_error_string(int code) {
+  switch (code) {
+    case GEOATTN_OK: return "ok";
+    case GEOATTN_ERR_INVALID: return "invalid argument (null pointer, non-positive size or unknown enum)";
+    case GEOATTN_ERR_UNSUPPORTED: return "unsupported shape/dtype (bf16: head_dim <= 192, fp32: head_dim <= 64)";
+    case GEOATTN_ERR_ALIGNMENT: return "tensor not TMA-compatible (head dim must be contiguous, base and strides 16-byte aligned)";
+    case GEOATTN_ERR_TMA: return "TMA descriptor encoding failed";
+    case GEOATTN_ERR_LAUNCH: return "CUDA kernel launch failed";
+    case GEOATTN_ERR_DEVICE: return "device-side bounded wait expired";
+  }
+  return "unknown geoattn status";
+}
+
+size_t geoattn_prior_bytes(const GeoAttnShape* shape) {
+  Dims d;
+  if (check_shape(shape, d)) return 0;
+  return 2 * prior_table_bytes(d);
+}
+
+int geoattn_prior_from_dense(const GeoAttnShape* shape, const float* dist, long long ld_dist, const float* ang,
+                             long long ld_ang, void* prior, void* stream) {
+  Dims d;
+  if (int rc = check_shape(shape, d)) return rc;
+  if (!dist || !ang || !prior || ld_dist < d.N || ld_ang < d.N) return GEOATTN_ERR_INVALID;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  void* pt = reinterpret_cast<uint8_t*>(prior) + prior_table_bytes(d);
+  dim3 grid(d.np / 32, d.np / 32), block(32, 8);
+  if (d.bf16) prior_dense_kernel<true><<<grid, block, 0, st>>>(dist, ld_dist, ang, ld_ang, d.N, d.np, prior, pt);
+  else prior_dense_kernel<false><<<grid, block, 0, st>>>(dist, ld_dist, ang, ld_ang, d.N, d.np, prior, pt);
+  return cudaGetLastError() == cudaSuccess ? GEOATTN_OK : GEOATTN_ERR_LAUNCH;
+}
+
+int geoattn_prior_from_coords(const GeoAttnShape* shape, const double* lat_deg, const double* lon_deg,
+                              const double* elev_ft, void* prior, float* dist_out, float* ang_out, void* stream) {
+  Dims d;
+  if (int rc = check_shape(shape, d)) return rc;
+  if (!lat_deg || !lon_deg || !elev_ft || (!prior && !dist_out && !ang_out)) return GEOATTN_ERR_INVALID;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  void* pt = prior ? reinterpret_cast<uint8_t*>(prior) + prior_table_bytes(d) : nullptr;
+  dim3 grid(d.np / 32, d.np / 32), block(32, 8);
+  if (d.bf16)
+    prior_coords_kernel<true><<<grid, block, 0, st>>>(lat_deg, lon_deg, elev_ft, d.N, d.np, prior, pt, dist_out, ang_out);
+  else
+    prior_coords_kernel<false><<<grid, block, 0, st>>>(lat_deg, lon_deg, elev_ft, d.N, d.np, prior, pt, dist_out, ang_out);
+  return cudaGetLastError() == cudaSuccess ? GEOATTN_OK : GEOATTN_ERR_LAUNCH;
+}
+
+size_t geoattn_stats_bytes(const GeoAttnShape* shape) {
+  Dims d;
+  if (check_shape(shape, d)) return 0;
+  return (size_t)3 * d.B * d.H * d.N * 4;
+}
+
+size_t geoattn_fwd_workspace_bytes(const GeoAttnShape* shape) {
+  Dims d;
+  if (check_shape(shape, d)) return 0;
+  return fwd_ws(d, nullptr, nullptr);
+}
+
+size_t geoattn_bwd_workspace_bytes(const GeoAttnShape* shape) {
+  Dims d;
+  if (check_shape(shape, d)) return 0;
+  return bwd_ws(d, nullptr, nullptr);
+}
+
+int geoattn_fwd(const GeoAttnFwdArgs* a, void* stream) {
+  if (!a) return GEOATTN_ERR_INVALID;
+  Dims d;
+  if (int rc = check_shape(&a->shape, d)) return rc;
+  if (!a->abg || !a->prior || !a->o || !a->stats || !a->workspace) return GEOATTN_ERR_INVALID;
+  if ((reinterpret_cast<uintptr_t>(a->workspace) & (kAlign - 1)) != 0) return GEOATTN_ERR_ALIGNMENT;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  FwdWs ws;
+  fwd_ws(d, reinterpret_cast<uint8_t*>(a->workspace), &ws);
+  if (cudaMemsetAsync(ws.status, 0, sizeof(int), st) != cudaSuccess) return GEOATTN_ERR_LAUNCH;
+  TileMaps maps;
+  std::memset(&maps, 0, sizeof(maps));
+  int rc;
+  if (d.bf16) {
+    if ((rc = map_user_bf16(&maps.q, a->q, d, kBM)) || (rc = map_user_bf16(&maps.k, a->k, d, 64)) ||
+        (rc = map_user_bf16(&maps.v, a->v, d, 64)))
+      return rc;
+  } else {
+    if ((rc = split(a->q, d, ws.qn, nullptr, st)) || (rc = split(a->k, d, ws.kn, nullptr, st)) ||
+        (rc = split(a->v, d, nullptr, ws.vt, st)))
+      return rc;
+    if ((rc = map_planes(&maps.q, ws.qn, d, kBM)) || (rc = map_planes(&maps.k, ws.kn, d, 32)) ||
+        (rc = map_transposed(&maps.v, ws.vt, d)))
+      return rc;
+  }
+  KParams p = base_params(d, a->abg, a->shape.per_head, a->prior);
+  p.o = a->o;
+  for (int i = 0; i < 4; ++i) p.o_str[i] = a->o_stride[i];
+  p.stats = a->stats;
+  p.status = ws.status;
+  if (d.bf16) {
+    if (d.DP == 64) return run_fwd<true, 64>(maps, p, d, st, a->events);
+    if (d.DP == 128) return run_fwd<true, 128>(maps, p, d, st, a->events);
+    return run_fwd<true, 192>(maps, p, d, st, a->events);
+  }
+  return run_fwd<false, 64>(maps, p, d, st, a->events);
+}
+
+int geoattn_bwd(const GeoAttnBwdArgs* a, void* stream) {
+  if (!a) return GEOATTN_ERR_INVALID;
+  Dims d;
+  if (int rc = check_shape(&a->shape, d)) return rc;
+  if (!a->abg || !a->prior || !a->stats || !a->dq || !a->dk || !a->dv || !a->dabg || !a->workspace ||
+      !a->o.data || !a->dout.data)
+    return GEOATTN_ERR_INVALID;
+  if ((reinterpret_cast<uintptr_t>(a->workspace) & (kAlign - 1)) != 0) return GEOATTN_ERR_ALIGNMENT;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  BwdWs ws;
+  bwd_ws(d, reinterpret_cast<uint8_t*>(a->workspace), &ws);
+  if (cudaMemsetAsync(ws.status, 0, sizeof(int), st) != cudaSuccess) return GEOATTN_ERR_LAUNCH;
+  TileMaps rm, cm;
+  std::memset(&rm, 0, sizeof(rm));
+  std::memset(&cm, 0, sizeof(cm));
+  int rc;
+  if (d.bf16) {
+    if ((rc = map_user_bf16(&rm.q, a->q, d, kBM)) || (rc = map_user_bf16(&rm.dout, a->dout, d, kBM)) ||
+        (rc = map_user_bf16(&rm.k, a->k, d, 64)) || (rc = map_user_bf16(&rm.v, a->v, d, 64)) ||
+        (rc = map_user_bf16(&cm.k, a->k, d, kBM)) || (rc = map_user_bf16(&cm.v, a->v, d, kBM)) ||
+        (rc = map_user_bf16(&cm.q, a->q, d, 64)) || (rc = map_user_bf16(&cm.dout, a->dout, d, 64)))
+      return rc;
+  } else {
+    if ((rc = split(a->q, d, ws.qn, ws.qt, st)) || (rc = split(a->k, d, ws.kn, ws.kt, st)) ||
+        (rc = split(a->v, d, ws.vn, nullptr, st)) || (rc = split(a->dout, d, ws.don, ws.dot, st)))
+      return rc;
+    if ((rc = map_planes(&rm.q, ws.qn, d, kBM)) || (rc = map_planes(&rm.dout, ws.don, d, kBM)) ||
+        (rc = map_planes(&rm.k, ws.kn, d, 32)) || (rc = map_planes(&rm.v, ws.vn, d, 32)) ||
+        (rc = map_transposed(&rm.kt, ws.kt, d)) || (rc = map_planes(&cm.k, ws.kn, d, kBM)) ||
+        (rc = map_planes(&cm.v, ws.vn, d, kBM)) || (rc = map_planes(&cm.q, ws.qn, d, 32)) ||
+        (rc = map_planes(&cm.dout, ws.don, d, 32)) || (rc = map_transposed(&cm.qt, ws.qt, d)) ||
+        (rc = map_transposed(&cm.dot, ws.dot, d)))
+      return rc;
+  }
+  KParams p = base_params(d, a->abg, a->shape.per_head, a->prior);
+  p.o_in = a->o.data;
+  p.dout = a->dout.data;
+  for (int i = 0; i < 4; ++i) {
+    p.oi_str[i] = a->o.stride[i];
+    p.do_str[i] = a->dout.stride[i];
+    p.dq_str[i] = a->dq_stride[i];
+    p.dk_str[i] = a->dk_stride[i];
+    p.dv_str[i] = a->dv_stride[i];
+  }
+  p.dq = a->dq;
+  p.dk = a->dk;
+  p.dv = a->dv;
+  p.stats = const_cast<float*>(a->stats);
+  p.rowrec = ws.rowrec;
+  p.part = ws.part;
+  p.status = ws.status;
+  if (d.bf16) {
+    if (d.DP == 64) rc = run_bwd<true, 64>(rm, cm, p, d, st, a->events);
+    else if (d.DP == 128) rc = run_bwd<true, 128>(rm, cm, p, d, st, a->events);
+    else rc = run_bwd<true, 192>(rm, cm, p, d, st, a->events);
+  } else {
+    rc = run_bwd<false, 64>(rm, cm, p, d, st, a->events);
+  }
+  if (rc) return rc;
+  finalize_abg_kernel<<<dim3(3, d.nabg), 256, 0, st>>>(ws.part, d.B, d.H, d.nrb, a->shape.per_head, a->dabg);
+  return cudaGetLastError() == cudaSuccess ? GEOATTN_OK : GEOATTN_ERR_LAUNCH;
+}
+
+int geoattn_read_status(const void* workspace, int* status, void* stream) {
+  if (!workspace || !status) return GEOATTN_ERR_INVALID;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (cudaMemcpyAsync(status, workspace, sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess)
+    return GEOATTN_ERR_LAUNCH;
+  if (cudaStreamSynchronize(st) != cudaSuccess) return GEOATTN_ERR_LAUNCH;
+  return GEOATTN_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,1011 @@
+// Geo-biased station attention for sm_100a: forward, backward row pass, backward key pass.
+//
+// Operator (fore_swe/custom_encoder_model.py:25-39):
+//   S = Q K^T / sqrt(d);  P1 = softmax(S);  Z = alpha*P1 + beta*Dp + gamma*Ap;  P2 = softmax(Z);  O = P2 V
+// with the geo prior Dp = 1/(1+dist_km), Ap = 1/(1+angle_deg) read from a per-call table (prior.cu).
+//
+// All kernels share one CTA shape: warps 0-3 are the element-wise warps (thread t owns TMEM lane t, i.e. one row
+// of every 128-row accumulator), warp 4 issues TMA loads, warp 5 issues tcgen05.mma. Every MMA is M = 128 with
+// fp32 accumulators in tensor memory. Shared-memory operand tiles use the 128-byte swizzle; one "region" is
+// rows x 128 bytes (64 bf16 or 32 fp32 along the contiguous dimension).
+//
+// Softmax #1 runs in log2 units: t = acc * (log2(e)/sqrt(d)) is formed by one rounded multiply, the same
+// instruction in every pass and kernel, so the backward recomputes exactly the forward's scaled scores.
+// Softmax #2 needs no running max: Z <= c = |alpha|+|beta|+|gamma| whenever dist, ang >= 0, so
+// e = 2^((Z - c) log2 e) lies in (0, 1].
+#pragma once
+#include <cuda_fp16.h>
+
+#include "sm100.cuh"
+
+namespace geoattn {
+
+constexpr int kBM = 128;        // rows per tile (TMEM lanes)
+constexpr int kThreads = 192;   // 4 element-wise warps + TMA warp + MMA warp
+constexpr int kTmaWarp = 4;
+constexpr int kMmaWarp = 5;
+constexpr float kLog2e = 1.4426950408889634f;
+
+__host__ __device__ constexpr int pow2_cols(int n) { return n <= 32 ? 32 : n <= 64 ? 64 : n <= 128 ? 128 : n <= 256 ? 256 : 512; }
+
+// ---------------------------------------------------------------------------------------------------------------
+// Launch parameters shared by the kernels (element strides; pointers are device pointers).
+// ---------------------------------------------------------------------------------------------------------------
+struct KParams {
+  int B, H, N, D;
+  int nrb;              // ceil(N / 128)
+  int np;               // prior table row stride (pairs) = nrb * 128
+  float scale_log2;     // log2(e) / sqrt(D)
+  float inv_sqrt_d;     // 1 / sqrt(D)
+  const float* abg;     // alpha[nabg], beta[nabg], gamma[nabg]
+  int per_head;         // nabg == H (else 1)
+  const void* prior;    // [np][np] pairs (Dp, Ap): half2 (bf16 path) or float2 (fp32 path)
+  const void* priorT;   // transposed table
+  void* o;              // forward output, strides o_str
+  long long o_str[4];
+  const void* o_in;     // backward: forward output (for delta2 = dO . O)
+  long long oi_str[4];
+  const void* dout;     // backward: dO
+  long long do_str[4];
+  void* dq;
+  long long dq_str[4];
+  void* dk;
+  long long dk_str[4];
+  void* dv;
+  long long dv_str[4];
+  float* stats;         // forward -> backward: [3][B*H*N] = m (log2 units), l1, l2
+  float* rowrec;        // backward row records [B*H*N][8] = m, 1/l1, 1/l2, delta1, delta2
+  double* part;         // [B*H*nrb][3] partial d(alpha), d(beta), d(gamma)
+  int* status;          // device status word (0 = ok)
+};
+
+struct Abg {
+  float a, b, g, c;
+};
+__device__ __forceinline__ Abg load_abg(const KParams& p, int h) {
+  const int n = p.per_head ? p.H : 1;
+  const int i = p.per_head ? h : 0;
+  Abg r;
+  r.a = __ldg(p.abg + i);
+  r.b = __ldg(p.abg + n + i);
+  r.g = __ldg(p.abg + 2 * n + i);
+  r.c = fabsf(r.a) + fabsf(r.b) + fabsf(r.g);
+  return r;
+}
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Element-wise warps wait warp-uniformly, so the collective tcgen05.ld that follows is never divergent.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, const WaitCtx& ctx) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity, ctx));
+}
+
+// Named barrier among the 128 element-wise threads only.
+__device__ __forceinline__ void ew_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// Byte offset of 16-byte chunk `q` (0..7) of row `r` inside a 128-byte-swizzled region.
+__device__ __forceinline__ uint32_t sw128(int r, int q) {
+  return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((q ^ (r & 7)) << 4));
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Prior loads: 32 consecutive pairs of one row.
+// ---------------------------------------------------------------------------------------------------------------
+template <bool F16>
+__device__ __forceinline__ void load_prior32(const void* table, int np, int row, int col0, float (&dp)[32],
+                                             float (&ap)[32]) {
+  if constexpr (F16) {
+    const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const __half2*>(table) + (size_t)row * np + col0);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      uint4 u = __ldg(src + i);
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        __half2 h2 = *reinterpret_cast<const __half2*>(&w[k]);
+        float2 f = __half22float2(h2);
+        dp[i * 4 + k] = f.x;
+        ap[i * 4 + k] = f.y;
+      }
+    }
+  } else {
+    const float4* src = reinterpret_cast<const float4*>(reinterpret_cast<const float2*>(table) + (size_t)row * np + col0);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      float4 f = __ldg(src + i);
+      dp[2 * i] = f.x;
+      ap[2 * i] = f.y;
+      dp[2 * i + 1] = f.z;
+      ap[2 * i + 1] = f.w;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Operand staging of element-wise results into a K-major A tile (one 128-byte region, 128 rows).
+// bf16: 32 values = 4 chunks of 8.  fp32 (TF32): 32 values = 8 chunks of 4, rounded to TF32 (nearest).
+// `piece` selects which 32 columns of the 128-byte row (bf16: 0..1; fp32: 0 only).
+// ---------------------------------------------------------------------------------------------------------------
+template <bool BF16>
+__device__ __forceinline__ void stage_row32(uint8_t* region, int row, int piece, const float (&v)[32]) {
+  if constexpr (BF16) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint32_t w[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        __nv_bfloat162 b2 = __floats2bfloat162_rn(v[q * 8 + 2 * k], v[q * 8 + 2 * k + 1]);
+        w[k] = *reinterpret_cast<uint32_t*>(&b2);
+      }
+      *reinterpret_cast<uint4*>(region + sw128(row, piece * 4 + q)) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  } else {
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      float4 f = make_float4(round_tf32(v[q * 4]), round_tf32(v[q * 4 + 1]), round_tf32(v[q * 4 + 2]),
+                             round_tf32(v[q * 4 + 3]));
+      *reinterpret_cast<float4*>(region + sw128(row, q)) = f;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Global stores of one accumulator row (32 values starting at column d0), masked to d < D.
+// ---------------------------------------------------------------------------------------------------------------
+template <bool BF16>
+__device__ __forceinline__ void store_row32(void* base, long long off, long long sd, int d0, int D, const float (&v)[32],
+                                            float scale) {
+  if constexpr (BF16) {
+    __nv_bfloat16* p = reinterpret_cast<__nv_bfloat16*>(base) + off;
+    if (sd == 1 && d0 + 32 <= D && ((reinterpret_cast<uintptr_t>(p + d0) & 15) == 0)) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint32_t w[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          __nv_bfloat162 b2 = __floats2bfloat162_rn(v[q * 8 + 2 * k] * scale, v[q * 8 + 2 * k + 1] * scale);
+          w[k] = *reinterpret_cast<uint32_t*>(&b2);
+        }
+        *reinterpret_cast<uint4*>(p + d0 + q * 8) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (d0 + i < D) p[(d0 + i) * sd] = __float2bfloat16_rn(v[i] * scale);
+    }
+  } else {
+    float* p = reinterpret_cast<float*>(base) + off;
+    if (sd == 1 && d0 + 32 <= D && ((reinterpret_cast<uintptr_t>(p + d0) & 15) == 0)) {
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        *reinterpret_cast<float4*>(p + d0 + q * 4) =
+            make_float4(v[q * 4] * scale, v[q * 4 + 1] * scale, v[q * 4 + 2] * scale, v[q * 4 + 3] * scale);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (d0 + i < D) p[(d0 + i) * sd] = v[i] * scale;
+    }
+  }
+}
+
+template <bool BF16>
+__device__ __forceinline__ float load_elem(const void* base, long long off) {
+  if constexpr (BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(base)[off]);
+  else return reinterpret_cast<const float*>(base)[off];
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Tile configuration. KB = elements per 128-byte row; every key/query chunk is KB wide so that a chunk row of the
+// element-wise outputs (P, dS, P2^T, dS^T) is exactly one swizzle row.
+// ---------------------------------------------------------------------------------------------------------------
+template <bool BF16, int DP_>
+struct Tile {
+  static constexpr bool kBF16 = BF16;
+  static constexpr int DP = DP_;
+  static constexpr int EB = BF16 ? 2 : 4;
+  static constexpr int KB = 128 / EB;       // 64 bf16 / 32 fp32
+  static constexpr int KS = BF16 ? 16 : 8;  // MMA K per instruction
+  static constexpr int NKB = DP / KB;       // 128-byte regions along D
+  static constexpr int CH = KB;             // chunk width (keys or queries)
+  static constexpr int PL = BF16 ? 1 : 2;   // planes of Q, K, V, dO: hi[, lo]
+  static constexpr int NTERM = BF16 ? 1 : 3;
+  static constexpr Kind KIND = BF16 ? Kind::kF16 : Kind::kTF32;
+  static constexpr uint32_t FMT = BF16 ? 1 : 2;
+  static_assert(DP % KB == 0, "padded head dim must be a whole number of 128-byte regions");
+};
+
+// Issue acc[128 x NB] (+)= A[128 x DP] . B[NB x DP]^T, both K-major, regions of 128 x 128 B (A) and NB x 128 B (B).
+// With NTERM == 3 the product is hi*hi + hi*lo + lo*hi (planes 0/1 at a_plane/b_plane byte strides).
+template <class T, int NB>
+__device__ __forceinline__ void mma_qk(uint32_t tmem_acc, uint32_t a_base, uint32_t a_plane, uint32_t b_base,
+                                       uint32_t b_plane) {
+  constexpr uint32_t idesc = instr_desc(T::FMT, 0, 0, 128, NB);
+  constexpr int STEPS = T::DP / T::KS;
+  int first = 1;
+#pragma unroll
+  for (int term = 0; term < T::NTERM; ++term) {
+    const uint32_t ap = (term == 2) ? a_plane : 0;  // (hi,hi), (hi,lo), (lo,hi)
+    const uint32_t bp = (term == 1) ? b_plane : 0;
+#pragma unroll
+    for (int s = 0; s < STEPS; ++s) {
+      const int kb = (s * T::KS) / T::KB;
+      const uint32_t w = (uint32_t)((s * T::KS) % T::KB) * T::EB;
+      const uint64_t ad = smem_desc_sw128(a_base + ap + kb * (128 * 128) + w, 16, 1024);
+      const uint64_t bd = smem_desc_sw128(b_base + bp + kb * (NB * 128) + w, 16, 1024);
+      mma_ss<T::KIND>(tmem_acc, ad, bd, idesc, first ? 0u : 1u);
+      first = 0;
+    }
+  }
+}
+
+// Issue acc[128 x DP] (+)= P[128 x CH] . V where P is one K-major region (128 x 128 B) and V is either
+//   bf16: the natural chunk [CH rows x DP] (MN-major B: regions per 64-wide D block of CH x 128 B), or
+//   fp32: the transposed chunk [DP rows x CH] (K-major B: one region of DP x 128 B).
+template <class T>
+__device__ __forceinline__ void mma_pv(uint32_t tmem_acc, uint32_t p_base, uint32_t v_base, bool accumulate) {
+  constexpr int STEPS = T::CH / T::KS;  // 4
+  if constexpr (T::kBF16) {
+    constexpr uint32_t idesc = instr_desc(T::FMT, 0, 1, 128, T::DP);
+#pragma unroll
+    for (int s = 0; s < STEPS; ++s) {
+      const uint64_t ad = smem_desc_sw128(p_base + s * 32, 16, 1024);
+      const uint64_t bd = smem_desc_sw128(v_base + s * T::KS * 128, T::CH * 128, 1024);
+      mma_ss<T::KIND>(tmem_acc, ad, bd, idesc, (accumulate || s > 0) ? 1u : 0u);
+    }
+  } else {
+    constexpr uint32_t idesc = instr_desc(T::FMT, 0, 0, 128, T::DP);
+#pragma unroll
+    for (int s = 0; s < STEPS; ++s) {
+      const uint64_t ad = smem_desc_sw128(p_base + s * 32, 16, 1024);
+      const uint64_t bd = smem_desc_sw128(v_base + s * 32, 16, 1024);
+      mma_ss<T::KIND>(tmem_acc, ad, bd, idesc, (accumulate || s > 0) ? 1u : 0u);
+    }
+  }
+}
+
+// TMA of one operand tile: `nrows` rows starting at `row0`, all NKB regions, planes 0..npl-1.
+// 4-D maps: (d, n, h, b[+plane*B]) for natural tensors.
+template <class T>
+__device__ __forceinline__ void tma_tile(uint8_t* dst, const CUtensorMap* map, uint64_t* bar, int nrows, int row0,
+                                         int h, int b, int B, int npl) {
+  for (int pl = 0; pl < npl; ++pl)
+    for (int kb = 0; kb < T::NKB; ++kb)
+      tma_load_4d(dst + (size_t)(pl * T::NKB + kb) * nrows * 128, map, bar, kb * T::KB, row0, h, b + pl * B);
+}
+// Transposed fp32 plane chunk: DP rows (d) x 32 columns (n) starting at column n0 -> one region of DP x 128 B.
+__device__ __forceinline__ void tma_tileT(uint8_t* dst, const CUtensorMap* map, uint64_t* bar, int n0, int h, int b) {
+  tma_load_4d(dst, map, bar, n0, 0, h, b);
+}
+
+struct TileMaps {
+  CUtensorMap q, k, v, dout, kt, qt, dot;  // unused entries are left zero
+};
+
+// ===============================================================================================================
+// Forward: one CTA per (128-query row block, b*h). Pass A: row max / sum of softmax #1 over all key chunks.
+// Pass B: recompute S, form P1, Z and e = 2^((Z-c) log2 e), accumulate O += e V and l2 = sum e.
+// ===============================================================================================================
+template <bool BF16, int DP>
+struct FwdCfg : Tile<BF16, DP> {
+  using T = Tile<BF16, DP>;
+  static constexpr int Q_BYTES = kBM * DP * T::EB;          // per plane
+  static constexpr int K_BYTES = T::CH * DP * T::EB;        // per plane per buffer
+  static constexpr int V_BYTES = T::CH * DP * T::EB;        // hi only (natural bf16 / transposed fp32)
+  static constexpr int P_BYTES = kBM * 128;
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_K = OFF_Q + T::PL * Q_BYTES;
+  static constexpr int OFF_V = OFF_K + 2 * T::PL * K_BYTES;
+  static constexpr int OFF_P = OFF_V + 2 * V_BYTES;
+  static constexpr int SMEM = OFF_P + 2 * P_BYTES + 1024;
+  static constexpr int TM_S = 0;
+  static constexpr int TM_O = 2 * T::CH;
+  static constexpr int TMEM_COLS = pow2_cols(2 * T::CH + DP);
+};
+
+template <bool BF16, int DP>
+__global__ void __launch_bounds__(kThreads, 1) geoattn_fwd_kernel(const __grid_constant__ TileMaps maps, const KParams p) {
+  using C = FwdCfg<BF16, DP>;
+  using T = typename C::T;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ uint64_t bar_q, bar_kfull[2], bar_kempty[2], bar_vfull[2], bar_vempty[2], bar_sfull[2], bar_sempty[2],
+      bar_pfull[2], bar_pempty[2], bar_ofull;
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ int abort_flag;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int rb = blockIdx.x, bh = blockIdx.y, b = bh / p.H, h = bh % p.H;
+  const int nchunks = (p.N + T::CH - 1) / T::CH;
+  WaitCtx ctx{&abort_flag, p.status};
+
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    mbar_init(&bar_q, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bar_kfull[i], 1);
+      mbar_init(&bar_kempty[i], 1);
+      mbar_init(&bar_vfull[i], 1);
+      mbar_init(&bar_vempty[i], 1);
+      mbar_init(&bar_sfull[i], 1);
+      mbar_init(&bar_sempty[i], 128);
+      mbar_init(&bar_pfull[i], 128);
+      mbar_init(&bar_pempty[i], 1);
+    }
+    mbar_init(&bar_ofull, 1);
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(&tmem_base_sh, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base_sh;
+  const uint32_t sbase = smem_u32(smem);
+
+  if (warp == kTmaWarp) {
+    if (lane == 0) {
+      prefetch_tmap(&maps.q);
+      prefetch_tmap(&maps.k);
+      prefetch_tmap(&maps.v);
+      mbar_arrive_expect_tx(&bar_q, T::PL * C::Q_BYTES);
+      tma_tile<T>(smem + C::OFF_Q, &maps.q, &bar_q, kBM, rb * kBM, h, b, p.B, T::PL);
+      int kc = 0, vc = 0;
+      bool ok = true;
+      for (int pass = 0; pass < 2 && ok; ++pass) {
+        for (int c = 0; c < nchunks && ok; ++c) {
+          const int ks = kc & 1;
+          if (!(ok = mbar_wait(&bar_kempty[ks], ((kc >> 1) & 1) ^ 1, ctx))) break;
+          mbar_arrive_expect_tx(&bar_kfull[ks], T::PL * C::K_BYTES);
+          tma_tile<T>(smem + C::OFF_K + ks * T::PL * C::K_BYTES, &maps.k, &bar_kfull[ks], T::CH, c * T::CH, h, b, p.B,
+                      T::PL);
+          ++kc;
+          if (pass == 1) {
+            const int vs = vc & 1;
+            if (!(ok = mbar_wait(&bar_vempty[vs], ((vc >> 1) & 1) ^ 1, ctx))) break;
+            mbar_arrive_expect_tx(&bar_vfull[vs], C::V_BYTES);
+            if constexpr (BF16)
+              tma_tile<T>(smem + C::OFF_V + vs * C::V_BYTES, &maps.v, &bar_vfull[vs], T::CH, c * T::CH, h, b, p.B, 1);
+            else
+              tma_tileT(smem + C::OFF_V + vs * C::V_BYTES, &maps.v, &bar_vfull[vs], c * T::CH, h, b);
+            ++vc;
+          }
+        }
+      }
+    }
+  } else if (warp == kMmaWarp) {
+    if (lane == 0) {
+      int kc = 0, sc = 0, pc = 0;
+      bool ok = mbar_wait(&bar_q, 0, ctx);
+      auto issue_s = [&](void) -> bool {
+        const int ks = kc & 1, ss = sc & 1;
+        if (!mbar_wait(&bar_kfull[ks], (kc >> 1) & 1, ctx)) return false;
+        if (!mbar_wait(&bar_sempty[ss], ((sc >> 1) & 1) ^ 1, ctx)) return false;
+        tc_fence_after();
+        mma_qk<T, T::CH>(tmem + C::TM_S + ss * T::CH, sbase + C::OFF_Q, C::Q_BYTES,
+                         sbase + C::OFF_K + ks * T::PL * C::K_BYTES, C::K_BYTES);
+        mma_commit(&bar_sfull[ss]);
+        mma_commit(&bar_kempty[ks]);
+        ++kc;
+        ++sc;
+        return true;
+      };
+      for (int c = 0; c < nchunks && ok; ++c) ok = issue_s();
+      if (ok) ok = issue_s();
+      for (int c = 0; c < nchunks && ok; ++c) {
+        if (c + 1 < nchunks && !(ok = issue_s())) break;
+        const int ps = pc & 1;
+        if (!(ok = mbar_wait(&bar_pfull[ps], (pc >> 1) & 1, ctx))) break;
+        if (!(ok = mbar_wait(&bar_vfull[ps], (pc >> 1) & 1, ctx))) break;
+        tc_fence_after();
+        mma_pv<T>(tmem + C::TM_O, sbase + C::OFF_P + ps * C::P_BYTES, sbase + C::OFF_V + ps * C::V_BYTES, c > 0);
+        mma_commit(&bar_pempty[ps]);
+        mma_commit(&bar_vempty[ps]);
+        ++pc;
+      }
+      if (ok) mma_commit(&bar_ofull);
+    }
+  } else {
+    // ---------------- element-wise warps ----------------
+    const int r = threadIdx.x;  // 0..127
+    const int row = rb * kBM + r;
+    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+    const Abg ab = load_abg(p, h);
+    const float sc_l2 = p.scale_log2;
+    float m = -INFINITY, l = 0.f;
+    int sc = 0;
+    bool ok = true;
+    // Pass A
+    for (int c = 0; c < nchunks && ok; ++c) {
+      const int ss = sc & 1;
+      if (!(ok = warp_wait(&bar_sfull[ss], (sc >> 1) & 1, ctx))) break;
+      tc_fence_after();
+#pragma unroll
+      for (int piece = 0; piece < T::CH / 32; ++piece) {
+        float v[32];
+        tmem_ld32(lane_base + C::TM_S + ss * T::CH + piece * 32, v);
+        const int col0 = c * T::CH + piece * 32;
+        float mx = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          v[j] = (col0 + j < p.N) ? v[j] * sc_l2 : -INFINITY;
+          mx = fmaxf(mx, v[j]);
+        }
+        const float mn = fmaxf(m, mx);
+        float s = 0.f;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) s += ex2(v[j] - mn);
+        l = l * ex2(m - mn) + s;
+        m = mn;
+      }
+      tc_fence_before();
+      mbar_arrive(&bar_sempty[ss]);
+      ++sc;
+    }
+    const float inv_l1 = __frcp_rn(l);
+    const float aL = ab.a * kLog2e, bL = ab.b * kLog2e, gL = ab.g * kLog2e, cL = ab.c * kLog2e;
+    const int prow = row < p.np ? row : 0;
+    float l2 = 0.f;
+    int pc = 0;
+    // Pass B
+    for (int c = 0; c < nchunks && ok; ++c) {
+      const int ss = sc & 1, ps = pc & 1;
+      if (!(ok = warp_wait(&bar_sfull[ss], (sc >> 1) & 1, ctx))) break;
+      if (!(ok = warp_wait(&bar_pempty[ps], ((pc >> 1) & 1) ^ 1, ctx))) break;
+      tc_fence_after();
+      uint8_t* preg = smem + C::OFF_P + ps * C::P_BYTES;
+#pragma unroll
+      for (int piece = 0; piece < T::CH / 32; ++piece) {
+        float v[32], dp[32], ap[32];
+        tmem_ld32(lane_base + C::TM_S + ss * T::CH + piece * 32, v);
+        const int col0 = c * T::CH + piece * 32;
+        load_prior32<BF16>(p.prior, p.np, prow, col0, dp, ap);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float t = v[j] * sc_l2;
+          const float p1 = ex2(t - m) * inv_l1;
+          const float z2 = fmaf(aL, p1, fmaf(bL, dp[j], fmaf(gL, ap[j], -cL)));
+          const float e = (col0 + j < p.N) ? ex2(z2) : 0.f;
+          l2 += e;
+          v[j] = e;
+        }
+        stage_row32<BF16>(preg, r, piece, v);
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&bar_pfull[ps]);
+      mbar_arrive(&bar_sempty[ss]);
+      ++sc;
+      ++pc;
+    }
+    if (ok) ok = warp_wait(&bar_ofull, 0, ctx);
+    tc_fence_after();
+    if (ok) {
+      const float inv_l2 = __frcp_rn(l2);
+      const long long ooff = (long long)b * p.o_str[0] + (long long)h * p.o_str[1] + (long long)row * p.o_str[2];
+#pragma unroll
+      for (int d0 = 0; d0 < DP; d0 += 32) {
+        float v[32];
+        tmem_ld32(lane_base + C::TM_O + d0, v);
+        if (row < p.N && d0 < p.D) store_row32<BF16>(p.o, ooff, p.o_str[3], d0, p.D, v, inv_l2);
+      }
+      if (row < p.N) {
+        const size_t s = (size_t)bh * p.N + row, n = (size_t)p.B * p.H * p.N;
+        p.stats[s] = m;
+        p.stats[n + s] = l;
+        p.stats[2 * n + s] = l2;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, C::TMEM_COLS);
+}
+
+// ===============================================================================================================
+// Backward row pass: one CTA per (128-query row block, b*h).
+// Sweep 1 recomputes S, dP = dO V^T, P1, P2 and accumulates, per row, with the shift delta2' = dO.O:
+//   r = sum w, a = sum w P1, b = sum P2 P1, c = sum w Dp, e = sum P2 Dp, f = sum w Ap, g = sum P2 Ap,
+//   where w = P2 (dP - delta2').  Then delta2 = delta2' + r (so rowsum(dZ) vanishes, as with
+//   delta2 = rowsum(P2 dP2) recomputed from tiles), and with dZ = w - r P2:
+//   sum dZ P1 = a - r b,  sum dZ Dp = c - r e,  sum dZ Ap = f - r g,  delta1 = alpha (a - r b).
+// Sweep 2 recomputes the tiles again, forms dS = P1 (alpha dZ - delta1) and accumulates dQ += dS K.
+// ===============================================================================================================
+template <bool BF16, int DP>
+struct RowsCfg : Tile<BF16, DP> {
+  using T = Tile<BF16, DP>;
+  static constexpr int Q_BYTES = kBM * DP * T::EB;    // per plane (Q and dO)
+  static constexpr int K_BYTES = T::CH * DP * T::EB;  // per plane per buffer (K and V chunks)
+  static constexpr int KT_BYTES = BF16 ? 0 : DP * 128;  // fp32: transposed K chunk (hi) for dQ
+  static constexpr int DS_BYTES = kBM * 128;
+  static constexpr int NDS = BF16 ? 2 : 1;            // dS / K^T buffers
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_DO = OFF_Q + T::PL * Q_BYTES;
+  static constexpr int OFF_K = OFF_DO + T::PL * Q_BYTES;
+  static constexpr int OFF_V = OFF_K + 2 * T::PL * K_BYTES;
+  static constexpr int OFF_KT = OFF_V + 2 * T::PL * K_BYTES;
+  static constexpr int OFF_DS = OFF_KT + NDS * KT_BYTES;
+  static constexpr int SMEM = OFF_DS + NDS * DS_BYTES + 1024;
+  static constexpr int TM_S = 0;                   // 2 buffers
+  static constexpr int TM_DP = 2 * T::CH;          // 2 buffers
+  static constexpr int TM_DQ = 4 * T::CH;
+  static constexpr int TMEM_COLS = pow2_cols(4 * T::CH + DP);
+};
+
+template <bool BF16, int DP>
+__global__ void __launch_bounds__(kThreads, 1) geoattn_bwd_rows_kernel(const __grid_constant__ TileMaps maps, const KParams p) {
+  using C = RowsCfg<BF16, DP>;
+  using T = typename C::T;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ uint64_t bar_q, bar_kfull[2], bar_kempty[2], bar_vfull[2], bar_vempty[2], bar_sfull[2], bar_sempty[2],
+      bar_dsfull[2], bar_dsempty[2], bar_ktfull[2], bar_ktempty[2], bar_dqfull;
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ int abort_flag;
+  __shared__ double red[4][3];
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int rb = blockIdx.x, bh = blockIdx.y, b = bh / p.H, h = bh % p.H;
+  const int nchunks = (p.N + T::CH - 1) / T::CH;
+  WaitCtx ctx{&abort_flag, p.status};
+
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    mbar_init(&bar_q, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bar_kfull[i], 1);
+      mbar_init(&bar_kempty[i], 1);
+      mbar_init(&bar_vfull[i], 1);
+      mbar_init(&bar_vempty[i], 1);
+      mbar_init(&bar_sfull[i], 1);
+      mbar_init(&bar_sempty[i], 128);
+      mbar_init(&bar_dsfull[i], 128);
+      mbar_init(&bar_dsempty[i], 1);
+      mbar_init(&bar_ktfull[i], 1);
+      mbar_init(&bar_ktempty[i], 1);
+    }
+    mbar_init(&bar_dqfull, 1);
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(&tmem_base_sh, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base_sh;
+  const uint32_t sbase = smem_u32(smem);
+
+  if (warp == kTmaWarp) {
+    if (lane == 0) {
+      prefetch_tmap(&maps.q);
+      prefetch_tmap(&maps.k);
+      prefetch_tmap(&maps.v);
+      prefetch_tmap(&maps.dout);
+      mbar_arrive_expect_tx(&bar_q, 2 * T::PL * C::Q_BYTES);
+      tma_tile<T>(smem + C::OFF_Q, &maps.q, &bar_q, kBM, rb * kBM, h, b, p.B, T::PL);
+      tma_tile<T>(smem + C::OFF_DO, &maps.dout, &bar_q, kBM, rb * kBM, h, b, p.B, T::PL);
+      int kc = 0, tc = 0;
+      bool ok = true;
+      for (int sweep = 0; sweep < 2 && ok; ++sweep) {
+        for (int c = 0; c < nchunks && ok; ++c) {
+          const int ks = kc & 1;
+          if (!(ok = mbar_wait(&bar_kempty[ks], ((kc >> 1) & 1) ^ 1, ctx))) break;
+          mbar_arrive_expect_tx(&bar_kfull[ks], T::PL * C::K_BYTES);
+          tma_tile<T>(smem + C::OFF_K + ks * T::PL * C::K_BYTES, &maps.k, &bar_kfull[ks], T::CH, c * T::CH, h, b, p.B,
+                      T::PL);
+          if (!(ok = mbar_wait(&bar_vempty[ks], ((kc >> 1) & 1) ^ 1, ctx))) break;
+          mbar_arrive_expect_tx(&bar_vfull[ks], T::PL * C::K_BYTES);
+          tma_tile<T>(smem + C::OFF_V + ks * T::PL * C::K_BYTES, &maps.v, &bar_vfull[ks], T::CH, c * T::CH, h, b, p.B,
+                      T::PL);
+          ++kc;
+          if constexpr (!BF16) {
+            if (sweep == 1) {
+              const int ts = tc % C::NDS;
+              if (!(ok = mbar_wait(&bar_ktempty[ts], ((tc / C::NDS) & 1) ^ 1, ctx))) break;
+              mbar_arrive_expect_tx(&bar_ktfull[ts], C::KT_BYTES);
+              tma_tileT(smem + C::OFF_KT + ts * C::KT_BYTES, &maps.kt, &bar_ktfull[ts], c * T::CH, h, b);
+              ++tc;
+            }
+          }
+        }
+      }
+    }
+  } else if (warp == kMmaWarp) {
+    if (lane == 0) {
+      int kc = 0, sc = 0, dc = 0;
+      bool ok = mbar_wait(&bar_q, 0, ctx);
+      auto issue = [&](bool release_k) -> bool {
+        const int ks = kc & 1, ss = sc & 1;
+        if (!mbar_wait(&bar_kfull[ks], (kc >> 1) & 1, ctx)) return false;
+        if (!mbar_wait(&bar_vfull[ks], (kc >> 1) & 1, ctx)) return false;
+        if (!mbar_wait(&bar_sempty[ss], ((sc >> 1) & 1) ^ 1, ctx)) return false;
+        tc_fence_after();
+        const uint32_t kb = sbase + C::OFF_K + ks * T::PL * C::K_BYTES;
+        const uint32_t vb = sbase + C::OFF_V + ks * T::PL * C::K_BYTES;
+        mma_qk<T, T::CH>(tmem + C::TM_S + ss * T::CH, sbase + C::OFF_Q, C::Q_BYTES, kb, C::K_BYTES);
+        mma_qk<T, T::CH>(tmem + C::TM_DP + ss * T::CH, sbase + C::OFF_DO, C::Q_BYTES, vb, C::K_BYTES);
+        mma_commit(&bar_sfull[ss]);
+        mma_commit(&bar_vempty[ks]);
+        if (release_k) mma_commit(&bar_kempty[ks]);
+        ++kc;
+        ++sc;
+        return true;
+      };
+      for (int c = 0; c < nchunks && ok; ++c) ok = issue(true);
+      const int kc0 = kc;  // first K use of sweep 2
+      if (ok) ok = issue(false);
+      for (int c = 0; c < nchunks && ok; ++c) {
+        if (c + 1 < nchunks && !(ok = issue(false))) break;
+        const int ds = dc % C::NDS;
+        if (!(ok = mbar_wait(&bar_dsfull[ds], (dc / C::NDS) & 1, ctx))) break;
+        const int ks = (kc0 + c) & 1;
+        uint32_t bsrc;
+        if constexpr (BF16) {
+          bsrc = sbase + C::OFF_K + ks * T::PL * C::K_BYTES;
+        } else {
+          if (!(ok = mbar_wait(&bar_ktfull[ds], (dc / C::NDS) & 1, ctx))) break;
+          bsrc = sbase + C::OFF_KT + ds * C::KT_BYTES;
+        }
+        tc_fence_after();
+        mma_pv<T>(tmem + C::TM_DQ, sbase + C::OFF_DS + ds * C::DS_BYTES, bsrc, c > 0);
+        mma_commit(&bar_dsempty[ds]);
+        if constexpr (!BF16) mma_commit(&bar_ktempty[ds]);
+        mma_commit(&bar_kempty[ks]);
+        ++dc;
+      }
+      if (ok) mma_commit(&bar_dqfull);
+    }
+  } else {
+    // ---------------- element-wise warps ----------------
+    const int r = threadIdx.x;
+    const int row = rb * kBM + r;
+    const bool valid = row < p.N;
+    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+    const Abg ab = load_abg(p, h);
+    const float sc_l2 = p.scale_log2;
+    const size_t nrows_all = (size_t)p.B * p.H * p.N;
+    const size_t srow = (size_t)bh * p.N + (valid ? row : 0);
+    float m = 0.f, inv_l1 = 0.f, inv_l2 = 0.f, d2s = 0.f;
+    if (valid) {
+      m = p.stats[srow];
+      inv_l1 = __frcp_rn(p.stats[nrows_all + srow]);
+      inv_l2 = __frcp_rn(p.stats[2 * nrows_all + srow]);
+      const long long oo = (long long)b * p.oi_str[0] + (long long)h * p.oi_str[1] + (long long)row * p.oi_str[2];
+      const long long od = (long long)b * p.do_str[0] + (long long)h * p.do_str[1] + (long long)row * p.do_str[2];
+      for (int d = 0; d < p.D; ++d)
+        d2s = fmaf(load_elem<BF16>(p.dout, od + d * p.do_str[3]), load_elem<BF16>(p.o_in, oo + d * p.oi_str[3]), d2s);
+    }
+    const float aL = ab.a * kLog2e, bL = ab.b * kLog2e, gL = ab.g * kLog2e, cL = ab.c * kLog2e;
+    const int prow = row < p.np ? row : 0;
+    float sr = 0.f, sa = 0.f, sb = 0.f, scc = 0.f, se = 0.f, sf = 0.f, sg = 0.f;
+    int sc = 0;
+    bool ok = true;
+    for (int c = 0; c < nchunks && ok; ++c) {
+      const int ss = sc & 1;
+      if (!(ok = warp_wait(&bar_sfull[ss], (sc >> 1) & 1, ctx))) break;
+      tc_fence_after();
+#pragma unroll 1
+      for (int piece = 0; piece < T::CH / 32; ++piece) {
+        float v[32], w[32];
+        tmem_ld32(lane_base + C::TM_S + ss * T::CH + piece * 32, v);
+        tmem_ld32(lane_base + C::TM_DP + ss * T::CH + piece * 32, w);
+        const int col0 = c * T::CH + piece * 32;
+        float dp[32], ap[32];
+        load_prior32<BF16>(p.prior, p.np, prow, col0, dp, ap);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const bool cv = col0 + j < p.N;
+          const float t = v[j] * sc_l2;
+          const float p1 = cv ? ex2(t - m) * inv_l1 : 0.f;
+          const float z2 = fmaf(aL, p1, fmaf(bL, dp[j], fmaf(gL, ap[j], -cL)));
+          const float p2 = cv ? ex2(z2) * inv_l2 : 0.f;
+          const float wv = p2 * (w[j] - d2s);
+          sr += wv;
+          sa = fmaf(wv, p1, sa);
+          sb = fmaf(p2, p1, sb);
+          scc = fmaf(wv, dp[j], scc);
+          se = fmaf(p2, dp[j], se);
+          sf = fmaf(wv, ap[j], sf);
+          sg = fmaf(p2, ap[j], sg);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&bar_sempty[ss]);
+      ++sc;
+    }
+    const float delta2 = d2s + sr;
+    const float ta = fmaf(-sr, sb, sa);
+    const float delta1 = ab.a * ta;
+    double ga = valid ? (double)ta : 0.0, gb = valid ? (double)fmaf(-sr, se, scc) : 0.0,
+           gg = valid ? (double)fmaf(-sr, sg, sf) : 0.0;
+    if (valid && ok) {
+      float* rec = p.rowrec + srow * 8;
+      *reinterpret_cast<float4*>(rec) = make_float4(m, inv_l1, inv_l2, delta1);
+      *reinterpret_cast<float4*>(rec + 4) = make_float4(delta2, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      ga += __shfl_down_sync(0xffffffffu, ga, off);
+      gb += __shfl_down_sync(0xffffffffu, gb, off);
+      gg += __shfl_down_sync(0xffffffffu, gg, off);
+    }
+    if (lane == 0) {
+      red[warp][0] = ga;
+      red[warp][1] = gb;
+      red[warp][2] = gg;
+    }
+    ew_sync();
+    if (threadIdx.x == 0) {
+      double* out = p.part + ((size_t)bh * p.nrb + rb) * 3;
+      out[0] = (red[0][0] + red[1][0]) + (red[2][0] + red[3][0]);
+      out[1] = (red[0][1] + red[1][1]) + (red[2][1] + red[3][1]);
+      out[2] = (red[0][2] + red[1][2]) + (red[2][2] + red[3][2]);
+    }
+    // Sweep 2
+    int dc = 0;
+    for (int c = 0; c < nchunks && ok; ++c) {
+      const int ss = sc & 1, ds = dc % C::NDS;
+      if (!(ok = warp_wait(&bar_sfull[ss], (sc >> 1) & 1, ctx))) break;
+      if (!(ok = warp_wait(&bar_dsempty[ds], ((dc / C::NDS) & 1) ^ 1, ctx))) break;
+      tc_fence_after();
+      uint8_t* dreg = smem + C::OFF_DS + ds * C::DS_BYTES;
+#pragma unroll 1
+      for (int piece = 0; piece < T::CH / 32; ++piece) {
+        float v[32], w[32];
+        tmem_ld32(lane_base + C::TM_S + ss * T::CH + piece * 32, v);
+        tmem_ld32(lane_base + C::TM_DP + ss * T::CH + piece * 32, w);
+        const int col0 = c * T::CH + piece * 32;
+        float dp[32], ap[32];
+        load_prior32<BF16>(p.prior, p.np, prow, col0, dp, ap);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const bool cv = col0 + j < p.N;
+          const float t = v[j] * sc_l2;
+          const float p1 = cv ? ex2(t - m) * inv_l1 : 0.f;
+          const float z2 = fmaf(aL, p1, fmaf(bL, dp[j], fmaf(gL, ap[j], -cL)));
+          const float p2 = cv ? ex2(z2) * inv_l2 : 0.f;
+          const float dz = p2 * (w[j] - delta2);
+          v[j] = p1 * fmaf(ab.a, dz, -delta1);
+        }
+        stage_row32<BF16>(dreg, r, piece, v);
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&bar_dsfull[ds]);
+      mbar_arrive(&bar_sempty[ss]);
+      ++sc;
+      ++dc;
+    }
+    if (ok) ok = warp_wait(&bar_dqfull, 0, ctx);
+    tc_fence_after();
+    if (ok) {
+      const long long qoff = (long long)b * p.dq_str[0] + (long long)h * p.dq_str[1] + (long long)row * p.dq_str[2];
+#pragma unroll 1
+      for (int d0 = 0; d0 < DP; d0 += 32) {
+        float v[32];
+        tmem_ld32(lane_base + C::TM_DQ + d0, v);  // collective: every lane loads, valid rows store
+        if (valid && d0 < p.D) store_row32<BF16>(p.dq, qoff, p.dq_str[3], d0, p.D, v, p.inv_sqrt_d);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, C::TMEM_COLS);
+}
+
+// ===============================================================================================================
+// Backward key pass: one CTA per (128-key block, b*h); keys on TMEM lanes. For each chunk of CH queries:
+//   S^T = K Q^T, dP^T = V dO^T; P1, P2, dZ, dS from the row records; dV += P2^T dO, dK += dS^T Q.
+// ===============================================================================================================
+template <bool BF16, int DP>
+struct ColsCfg : Tile<BF16, DP> {
+  using T = Tile<BF16, DP>;
+  static constexpr int NB = (BF16 && DP <= 128) ? 2 : 1;   // buffers for query chunks / staged tiles / S^T
+  static constexpr int K_BYTES = kBM * DP * T::EB;          // per plane (K and V blocks)
+  static constexpr int Q_BYTES = T::CH * DP * T::EB;        // per plane per buffer (Q and dO chunks)
+  static constexpr int QT_BYTES = BF16 ? 0 : DP * 128;      // fp32: transposed Q / dO chunk (hi)
+  static constexpr int ST_BYTES = kBM * 128;                // P2^T or dS^T tile
+  static constexpr int OFF_K = 0;
+  static constexpr int OFF_V = OFF_K + T::PL * K_BYTES;
+  static constexpr int OFF_Q = OFF_V + T::PL * K_BYTES;
+  static constexpr int OFF_DO = OFF_Q + NB * T::PL * Q_BYTES;
+  static constexpr int OFF_QT = OFF_DO + NB * T::PL * Q_BYTES;
+  static constexpr int OFF_DOT = OFF_QT + NB * QT_BYTES;
+  static constexpr int OFF_P2 = OFF_DOT + NB * QT_BYTES;
+  static constexpr int OFF_DS = OFF_P2 + NB * ST_BYTES;
+  static constexpr int SMEM = OFF_DS + NB * ST_BYTES + 1024;
+  static constexpr int TM_S = 0;
+  static constexpr int TM_DP = NB * T::CH;
+  static constexpr int TM_DK = 2 * NB * T::CH;
+  static constexpr int TM_DV = TM_DK + DP;
+  static constexpr int TMEM_COLS = pow2_cols(2 * NB * T::CH + 2 * DP);
+};
+
+template <bool BF16, int DP>
+__global__ void __launch_bounds__(kThreads, 1) geoattn_bwd_cols_kernel(const __grid_constant__ TileMaps maps, const KParams p) {
+  using C = ColsCfg<BF16, DP>;
+  using T = typename C::T;
+  constexpr int NB = C::NB;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ uint64_t bar_kv, bar_qfull[2], bar_qempty[2], bar_sfull[2], bar_sempty[2], bar_tfull[2], bar_tempty[2],
+      bar_done;
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ int abort_flag;
+  __shared__ __align__(16) float rec_sh[2][T::CH][8];
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int kblk = blockIdx.x, bh = blockIdx.y, b = bh / p.H, h = bh % p.H;
+  const int nchunks = (p.N + T::CH - 1) / T::CH;
+  WaitCtx ctx{&abort_flag, p.status};
+
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    mbar_init(&bar_kv, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bar_qfull[i], 1);
+      mbar_init(&bar_qempty[i], 1);
+      mbar_init(&bar_sfull[i], 1);
+      mbar_init(&bar_sempty[i], 128);
+      mbar_init(&bar_tfull[i], 128);
+      mbar_init(&bar_tempty[i], 1);
+    }
+    mbar_init(&bar_done, 1);
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(&tmem_base_sh, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base_sh;
+  const uint32_t sbase = smem_u32(smem);
+
+  if (warp == kTmaWarp) {
+    if (lane == 0) {
+      prefetch_tmap(&maps.q);
+      prefetch_tmap(&maps.k);
+      prefetch_tmap(&maps.v);
+      prefetch_tmap(&maps.dout);
+      mbar_arrive_expect_tx(&bar_kv, 2 * T::PL * C::K_BYTES);
+      tma_tile<T>(smem + C::OFF_K, &maps.k, &bar_kv, kBM, kblk * kBM, h, b, p.B, T::PL);
+      tma_tile<T>(smem + C::OFF_V, &maps.v, &bar_kv, kBM, kblk * kBM, h, b, p.B, T::PL);
+      for (int c = 0; c < nchunks; ++c) {
+        const int qs = c % NB;
+        if (!mbar_wait(&bar_qempty[qs], ((c / NB) & 1) ^ 1, ctx)) break;
+        mbar_arrive_expect_tx(&bar_qfull[qs], 2 * T::PL * C::Q_BYTES + 2 * C::QT_BYTES);
+        tma_tile<T>(smem + C::OFF_Q + qs * T::PL * C::Q_BYTES, &maps.q, &bar_qfull[qs], T::CH, c * T::CH, h, b, p.B,
+                    T::PL);
+        tma_tile<T>(smem + C::OFF_DO + qs * T::PL * C::Q_BYTES, &maps.dout, &bar_qfull[qs], T::CH, c * T::CH, h, b,
+                    p.B, T::PL);
+        if constexpr (!BF16) {
+          tma_tileT(smem + C::OFF_QT + qs * C::QT_BYTES, &maps.qt, &bar_qfull[qs], c * T::CH, h, b);
+          tma_tileT(smem + C::OFF_DOT + qs * C::QT_BYTES, &maps.dot, &bar_qfull[qs], c * T::CH, h, b);
+        }
+      }
+    }
+  } else if (warp == kMmaWarp) {
+    if (lane == 0) {
+      bool ok = mbar_wait(&bar_kv, 0, ctx);
+      auto issue_s = [&](int c) -> bool {
+        const int qs = c % NB;
+        if (!mbar_wait(&bar_qfull[qs], (c / NB) & 1, ctx)) return false;
+        if (!mbar_wait(&bar_sempty[qs], ((c / NB) & 1) ^ 1, ctx)) return false;
+        tc_fence_after();
+        mma_qk<T, T::CH>(tmem + C::TM_S + qs * T::CH, sbase + C::OFF_K, C::K_BYTES,
+                         sbase + C::OFF_Q + qs * T::PL * C::Q_BYTES, C::Q_BYTES);
+        mma_qk<T, T::CH>(tmem + C::TM_DP + qs * T::CH, sbase + C::OFF_V, C::K_BYTES,
+                         sbase + C::OFF_DO + qs * T::PL * C::Q_BYTES, C::Q_BYTES);
+        mma_commit(&bar_sfull[qs]);
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      for (int c = 0; c < nchunks && ok; ++c) {
+        if (NB == 2 && c + 1 < nchunks && !(ok = issue_s(c + 1))) break;
+        const int qs = c % NB;
+        if (!(ok = mbar_wait(&bar_tfull[qs], (c / NB) & 1, ctx))) break;
+        tc_fence_after();
+        uint32_t dob, qb;
+        if constexpr (BF16) {
+          dob = sbase + C::OFF_DO + qs * C::Q_BYTES;
+          qb = sbase + C::OFF_Q + qs * C::Q_BYTES;
+        } else {
+          dob = sbase + C::OFF_DOT + qs * C::QT_BYTES;
+          qb = sbase + C::OFF_QT + qs * C::QT_BYTES;
+        }
+        mma_pv<T>(tmem + C::TM_DV, sbase + C::OFF_P2 + qs * C::ST_BYTES, dob, c > 0);
+        mma_pv<T>(tmem + C::TM_DK, sbase + C::OFF_DS + qs * C::ST_BYTES, qb, c > 0);
+        mma_commit(&bar_tempty[qs]);
+        mma_commit(&bar_qempty[qs]);
+        if (NB == 1 && c + 1 < nchunks && !(ok = issue_s(c + 1))) break;
+      }
+      if (ok) mma_commit(&bar_done);
+    }
+  } else {
+    // ---------------- element-wise warps: thread = key ----------------
+    const int r = threadIdx.x;
+    const int key = kblk * kBM + r;
+    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+    const Abg ab = load_abg(p, h);
+    const float sc_l2 = p.scale_log2;
+    const float aL = ab.a * kLog2e, bL = ab.b * kLog2e, gL = ab.g * kLog2e, cL = ab.c * kLog2e;
+    const int pkey = key < p.np ? key : 0;
+    const bool kvalid = key < p.N;
+    bool ok = true;
+    for (int c = 0; c < nchunks; ++c) {
+      const int qs = c % NB;
+      // row records of this query chunk -> shared memory (double-buffered by chunk parity). The named barrier is
+      // reached once per chunk by every element-wise thread, also after an abort, so it can never wait forever.
+      float(*rec)[8] = rec_sh[c & 1];
+      if (r < T::CH) {
+        const int q = c * T::CH + r;
+        float4 a = make_float4(0.f, 0.f, 0.f, 0.f), bb = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (q < p.N) {
+          const float* src = p.rowrec + ((size_t)bh * p.N + q) * 8;
+          a = *reinterpret_cast<const float4*>(src);
+          bb = *reinterpret_cast<const float4*>(src + 4);
+        }
+        *reinterpret_cast<float4*>(&rec[r][0]) = a;
+        *reinterpret_cast<float4*>(&rec[r][4]) = bb;
+      }
+      ew_sync();
+      if (!ok) continue;
+      if (!(ok = warp_wait(&bar_sfull[qs], (c / NB) & 1, ctx))) continue;
+      if (!(ok = warp_wait(&bar_tempty[qs], ((c / NB) & 1) ^ 1, ctx))) continue;
+      tc_fence_after();
+      uint8_t* p2reg = smem + C::OFF_P2 + qs * C::ST_BYTES;
+      uint8_t* dsreg = smem + C::OFF_DS + qs * C::ST_BYTES;
+#pragma unroll 1
+      for (int piece = 0; piece < T::CH / 32; ++piece) {
+        float v[32], w[32], dp[32], ap[32];
+        tmem_ld32(lane_base + C::TM_S + qs * T::CH + piece * 32, v);
+        tmem_ld32(lane_base + C::TM_DP + qs * T::CH + piece * 32, w);
+        load_prior32<BF16>(p.priorT, p.np, pkey, c * T::CH + piece * 32, dp, ap);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float4 ra = *reinterpret_cast<const float4*>(&rec[piece * 32 + j][0]);  // m, 1/l1, 1/l2, delta1
+          const float d2 = rec[piece * 32 + j][4];
+          const float t = v[j] * sc_l2;
+          const float p1 = ex2(t - ra.x) * ra.y;
+          const float z2 = fmaf(aL, p1, fmaf(bL, dp[j], fmaf(gL, ap[j], -cL)));
+          const float p2 = ex2(z2) * ra.z;
+          const float dz = p2 * (w[j] - d2);
+          v[j] = kvalid ? p2 : 0.f;
+          w[j] = kvalid ? p1 * fmaf(ab.a, dz, -ra.w) : 0.f;
+        }
+        stage_row32<BF16>(p2reg, r, piece, v);
+        stage_row32<BF16>(dsreg, r, piece, w);
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&bar_tfull[qs]);
+      mbar_arrive(&bar_sempty[qs]);
+    }
+    if (ok) ok = warp_wait(&bar_done, 0, ctx);
+    tc_fence_after();
+    if (ok) {
+      const bool valid = key < p.N;
+      const long long koff = (long long)b * p.dk_str[0] + (long long)h * p.dk_str[1] + (long long)key * p.dk_str[2];
+      const long long voff = (long long)b * p.dv_str[0] + (long long)h * p.dv_str[1] + (long long)key * p.dv_str[2];
+#pragma unroll 1
+      for (int d0 = 0; d0 < DP; d0 += 32) {
+        float v[32];
+        tmem_ld32(lane_base + C::TM_DK + d0, v);
+        if (valid && d0 < p.D) store_row32<BF16>(p.dk, koff, p.dk_str[3], d0, p.D, v, p.inv_sqrt_d);
+        tmem_ld32(lane_base + C::TM_DV + d0, v);
+        if (valid && d0 < p.D) store_row32<BF16>(p.dv, voff, p.dv_str[3], d0, p.D, v, 1.0f);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, C::TMEM_COLS);
+}
+
+}  // namespace geoattn

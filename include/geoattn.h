@@ -1,0 +1,131 @@
+/* C ABI of the B200 (sm_100a) geo-biased station attention library, libgeoattn.so.
+ *
+ * The reference implements this path in Python: the operator is
+ *   MultiHeadAttention.scaled_dot_product_attention        fore_swe/custom_encoder_model.py:25-39
+ * its fused replacement is
+ *   FusedGeoAttentionV2.forward / .backward                 foreswe_bench/geo_attention_v2.py:401-461
+ *   fused_geo_attention_v2(q, k, v, dist, ang, a, b, g)     foreswe_bench/geo_attention_v2.py:464-465
+ * and the bias construction is
+ *   DataLoader.getDistanceAndAngularity (+ helpers)         fore_swe/extended_dl_forecasting.py:305-352
+ * A Python (ctypes) binding of every entry point below lives in
+ * foreswe_gpu_optimization_b200/_lib.py; INTEGRATION.md shows it.
+ *
+ * Conventions: all data pointers are device pointers; tensors are [B, H, N, D] with element strides; the
+ * library never allocates or frees device memory (callers pass outputs and workspaces sized by the *_bytes
+ * functions); every call is asynchronous on `stream` (a cudaStream_t, NULL = legacy default stream), performs no
+ * host synchronisation and is safe to capture in a CUDA graph. Every entry point returns a GEOATTN_* status code.
+ */
+#ifndef GEOATTN_H_
+#define GEOATTN_H_
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GEOATTN_VERSION 1
+
+enum {
+  GEOATTN_OK = 0,
+  GEOATTN_ERR_INVALID = 1,     /* null pointer, non-positive size, bad enum */
+  GEOATTN_ERR_UNSUPPORTED = 2, /* head_dim / dtype combination without a kernel */
+  GEOATTN_ERR_ALIGNMENT = 3,   /* tensor base or stride not 16-byte aligned, or head dim not contiguous */
+  GEOATTN_ERR_TMA = 4,         /* TMA descriptor encoding failed */
+  GEOATTN_ERR_LAUNCH = 5,      /* CUDA launch error */
+  GEOATTN_ERR_DEVICE = 6       /* a kernel's bounded wait expired (reported through geoattn_read_status) */
+};
+
+enum { GEOATTN_DTYPE_BF16 = 0, GEOATTN_DTYPE_FP32 = 1 };
+
+/* Problem shape. dtype is the storage type of q, k, v, o, dO, dQ, dK, dV:
+ *   BF16 -> bf16 tensor-core path (kind::f16), geo prior kept as fp16 pairs;
+ *   FP32 -> TF32 tensor-core path (kind::tf32) with 3-term split products for QK^T and dO V^T
+ *           (round-to-nearest hi/lo operands), 1-term for the rest; geo prior kept in fp32.
+ * Supported head_dim: BF16 1..192, FP32 1..64. n >= 1 (any size).                                        */
+typedef struct {
+  int batch, heads, n, head_dim;
+  int dtype;
+  int per_head; /* alpha/beta/gamma hold `heads` values each (else 1): reference parameters are scalars
+                   (custom_encoder_model.py:16-18) */
+} GeoAttnShape;
+
+typedef struct {
+  const void* data;
+  long long stride[4]; /* element strides of [B, H, N, D]; stride[3] must be 1 */
+} GeoAttnTensor;
+
+/* ---- geometry: station coordinates -> geo prior (replaces the host float64 construction) ---------------- */
+size_t geoattn_prior_bytes(const GeoAttnShape* shape);
+
+/* Prior from dense [n, n] fp32 distance (km) and angle (degrees) matrices (row strides ld_*), i.e. the
+ * reference's (distances, angularities) arguments: Dp = 1/(1+dist), Ap = 1/(1+ang) (custom_encoder_model.py:32-33).
+ * Requires dist, ang >= 0.                                                                                  */
+int geoattn_prior_from_dense(const GeoAttnShape* shape, const float* dist, long long ld_dist, const float* ang,
+                             long long ld_ang, void* prior, void* stream);
+
+/* Prior straight from per-station coordinates (float64 degrees, elevation in feet): great-circle distance on
+ * the 6371 km sphere and Kahan's 2*atan2 angle between the reference's station vectors
+ * (extended_dl_forecasting.py:20-30, :305-344), evaluated in float64 on the device and rounded to fp32 like the
+ * reference's fp32 copies; no [n, n] matrix is produced. dist_out / ang_out (may be NULL) receive the
+ * fp32 matrices with row stride n.                                                                          */
+int geoattn_prior_from_coords(const GeoAttnShape* shape, const double* lat_deg, const double* lon_deg,
+                              const double* elev_ft, void* prior, float* dist_out, float* ang_out, void* stream);
+
+/* ---- forward ------------------------------------------------------------------------------------------- */
+size_t geoattn_stats_bytes(const GeoAttnShape* shape);          /* row statistics kept for the backward */
+size_t geoattn_fwd_workspace_bytes(const GeoAttnShape* shape);
+
+typedef struct {
+  GeoAttnShape shape;
+  GeoAttnTensor q, k, v;
+  const float* abg;   /* device fp32 [3 * nabg]: alpha..., beta..., gamma... (nabg = per_head ? heads : 1) */
+  const void* prior;  /* from geoattn_prior_* for the same n and dtype */
+  void* o;            /* output, dtype of the inputs */
+  long long o_stride[4];
+  float* stats;       /* geoattn_stats_bytes */
+  void* workspace;    /* geoattn_fwd_workspace_bytes, 256-byte aligned */
+  void* const* events; /* optional (NULL = none): 2 cudaEvent_t recorded on `stream` around the attention
+                          kernel, for per-kernel timing */
+} GeoAttnFwdArgs;
+
+/* O = softmax(alpha*softmax(QK^T/sqrt(d)) + beta*Dp + gamma*Ap) V; replaces FusedGeoAttentionV2.forward
+ * (geo_attention_v2.py:402-425). */
+int geoattn_fwd(const GeoAttnFwdArgs* args, void* stream);
+
+/* ---- backward ------------------------------------------------------------------------------------------ */
+size_t geoattn_bwd_workspace_bytes(const GeoAttnShape* shape);
+
+typedef struct {
+  GeoAttnShape shape;
+  GeoAttnTensor q, k, v, o, dout;
+  const float* abg;
+  const void* prior;
+  const float* stats; /* written by geoattn_fwd for the same inputs */
+  void* dq;
+  long long dq_stride[4];
+  void* dk;
+  long long dk_stride[4];
+  void* dv;
+  long long dv_stride[4];
+  float* dabg;        /* fp32 [3 * nabg]: d alpha..., d beta..., d gamma... (summed over batch, rows) */
+  void* workspace;    /* geoattn_bwd_workspace_bytes, 256-byte aligned */
+  void* const* events; /* optional (NULL = none): 3 cudaEvent_t recorded on `stream` before the row-pass kernel,
+                          between the row-pass and key-pass kernels, and after the key-pass kernel */
+} GeoAttnBwdArgs;
+
+/* dQ, dK, dV and the bias-parameter gradients; replaces FusedGeoAttentionV2.backward
+ * (geo_attention_v2.py:428-461). Deterministic: no atomics, fixed reduction order. */
+int geoattn_bwd(const GeoAttnBwdArgs* args, void* stream);
+
+/* ---- diagnostics --------------------------------------------------------------------------------------- */
+/* Copies the device status word of a workspace (0 = ok, 1 = a bounded wait expired) to *status. Synchronises
+ * the stream; for tests and debugging only. */
+int geoattn_read_status(const void* workspace, int* status, void* stream);
+const char* geoattn_error_string(int code);
+int geoattn_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* GEOATTN_H_ */

@@ -99,6 +99,22 @@ def round_tf32(x):
     return ((i + 0x1000) & -8192).view(torch.float32)
 
 
+class _TF32MatMul(torch.autograd.Function):
+    """Matmul whose forward and backward products all take TF32-rounded operands (eager TF32 under cuBLAS)."""
+
+    @staticmethod
+    def forward(ctx, a, b):
+        ctx.save_for_backward(a, b)
+        return (round_tf32(a).double() @ round_tf32(b).double()).to(a.dtype)
+
+    @staticmethod
+    def backward(ctx, g):
+        a, b = ctx.saved_tensors
+        ga = (round_tf32(g).double() @ round_tf32(b).double().transpose(-2, -1)).to(a.dtype)
+        gb = (round_tf32(a).double().transpose(-2, -1) @ round_tf32(g).double()).to(b.dtype)
+        return ga, gb
+
+
 def tf32_matmul(a, b):
     """Matmul with TF32-rounded operands and a wide accumulator: the error model of eager TF32."""
-    return (round_tf32(a).double() @ round_tf32(b).double()).to(a.dtype)
+    return _TF32MatMul.apply(a, b)

@@ -1,0 +1,229 @@
+"""Parity of the B200 kernels (through libgeoattn's C ABI) with the float64 oracle on seeded inputs.
+
+Tolerances (rel-L2 against the FP32 operator): TF32 path 5e-4, BF16 path 8e-3, for the output and every gradient;
+saturated inputs must stay finite. The oracle is evaluated on exactly the values the kernels see (bf16 inputs are
+compared with the oracle on the same bf16 values).
+"""
+import glob
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from helpers import KEYS, TOL, attn_inputs, dense_geometry, rel_l2, run_device, stations
+from oracle import acceptance
+from oracle import geo_attention as oga
+
+pytestmark = pytest.mark.gpu
+GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+@pytest.fixture(scope="module")
+def ops():
+    import foreswe_gpu_optimization_b200 as g
+    return g
+
+
+def _oracle(q, k, v, dist, ang, a, b, c, do):
+    return oga.grads(q.double(), k.double(), v.double(), dist.double(), ang.double(), a, b, c, do.double())
+
+
+def _check(res, ref, tol, label):
+    bad = {}
+    for key in KEYS:
+        assert torch.isfinite(res[key].float()).all(), (label, key, "non-finite")
+        e = rel_l2(res[key], ref[key])
+        if not e <= tol:
+            bad[key] = e
+    assert not bad, "%s: rel-L2 above %.1e: %s" % (label, tol, bad)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32], ids=["bf16", "tf32"])
+@pytest.mark.parametrize("qscale", [1.0, 30.0], ids=["plain", "saturated_x30"])
+def test_c2_shape_coordinate_geometry(ops, dtype, qscale):
+    """N = 512 stations, D = 64, per-head parameters, prior from coordinates (the north-star call)."""
+    B, H, N, D = 2, 4, 512, 64
+    q, k, v, a, b, c, do = attn_inputs(B, H, N, D, seed=1, qscale=qscale, dtype=dtype)
+    lat, lon, el = stations(N, seed=2)
+    geom = ops.StationGeometry(lat, lon, el)
+    res = run_device(lambda *x: ops.geo_attention(x[0], x[1], x[2], geom, *x[3:]), q, k, v, a, b, c, do)
+    dist, ang = dense_geometry(lat, lon, el)
+    _check(res, _oracle(q, k, v, dist, ang, a, b, c, do), TOL[dtype], "C2 %s x%g" % (dtype, qscale))
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32], ids=["bf16", "tf32"])
+@pytest.mark.parametrize("N,D", [(1, 64), (33, 48), (100, 64), (129, 8), (200, 64), (300, 24)])
+def test_ragged_shapes_dense_prior(ops, dtype, N, D):
+    """N not a multiple of the tiles, D below the 64-wide tile; reference call with dense dist/ang."""
+    B, H = 1, 3
+    q, k, v, a, b, c, do = attn_inputs(B, H, N, D, seed=N + D, qscale=3.0, per_head=False, dtype=dtype)
+    g = torch.Generator().manual_seed(N)
+    dist = torch.rand(N, N, generator=g) * 1500
+    ang = torch.rand(N, N, generator=g) * 20
+    res = run_device(lambda *x: ops.fused_geo_attention_v2(x[0], x[1], x[2], dist.cuda(), ang.cuda(), *x[3:]),
+                     q, k, v, a, b, c, do)
+    _check(res, _oracle(q, k, v, dist, ang, a, b, c, do), TOL[dtype], "N=%d D=%d" % (N, D))
+
+
+@pytest.mark.parametrize("D", [128, 192, 96, 160])
+def test_bf16_wide_heads(ops, D):
+    """bf16 head dims up to the production d_k = 192 (3 x 1024 / 16)."""
+    B, H, N = 1, 2, 384
+    q, k, v, a, b, c, do = attn_inputs(B, H, N, D, seed=D, qscale=2.0, dtype=torch.bfloat16)
+    lat, lon, el = stations(N, seed=D)
+    geom = ops.StationGeometry(lat, lon, el)
+    res = run_device(lambda *x: ops.geo_attention(x[0], x[1], x[2], geom, *x[3:]), q, k, v, a, b, c, do)
+    dist, ang = dense_geometry(lat, lon, el)
+    _check(res, _oracle(q, k, v, dist, ang, a, b, c, do), TOL[torch.bfloat16], "D=%d" % D)
+
+
+@pytest.mark.parametrize("case", acceptance.CASES)
+def test_reference_regimes_tf32(ops, case):
+    """The reference's six synthetic regimes (foreswe_bench/attn_check.py:20-45) at D = 64 on the TF32 path:
+    within the TF32 tolerance of the oracle, finite, and within 10x eager TF32's max-abs error."""
+    inp = acceptance.case_inputs(case, B=1, H=2, N=128, D=64, seed=0)
+    do = acceptance.grad_seed_do(inp[0].shape)
+    q, k, v, dist, ang, a, b, c = inp
+    res = run_device(lambda *x: ops.fused_geo_attention_v2(x[0], x[1], x[2], dist.cuda(), ang.cuda(), *x[3:]),
+                     q, k, v, a, b, c, do)
+    ref = acceptance.reference(inp, do)
+    for key in KEYS:
+        assert torch.isfinite(res[key]).all(), (case, key)
+    ev = acceptance.evaluate(res, inp, do, "tf32", ref=ref)
+    bad = {k: (r["candidate"]["max_abs"], r["bound"]) for k, r in ev.items() if not r["passed"]}
+    assert not bad, "%s: above 10x eager TF32: %s" % (case, bad)
+
+
+@pytest.mark.parametrize("path", sorted(glob.glob(os.path.join(GOLD, "attn_*.npz"))),
+                         ids=lambda p: os.path.basename(p)[5:-4])
+def test_reference_golden_vectors_tf32(ops, path):
+    """Golden vectors produced by the reference's eager operator (float64 autograd) through the TF32 path."""
+    z = np.load(path)
+    q, k, v, dist, ang = (torch.from_numpy(z[n]).float() for n in ("q", "k", "v", "dist", "ang"))
+    a, b, c = (torch.from_numpy(z[n]).float().reshape(-1) for n in ("alpha", "beta", "gamma"))
+    do = torch.from_numpy(z["do"]).float()
+    res = run_device(lambda *x: ops.fused_geo_attention_v2(x[0], x[1], x[2], dist.cuda(), ang.cuda(), *x[3:]),
+                     q, k, v, a, b, c, do)
+    for key in KEYS:
+        gold = torch.from_numpy(z[key]).reshape(res[key].shape)
+        assert rel_l2(res[key], gold) <= 5e-4, (key, rel_l2(res[key], gold))
+
+
+def test_split_heads_strided_views(ops):
+    """Q/K/V as the transposed split_heads views of [B, N, H*D] (custom_encoder_model.py:41-43); gradients keep
+    the input strides."""
+    B, N, H, D = 2, 160, 4, 64
+    g = torch.Generator().manual_seed(5)
+    base = [torch.randn(B, N, H * D, generator=g).cuda().to(torch.bfloat16) * 0.4 for _ in range(3)]
+    views = [t.view(B, N, H, D).transpose(1, 2).detach().requires_grad_(True) for t in base]
+    a, b, c = (torch.tensor([x], device="cuda", requires_grad=True) for x in (0.5, -0.3, 0.2))
+    dist = torch.rand(N, N, generator=g).cuda() * 900
+    ang = torch.rand(N, N, generator=g).cuda() * 12
+    o = ops.fused_geo_attention_v2(*views, dist, ang, a, b, c)
+    do = torch.randn(o.shape, generator=g).cuda().to(torch.bfloat16)
+    o.backward(do)
+    for x in views:
+        assert x.grad.stride() == x.stride()
+    ref = oga.grads(*(t.detach().double().cpu() for t in views), dist.cpu().double(), ang.cpu().double(),
+                    a.detach().cpu(), b.detach().cpu(), c.detach().cpu(), do.double().cpu())
+    res = dict(output=o.detach().cpu(), dQ=views[0].grad.cpu(), dK=views[1].grad.cpu(), dV=views[2].grad.cpu(),
+               dalpha=a.grad.cpu(), dbeta=b.grad.cpu(), dgamma=c.grad.cpu())
+    _check(res, ref, TOL[torch.bfloat16], "strided")
+
+
+def test_device_geometry_matches_oracle(ops):
+    """Device float64 haversine / Kahan angle, rounded to fp32, equal the oracle's within an ulp."""
+    z = np.load(os.path.join(GOLD, "geometry.npz"))
+    geom = ops.StationGeometry(z["lat"], z["lon"], z["elev_ft"])
+    dist, ang = geom.distance_and_angularity()
+    np.testing.assert_allclose(dist.cpu().numpy(), z["dist_km"].astype(np.float32), rtol=2.5e-7, atol=1e-6)
+    np.testing.assert_allclose(ang.cpu().numpy(), z["ang_deg"].astype(np.float32), rtol=2.5e-7, atol=1e-6)
+    lat, lon, el = stations(300, seed=9)
+    d2, a2 = ops.StationGeometry(lat, lon, el).distance_and_angularity()
+    rd, ra = dense_geometry(lat, lon, el)
+    torch.testing.assert_close(d2.cpu(), rd, rtol=2.5e-7, atol=1e-6)
+    torch.testing.assert_close(a2.cpu(), ra, rtol=2.5e-7, atol=1e-6)
+
+
+def test_coordinate_and_dense_priors_agree(ops):
+    """geo_attention(geometry) and fused_geo_attention_v2(dist, ang) give identical results."""
+    B, H, N, D = 1, 2, 200, 64
+    q, k, v, a, b, c, do = attn_inputs(B, H, N, D, seed=3, dtype=torch.float32)
+    lat, lon, el = stations(N, seed=4)
+    geom = ops.StationGeometry(lat, lon, el)
+    dist, ang = geom.distance_and_angularity()
+    r1 = run_device(lambda *x: ops.geo_attention(x[0], x[1], x[2], geom, *x[3:]), q, k, v, a, b, c, do)
+    r2 = run_device(lambda *x: ops.fused_geo_attention_v2(x[0], x[1], x[2], dist, ang, *x[3:]), q, k, v, a, b, c, do)
+    for key in KEYS:
+        assert torch.equal(r1[key], r2[key]), key
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32], ids=["bf16", "tf32"])
+def test_deterministic_and_graph_replay_bitwise(ops, dtype):
+    """Two direct launches agree bitwise, and a CUDA-graph capture of fwd+bwd replays bitwise equal to direct
+    launches for fresh inputs (tests/test_gpu_geo_attention_v2.py:85-114 in the reference)."""
+    B, H, N, D = 1, 2, 256, 64
+    lat, lon, el = stations(N, seed=11)
+    geom = ops.StationGeometry(lat, lon, el)
+    fn = lambda *x: ops.geo_attention(x[0], x[1], x[2], geom, *x[3:])
+    ins = [attn_inputs(B, H, N, D, seed=s, qscale=4.0, dtype=dtype) for s in (21, 22)]
+    r1 = run_device(fn, *ins[0])
+    r2 = run_device(fn, *ins[0])
+    for key in KEYS:
+        assert torch.equal(r1[key], r2[key]), key
+    dev = torch.device("cuda")
+    static = [t.to(dev).detach().clone().requires_grad_(True) for t in ins[0][:6]]
+    do = ins[0][6].to(dev)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(2):
+            for t in static:
+                t.grad = None
+            fn(*static).backward(do)
+    torch.cuda.current_stream().wait_stream(s)
+    for t in static:
+        t.grad = None
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        out = fn(*static)
+        out.backward(do)
+    for inp in ins:
+        with torch.no_grad():
+            for t, src in zip(static, inp[:6]):
+                t.copy_(src.to(dev))
+            do.copy_(inp[6].to(dev))
+        graph.replay()
+        ref = run_device(fn, *inp)
+        assert torch.equal(out.detach().cpu(), ref["output"])
+        for i, key in zip(range(6), ("dQ", "dK", "dV", "dalpha", "dbeta", "dgamma")):
+            assert torch.equal(static[i].grad.cpu(), ref[key]), key
+
+
+def test_status_word_clean_and_errors_raise(ops):
+    """No bounded wait expires on a normal launch; unsupported shapes raise through geoattn_error_string."""
+    from foreswe_gpu_optimization_b200 import _lib
+    import ctypes
+    B, H, N, D = 1, 1, 64, 64
+    sh = _lib.Shape(B, H, N, D, _lib.DTYPE_FP32, 0)
+    L = _lib.lib()
+    ws = torch.zeros(L.geoattn_fwd_workspace_bytes(ctypes.byref(sh)), dtype=torch.uint8, device="cuda")
+    q, k, v, a, b, c, do = attn_inputs(B, H, N, D, per_head=False)
+    dist = torch.rand(N, N).cuda() * 100
+    ang = torch.rand(N, N).cuda() * 5
+    prior = ops.prior_from_dense(dist, ang, torch.float32)
+    abg = torch.cat([a, b, c]).cuda()
+    qd, kd, vd = q.cuda(), k.cuda(), v.cuda()
+    o = torch.empty_like(qd)
+    stats = torch.empty(3 * N, device="cuda")
+    args = _lib.FwdArgs(sh, _lib.tensor_arg(qd), _lib.tensor_arg(kd), _lib.tensor_arg(vd),
+                        ctypes.c_void_p(abg.data_ptr()), ctypes.c_void_p(prior.data_ptr()),
+                        ctypes.c_void_p(o.data_ptr()), _lib.c_ll4(*o.stride()), ctypes.c_void_p(stats.data_ptr()),
+                        ctypes.c_void_p(ws.data_ptr()))
+    _lib.check(L.geoattn_fwd(ctypes.byref(args), None))
+    from foreswe_gpu_optimization_b200.geo_attention_v2 import read_status
+    assert read_status(ws) == 0
+    with pytest.raises(_lib.GeoAttnError):
+        x = torch.randn(1, 1, 16, 80, device="cuda")
+        ops.fused_geo_attention_v2(x, x, x, dist[:16, :16], ang[:16, :16], a.cuda(), b.cuda(), c.cuda())

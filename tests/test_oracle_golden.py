@@ -110,3 +110,12 @@ def test_acceptance_rule_flags_planted_error():
     bad["dQ"] = good["dQ"].clone()
     bad["dQ"][0, 0, 0, 0] += 1e-3
     assert not acceptance.evaluate(bad, inp, do, "fp32")["dQ"]["passed"]
+
+
+def test_eager_tf32_error_model_is_differentiable_and_lossier():
+    inp = acceptance.case_inputs("moderate", B=1, H=2, N=24, D=16, seed=1)
+    do = acceptance.grad_seed_do(inp[0].shape)
+    ref = acceptance.reference(inp, do)
+    e32, etf = acceptance.eager(inp, do, "fp32"), acceptance.eager(inp, do, "tf32")
+    for k in ("output", "dQ", "dK", "dV"):
+        assert acceptance.err(etf[k], ref[k])["max_abs"] > acceptance.err(e32[k], ref[k])["max_abs"]
