@@ -151,7 +151,7 @@ def cpu_reference(seconds, threads):
         oga.grads(q, k, v, dist, ang, a, b, c, do, dtype=torch.float32)
         reps += 1
         el_s = time.perf_counter() - t0
-        if el_s >= seconds or reps >= 200:
+        if el_s >= seconds or reps >= 5000:
             break
     return flops(1) * reps / el_s / 1e12, reps, el_s
 
@@ -219,8 +219,12 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-eager", action="store_true")
+    ap.add_argument("--batch", type=int, default=None, help="override the global batch (small cases for profiling)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
+    if args.batch:
+        global B_TOTAL
+        B_TOTAL = args.batch
     if args.impl == "reference":
         return run_reference(args)
 
@@ -244,7 +248,7 @@ def main():
     geom.prior(torch.bfloat16)
     (qh, kh, vh, doh), (a0, b0, c0) = inputs(b, 1000 + rank, "cpu")
     q, k, v, do = (t.to(dev) for t in (qh, kh, vh, doh))
-    params = [t.clone().requires_grad_(True) for t in (a0, b0, c0)]
+    params = [t.to(dev).requires_grad_(True) for t in (a0, b0, c0)]
     x = [t.detach().requires_grad_(True) for t in (q, k, v)]
 
     def allreduce_bias_grads():

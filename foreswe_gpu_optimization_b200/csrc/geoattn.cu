@@ -190,6 +190,18 @@ struct Dims {
   int nabg;
 };
 
+// Every data pointer handed to a kernel must be device (or managed) memory: a host pointer would be dereferenced
+// by the GPU. Checked on the host before any launch.
+bool dev_ptr(const void* p) {
+  if (!p) return false;
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();  // clear the sticky-free error of an unregistered host pointer
+    return false;
+  }
+  return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
+}
+
 int check_shape(const GeoAttnShape* s, Dims& d) {
   if (!s || s->batch <= 0 || s->heads <= 0 || s->n <= 0 || s->head_dim <= 0) return GEOATTN_ERR_INVALID;
   if (s->dtype != GEOATTN_DTYPE_BF16 && s->dtype != GEOATTN_DTYPE_FP32) return GEOATTN_ERR_INVALID;
@@ -387,7 +399,7 @@ int geoattn_prior_from_dense(const GeoAttnShape* shape, const float* dist, long 
                              long long ld_ang, void* prior, void* stream) {
   Dims d;
   if (int rc = check_shape(shape, d)) return rc;
-  if (!dist || !ang || !prior || ld_dist < d.N || ld_ang < d.N) return GEOATTN_ERR_INVALID;
+  if (!dev_ptr(dist) || !dev_ptr(ang) || !dev_ptr(prior) || ld_dist < d.N || ld_ang < d.N) return GEOATTN_ERR_INVALID;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   void* pt = reinterpret_cast<uint8_t*>(prior) + prior_table_bytes(d);
   dim3 grid(d.np / 32, d.np / 32), block(32, 8);
@@ -400,7 +412,10 @@ int geoattn_prior_from_coords(const GeoAttnShape* shape, const double* lat_deg, 
                               const double* elev_ft, void* prior, float* dist_out, float* ang_out, void* stream) {
   Dims d;
   if (int rc = check_shape(shape, d)) return rc;
-  if (!lat_deg || !lon_deg || !elev_ft || (!prior && !dist_out && !ang_out)) return GEOATTN_ERR_INVALID;
+  if (!dev_ptr(lat_deg) || !dev_ptr(lon_deg) || !dev_ptr(elev_ft) || (!prior && !dist_out && !ang_out))
+    return GEOATTN_ERR_INVALID;
+  if ((prior && !dev_ptr(prior)) || (dist_out && !dev_ptr(dist_out)) || (ang_out && !dev_ptr(ang_out)))
+    return GEOATTN_ERR_INVALID;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   void* pt = prior ? reinterpret_cast<uint8_t*>(prior) + prior_table_bytes(d) : nullptr;
   dim3 grid(d.np / 32, d.np / 32), block(32, 8);
@@ -433,7 +448,9 @@ int geoattn_fwd(const GeoAttnFwdArgs* a, void* stream) {
   if (!a) return GEOATTN_ERR_INVALID;
   Dims d;
   if (int rc = check_shape(&a->shape, d)) return rc;
-  if (!a->abg || !a->prior || !a->o || !a->stats || !a->workspace) return GEOATTN_ERR_INVALID;
+  if (!dev_ptr(a->abg) || !dev_ptr(a->prior) || !dev_ptr(a->o) || !dev_ptr(a->stats) || !dev_ptr(a->workspace) ||
+      !dev_ptr(a->q.data) || !dev_ptr(a->k.data) || !dev_ptr(a->v.data))
+    return GEOATTN_ERR_INVALID;
   if ((reinterpret_cast<uintptr_t>(a->workspace) & (kAlign - 1)) != 0) return GEOATTN_ERR_ALIGNMENT;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   FwdWs ws;
@@ -471,8 +488,9 @@ int geoattn_bwd(const GeoAttnBwdArgs* a, void* stream) {
   if (!a) return GEOATTN_ERR_INVALID;
   Dims d;
   if (int rc = check_shape(&a->shape, d)) return rc;
-  if (!a->abg || !a->prior || !a->stats || !a->dq || !a->dk || !a->dv || !a->dabg || !a->workspace ||
-      !a->o.data || !a->dout.data)
+  if (!dev_ptr(a->abg) || !dev_ptr(a->prior) || !dev_ptr(a->stats) || !dev_ptr(a->dq) || !dev_ptr(a->dk) ||
+      !dev_ptr(a->dv) || !dev_ptr(a->dabg) || !dev_ptr(a->workspace) || !dev_ptr(a->o.data) ||
+      !dev_ptr(a->dout.data) || !dev_ptr(a->q.data) || !dev_ptr(a->k.data) || !dev_ptr(a->v.data))
     return GEOATTN_ERR_INVALID;
   if ((reinterpret_cast<uintptr_t>(a->workspace) & (kAlign - 1)) != 0) return GEOATTN_ERR_ALIGNMENT;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
@@ -531,7 +549,7 @@ int geoattn_bwd(const GeoAttnBwdArgs* a, void* stream) {
 }
 
 int geoattn_read_status(const void* workspace, int* status, void* stream) {
-  if (!workspace || !status) return GEOATTN_ERR_INVALID;
+  if (!dev_ptr(workspace) || !status) return GEOATTN_ERR_INVALID;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (cudaMemcpyAsync(status, workspace, sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess)
     return GEOATTN_ERR_LAUNCH;

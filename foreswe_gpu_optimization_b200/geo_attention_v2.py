@@ -64,13 +64,13 @@ def _tma_ready(t):
     return buf[..., :D]
 
 
-def _abg(alpha, beta, gamma, H):
+def _abg(alpha, beta, gamma, H, device):
     sizes = {alpha.numel(), beta.numel(), gamma.numel()}
     if len(sizes) != 1 or sizes.pop() not in (1, H):
         raise ValueError("alpha, beta, gamma must all have 1 or H entries")
     per_head = int(alpha.numel() == H and H > 1)
-    abg = torch.cat([alpha.reshape(-1), beta.reshape(-1), gamma.reshape(-1)]).detach().float().contiguous()
-    return abg, per_head
+    abg = torch.cat([t.detach().reshape(-1).to(device=device, dtype=torch.float32) for t in (alpha, beta, gamma)])
+    return abg.contiguous(), per_head
 
 
 def _shape(q, per_head):
@@ -90,7 +90,9 @@ class FusedGeoAttentionV2(torch.autograd.Function):
         if not q.is_cuda:
             raise RuntimeError("geo attention runs on CUDA tensors only (no CPU path)")
         B, H, N, D = q.shape
-        abg, per_head = _abg(alpha, beta, gamma, H)
+        if prior.device != q.device:
+            raise ValueError("the geo prior lives on %s, q on %s" % (prior.device, q.device))
+        abg, per_head = _abg(alpha, beta, gamma, H, q.device)
         q, k, v = _tma_ready(q), _tma_ready(k), _tma_ready(v)
         sh = _shape(q, per_head)
         L = _lib.lib()

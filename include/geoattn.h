@@ -28,7 +28,7 @@ extern "C" {
 
 enum {
   GEOATTN_OK = 0,
-  GEOATTN_ERR_INVALID = 1,     /* null pointer, non-positive size, bad enum */
+  GEOATTN_ERR_INVALID = 1,     /* null or non-device pointer, non-positive size, bad enum */
   GEOATTN_ERR_UNSUPPORTED = 2, /* head_dim / dtype combination without a kernel */
   GEOATTN_ERR_ALIGNMENT = 3,   /* tensor base or stride not 16-byte aligned, or head dim not contiguous */
   GEOATTN_ERR_TMA = 4,         /* TMA descriptor encoding failed */

@@ -98,16 +98,23 @@ def test_reference_regimes_tf32(ops, case):
 @pytest.mark.parametrize("path", sorted(glob.glob(os.path.join(GOLD, "attn_*.npz"))),
                          ids=lambda p: os.path.basename(p)[5:-4])
 def test_reference_golden_vectors_tf32(ops, path):
-    """Golden vectors produced by the reference's eager operator (float64 autograd) through the TF32 path."""
+    """Golden vectors produced by the reference's eager operator (float64 autograd) through the TF32 path: each
+    quantity within the TF32 rel-L2 tolerance of the golden value, or -- where the golden value itself is
+    vanishingly small (saturated rows: dQ ~ 1e-29 in near_one_hot) -- within the reference's own acceptance rule,
+    10x eager TF32's max-abs error (foreswe_bench/attn_check.py:68-81)."""
     z = np.load(path)
     q, k, v, dist, ang = (torch.from_numpy(z[n]).float() for n in ("q", "k", "v", "dist", "ang"))
     a, b, c = (torch.from_numpy(z[n]).float().reshape(-1) for n in ("alpha", "beta", "gamma"))
     do = torch.from_numpy(z["do"]).float()
     res = run_device(lambda *x: ops.fused_geo_attention_v2(x[0], x[1], x[2], dist.cuda(), ang.cuda(), *x[3:]),
                      q, k, v, a, b, c, do)
+    gold = {key: torch.from_numpy(z[key]).reshape(res[key].shape) for key in KEYS}
+    inp = [q, k, v, dist, ang, a, b, c]
+    ev = acceptance.evaluate(res, inp, do, "tf32", ref=gold)
     for key in KEYS:
-        gold = torch.from_numpy(z[key]).reshape(res[key].shape)
-        assert rel_l2(res[key], gold) <= 5e-4, (key, rel_l2(res[key], gold))
+        e = rel_l2(res[key], gold[key])
+        assert torch.isfinite(res[key]).all(), key
+        assert e <= 5e-4 or ev[key]["passed"], (key, e, ev[key]["candidate"]["max_abs"], ev[key]["bound"])
 
 
 def test_split_heads_strided_views(ops):
@@ -227,3 +234,9 @@ def test_status_word_clean_and_errors_raise(ops):
     with pytest.raises(_lib.GeoAttnError):
         x = torch.randn(1, 1, 16, 80, device="cuda")
         ops.fused_geo_attention_v2(x, x, x, dist[:16, :16], ang[:16, :16], a.cuda(), b.cuda(), c.cuda())
+    # a host pointer where the library expects device memory is rejected before any launch
+    bad = _lib.FwdArgs(sh, _lib.tensor_arg(qd), _lib.tensor_arg(kd), _lib.tensor_arg(vd),
+                       ctypes.c_void_p(torch.cat([a, b, c]).data_ptr()), ctypes.c_void_p(prior.data_ptr()),
+                       ctypes.c_void_p(o.data_ptr()), _lib.c_ll4(*o.stride()), ctypes.c_void_p(stats.data_ptr()),
+                       ctypes.c_void_p(ws.data_ptr()))
+    assert L.geoattn_fwd(ctypes.byref(bad), None) == 1
