@@ -14,7 +14,8 @@ DTYPE_BF16, DTYPE_FP32 = 0, 1
 
 EXPORTED = ("geoattn_version", "geoattn_error_string", "geoattn_prior_bytes", "geoattn_prior_from_dense",
             "geoattn_prior_from_coords", "geoattn_stats_bytes", "geoattn_fwd_workspace_bytes",
-            "geoattn_bwd_workspace_bytes", "geoattn_fwd", "geoattn_bwd", "geoattn_read_status")
+            "geoattn_bwd_workspace_bytes", "geoattn_fwd", "geoattn_bwd", "geoattn_bwd_noalloc",
+            "geoattn_read_status")
 
 c_ll4 = ctypes.c_longlong * 4
 
@@ -78,6 +79,8 @@ def lib():
         L.geoattn_fwd.argtypes = [ctypes.POINTER(FwdArgs), ctypes.c_void_p]
         L.geoattn_bwd.restype = ctypes.c_int
         L.geoattn_bwd.argtypes = [ctypes.POINTER(BwdArgs), ctypes.c_void_p]
+        L.geoattn_bwd_noalloc.restype = ctypes.c_int
+        L.geoattn_bwd_noalloc.argtypes = [ctypes.POINTER(BwdArgs), ctypes.c_void_p]
         L.geoattn_read_status.restype = ctypes.c_int
         L.geoattn_read_status.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int), ctypes.c_void_p]
         _LIB = L

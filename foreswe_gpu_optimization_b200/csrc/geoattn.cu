@@ -5,6 +5,7 @@
 #include <cmath>
 #include <cstdint>
 #include <cstring>
+#include <mutex>
 
 #include "../../include/geoattn.h"
 #include "geoattn_kernels.cuh"
@@ -385,6 +386,8 @@ const char* geoattn_error_string(int code) {
     case GEOATTN_ERR_TMA: return "TMA descriptor encoding failed";
     case GEOATTN_ERR_LAUNCH: return "CUDA kernel launch failed";
     case GEOATTN_ERR_DEVICE: return "device-side bounded wait expired";
+    case GEOATTN_ERR_SCRATCH:
+      return "problem needs more backward workspace than geoattn_bwd_noalloc's static 16 MiB device buffer";
   }
   return "unknown geoattn status";
 }
@@ -558,3 +561,55 @@ int geoattn_read_status(const void* workspace, int* status, void* stream) {
 }
 
 }  // extern "C"
+
+// ===============================================================================================================
+// Allocation-free backward.
+//
+// Some callers of this library cannot allocate device memory for the backward's workspace: plugin or custom-op
+// hosts that own every device buffer and hand an operator only its inputs and outputs, and code whose memory
+// plan is fixed up front (an allocation there would synchronise the device or break the plan). For them,
+// geoattn_bwd_noalloc takes its scratch (row records, bias-gradient partials, status word) from the static device
+// array below instead of args->workspace. The array is 16 MiB in every device that loads the library, for the
+// life of the process. Every call shares it and it keeps the last call's contents, so calls that overlap on the
+// GPU (other streams, other threads) race; the status word is cleared at the start of each call and every other
+// byte a call reads is written earlier in the same call. The first call on a device looks the array's address up
+// (cudaGetSymbolAddress, that device current) and caches it; make that first call outside any stream capture.
+// ===============================================================================================================
+namespace geoattn {
+constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+namespace {
+constexpr int kMaxDevices = 64;
+
+int noalloc_scratch(void** out) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) return GEOATTN_ERR_LAUNCH;
+  if (dev < 0 || dev >= kMaxDevices) return GEOATTN_ERR_INVALID;
+  static std::mutex mu;
+  static void* addr[kMaxDevices] = {};
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) return GEOATTN_ERR_LAUNCH;
+    addr[dev] = p;
+  }
+  *out = addr[dev];
+  return GEOATTN_OK;
+}
+}  // namespace
+}  // namespace geoattn
+
+extern "C" int geoattn_bwd_noalloc(const GeoAttnBwdArgs* a, void* stream) {
+  using namespace geoattn;
+  if (!a) return GEOATTN_ERR_INVALID;
+  Dims d;
+  if (int rc = check_shape(&a->shape, d)) return rc;
+  if (!d.bf16) return GEOATTN_ERR_UNSUPPORTED;  // the FP32 path's operand planes do not fit a modest static buffer
+  if (bwd_ws(d, nullptr, nullptr) > kNoAllocScratchBytes) return GEOATTN_ERR_SCRATCH;
+  void* scratch = nullptr;
+  if (int rc = noalloc_scratch(&scratch)) return rc;
+  GeoAttnBwdArgs b = *a;
+  b.workspace = scratch;
+  return geoattn_bwd(&b, stream);
+}

@@ -33,7 +33,8 @@ enum {
   GEOATTN_ERR_ALIGNMENT = 3,   /* tensor base or stride not 16-byte aligned, or head dim not contiguous */
   GEOATTN_ERR_TMA = 4,         /* TMA descriptor encoding failed */
   GEOATTN_ERR_LAUNCH = 5,      /* CUDA launch error */
-  GEOATTN_ERR_DEVICE = 6       /* a kernel's bounded wait expired (reported through geoattn_read_status) */
+  GEOATTN_ERR_DEVICE = 6,      /* a kernel's bounded wait expired (reported through geoattn_read_status) */
+  GEOATTN_ERR_SCRATCH = 7      /* geoattn_bwd_noalloc: workspace larger than its static buffer */
 };
 
 enum { GEOATTN_DTYPE_BF16 = 0, GEOATTN_DTYPE_FP32 = 1 };
@@ -117,6 +118,18 @@ typedef struct {
 /* dQ, dK, dV and the bias-parameter gradients; replaces FusedGeoAttentionV2.backward
  * (geo_attention_v2.py:428-461). Deterministic: no atomics, fixed reduction order. */
 int geoattn_bwd(const GeoAttnBwdArgs* args, void* stream);
+
+/* Allocation-free backward (no counterpart in the reference, which always allocates through PyTorch).
+ * For callers that cannot allocate device memory themselves -- plugin/custom-op hosts that own every device buffer
+ * and give an operator only its inputs and outputs, or code with a fixed memory plan where an allocation would
+ * synchronise the device. Same arguments and results as geoattn_bwd, except that args->workspace is ignored: the
+ * scratch comes from a static 16 MiB device array that the library holds on every device that loads it until the
+ * process exits. Limits: BF16 only (GEOATTN_ERR_UNSUPPORTED for FP32); geoattn_bwd_workspace_bytes(shape) must be
+ * <= 16 MiB (about B*H*N <= 500,000 rows, e.g. 32 issue dates x 16 heads x 512 stations), else
+ * GEOATTN_ERR_SCRATCH before any launch. All calls share the array, so calls that overlap on the GPU race. The
+ * first call on a device looks up the array's address (cudaGetSymbolAddress); make it before any stream capture.
+ * It allocates nothing (no cudaMalloc/cudaFree, no allocating library call).                                  */
+int geoattn_bwd_noalloc(const GeoAttnBwdArgs* args, void* stream);
 
 /* ---- diagnostics --------------------------------------------------------------------------------------- */
 /* Copies the device status word of a workspace (0 = ok, 1 = a bounded wait expired) to *status. Synchronises

@@ -1,0 +1,85 @@
+"""geoattn_bwd_noalloc: the backward for callers that cannot allocate device memory.
+
+Plugin/custom-op hosts that own every device buffer (and code with a fixed memory plan) cannot hand the backward a
+workspace; geoattn_bwd_noalloc takes its scratch from a static device array inside the library instead. This test
+calls it through the C ABI twice in a row, on different inputs, and checks each result against geoattn_bwd (the
+entry point that takes a caller-allocated workspace) within the BF16 tolerance used by the other parity tests.
+It lives in its own file, collected last, and passes alone in a fresh process as well as after the other tests.
+"""
+import ctypes
+
+import pytest
+import torch
+
+from helpers import attn_inputs, rel_l2, stations
+
+pytestmark = pytest.mark.gpu
+TOL = 8e-3
+
+
+@pytest.fixture(scope="module")
+def L():
+    from foreswe_gpu_optimization_b200 import _lib, build
+    build.build()
+    return _lib.lib()
+
+
+def _forward(L, q, k, v, abg, prior, per_head):
+    from foreswe_gpu_optimization_b200 import _lib
+    B, H, N, D = q.shape
+    sh = _lib.Shape(B, H, N, D, _lib.DTYPE_BF16, per_head)
+    o = torch.empty_like(q)
+    stats = torch.empty(L.geoattn_stats_bytes(ctypes.byref(sh)) // 4, dtype=torch.float32, device=q.device)
+    ws = torch.empty(L.geoattn_fwd_workspace_bytes(ctypes.byref(sh)), dtype=torch.uint8, device=q.device)
+    args = _lib.FwdArgs(sh, _lib.tensor_arg(q), _lib.tensor_arg(k), _lib.tensor_arg(v),
+                        ctypes.c_void_p(abg.data_ptr()), ctypes.c_void_p(prior.data_ptr()),
+                        ctypes.c_void_p(o.data_ptr()), _lib.c_ll4(*o.stride()), ctypes.c_void_p(stats.data_ptr()),
+                        ctypes.c_void_p(ws.data_ptr()))
+    _lib.check(L.geoattn_fwd(ctypes.byref(args), None))
+    return sh, o, stats
+
+
+def _backward(L, entry, sh, q, k, v, o, do, abg, prior, stats, nabg):
+    from foreswe_gpu_optimization_b200 import _lib
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    dabg = torch.empty(3 * nabg, dtype=torch.float32, device=q.device)
+    ws = None
+    if entry == "geoattn_bwd":
+        ws = torch.empty(L.geoattn_bwd_workspace_bytes(ctypes.byref(sh)), dtype=torch.uint8, device=q.device)
+    args = _lib.BwdArgs(sh, _lib.tensor_arg(q), _lib.tensor_arg(k), _lib.tensor_arg(v), _lib.tensor_arg(o),
+                        _lib.tensor_arg(do), ctypes.c_void_p(abg.data_ptr()), ctypes.c_void_p(prior.data_ptr()),
+                        ctypes.c_void_p(stats.data_ptr()), ctypes.c_void_p(dq.data_ptr()), _lib.c_ll4(*dq.stride()),
+                        ctypes.c_void_p(dk.data_ptr()), _lib.c_ll4(*dk.stride()), ctypes.c_void_p(dv.data_ptr()),
+                        _lib.c_ll4(*dv.stride()), ctypes.c_void_p(dabg.data_ptr()),
+                        ctypes.c_void_p(ws.data_ptr() if ws is not None else None))
+    _lib.check(getattr(L, entry)(ctypes.byref(args), None))
+    torch.cuda.synchronize()
+    return dict(dQ=dq.cpu(), dK=dk.cpu(), dV=dv.cpu(), dabg=dabg.cpu())
+
+
+def test_noalloc_backward_matches_workspace_backward_twice(L):
+    from foreswe_gpu_optimization_b200 import StationGeometry
+    B, H, N, D = 2, 4, 512, 64
+    lat, lon, el = stations(N, seed=31)
+    geom = StationGeometry(lat, lon, el)
+    prior = geom.prior(torch.bfloat16)
+    for seed in (41, 42):   # two calls in a row; the static scratch keeps the previous call's contents
+        q, k, v, a, b, c, do = attn_inputs(B, H, N, D, seed=seed, qscale=3.0, dtype=torch.bfloat16)
+        q, k, v, do = (t.cuda() for t in (q, k, v, do))
+        abg = torch.cat([a, b, c]).cuda()
+        sh, o, stats = _forward(L, q, k, v, abg, prior, per_head=1)
+        ref = _backward(L, "geoattn_bwd", sh, q, k, v, o, do, abg, prior, stats, H)
+        got = _backward(L, "geoattn_bwd_noalloc", sh, q, k, v, o, do, abg, prior, stats, H)
+        for key in ref:
+            assert torch.isfinite(got[key].float()).all(), key
+            assert rel_l2(got[key], ref[key]) <= TOL, (seed, key, rel_l2(got[key], ref[key]))
+
+
+def test_noalloc_rejects_sizes_beyond_its_buffer(L):
+    from foreswe_gpu_optimization_b200 import _lib
+    args = _lib.BwdArgs()
+    args.shape = _lib.Shape(256, 16, 512, 128, _lib.DTYPE_BF16, 1)      # ~67 MB of row records > 16 MiB
+    assert L.geoattn_bwd_noalloc(ctypes.byref(args), None) == 7
+    args.shape = _lib.Shape(1, 1, 64, 64, _lib.DTYPE_FP32, 0)
+    assert L.geoattn_bwd_noalloc(ctypes.byref(args), None) == 2
+    assert b"16 MiB" in L.geoattn_error_string(7)
