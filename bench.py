@@ -242,7 +242,9 @@ def main():
         tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
     if B_TOTAL % world:
         raise SystemExit("world size must divide %d" % B_TOTAL)
-    b = B_TOTAL // world
+    from foreswe_gpu_optimization_b200.dp import shard
+    s0, s1 = shard(B_TOTAL, world, rank)
+    b = s1 - s0
     lat, lon, el = stations(0)
     geom = g.StationGeometry(lat, lon, el, device=dev)
     geom.prior(torch.bfloat16)
@@ -251,12 +253,10 @@ def main():
     params = [t.to(dev).requires_grad_(True) for t in (a0, b0, c0)]
     x = [t.detach().requires_grad_(True) for t in (q, k, v)]
 
+    from foreswe_gpu_optimization_b200.dp import allreduce_bias_grads as _allreduce
+
     def allreduce_bias_grads():
-        if dist_on:
-            flat = torch.cat([p.grad for p in params])
-            tdist.all_reduce(flat)
-            for i, p in enumerate(params):
-                p.grad.copy_(flat[i * H:(i + 1) * H])
+        _allreduce(params)
 
     def step(qq, kk, vv, dd):
         for t in x + params:
