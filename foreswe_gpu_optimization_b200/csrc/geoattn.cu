@@ -311,6 +311,15 @@ int map_transposed(CUtensorMap* m, const float* base, const Dims& d) {
   return make_tmap(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base, dims, str, box) ? GEOATTN_OK : GEOATTN_ERR_TMA;
 }
 
+// TMA map over a prior table ([np][np] pairs viewed as 32-bit words; box: 32 words x 128 rows).
+int map_prior(CUtensorMap* m, const void* table, const Dims& d) {
+  const uint64_t words = (uint64_t)d.np * (d.bf16 ? 1 : 2);
+  const uint64_t dims[2] = {words, (uint64_t)d.np};
+  const uint64_t str[1] = {words * 4};
+  const uint32_t box[2] = {32, (uint32_t)kBM};
+  return make_tmap(m, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, table, dims, str, box) ? GEOATTN_OK : GEOATTN_ERR_TMA;
+}
+
 int split(const GeoAttnTensor& t, const Dims& d, float* nat, float* tr, cudaStream_t st) {
   if (!t.data) return GEOATTN_ERR_INVALID;
   dim3 grid((d.np + 31) / 32, d.DP / 32, d.B * d.H), block(32, 8);
@@ -338,10 +347,10 @@ KParams base_params(const Dims& d, const float* abg, int per_head, const void* p
 }
 
 template <class K>
-int launch(K kernel, int smem, dim3 grid, cudaStream_t st, const TileMaps& maps, const KParams& p) {
+int launch(K kernel, int smem, int threads, dim3 grid, cudaStream_t st, const TileMaps& maps, const KParams& p) {
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return GEOATTN_ERR_LAUNCH;
-  kernel<<<grid, kThreads, smem, st>>>(maps, p);
+  kernel<<<grid, threads, smem, st>>>(maps, p);
   return cudaGetLastError() == cudaSuccess ? GEOATTN_OK : GEOATTN_ERR_LAUNCH;
 }
 
@@ -352,7 +361,8 @@ inline void record(void* const* ev, int i, cudaStream_t st) {
 template <bool BF16, int DP>
 int run_fwd(const TileMaps& maps, const KParams& p, const Dims& d, cudaStream_t st, void* const* ev) {
   record(ev, 0, st);
-  int rc = launch(geoattn_fwd_kernel<BF16, DP>, FwdCfg<BF16, DP>::SMEM, dim3(d.nrb, d.B * d.H), st, maps, p);
+  int rc = launch(geoattn_fwd_kernel<BF16, DP>, FwdCfg<BF16, DP>::SMEM, Tile<BF16, DP>::NTHREADS,
+                  dim3(d.nrb, d.B * d.H), st, maps, p);
   record(ev, 1, st);
   return rc;
 }
@@ -360,10 +370,12 @@ template <bool BF16, int DP>
 int run_bwd(const TileMaps& rmaps, const TileMaps& cmaps, const KParams& p, const Dims& d, cudaStream_t st,
             void* const* ev) {
   record(ev, 0, st);
-  int rc = launch(geoattn_bwd_rows_kernel<BF16, DP>, RowsCfg<BF16, DP>::SMEM, dim3(d.nrb, d.B * d.H), st, rmaps, p);
+  int rc = launch(geoattn_bwd_rows_kernel<BF16, DP>, RowsCfg<BF16, DP>::SMEM, Tile<BF16, DP>::NTHREADS,
+                  dim3(d.nrb, d.B * d.H), st, rmaps, p);
   if (rc) return rc;
   record(ev, 1, st);
-  rc = launch(geoattn_bwd_cols_kernel<BF16, DP>, ColsCfg<BF16, DP>::SMEM, dim3(d.nrb, d.B * d.H), st, cmaps, p);
+  rc = launch(geoattn_bwd_cols_kernel<BF16, DP>, ColsCfg<BF16, DP>::SMEM, Tile<BF16, DP>::NTHREADS,
+              dim3(d.nrb, d.B * d.H), st, cmaps, p);
   record(ev, 2, st);
   return rc;
 }
@@ -474,6 +486,7 @@ int geoattn_fwd(const GeoAttnFwdArgs* a, void* stream) {
         (rc = map_transposed(&maps.v, ws.vt, d)))
       return rc;
   }
+  if ((rc = map_prior(&maps.prior, a->prior, d))) return rc;
   KParams p = base_params(d, a->abg, a->shape.per_head, a->prior);
   p.o = a->o;
   for (int i = 0; i < 4; ++i) p.o_str[i] = a->o_stride[i];
@@ -522,6 +535,9 @@ int geoattn_bwd(const GeoAttnBwdArgs* a, void* stream) {
         (rc = map_transposed(&cm.dot, ws.dot, d)))
       return rc;
   }
+  if ((rc = map_prior(&rm.prior, a->prior, d)) ||
+      (rc = map_prior(&cm.prior, reinterpret_cast<const uint8_t*>(a->prior) + prior_table_bytes(d), d)))
+    return rc;
   KParams p = base_params(d, a->abg, a->shape.per_head, a->prior);
   p.o_in = a->o.data;
   p.dout = a->dout.data;

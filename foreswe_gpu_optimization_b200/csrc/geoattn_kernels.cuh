@@ -4,10 +4,12 @@
 //   S = Q K^T / sqrt(d);  P1 = softmax(S);  Z = alpha*P1 + beta*Dp + gamma*Ap;  P2 = softmax(Z);  O = P2 V
 // with the geo prior Dp = 1/(1+dist_km), Ap = 1/(1+angle_deg) read from a per-call table (prior.cu).
 //
-// All kernels share one CTA shape: warps 0-3 are the element-wise warps (thread t owns TMEM lane t, i.e. one row
-// of every 128-row accumulator), warp 4 issues TMA loads, warp 5 issues tcgen05.mma. Every MMA is M = 128 with
-// fp32 accumulators in tensor memory. Shared-memory operand tiles use the 128-byte swizzle; one "region" is
-// rows x 128 bytes (64 bf16 or 32 fp32 along the contiguous dimension).
+// All kernels share one CTA shape: EW element-wise warpgroups (EW = 2 for bf16, 1 for fp32; a thread of warp w owns
+// TMEM lane 32*(w%4) + lane, i.e. one row of every 128-row accumulator, and warpgroup w/4 owns every EW-th 32-column
+// piece of each chunk), then one warp that issues TMA loads and one that issues tcgen05.mma. Every MMA is M = 128
+// with fp32 accumulators in tensor memory. Shared-memory operand tiles use the 128-byte swizzle; one "region" is
+// rows x 128 bytes (64 bf16 or 32 fp32 along the contiguous dimension). The geo-prior tile of each chunk is staged
+// into shared memory by the TMA warp ahead of use (or, where shared memory is full, read from L2 directly).
 //
 // Softmax #1 runs in log2 units: t = acc * (log2(e)/sqrt(d)) is formed by one rounded multiply, the same
 // instruction in every pass and kernel, so the backward recomputes exactly the forward's scaled scores.
@@ -21,9 +23,6 @@
 namespace geoattn {
 
 constexpr int kBM = 128;        // rows per tile (TMEM lanes)
-constexpr int kThreads = 192;   // 4 element-wise warps + TMA warp + MMA warp
-constexpr int kTmaWarp = 4;
-constexpr int kMmaWarp = 5;
 constexpr float kLog2e = 1.4426950408889634f;
 
 __host__ __device__ constexpr int pow2_cols(int n) { return n <= 32 ? 32 : n <= 64 ? 64 : n <= 128 ? 128 : n <= 256 ? 256 : 512; }
@@ -84,8 +83,8 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, const 
   return __all_sync(0xffffffffu, mbar_wait(bar, parity, ctx));
 }
 
-// Named barrier among the 128 element-wise threads only.
-__device__ __forceinline__ void ew_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// Named barrier among the element-wise threads only (nthreads = 128 * EW).
+__device__ __forceinline__ void ew_sync(int nthreads) { asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory"); }
 
 // Byte offset of 16-byte chunk `q` (0..7) of row `r` inside a 128-byte-swizzled region.
 __device__ __forceinline__ uint32_t sw128(int r, int q) {
@@ -122,6 +121,40 @@ __device__ __forceinline__ void load_prior32(const void* table, int np, int row,
       dp[2 * i + 1] = f.z;
       ap[2 * i + 1] = f.w;
     }
+  }
+}
+
+// Prior tile staged by TMA: [128 rows][64 pair-columns as 32-bit words] as two 128-byte-swizzled regions of
+// 128 x 128 B. bf16 path: half2 pairs, piece p (32 pairs) = region p. fp32 path: float2 pairs, the single piece
+// (32 pairs) spans both regions (16 pairs each).
+constexpr int kPriorTileBytes = 2 * kBM * 128;
+
+template <bool F16>
+__device__ __forceinline__ void prior32_smem(const uint8_t* tile, int r, int piece, float (&dp)[32], float (&ap)[32]) {
+  if constexpr (F16) {
+    const uint8_t* reg = tile + piece * (kBM * 128);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const uint4 u = *reinterpret_cast<const uint4*>(reg + sw128(r, q));
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[k]));
+        dp[q * 4 + k] = f.x;
+        ap[q * 4 + k] = f.y;
+      }
+    }
+  } else {
+#pragma unroll
+    for (int rg = 0; rg < 2; ++rg)
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float4 f = *reinterpret_cast<const float4*>(tile + rg * (kBM * 128) + sw128(r, q));
+        dp[rg * 16 + q * 2] = f.x;
+        ap[rg * 16 + q * 2] = f.y;
+        dp[rg * 16 + q * 2 + 1] = f.z;
+        ap[rg * 16 + q * 2 + 1] = f.w;
+      }
   }
 }
 
@@ -200,7 +233,8 @@ __device__ __forceinline__ float load_elem(const void* base, long long off) {
 
 // ---------------------------------------------------------------------------------------------------------------
 // Tile configuration. KB = elements per 128-byte row; every key/query chunk is KB wide so that a chunk row of the
-// element-wise outputs (P, dS, P2^T, dS^T) is exactly one swizzle row.
+// element-wise outputs (P, dS, P2^T, dS^T) is exactly one swizzle row, and a chunk row of the prior (CH pairs) is
+// 256 bytes = two swizzle regions.
 // ---------------------------------------------------------------------------------------------------------------
 template <bool BF16, int DP_>
 struct Tile {
@@ -211,12 +245,34 @@ struct Tile {
   static constexpr int KS = BF16 ? 16 : 8;  // MMA K per instruction
   static constexpr int NKB = DP / KB;       // 128-byte regions along D
   static constexpr int CH = KB;             // chunk width (keys or queries)
+  static constexpr int PIECES = CH / 32;    // 32-column pieces per chunk
   static constexpr int PL = BF16 ? 1 : 2;   // planes of Q, K, V, dO: hi[, lo]
   static constexpr int NTERM = BF16 ? 1 : 3;
   static constexpr Kind KIND = BF16 ? Kind::kF16 : Kind::kTF32;
   static constexpr uint32_t FMT = BF16 ? 1 : 2;
+  static constexpr int EW = BF16 ? 2 : 1;   // element-wise warpgroups
+  static constexpr int EWT = 128 * EW;      // element-wise threads
+  static constexpr int NTHREADS = EWT + 64;
+  static constexpr int TMA_WARP = 4 * EW;
+  static constexpr int MMA_WARP = 4 * EW + 1;
   static_assert(DP % KB == 0, "padded head dim must be a whole number of 128-byte regions");
+  static_assert(PIECES % EW == 0, "each warpgroup owns whole pieces");
 };
+
+// Element-wise thread identity.
+struct Ew {
+  int r;          // TMEM lane = row of the 128-row accumulator
+  int wg;         // warpgroup
+  uint32_t lane_base;
+};
+__device__ __forceinline__ Ew ew_id(uint32_t tmem) {
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  Ew e;
+  e.r = (warp & 3) * 32 + lane;
+  e.wg = warp >> 2;
+  e.lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+  return e;
+}
 
 // Issue acc[128 x NB] (+)= A[128 x DP] . B[NB x DP]^T, both K-major, regions of 128 x 128 B (A) and NB x 128 B (B).
 // With NTERM == 3 the product is hi*hi + hi*lo + lo*hi (planes 0/1 at a_plane/b_plane byte strides).
@@ -280,10 +336,26 @@ __device__ __forceinline__ void tma_tile(uint8_t* dst, const CUtensorMap* map, u
 __device__ __forceinline__ void tma_tileT(uint8_t* dst, const CUtensorMap* map, uint64_t* bar, int n0, int h, int b) {
   tma_load_4d(dst, map, bar, n0, 0, h, b);
 }
+// Prior tile of chunk c: rows [row0, row0+128), pair columns [c*CH, c*CH+CH) = 64 32-bit words.
+__device__ __forceinline__ void tma_prior(uint8_t* dst, const CUtensorMap* map, uint64_t* bar, int row0, int c) {
+  tma_load_2d(dst, map, bar, c * 64, row0);
+  tma_load_2d(dst + kBM * 128, map, bar, c * 64 + 32, row0);
+}
 
 struct TileMaps {
-  CUtensorMap q, k, v, dout, kt, qt, dot;  // unused entries are left zero
+  CUtensorMap q, k, v, dout, kt, qt, dot, prior;  // unused entries are left zero
 };
+
+// Prior access for one chunk: staged tile in shared memory, or the table in global memory.
+template <bool F16, bool STAGED>
+__device__ __forceinline__ void prior_piece(const uint8_t* tile, const void* table, int np, int row, int r, int c,
+                                            int piece, float (&dp)[32], float (&ap)[32]) {
+  if constexpr (STAGED) {
+    prior32_smem<F16>(tile, r, piece, dp, ap);
+  } else {
+    load_prior32<F16>(table, np, row, c * (F16 ? 64 : 32) + piece * 32, dp, ap);
+  }
+}
 
 // ===============================================================================================================
 // Forward: one CTA per (128-query row block, b*h). Pass A: row max / sum of softmax #1 over all key chunks.
@@ -292,6 +364,7 @@ struct TileMaps {
 template <bool BF16, int DP>
 struct FwdCfg : Tile<BF16, DP> {
   using T = Tile<BF16, DP>;
+  static constexpr int NPR = (BF16 && DP > 128) ? 1 : 2;  // staged prior buffers
   static constexpr int Q_BYTES = kBM * DP * T::EB;          // per plane
   static constexpr int K_BYTES = T::CH * DP * T::EB;        // per plane per buffer
   static constexpr int V_BYTES = T::CH * DP * T::EB;        // hi only (natural bf16 / transposed fp32)
@@ -300,22 +373,26 @@ struct FwdCfg : Tile<BF16, DP> {
   static constexpr int OFF_K = OFF_Q + T::PL * Q_BYTES;
   static constexpr int OFF_V = OFF_K + 2 * T::PL * K_BYTES;
   static constexpr int OFF_P = OFF_V + 2 * V_BYTES;
-  static constexpr int SMEM = OFF_P + 2 * P_BYTES + 1024;
+  static constexpr int OFF_PR = OFF_P + 2 * P_BYTES;
+  static constexpr int SMEM = OFF_PR + NPR * kPriorTileBytes + 1024;
   static constexpr int TM_S = 0;
   static constexpr int TM_O = 2 * T::CH;
   static constexpr int TMEM_COLS = pow2_cols(2 * T::CH + DP);
 };
 
 template <bool BF16, int DP>
-__global__ void __launch_bounds__(kThreads, 1) geoattn_fwd_kernel(const __grid_constant__ TileMaps maps, const KParams p) {
+__global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
+    geoattn_fwd_kernel(const __grid_constant__ TileMaps maps, const KParams p) {
   using C = FwdCfg<BF16, DP>;
   using T = typename C::T;
+  constexpr int NPR = C::NPR;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ uint64_t bar_q, bar_kfull[2], bar_kempty[2], bar_vfull[2], bar_vempty[2], bar_sfull[2], bar_sempty[2],
-      bar_pfull[2], bar_pempty[2], bar_ofull;
+      bar_pfull[2], bar_pempty[2], bar_prfull[2], bar_prempty[2], bar_ofull;
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_flag;
+  __shared__ float xch[2][2][kBM];  // cross-warpgroup row statistics
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int rb = blockIdx.x, bh = blockIdx.y, b = bh / p.H, h = bh % p.H;
   const int nchunks = (p.N + T::CH - 1) / T::CH;
@@ -330,9 +407,11 @@ __global__ void __launch_bounds__(kThreads, 1) geoattn_fwd_kernel(const __grid_c
       mbar_init(&bar_vfull[i], 1);
       mbar_init(&bar_vempty[i], 1);
       mbar_init(&bar_sfull[i], 1);
-      mbar_init(&bar_sempty[i], 128);
-      mbar_init(&bar_pfull[i], 128);
+      mbar_init(&bar_sempty[i], T::EWT);
+      mbar_init(&bar_pfull[i], T::EWT);
       mbar_init(&bar_pempty[i], 1);
+      mbar_init(&bar_prfull[i], 1);
+      mbar_init(&bar_prempty[i], T::EWT);
     }
     mbar_init(&bar_ofull, 1);
     fence_barrier_init();
@@ -347,11 +426,12 @@ __global__ void __launch_bounds__(kThreads, 1) geoattn_fwd_kernel(const __grid_c
   const uint32_t tmem = tmem_base_sh;
   const uint32_t sbase = smem_u32(smem);
 
-  if (warp == kTmaWarp) {
+  if (warp == T::TMA_WARP) {
     if (lane == 0) {
       prefetch_tmap(&maps.q);
       prefetch_tmap(&maps.k);
       prefetch_tmap(&maps.v);
+      prefetch_tmap(&maps.prior);
       mbar_arrive_expect_tx(&bar_q, T::PL * C::Q_BYTES);
       tma_tile<T>(smem + C::OFF_Q, &maps.q, &bar_q, kBM, rb * kBM, h, b, p.B, T::PL);
       int kc = 0, vc = 0;
@@ -372,12 +452,16 @@ __global__ void __launch_bounds__(kThreads, 1) geoattn_fwd_kernel(const __grid_c
               tma_tile<T>(smem + C::OFF_V + vs * C::V_BYTES, &maps.v, &bar_vfull[vs], T::CH, c * T::CH, h, b, p.B, 1);
             else
               tma_tileT(smem + C::OFF_V + vs * C::V_BYTES, &maps.v, &bar_vfull[vs], c * T::CH, h, b);
+            const int ps = c % NPR;
+            if (!(ok = mbar_wait(&bar_prempty[ps], ((c / NPR) & 1) ^ 1, ctx))) break;
+            mbar_arrive_expect_tx(&bar_prfull[ps], kPriorTileBytes);
+            tma_prior(smem + C::OFF_PR + ps * kPriorTileBytes, &maps.prior, &bar_prfull[ps], rb * kBM, c);
             ++vc;
           }
         }
       }
     }
-  } else if (warp == kMmaWarp) {
+  } else if (warp == T::MMA_WARP) {
     if (lane == 0) {
       int kc = 0, sc = 0, pc = 0;
       bool ok = mbar_wait(&bar_q, 0, ctx);
@@ -411,23 +495,22 @@ __global__ void __launch_bounds__(kThreads, 1) geoattn_fwd_kernel(const __grid_c
     }
   } else {
     // ---------------- element-wise warps ----------------
-    const int r = threadIdx.x;  // 0..127
-    const int row = rb * kBM + r;
-    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+    const Ew e = ew_id(tmem);
+    const int row = rb * kBM + e.r;
     const Abg ab = load_abg(p, h);
     const float sc_l2 = p.scale_log2;
     float m = -INFINITY, l = 0.f;
     int sc = 0;
     bool ok = true;
-    // Pass A
+    // Pass A: running max and sum over this warpgroup's pieces
     for (int c = 0; c < nchunks && ok; ++c) {
       const int ss = sc & 1;
       if (!(ok = warp_wait(&bar_sfull[ss], (sc >> 1) & 1, ctx))) break;
       tc_fence_after();
 #pragma unroll
-      for (int piece = 0; piece < T::CH / 32; ++piece) {
+      for (int piece = e.wg; piece < T::PIECES; piece += T::EW) {
         float v[32];
-        tmem_ld32(lane_base + C::TM_S + ss * T::CH + piece * 32, v);
+        tmem_ld32(e.lane_base + C::TM_S + ss * T::CH + piece * 32, v);
         const int col0 = c * T::CH + piece * 32;
         float mx = -INFINITY;
 #pragma unroll
@@ -436,51 +519,69 @@ __global__ void __launch_bounds__(kThreads, 1) geoattn_fwd_kernel(const __grid_c
           mx = fmaxf(mx, v[j]);
         }
         const float mn = fmaxf(m, mx);
+        // a warpgroup whose columns so far are all masked keeps m = -inf, l = 0 (never 2^(-inf - -inf))
+        const float mref = (mn == -INFINITY) ? 0.f : mn;
         float s = 0.f;
 #pragma unroll
-        for (int j = 0; j < 32; ++j) s += ex2(v[j] - mn);
-        l = l * ex2(m - mn) + s;
+        for (int j = 0; j < 32; ++j) s += ex2(v[j] - mref);
+        l = l * ex2(m - mref) + s;
         m = mn;
       }
       tc_fence_before();
       mbar_arrive(&bar_sempty[ss]);
       ++sc;
     }
+    if constexpr (T::EW == 2) {  // combine the two warpgroups' statistics (same order in both)
+      xch[0][e.wg][e.r] = m;
+      xch[1][e.wg][e.r] = l;
+      ew_sync(T::EWT);
+      const float m0 = xch[0][0][e.r], m1 = xch[0][1][e.r], l0 = xch[1][0][e.r], l1 = xch[1][1][e.r];
+      m = fmaxf(m0, m1);
+      l = l0 * ex2(m0 - m) + l1 * ex2(m1 - m);
+      ew_sync(T::EWT);
+    }
     const float inv_l1 = __frcp_rn(l);
     const float aL = ab.a * kLog2e, bL = ab.b * kLog2e, gL = ab.g * kLog2e, cL = ab.c * kLog2e;
-    const int prow = row < p.np ? row : 0;
     float l2 = 0.f;
     int pc = 0;
     // Pass B
     for (int c = 0; c < nchunks && ok; ++c) {
-      const int ss = sc & 1, ps = pc & 1;
+      const int ss = sc & 1, ps = pc & 1, prs = c % NPR;
       if (!(ok = warp_wait(&bar_sfull[ss], (sc >> 1) & 1, ctx))) break;
       if (!(ok = warp_wait(&bar_pempty[ps], ((pc >> 1) & 1) ^ 1, ctx))) break;
+      if (!(ok = warp_wait(&bar_prfull[prs], (c / NPR) & 1, ctx))) break;
       tc_fence_after();
       uint8_t* preg = smem + C::OFF_P + ps * C::P_BYTES;
+      const uint8_t* prt = smem + C::OFF_PR + prs * kPriorTileBytes;
 #pragma unroll
-      for (int piece = 0; piece < T::CH / 32; ++piece) {
+      for (int piece = e.wg; piece < T::PIECES; piece += T::EW) {
         float v[32], dp[32], ap[32];
-        tmem_ld32(lane_base + C::TM_S + ss * T::CH + piece * 32, v);
+        tmem_ld32(e.lane_base + C::TM_S + ss * T::CH + piece * 32, v);
         const int col0 = c * T::CH + piece * 32;
-        load_prior32<BF16>(p.prior, p.np, prow, col0, dp, ap);
+        prior32_smem<BF16>(prt, e.r, piece, dp, ap);
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
           const float t = v[j] * sc_l2;
           const float p1 = ex2(t - m) * inv_l1;
           const float z2 = fmaf(aL, p1, fmaf(bL, dp[j], fmaf(gL, ap[j], -cL)));
-          const float e = (col0 + j < p.N) ? ex2(z2) : 0.f;
-          l2 += e;
-          v[j] = e;
+          const float ev = (col0 + j < p.N) ? ex2(z2) : 0.f;
+          l2 += ev;
+          v[j] = ev;
         }
-        stage_row32<BF16>(preg, r, piece, v);
+        stage_row32<BF16>(preg, e.r, piece, v);
       }
       fence_proxy_async_smem();
       tc_fence_before();
+      mbar_arrive(&bar_prempty[prs]);
       mbar_arrive(&bar_pfull[ps]);
       mbar_arrive(&bar_sempty[ss]);
       ++sc;
       ++pc;
+    }
+    if constexpr (T::EW == 2) {
+      xch[0][e.wg][e.r] = l2;
+      ew_sync(T::EWT);
+      l2 = xch[0][0][e.r] + xch[0][1][e.r];
     }
     if (ok) ok = warp_wait(&bar_ofull, 0, ctx);
     tc_fence_after();
@@ -488,12 +589,12 @@ __global__ void __launch_bounds__(kThreads, 1) geoattn_fwd_kernel(const __grid_c
       const float inv_l2 = __frcp_rn(l2);
       const long long ooff = (long long)b * p.o_str[0] + (long long)h * p.o_str[1] + (long long)row * p.o_str[2];
 #pragma unroll
-      for (int d0 = 0; d0 < DP; d0 += 32) {
+      for (int d0 = e.wg * 32; d0 < DP; d0 += 32 * T::EW) {
         float v[32];
-        tmem_ld32(lane_base + C::TM_O + d0, v);
+        tmem_ld32(e.lane_base + C::TM_O + d0, v);
         if (row < p.N && d0 < p.D) store_row32<BF16>(p.o, ooff, p.o_str[3], d0, p.D, v, inv_l2);
       }
-      if (row < p.N) {
+      if (row < p.N && e.wg == 0) {
         const size_t s = (size_t)bh * p.N + row, n = (size_t)p.B * p.H * p.N;
         p.stats[s] = m;
         p.stats[n + s] = l;
@@ -518,6 +619,8 @@ __global__ void __launch_bounds__(kThreads, 1) geoattn_fwd_kernel(const __grid_c
 template <bool BF16, int DP>
 struct RowsCfg : Tile<BF16, DP> {
   using T = Tile<BF16, DP>;
+  static constexpr int NKV = (!BF16 || DP > 128) ? 1 : 2;  // K/V chunk buffers
+  static constexpr int NPR = (BF16 && DP <= 128) ? 2 : 1;   // staged prior buffers
   static constexpr int Q_BYTES = kBM * DP * T::EB;    // per plane (Q and dO)
   static constexpr int K_BYTES = T::CH * DP * T::EB;  // per plane per buffer (K and V chunks)
   static constexpr int KT_BYTES = BF16 ? 0 : DP * 128;  // fp32: transposed K chunk (hi) for dQ
@@ -526,10 +629,11 @@ struct RowsCfg : Tile<BF16, DP> {
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_DO = OFF_Q + T::PL * Q_BYTES;
   static constexpr int OFF_K = OFF_DO + T::PL * Q_BYTES;
-  static constexpr int OFF_V = OFF_K + 2 * T::PL * K_BYTES;
-  static constexpr int OFF_KT = OFF_V + 2 * T::PL * K_BYTES;
+  static constexpr int OFF_V = OFF_K + NKV * T::PL * K_BYTES;
+  static constexpr int OFF_KT = OFF_V + NKV * T::PL * K_BYTES;
   static constexpr int OFF_DS = OFF_KT + NDS * KT_BYTES;
-  static constexpr int SMEM = OFF_DS + NDS * DS_BYTES + 1024;
+  static constexpr int OFF_PR = OFF_DS + NDS * DS_BYTES;
+  static constexpr int SMEM = OFF_PR + NPR * kPriorTileBytes + 1024;
   static constexpr int TM_S = 0;                   // 2 buffers
   static constexpr int TM_DP = 2 * T::CH;          // 2 buffers
   static constexpr int TM_DQ = 4 * T::CH;
@@ -537,16 +641,18 @@ struct RowsCfg : Tile<BF16, DP> {
 };
 
 template <bool BF16, int DP>
-__global__ void __launch_bounds__(kThreads, 1) geoattn_bwd_rows_kernel(const __grid_constant__ TileMaps maps, const KParams p) {
+__global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
+    geoattn_bwd_rows_kernel(const __grid_constant__ TileMaps maps, const KParams p) {
   using C = RowsCfg<BF16, DP>;
   using T = typename C::T;
+  constexpr int NKV = C::NKV, NPR = C::NPR;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ uint64_t bar_q, bar_kfull[2], bar_kempty[2], bar_vfull[2], bar_vempty[2], bar_sfull[2], bar_sempty[2],
-      bar_dsfull[2], bar_dsempty[2], bar_ktfull[2], bar_ktempty[2], bar_dqfull;
+      bar_dsfull[2], bar_dsempty[2], bar_ktfull[2], bar_ktempty[2], bar_prfull[2], bar_prempty[2], bar_dqfull;
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_flag;
-  __shared__ double red[4][3];
+  __shared__ double red[8][3];
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int rb = blockIdx.x, bh = blockIdx.y, b = bh / p.H, h = bh % p.H;
   const int nchunks = (p.N + T::CH - 1) / T::CH;
@@ -561,11 +667,13 @@ __global__ void __launch_bounds__(kThreads, 1) geoattn_bwd_rows_kernel(const __g
       mbar_init(&bar_vfull[i], 1);
       mbar_init(&bar_vempty[i], 1);
       mbar_init(&bar_sfull[i], 1);
-      mbar_init(&bar_sempty[i], 128);
-      mbar_init(&bar_dsfull[i], 128);
+      mbar_init(&bar_sempty[i], T::EWT);
+      mbar_init(&bar_dsfull[i], T::EWT);
       mbar_init(&bar_dsempty[i], 1);
       mbar_init(&bar_ktfull[i], 1);
       mbar_init(&bar_ktempty[i], 1);
+      mbar_init(&bar_prfull[i], 1);
+      mbar_init(&bar_prempty[i], T::EWT);
     }
     mbar_init(&bar_dqfull, 1);
     fence_barrier_init();
@@ -580,25 +688,32 @@ __global__ void __launch_bounds__(kThreads, 1) geoattn_bwd_rows_kernel(const __g
   const uint32_t tmem = tmem_base_sh;
   const uint32_t sbase = smem_u32(smem);
 
-  if (warp == kTmaWarp) {
+  if (warp == T::TMA_WARP) {
     if (lane == 0) {
       prefetch_tmap(&maps.q);
       prefetch_tmap(&maps.k);
       prefetch_tmap(&maps.v);
       prefetch_tmap(&maps.dout);
+      prefetch_tmap(&maps.prior);
       mbar_arrive_expect_tx(&bar_q, 2 * T::PL * C::Q_BYTES);
       tma_tile<T>(smem + C::OFF_Q, &maps.q, &bar_q, kBM, rb * kBM, h, b, p.B, T::PL);
       tma_tile<T>(smem + C::OFF_DO, &maps.dout, &bar_q, kBM, rb * kBM, h, b, p.B, T::PL);
-      int kc = 0, tc = 0;
+      int kc = 0, tc = 0, pc = 0;
       bool ok = true;
       for (int sweep = 0; sweep < 2 && ok; ++sweep) {
         for (int c = 0; c < nchunks && ok; ++c) {
-          const int ks = kc & 1;
-          if (!(ok = mbar_wait(&bar_kempty[ks], ((kc >> 1) & 1) ^ 1, ctx))) break;
+          // the prior tile first: it only waits for the element-wise warps, while K may wait for dQ's MMA
+          const int ps = pc % NPR;
+          if (!(ok = mbar_wait(&bar_prempty[ps], ((pc / NPR) & 1) ^ 1, ctx))) break;
+          mbar_arrive_expect_tx(&bar_prfull[ps], kPriorTileBytes);
+          tma_prior(smem + C::OFF_PR + ps * kPriorTileBytes, &maps.prior, &bar_prfull[ps], rb * kBM, c);
+          ++pc;
+          const int ks = kc % NKV;
+          if (!(ok = mbar_wait(&bar_kempty[ks], ((kc / NKV) & 1) ^ 1, ctx))) break;
           mbar_arrive_expect_tx(&bar_kfull[ks], T::PL * C::K_BYTES);
           tma_tile<T>(smem + C::OFF_K + ks * T::PL * C::K_BYTES, &maps.k, &bar_kfull[ks], T::CH, c * T::CH, h, b, p.B,
                       T::PL);
-          if (!(ok = mbar_wait(&bar_vempty[ks], ((kc >> 1) & 1) ^ 1, ctx))) break;
+          if (!(ok = mbar_wait(&bar_vempty[ks], ((kc / NKV) & 1) ^ 1, ctx))) break;
           mbar_arrive_expect_tx(&bar_vfull[ks], T::PL * C::K_BYTES);
           tma_tile<T>(smem + C::OFF_V + ks * T::PL * C::K_BYTES, &maps.v, &bar_vfull[ks], T::CH, c * T::CH, h, b, p.B,
                       T::PL);
@@ -615,14 +730,14 @@ __global__ void __launch_bounds__(kThreads, 1) geoattn_bwd_rows_kernel(const __g
         }
       }
     }
-  } else if (warp == kMmaWarp) {
+  } else if (warp == T::MMA_WARP) {
     if (lane == 0) {
       int kc = 0, sc = 0, dc = 0;
       bool ok = mbar_wait(&bar_q, 0, ctx);
       auto issue = [&](bool release_k) -> bool {
-        const int ks = kc & 1, ss = sc & 1;
-        if (!mbar_wait(&bar_kfull[ks], (kc >> 1) & 1, ctx)) return false;
-        if (!mbar_wait(&bar_vfull[ks], (kc >> 1) & 1, ctx)) return false;
+        const int ks = kc % NKV, ss = sc & 1;
+        if (!mbar_wait(&bar_kfull[ks], (kc / NKV) & 1, ctx)) return false;
+        if (!mbar_wait(&bar_vfull[ks], (kc / NKV) & 1, ctx)) return false;
         if (!mbar_wait(&bar_sempty[ss], ((sc >> 1) & 1) ^ 1, ctx)) return false;
         tc_fence_after();
         const uint32_t kb = sbase + C::OFF_K + ks * T::PL * C::K_BYTES;
@@ -636,19 +751,15 @@ __global__ void __launch_bounds__(kThreads, 1) geoattn_bwd_rows_kernel(const __g
         ++sc;
         return true;
       };
-      for (int c = 0; c < nchunks && ok; ++c) ok = issue(true);
-      const int kc0 = kc;  // first K use of sweep 2
-      if (ok) ok = issue(false);
-      for (int c = 0; c < nchunks && ok; ++c) {
-        if (c + 1 < nchunks && !(ok = issue(false))) break;
+      auto issue_dq = [&](int c, int kc0) -> bool {
         const int ds = dc % C::NDS;
-        if (!(ok = mbar_wait(&bar_dsfull[ds], (dc / C::NDS) & 1, ctx))) break;
-        const int ks = (kc0 + c) & 1;
+        if (!mbar_wait(&bar_dsfull[ds], (dc / C::NDS) & 1, ctx)) return false;
+        const int ks = (kc0 + c) % NKV;
         uint32_t bsrc;
         if constexpr (BF16) {
           bsrc = sbase + C::OFF_K + ks * T::PL * C::K_BYTES;
         } else {
-          if (!(ok = mbar_wait(&bar_ktfull[ds], (dc / C::NDS) & 1, ctx))) break;
+          if (!mbar_wait(&bar_ktfull[ds], (dc / C::NDS) & 1, ctx)) return false;
           bsrc = sbase + C::OFF_KT + ds * C::KT_BYTES;
         }
         tc_fence_after();
@@ -657,73 +768,146 @@ __global__ void __launch_bounds__(kThreads, 1) geoattn_bwd_rows_kernel(const __g
         if constexpr (!BF16) mma_commit(&bar_ktempty[ds]);
         mma_commit(&bar_kempty[ks]);
         ++dc;
+        return true;
+      };
+      for (int c = 0; c < nchunks && ok; ++c) ok = issue(true);
+      const int kc0 = kc;  // first K use of sweep 2
+      if (ok) ok = issue(false);
+      for (int c = 0; c < nchunks && ok; ++c) {
+        if constexpr (NKV == 2) {  // look ahead: S/dP of the next chunk overlap the element-wise work on this one
+          if (c + 1 < nchunks && !(ok = issue(false))) break;
+          if (!(ok = issue_dq(c, kc0))) break;
+        } else {                   // one K/V buffer: the next chunk's K can only arrive after this chunk's dQ
+          if (!(ok = issue_dq(c, kc0))) break;
+          if (c + 1 < nchunks && !(ok = issue(false))) break;
+        }
       }
       if (ok) mma_commit(&bar_dqfull);
     }
   } else {
     // ---------------- element-wise warps ----------------
-    const int r = threadIdx.x;
-    const int row = rb * kBM + r;
+    const Ew e = ew_id(tmem);
+    const int row = rb * kBM + e.r;
     const bool valid = row < p.N;
-    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
     const Abg ab = load_abg(p, h);
     const float sc_l2 = p.scale_log2;
     const size_t nrows_all = (size_t)p.B * p.H * p.N;
     const size_t srow = (size_t)bh * p.N + (valid ? row : 0);
     float m = 0.f, inv_l1 = 0.f, inv_l2 = 0.f, d2s = 0.f;
+    bool ok = true;
     if (valid) {
       m = p.stats[srow];
       inv_l1 = __frcp_rn(p.stats[nrows_all + srow]);
       inv_l2 = __frcp_rn(p.stats[2 * nrows_all + srow]);
-      const long long oo = (long long)b * p.oi_str[0] + (long long)h * p.oi_str[1] + (long long)row * p.oi_str[2];
-      const long long od = (long long)b * p.do_str[0] + (long long)h * p.do_str[1] + (long long)row * p.do_str[2];
-      for (int d = 0; d < p.D; ++d)
-        d2s = fmaf(load_elem<BF16>(p.dout, od + d * p.do_str[3]), load_elem<BF16>(p.o_in, oo + d * p.oi_str[3]), d2s);
+    }
+    // delta2' = dO . O per row. bf16: dO from the TMA-loaded tile in shared memory and O with 16-byte loads, the
+    // row's 16-byte chunks split between the warpgroups; fp32: straight from global memory.
+    const long long oo = (long long)b * p.oi_str[0] + (long long)h * p.oi_str[1] + (long long)row * p.oi_str[2];
+    if constexpr (BF16) {
+      ok = warp_wait(&bar_q, 0, ctx);
+      const __nv_bfloat16* orow = reinterpret_cast<const __nv_bfloat16*>(p.o_in) + oo;
+      const bool vec = p.oi_str[3] == 1 && (reinterpret_cast<uintptr_t>(orow) & 15) == 0;
+      if (ok && valid) {
+        for (int ch = e.wg; ch < T::NKB * 8; ch += T::EW) {
+          const int kb = ch >> 3, q = ch & 7, d0 = kb * 64 + q * 8;
+          if (d0 >= p.D) continue;
+          const uint4 du = *reinterpret_cast<const uint4*>(smem + C::OFF_DO + kb * (kBM * 128) + sw128(e.r, q));
+          const uint32_t dw[4] = {du.x, du.y, du.z, du.w};
+          float ov[8];
+          if (vec && d0 + 8 <= p.D) {
+            const uint4 u = *reinterpret_cast<const uint4*>(orow + d0);
+            const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[k]));
+              ov[2 * k] = f.x;
+              ov[2 * k + 1] = f.y;
+            }
+          } else {
+#pragma unroll
+            for (int k = 0; k < 8; ++k) ov[k] = d0 + k < p.D ? __bfloat162float(orow[(d0 + k) * p.oi_str[3]]) : 0.f;
+          }
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&dw[k]));
+            d2s = fmaf(f.x, ov[2 * k], d2s);
+            d2s = fmaf(f.y, ov[2 * k + 1], d2s);
+          }
+        }
+      }
+      if constexpr (T::EW == 2) {
+        float* xs = reinterpret_cast<float*>(smem + C::OFF_DS) + 14 * kBM;
+        xs[e.wg * kBM + e.r] = d2s;
+        ew_sync(T::EWT);
+        d2s = xs[e.r] + xs[kBM + e.r];
+      }
+    } else {
+      if (valid) {
+        const long long od = (long long)b * p.do_str[0] + (long long)h * p.do_str[1] + (long long)row * p.do_str[2];
+        for (int d = 0; d < p.D; ++d)
+          d2s = fmaf(load_elem<BF16>(p.dout, od + d * p.do_str[3]), load_elem<BF16>(p.o_in, oo + d * p.oi_str[3]), d2s);
+      }
     }
     const float aL = ab.a * kLog2e, bL = ab.b * kLog2e, gL = ab.g * kLog2e, cL = ab.c * kLog2e;
-    const int prow = row < p.np ? row : 0;
-    float sr = 0.f, sa = 0.f, sb = 0.f, scc = 0.f, se = 0.f, sf = 0.f, sg = 0.f;
-    int sc = 0;
-    bool ok = true;
+    float acc[7] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // r, a, b, c, e, f, g
+    int sc = 0, pc = 0;
     for (int c = 0; c < nchunks && ok; ++c) {
-      const int ss = sc & 1;
+      const int ss = sc & 1, prs = pc % NPR;
       if (!(ok = warp_wait(&bar_sfull[ss], (sc >> 1) & 1, ctx))) break;
+      if (!(ok = warp_wait(&bar_prfull[prs], (pc / NPR) & 1, ctx))) break;
       tc_fence_after();
+      const uint8_t* prt = smem + C::OFF_PR + prs * kPriorTileBytes;
 #pragma unroll 1
-      for (int piece = 0; piece < T::CH / 32; ++piece) {
-        float v[32], w[32];
-        tmem_ld32(lane_base + C::TM_S + ss * T::CH + piece * 32, v);
-        tmem_ld32(lane_base + C::TM_DP + ss * T::CH + piece * 32, w);
+      for (int piece = e.wg; piece < T::PIECES; piece += T::EW) {
+        uint32_t vs[32], ws[32];
+        tmem_ld32_issue(e.lane_base + C::TM_S + ss * T::CH + piece * 32, vs);
+        tmem_ld32_issue(e.lane_base + C::TM_DP + ss * T::CH + piece * 32, ws);
         const int col0 = c * T::CH + piece * 32;
         float dp[32], ap[32];
-        load_prior32<BF16>(p.prior, p.np, prow, col0, dp, ap);
+        prior32_smem<BF16>(prt, e.r, piece, dp, ap);
+        tmem_wait32(vs);
+        tmem_pin32(ws);
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
           const bool cv = col0 + j < p.N;
-          const float t = v[j] * sc_l2;
+          const float t = __uint_as_float(vs[j]) * sc_l2;
           const float p1 = cv ? ex2(t - m) * inv_l1 : 0.f;
           const float z2 = fmaf(aL, p1, fmaf(bL, dp[j], fmaf(gL, ap[j], -cL)));
           const float p2 = cv ? ex2(z2) * inv_l2 : 0.f;
-          const float wv = p2 * (w[j] - d2s);
-          sr += wv;
-          sa = fmaf(wv, p1, sa);
-          sb = fmaf(p2, p1, sb);
-          scc = fmaf(wv, dp[j], scc);
-          se = fmaf(p2, dp[j], se);
-          sf = fmaf(wv, ap[j], sf);
-          sg = fmaf(p2, ap[j], sg);
+          const float wv = p2 * (__uint_as_float(ws[j]) - d2s);
+          acc[0] += wv;
+          acc[1] = fmaf(wv, p1, acc[1]);
+          acc[2] = fmaf(p2, p1, acc[2]);
+          acc[3] = fmaf(wv, dp[j], acc[3]);
+          acc[4] = fmaf(p2, dp[j], acc[4]);
+          acc[5] = fmaf(wv, ap[j], acc[5]);
+          acc[6] = fmaf(p2, ap[j], acc[6]);
         }
       }
       tc_fence_before();
+      mbar_arrive(&bar_prempty[prs]);
       mbar_arrive(&bar_sempty[ss]);
       ++sc;
+      ++pc;
     }
+    if constexpr (T::EW == 2) {
+      // combine the two warpgroups' row sums through the (still unused) dS buffer, warpgroup 0's first
+      float* xs = reinterpret_cast<float*>(smem + C::OFF_DS);
+#pragma unroll
+      for (int k = 0; k < 7; ++k) xs[(e.wg * 7 + k) * kBM + e.r] = acc[k];
+      ew_sync(T::EWT);
+#pragma unroll
+      for (int k = 0; k < 7; ++k) acc[k] = xs[k * kBM + e.r] + xs[(7 + k) * kBM + e.r];
+      ew_sync(T::EWT);
+    }
+    const float sr = acc[0];
     const float delta2 = d2s + sr;
-    const float ta = fmaf(-sr, sb, sa);
+    const float ta = fmaf(-sr, acc[2], acc[1]);
     const float delta1 = ab.a * ta;
-    double ga = valid ? (double)ta : 0.0, gb = valid ? (double)fmaf(-sr, se, scc) : 0.0,
-           gg = valid ? (double)fmaf(-sr, sg, sf) : 0.0;
-    if (valid && ok) {
+    const bool mine = valid && e.wg == 0;
+    double ga = mine ? (double)ta : 0.0, gb = mine ? (double)fmaf(-sr, acc[4], acc[3]) : 0.0,
+           gg = mine ? (double)fmaf(-sr, acc[6], acc[5]) : 0.0;
+    if (mine && ok) {
       float* rec = p.rowrec + srow * 8;
       *reinterpret_cast<float4*>(rec) = make_float4(m, inv_l1, inv_l2, delta1);
       *reinterpret_cast<float4*>(rec + 4) = make_float4(delta2, 0.f, 0.f, 0.f);
@@ -739,7 +923,7 @@ __global__ void __launch_bounds__(kThreads, 1) geoattn_bwd_rows_kernel(const __g
       red[warp][1] = gb;
       red[warp][2] = gg;
     }
-    ew_sync();
+    ew_sync(T::EWT);
     if (threadIdx.x == 0) {
       double* out = p.part + ((size_t)bh * p.nrb + rb) * 3;
       out[0] = (red[0][0] + red[1][0]) + (red[2][0] + red[3][0]);
@@ -749,46 +933,52 @@ __global__ void __launch_bounds__(kThreads, 1) geoattn_bwd_rows_kernel(const __g
     // Sweep 2
     int dc = 0;
     for (int c = 0; c < nchunks && ok; ++c) {
-      const int ss = sc & 1, ds = dc % C::NDS;
+      const int ss = sc & 1, ds = dc % C::NDS, prs = pc % NPR;
       if (!(ok = warp_wait(&bar_sfull[ss], (sc >> 1) & 1, ctx))) break;
       if (!(ok = warp_wait(&bar_dsempty[ds], ((dc / C::NDS) & 1) ^ 1, ctx))) break;
+      if (!(ok = warp_wait(&bar_prfull[prs], (pc / NPR) & 1, ctx))) break;
       tc_fence_after();
       uint8_t* dreg = smem + C::OFF_DS + ds * C::DS_BYTES;
+      const uint8_t* prt = smem + C::OFF_PR + prs * kPriorTileBytes;
 #pragma unroll 1
-      for (int piece = 0; piece < T::CH / 32; ++piece) {
-        float v[32], w[32];
-        tmem_ld32(lane_base + C::TM_S + ss * T::CH + piece * 32, v);
-        tmem_ld32(lane_base + C::TM_DP + ss * T::CH + piece * 32, w);
+      for (int piece = e.wg; piece < T::PIECES; piece += T::EW) {
+        uint32_t vs[32], ws[32];
+        tmem_ld32_issue(e.lane_base + C::TM_S + ss * T::CH + piece * 32, vs);
+        tmem_ld32_issue(e.lane_base + C::TM_DP + ss * T::CH + piece * 32, ws);
         const int col0 = c * T::CH + piece * 32;
-        float dp[32], ap[32];
-        load_prior32<BF16>(p.prior, p.np, prow, col0, dp, ap);
+        float dp[32], ap[32], v[32];
+        prior32_smem<BF16>(prt, e.r, piece, dp, ap);
+        tmem_wait32(vs);
+        tmem_pin32(ws);
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
           const bool cv = col0 + j < p.N;
-          const float t = v[j] * sc_l2;
+          const float t = __uint_as_float(vs[j]) * sc_l2;
           const float p1 = cv ? ex2(t - m) * inv_l1 : 0.f;
           const float z2 = fmaf(aL, p1, fmaf(bL, dp[j], fmaf(gL, ap[j], -cL)));
           const float p2 = cv ? ex2(z2) * inv_l2 : 0.f;
-          const float dz = p2 * (w[j] - delta2);
+          const float dz = p2 * (__uint_as_float(ws[j]) - delta2);
           v[j] = p1 * fmaf(ab.a, dz, -delta1);
         }
-        stage_row32<BF16>(dreg, r, piece, v);
+        stage_row32<BF16>(dreg, e.r, piece, v);
       }
       fence_proxy_async_smem();
       tc_fence_before();
+      mbar_arrive(&bar_prempty[prs]);
       mbar_arrive(&bar_dsfull[ds]);
       mbar_arrive(&bar_sempty[ss]);
       ++sc;
       ++dc;
+      ++pc;
     }
     if (ok) ok = warp_wait(&bar_dqfull, 0, ctx);
     tc_fence_after();
     if (ok) {
       const long long qoff = (long long)b * p.dq_str[0] + (long long)h * p.dq_str[1] + (long long)row * p.dq_str[2];
 #pragma unroll 1
-      for (int d0 = 0; d0 < DP; d0 += 32) {
+      for (int d0 = e.wg * 32; d0 < DP; d0 += 32 * T::EW) {
         float v[32];
-        tmem_ld32(lane_base + C::TM_DQ + d0, v);  // collective: every lane loads, valid rows store
+        tmem_ld32(e.lane_base + C::TM_DQ + d0, v);  // collective: every lane loads, valid rows store
         if (valid && d0 < p.D) store_row32<BF16>(p.dq, qoff, p.dq_str[3], d0, p.D, v, p.inv_sqrt_d);
       }
     }
@@ -805,7 +995,9 @@ __global__ void __launch_bounds__(kThreads, 1) geoattn_bwd_rows_kernel(const __g
 template <bool BF16, int DP>
 struct ColsCfg : Tile<BF16, DP> {
   using T = Tile<BF16, DP>;
-  static constexpr int NB = (BF16 && DP <= 128) ? 2 : 1;   // buffers for query chunks / staged tiles / S^T
+  static constexpr int NB = (BF16 && DP <= 128) ? 2 : 1;   // buffers for query chunks and S^T / dP^T
+  static constexpr int NST = (BF16 && DP <= 64) ? 2 : 1;   // buffers for the staged P2^T / dS^T tiles
+  static constexpr int NPR = !BF16 ? 0 : (DP <= 64 ? 2 : 1);  // staged prior buffers (0: read from L2)
   static constexpr int K_BYTES = kBM * DP * T::EB;          // per plane (K and V blocks)
   static constexpr int Q_BYTES = T::CH * DP * T::EB;        // per plane per buffer (Q and dO chunks)
   static constexpr int QT_BYTES = BF16 ? 0 : DP * 128;      // fp32: transposed Q / dO chunk (hi)
@@ -817,8 +1009,9 @@ struct ColsCfg : Tile<BF16, DP> {
   static constexpr int OFF_QT = OFF_DO + NB * T::PL * Q_BYTES;
   static constexpr int OFF_DOT = OFF_QT + NB * QT_BYTES;
   static constexpr int OFF_P2 = OFF_DOT + NB * QT_BYTES;
-  static constexpr int OFF_DS = OFF_P2 + NB * ST_BYTES;
-  static constexpr int SMEM = OFF_DS + NB * ST_BYTES + 1024;
+  static constexpr int OFF_DS = OFF_P2 + NST * ST_BYTES;
+  static constexpr int OFF_PR = OFF_DS + NST * ST_BYTES;
+  static constexpr int SMEM = OFF_PR + NPR * kPriorTileBytes + 1024;
   static constexpr int TM_S = 0;
   static constexpr int TM_DP = NB * T::CH;
   static constexpr int TM_DK = 2 * NB * T::CH;
@@ -827,14 +1020,15 @@ struct ColsCfg : Tile<BF16, DP> {
 };
 
 template <bool BF16, int DP>
-__global__ void __launch_bounds__(kThreads, 1) geoattn_bwd_cols_kernel(const __grid_constant__ TileMaps maps, const KParams p) {
+__global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
+    geoattn_bwd_cols_kernel(const __grid_constant__ TileMaps maps, const KParams p) {
   using C = ColsCfg<BF16, DP>;
   using T = typename C::T;
-  constexpr int NB = C::NB;
+  constexpr int NB = C::NB, NST = C::NST, NPR = C::NPR;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ uint64_t bar_kv, bar_qfull[2], bar_qempty[2], bar_sfull[2], bar_sempty[2], bar_tfull[2], bar_tempty[2],
-      bar_done;
+      bar_prfull[2], bar_prempty[2], bar_done;
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_flag;
   __shared__ __align__(16) float rec_sh[2][T::CH][8];
@@ -850,9 +1044,11 @@ __global__ void __launch_bounds__(kThreads, 1) geoattn_bwd_cols_kernel(const __g
       mbar_init(&bar_qfull[i], 1);
       mbar_init(&bar_qempty[i], 1);
       mbar_init(&bar_sfull[i], 1);
-      mbar_init(&bar_sempty[i], 128);
-      mbar_init(&bar_tfull[i], 128);
+      mbar_init(&bar_sempty[i], T::EWT);
+      mbar_init(&bar_tfull[i], T::EWT);
       mbar_init(&bar_tempty[i], 1);
+      mbar_init(&bar_prfull[i], 1);
+      mbar_init(&bar_prempty[i], T::EWT);
     }
     mbar_init(&bar_done, 1);
     fence_barrier_init();
@@ -867,7 +1063,7 @@ __global__ void __launch_bounds__(kThreads, 1) geoattn_bwd_cols_kernel(const __g
   const uint32_t tmem = tmem_base_sh;
   const uint32_t sbase = smem_u32(smem);
 
-  if (warp == kTmaWarp) {
+  if (warp == T::TMA_WARP) {
     if (lane == 0) {
       prefetch_tmap(&maps.q);
       prefetch_tmap(&maps.k);
@@ -888,9 +1084,15 @@ __global__ void __launch_bounds__(kThreads, 1) geoattn_bwd_cols_kernel(const __g
           tma_tileT(smem + C::OFF_QT + qs * C::QT_BYTES, &maps.qt, &bar_qfull[qs], c * T::CH, h, b);
           tma_tileT(smem + C::OFF_DOT + qs * C::QT_BYTES, &maps.dot, &bar_qfull[qs], c * T::CH, h, b);
         }
+        if constexpr (NPR > 0) {
+          const int ps = c % NPR;
+          if (!mbar_wait(&bar_prempty[ps], ((c / NPR) & 1) ^ 1, ctx)) break;
+          mbar_arrive_expect_tx(&bar_prfull[ps], kPriorTileBytes);
+          tma_prior(smem + C::OFF_PR + ps * kPriorTileBytes, &maps.prior, &bar_prfull[ps], kblk * kBM, c);
+        }
       }
     }
-  } else if (warp == kMmaWarp) {
+  } else if (warp == T::MMA_WARP) {
     if (lane == 0) {
       bool ok = mbar_wait(&bar_kv, 0, ctx);
       auto issue_s = [&](int c) -> bool {
@@ -908,8 +1110,8 @@ __global__ void __launch_bounds__(kThreads, 1) geoattn_bwd_cols_kernel(const __g
       if (ok) ok = issue_s(0);
       for (int c = 0; c < nchunks && ok; ++c) {
         if (NB == 2 && c + 1 < nchunks && !(ok = issue_s(c + 1))) break;
-        const int qs = c % NB;
-        if (!(ok = mbar_wait(&bar_tfull[qs], (c / NB) & 1, ctx))) break;
+        const int qs = c % NB, ts = c % NST;
+        if (!(ok = mbar_wait(&bar_tfull[ts], (c / NST) & 1, ctx))) break;
         tc_fence_after();
         uint32_t dob, qb;
         if constexpr (BF16) {
@@ -919,9 +1121,9 @@ __global__ void __launch_bounds__(kThreads, 1) geoattn_bwd_cols_kernel(const __g
           dob = sbase + C::OFF_DOT + qs * C::QT_BYTES;
           qb = sbase + C::OFF_QT + qs * C::QT_BYTES;
         }
-        mma_pv<T>(tmem + C::TM_DV, sbase + C::OFF_P2 + qs * C::ST_BYTES, dob, c > 0);
-        mma_pv<T>(tmem + C::TM_DK, sbase + C::OFF_DS + qs * C::ST_BYTES, qb, c > 0);
-        mma_commit(&bar_tempty[qs]);
+        mma_pv<T>(tmem + C::TM_DV, sbase + C::OFF_P2 + ts * C::ST_BYTES, dob, c > 0);
+        mma_pv<T>(tmem + C::TM_DK, sbase + C::OFF_DS + ts * C::ST_BYTES, qb, c > 0);
+        mma_commit(&bar_tempty[ts]);
         mma_commit(&bar_qempty[qs]);
         if (NB == 1 && c + 1 < nchunks && !(ok = issue_s(c + 1))) break;
       }
@@ -929,9 +1131,8 @@ __global__ void __launch_bounds__(kThreads, 1) geoattn_bwd_cols_kernel(const __g
     }
   } else {
     // ---------------- element-wise warps: thread = key ----------------
-    const int r = threadIdx.x;
-    const int key = kblk * kBM + r;
-    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+    const Ew e = ew_id(tmem);
+    const int key = kblk * kBM + e.r;
     const Abg ab = load_abg(p, h);
     const float sc_l2 = p.scale_log2;
     const float aL = ab.a * kLog2e, bL = ab.b * kLog2e, gL = ab.g * kLog2e, cL = ab.c * kLog2e;
@@ -939,67 +1140,74 @@ __global__ void __launch_bounds__(kThreads, 1) geoattn_bwd_cols_kernel(const __g
     const bool kvalid = key < p.N;
     bool ok = true;
     for (int c = 0; c < nchunks; ++c) {
-      const int qs = c % NB;
+      const int qs = c % NB, ts = c % NST;
       // row records of this query chunk -> shared memory (double-buffered by chunk parity). The named barrier is
       // reached once per chunk by every element-wise thread, also after an abort, so it can never wait forever.
       float(*rec)[8] = rec_sh[c & 1];
-      if (r < T::CH) {
-        const int q = c * T::CH + r;
+      if (threadIdx.x < T::CH) {
+        const int q = c * T::CH + threadIdx.x;
         float4 a = make_float4(0.f, 0.f, 0.f, 0.f), bb = make_float4(0.f, 0.f, 0.f, 0.f);
         if (q < p.N) {
           const float* src = p.rowrec + ((size_t)bh * p.N + q) * 8;
           a = *reinterpret_cast<const float4*>(src);
           bb = *reinterpret_cast<const float4*>(src + 4);
         }
-        *reinterpret_cast<float4*>(&rec[r][0]) = a;
-        *reinterpret_cast<float4*>(&rec[r][4]) = bb;
+        *reinterpret_cast<float4*>(&rec[threadIdx.x][0]) = a;
+        *reinterpret_cast<float4*>(&rec[threadIdx.x][4]) = bb;
       }
-      ew_sync();
+      ew_sync(T::EWT);
       if (!ok) continue;
       if (!(ok = warp_wait(&bar_sfull[qs], (c / NB) & 1, ctx))) continue;
-      if (!(ok = warp_wait(&bar_tempty[qs], ((c / NB) & 1) ^ 1, ctx))) continue;
+      if (!(ok = warp_wait(&bar_tempty[ts], ((c / NST) & 1) ^ 1, ctx))) continue;
+      if constexpr (NPR > 0)
+        if (!(ok = warp_wait(&bar_prfull[c % NPR], (c / NPR) & 1, ctx))) continue;
       tc_fence_after();
-      uint8_t* p2reg = smem + C::OFF_P2 + qs * C::ST_BYTES;
-      uint8_t* dsreg = smem + C::OFF_DS + qs * C::ST_BYTES;
+      uint8_t* p2reg = smem + C::OFF_P2 + ts * C::ST_BYTES;
+      uint8_t* dsreg = smem + C::OFF_DS + ts * C::ST_BYTES;
+      const uint8_t* prt = smem + C::OFF_PR + (NPR > 0 ? (c % (NPR > 0 ? NPR : 1)) : 0) * kPriorTileBytes;
 #pragma unroll 1
-      for (int piece = 0; piece < T::CH / 32; ++piece) {
-        float v[32], w[32], dp[32], ap[32];
-        tmem_ld32(lane_base + C::TM_S + qs * T::CH + piece * 32, v);
-        tmem_ld32(lane_base + C::TM_DP + qs * T::CH + piece * 32, w);
-        load_prior32<BF16>(p.priorT, p.np, pkey, c * T::CH + piece * 32, dp, ap);
+      for (int piece = e.wg; piece < T::PIECES; piece += T::EW) {
+        uint32_t vs[32], ws[32];
+        tmem_ld32_issue(e.lane_base + C::TM_S + qs * T::CH + piece * 32, vs);
+        tmem_ld32_issue(e.lane_base + C::TM_DP + qs * T::CH + piece * 32, ws);
+        float dp[32], ap[32];
+        prior_piece<BF16, (NPR > 0)>(prt, p.priorT, p.np, pkey, e.r, c, piece, dp, ap);
+        tmem_wait32(vs);
+        tmem_pin32(ws);
+        float v[32], w[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
           const float4 ra = *reinterpret_cast<const float4*>(&rec[piece * 32 + j][0]);  // m, 1/l1, 1/l2, delta1
           const float d2 = rec[piece * 32 + j][4];
-          const float t = v[j] * sc_l2;
+          const float t = __uint_as_float(vs[j]) * sc_l2;
           const float p1 = ex2(t - ra.x) * ra.y;
           const float z2 = fmaf(aL, p1, fmaf(bL, dp[j], fmaf(gL, ap[j], -cL)));
           const float p2 = ex2(z2) * ra.z;
-          const float dz = p2 * (w[j] - d2);
+          const float dz = p2 * (__uint_as_float(ws[j]) - d2);
           v[j] = kvalid ? p2 : 0.f;
           w[j] = kvalid ? p1 * fmaf(ab.a, dz, -ra.w) : 0.f;
         }
-        stage_row32<BF16>(p2reg, r, piece, v);
-        stage_row32<BF16>(dsreg, r, piece, w);
+        stage_row32<BF16>(p2reg, e.r, piece, v);
+        stage_row32<BF16>(dsreg, e.r, piece, w);
       }
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(&bar_tfull[qs]);
+      if constexpr (NPR > 0) mbar_arrive(&bar_prempty[c % NPR]);
+      mbar_arrive(&bar_tfull[ts]);
       mbar_arrive(&bar_sempty[qs]);
     }
     if (ok) ok = warp_wait(&bar_done, 0, ctx);
     tc_fence_after();
     if (ok) {
-      const bool valid = key < p.N;
       const long long koff = (long long)b * p.dk_str[0] + (long long)h * p.dk_str[1] + (long long)key * p.dk_str[2];
       const long long voff = (long long)b * p.dv_str[0] + (long long)h * p.dv_str[1] + (long long)key * p.dv_str[2];
 #pragma unroll 1
-      for (int d0 = 0; d0 < DP; d0 += 32) {
+      for (int d0 = e.wg * 32; d0 < DP; d0 += 32 * T::EW) {
         float v[32];
-        tmem_ld32(lane_base + C::TM_DK + d0, v);
-        if (valid && d0 < p.D) store_row32<BF16>(p.dk, koff, p.dk_str[3], d0, p.D, v, p.inv_sqrt_d);
-        tmem_ld32(lane_base + C::TM_DV + d0, v);
-        if (valid && d0 < p.D) store_row32<BF16>(p.dv, voff, p.dv_str[3], d0, p.D, v, 1.0f);
+        tmem_ld32(e.lane_base + C::TM_DK + d0, v);
+        if (kvalid && d0 < p.D) store_row32<BF16>(p.dk, koff, p.dk_str[3], d0, p.D, v, p.inv_sqrt_d);
+        tmem_ld32(e.lane_base + C::TM_DV + d0, v);
+        if (kvalid && d0 < p.D) store_row32<BF16>(p.dv, voff, p.dv_str[3], d0, p.D, v, 1.0f);
       }
     }
   }
