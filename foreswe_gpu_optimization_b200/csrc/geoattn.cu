@@ -221,7 +221,7 @@ int check_shape(const GeoAttnShape* s, Dims& d) {
     if (d.D > 64) return GEOATTN_ERR_UNSUPPORTED;
     d.DP = 64;
   }
-  if ((long long)d.B * d.H > 65535) return GEOATTN_ERR_UNSUPPORTED;  // grid.y
+  if ((long long)d.nrb * d.B * d.H > (1ll << 30)) return GEOATTN_ERR_UNSUPPORTED;  // tile index fits an int
   return GEOATTN_OK;
 }
 
@@ -346,6 +346,21 @@ KParams base_params(const Dims& d, const float* abg, int per_head, const void* p
   return p;
 }
 
+// Persistent grid: one CTA per SM (every attention kernel holds an SM's tensor memory), at most one per tile.
+dim3 persistent_grid(const Dims& d) {
+  static int sms[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (!sms[dev]) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    sms[dev] = n;
+  }
+  const long long tiles = (long long)d.nrb * d.B * d.H;
+  return dim3((unsigned)(tiles < sms[dev] ? tiles : sms[dev]));
+}
+
 template <class K>
 int launch(K kernel, int smem, int threads, dim3 grid, cudaStream_t st, const TileMaps& maps, const KParams& p) {
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
@@ -362,7 +377,7 @@ template <bool BF16, int DP>
 int run_fwd(const TileMaps& maps, const KParams& p, const Dims& d, cudaStream_t st, void* const* ev) {
   record(ev, 0, st);
   int rc = launch(geoattn_fwd_kernel<BF16, DP>, FwdCfg<BF16, DP>::SMEM, Tile<BF16, DP>::NTHREADS,
-                  dim3(d.nrb, d.B * d.H), st, maps, p);
+                  persistent_grid(d), st, maps, p);
   record(ev, 1, st);
   return rc;
 }
@@ -371,11 +386,11 @@ int run_bwd(const TileMaps& rmaps, const TileMaps& cmaps, const KParams& p, cons
             void* const* ev) {
   record(ev, 0, st);
   int rc = launch(geoattn_bwd_rows_kernel<BF16, DP>, RowsCfg<BF16, DP>::SMEM, Tile<BF16, DP>::NTHREADS,
-                  dim3(d.nrb, d.B * d.H), st, rmaps, p);
+                  persistent_grid(d), st, rmaps, p);
   if (rc) return rc;
   record(ev, 1, st);
   rc = launch(geoattn_bwd_cols_kernel<BF16, DP>, ColsCfg<BF16, DP>::SMEM, Tile<BF16, DP>::NTHREADS,
-              dim3(d.nrb, d.B * d.H), st, cmaps, p);
+              persistent_grid(d), st, cmaps, p);
   record(ev, 2, st);
   return rc;
 }

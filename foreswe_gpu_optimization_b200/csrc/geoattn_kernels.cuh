@@ -18,6 +18,8 @@
 #pragma once
 #include <cuda_fp16.h>
 
+#include <type_traits>
+
 #include "sm100.cuh"
 
 namespace geoattn {
@@ -388,19 +390,20 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
   constexpr int NPR = C::NPR;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  __shared__ uint64_t bar_q, bar_kfull[2], bar_kempty[2], bar_vfull[2], bar_vempty[2], bar_sfull[2], bar_sempty[2],
-      bar_pfull[2], bar_pempty[2], bar_prfull[2], bar_prempty[2], bar_ofull;
+  __shared__ uint64_t bar_qfull, bar_qempty, bar_kfull[2], bar_kempty[2], bar_vfull[2], bar_vempty[2], bar_sfull[2],
+      bar_sempty[2], bar_pfull[2], bar_pempty[2], bar_prfull[2], bar_prempty[2], bar_ofull;
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_flag;
-  __shared__ float xch[2][2][kBM];  // cross-warpgroup row statistics
+  __shared__ float xch[3][Tile<BF16, DP>::EW][kBM];  // cross-warpgroup row statistics: m, l1, l2
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int rb = blockIdx.x, bh = blockIdx.y, b = bh / p.H, h = bh % p.H;
   const int nchunks = (p.N + T::CH - 1) / T::CH;
+  const int ntiles = p.nrb * p.B * p.H;  // tile = (128-query row block, b*h); persistent CTAs stride over tiles
   WaitCtx ctx{&abort_flag, p.status};
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
-    mbar_init(&bar_q, 1);
+    mbar_init(&bar_qfull, 1);
+    mbar_init(&bar_qempty, 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bar_kfull[i], 1);
       mbar_init(&bar_kempty[i], 1);
@@ -432,39 +435,45 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       prefetch_tmap(&maps.k);
       prefetch_tmap(&maps.v);
       prefetch_tmap(&maps.prior);
-      mbar_arrive_expect_tx(&bar_q, T::PL * C::Q_BYTES);
-      tma_tile<T>(smem + C::OFF_Q, &maps.q, &bar_q, kBM, rb * kBM, h, b, p.B, T::PL);
-      int kc = 0, vc = 0;
+      int kc = 0, vc = 0, prc = 0, it = 0;
       bool ok = true;
-      for (int pass = 0; pass < 2 && ok; ++pass) {
-        for (int c = 0; c < nchunks && ok; ++c) {
-          const int ks = kc & 1;
-          if (!(ok = mbar_wait(&bar_kempty[ks], ((kc >> 1) & 1) ^ 1, ctx))) break;
-          mbar_arrive_expect_tx(&bar_kfull[ks], T::PL * C::K_BYTES);
-          tma_tile<T>(smem + C::OFF_K + ks * T::PL * C::K_BYTES, &maps.k, &bar_kfull[ks], T::CH, c * T::CH, h, b, p.B,
-                      T::PL);
-          ++kc;
-          if (pass == 1) {
-            const int vs = vc & 1;
-            if (!(ok = mbar_wait(&bar_vempty[vs], ((vc >> 1) & 1) ^ 1, ctx))) break;
-            mbar_arrive_expect_tx(&bar_vfull[vs], C::V_BYTES);
-            if constexpr (BF16)
-              tma_tile<T>(smem + C::OFF_V + vs * C::V_BYTES, &maps.v, &bar_vfull[vs], T::CH, c * T::CH, h, b, p.B, 1);
-            else
-              tma_tileT(smem + C::OFF_V + vs * C::V_BYTES, &maps.v, &bar_vfull[vs], c * T::CH, h, b);
-            const int ps = c % NPR;
-            if (!(ok = mbar_wait(&bar_prempty[ps], ((c / NPR) & 1) ^ 1, ctx))) break;
-            mbar_arrive_expect_tx(&bar_prfull[ps], kPriorTileBytes);
-            tma_prior(smem + C::OFF_PR + ps * kPriorTileBytes, &maps.prior, &bar_prfull[ps], rb * kBM, c);
-            ++vc;
+      for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++it) {
+        const int rb = tile % p.nrb, bh = tile / p.nrb, b = bh / p.H, h = bh % p.H;
+        // Q of this tile once the previous tile's last score MMA has read the old one
+        if (!(ok = mbar_wait(&bar_qempty, (it & 1) ^ 1, ctx))) break;
+        mbar_arrive_expect_tx(&bar_qfull, T::PL * C::Q_BYTES);
+        tma_tile<T>(smem + C::OFF_Q, &maps.q, &bar_qfull, kBM, rb * kBM, h, b, p.B, T::PL);
+        for (int pass = 0; pass < 2 && ok; ++pass) {
+          for (int c = 0; c < nchunks && ok; ++c) {
+            const int ks = kc & 1;
+            if (!(ok = mbar_wait(&bar_kempty[ks], ((kc >> 1) & 1) ^ 1, ctx))) break;
+            mbar_arrive_expect_tx(&bar_kfull[ks], T::PL * C::K_BYTES);
+            tma_tile<T>(smem + C::OFF_K + ks * T::PL * C::K_BYTES, &maps.k, &bar_kfull[ks], T::CH, c * T::CH, h, b,
+                        p.B, T::PL);
+            ++kc;
+            if (pass == 1) {
+              const int vs = vc & 1;
+              if (!(ok = mbar_wait(&bar_vempty[vs], ((vc >> 1) & 1) ^ 1, ctx))) break;
+              mbar_arrive_expect_tx(&bar_vfull[vs], C::V_BYTES);
+              if constexpr (BF16)
+                tma_tile<T>(smem + C::OFF_V + vs * C::V_BYTES, &maps.v, &bar_vfull[vs], T::CH, c * T::CH, h, b, p.B, 1);
+              else
+                tma_tileT(smem + C::OFF_V + vs * C::V_BYTES, &maps.v, &bar_vfull[vs], c * T::CH, h, b);
+              const int ps = prc % NPR;
+              if (!(ok = mbar_wait(&bar_prempty[ps], ((prc / NPR) & 1) ^ 1, ctx))) break;
+              mbar_arrive_expect_tx(&bar_prfull[ps], kPriorTileBytes);
+              tma_prior(smem + C::OFF_PR + ps * kPriorTileBytes, &maps.prior, &bar_prfull[ps], rb * kBM, c);
+              ++prc;
+              ++vc;
+            }
           }
         }
       }
     }
   } else if (warp == T::MMA_WARP) {
     if (lane == 0) {
-      int kc = 0, sc = 0, pc = 0;
-      bool ok = mbar_wait(&bar_q, 0, ctx);
+      int kc = 0, sc = 0, pc = 0, it = 0;
+      bool ok = true;
       auto issue_s = [&](void) -> bool {
         const int ks = kc & 1, ss = sc & 1;
         if (!mbar_wait(&bar_kfull[ks], (kc >> 1) & 1, ctx)) return false;
@@ -478,128 +487,158 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         ++sc;
         return true;
       };
-      for (int c = 0; c < nchunks && ok; ++c) ok = issue_s();
-      if (ok) ok = issue_s();
-      for (int c = 0; c < nchunks && ok; ++c) {
-        if (c + 1 < nchunks && !(ok = issue_s())) break;
-        const int ps = pc & 1;
-        if (!(ok = mbar_wait(&bar_pfull[ps], (pc >> 1) & 1, ctx))) break;
-        if (!(ok = mbar_wait(&bar_vfull[ps], (pc >> 1) & 1, ctx))) break;
-        tc_fence_after();
-        mma_pv<T>(tmem + C::TM_O, sbase + C::OFF_P + ps * C::P_BYTES, sbase + C::OFF_V + ps * C::V_BYTES, c > 0);
-        mma_commit(&bar_pempty[ps]);
-        mma_commit(&bar_vempty[ps]);
-        ++pc;
+      for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++it) {
+        if (!(ok = mbar_wait(&bar_qfull, it & 1, ctx))) break;
+        for (int c = 0; c < nchunks && ok; ++c) ok = issue_s();
+        if (ok) ok = issue_s();
+        for (int c = 0; c < nchunks && ok; ++c) {
+          if (c + 1 < nchunks && !(ok = issue_s())) break;
+          if (c + 1 == nchunks) mma_commit(&bar_qempty);  // every score MMA of this tile has been issued
+          const int ps = pc & 1;
+          if (!(ok = mbar_wait(&bar_pfull[ps], (pc >> 1) & 1, ctx))) break;
+          if (!(ok = mbar_wait(&bar_vfull[ps], (pc >> 1) & 1, ctx))) break;
+          tc_fence_after();
+          mma_pv<T>(tmem + C::TM_O, sbase + C::OFF_P + ps * C::P_BYTES, sbase + C::OFF_V + ps * C::V_BYTES, c > 0);
+          mma_commit(&bar_pempty[ps]);
+          mma_commit(&bar_vempty[ps]);
+          ++pc;
+        }
+        if (ok) mma_commit(&bar_ofull);
       }
-      if (ok) mma_commit(&bar_ofull);
     }
   } else {
     // ---------------- element-wise warps ----------------
     const Ew e = ew_id(tmem);
-    const int row = rb * kBM + e.r;
-    const Abg ab = load_abg(p, h);
     const float sc_l2 = p.scale_log2;
-    float m = -INFINITY, l = 0.f;
-    int sc = 0;
+    int sc = 0, pc = 0, prc = 0, it = 0;
     bool ok = true;
-    // Pass A: running max and sum over this warpgroup's pieces
-    for (int c = 0; c < nchunks && ok; ++c) {
-      const int ss = sc & 1;
-      if (!(ok = warp_wait(&bar_sfull[ss], (sc >> 1) & 1, ctx))) break;
-      tc_fence_after();
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++it) {
+      const int rb = tile % p.nrb, bh = tile / p.nrb, b = bh / p.H, h = bh % p.H;
+      const int row = rb * kBM + e.r;
+      const Abg ab = load_abg(p, h);
+      float m = -INFINITY, l = 0.f;
+      // Pass A: running max and sum over this warpgroup's pieces
+      for (int c = 0; c < nchunks && ok; ++c) {
+        const int ss = sc & 1;
+        if (!(ok = warp_wait(&bar_sfull[ss], (sc >> 1) & 1, ctx))) break;
+        tc_fence_after();
 #pragma unroll
-      for (int piece = e.wg; piece < T::PIECES; piece += T::EW) {
-        float v[32];
-        tmem_ld32(e.lane_base + C::TM_S + ss * T::CH + piece * 32, v);
-        const int col0 = c * T::CH + piece * 32;
-        float mx = -INFINITY;
+        for (int piece = e.wg; piece < T::PIECES; piece += T::EW) {
+          float v[32];
+          tmem_ld32(e.lane_base + C::TM_S + ss * T::CH + piece * 32, v);
+          const int nvalid = p.N - (c * T::CH + piece * 32);  // >= 32: no masked column in this piece
+          if (nvalid >= 32) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          v[j] = (col0 + j < p.N) ? v[j] * sc_l2 : -INFINITY;
-          mx = fmaxf(mx, v[j]);
+            for (int j = 0; j < 32; ++j) v[j] *= sc_l2;
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = (j < nvalid) ? v[j] * sc_l2 : -INFINITY;
+          }
+          // four independent partial maxima / sums keep the dependency chains short
+          float mx4[4] = {v[0], v[1], v[2], v[3]};
+#pragma unroll
+          for (int j = 4; j < 32; ++j) mx4[j & 3] = fmaxf(mx4[j & 3], v[j]);
+          const float mn = fmaxf(m, fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])));
+          // a warpgroup whose columns so far are all masked keeps m = -inf, l = 0 (never 2^(-inf - -inf))
+          const float mref = (mn == -INFINITY) ? 0.f : mn;
+          float s4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int j = 0; j < 32; ++j) s4[j & 3] += ex2(v[j] - mref);
+          l = l * ex2(m - mref) + ((s4[0] + s4[1]) + (s4[2] + s4[3]));
+          m = mn;
         }
-        const float mn = fmaxf(m, mx);
-        // a warpgroup whose columns so far are all masked keeps m = -inf, l = 0 (never 2^(-inf - -inf))
-        const float mref = (mn == -INFINITY) ? 0.f : mn;
-        float s = 0.f;
-#pragma unroll
-        for (int j = 0; j < 32; ++j) s += ex2(v[j] - mref);
-        l = l * ex2(m - mref) + s;
-        m = mn;
+        tc_fence_before();
+        mbar_arrive(&bar_sempty[ss]);
+        ++sc;
       }
-      tc_fence_before();
-      mbar_arrive(&bar_sempty[ss]);
-      ++sc;
-    }
-    if constexpr (T::EW == 2) {  // combine the two warpgroups' statistics (same order in both)
-      xch[0][e.wg][e.r] = m;
-      xch[1][e.wg][e.r] = l;
-      ew_sync(T::EWT);
-      const float m0 = xch[0][0][e.r], m1 = xch[0][1][e.r], l0 = xch[1][0][e.r], l1 = xch[1][1][e.r];
-      m = fmaxf(m0, m1);
-      l = l0 * ex2(m0 - m) + l1 * ex2(m1 - m);
-      ew_sync(T::EWT);
-    }
-    const float inv_l1 = __frcp_rn(l);
-    const float aL = ab.a * kLog2e, bL = ab.b * kLog2e, gL = ab.g * kLog2e, cL = ab.c * kLog2e;
-    float l2 = 0.f;
-    int pc = 0;
-    // Pass B
-    for (int c = 0; c < nchunks && ok; ++c) {
-      const int ss = sc & 1, ps = pc & 1, prs = c % NPR;
-      if (!(ok = warp_wait(&bar_sfull[ss], (sc >> 1) & 1, ctx))) break;
-      if (!(ok = warp_wait(&bar_pempty[ps], ((pc >> 1) & 1) ^ 1, ctx))) break;
-      if (!(ok = warp_wait(&bar_prfull[prs], (c / NPR) & 1, ctx))) break;
-      tc_fence_after();
-      uint8_t* preg = smem + C::OFF_P + ps * C::P_BYTES;
-      const uint8_t* prt = smem + C::OFF_PR + prs * kPriorTileBytes;
+      if constexpr (T::EW > 1) {  // combine the warpgroups' statistics (same order in every warpgroup)
+        xch[0][e.wg][e.r] = m;
+        xch[1][e.wg][e.r] = l;
+        ew_sync(T::EWT);
+        m = xch[0][0][e.r];
 #pragma unroll
-      for (int piece = e.wg; piece < T::PIECES; piece += T::EW) {
-        float v[32], dp[32], ap[32];
-        tmem_ld32(e.lane_base + C::TM_S + ss * T::CH + piece * 32, v);
-        const int col0 = c * T::CH + piece * 32;
-        prior32_smem<BF16>(prt, e.r, piece, dp, ap);
+        for (int w = 1; w < T::EW; ++w) m = fmaxf(m, xch[0][w][e.r]);
+        l = 0.f;
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const float t = v[j] * sc_l2;
-          const float p1 = ex2(t - m) * inv_l1;
-          const float z2 = fmaf(aL, p1, fmaf(bL, dp[j], fmaf(gL, ap[j], -cL)));
-          const float ev = (col0 + j < p.N) ? ex2(z2) : 0.f;
-          l2 += ev;
-          v[j] = ev;
+        for (int w = 0; w < T::EW; ++w) {
+          const float mw = xch[0][w][e.r];
+          l += (mw == -INFINITY) ? 0.f : xch[1][w][e.r] * ex2(mw - m);
         }
-        stage_row32<BF16>(preg, e.r, piece, v);
+        ew_sync(T::EWT);
       }
-      fence_proxy_async_smem();
-      tc_fence_before();
-      mbar_arrive(&bar_prempty[prs]);
-      mbar_arrive(&bar_pfull[ps]);
-      mbar_arrive(&bar_sempty[ss]);
-      ++sc;
-      ++pc;
-    }
-    if constexpr (T::EW == 2) {
-      xch[0][e.wg][e.r] = l2;
-      ew_sync(T::EWT);
-      l2 = xch[0][0][e.r] + xch[0][1][e.r];
-    }
-    if (ok) ok = warp_wait(&bar_ofull, 0, ctx);
-    tc_fence_after();
-    if (ok) {
-      const float inv_l2 = __frcp_rn(l2);
-      const long long ooff = (long long)b * p.o_str[0] + (long long)h * p.o_str[1] + (long long)row * p.o_str[2];
+      const float inv_l1 = __frcp_rn(l);
+      const float aL = ab.a * kLog2e, bL = ab.b * kLog2e, gL = ab.g * kLog2e, cL = ab.c * kLog2e;
+      float l2 = 0.f;
+      // Pass B
+      for (int c = 0; c < nchunks && ok; ++c) {
+        const int ss = sc & 1, ps = pc & 1, prs = prc % NPR;
+        if (!(ok = warp_wait(&bar_sfull[ss], (sc >> 1) & 1, ctx))) break;
+        if (!(ok = warp_wait(&bar_pempty[ps], ((pc >> 1) & 1) ^ 1, ctx))) break;
+        if (!(ok = warp_wait(&bar_prfull[prs], (prc / NPR) & 1, ctx))) break;
+        tc_fence_after();
+        uint8_t* preg = smem + C::OFF_P + ps * C::P_BYTES;
+        const uint8_t* prt = smem + C::OFF_PR + prs * kPriorTileBytes;
 #pragma unroll
-      for (int d0 = e.wg * 32; d0 < DP; d0 += 32 * T::EW) {
-        float v[32];
-        tmem_ld32(e.lane_base + C::TM_O + d0, v);
-        if (row < p.N && d0 < p.D) store_row32<BF16>(p.o, ooff, p.o_str[3], d0, p.D, v, inv_l2);
+        for (int piece = e.wg; piece < T::PIECES; piece += T::EW) {
+          uint32_t vs[32];
+          float v[32], dp[32], ap[32];
+          tmem_ld32_issue(e.lane_base + C::TM_S + ss * T::CH + piece * 32, vs);
+          prior32_smem<BF16>(prt, e.r, piece, dp, ap);  // overlaps the tensor-memory load
+          tmem_wait32(vs);
+          const int nvalid = p.N - (c * T::CH + piece * 32);
+          float l24[4] = {0.f, 0.f, 0.f, 0.f};
+          auto body = [&](auto masked) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float t = __uint_as_float(vs[j]) * sc_l2;
+              const float p1 = ex2(t - m) * inv_l1;
+              const float z2 = fmaf(aL, p1, fmaf(bL, dp[j], fmaf(gL, ap[j], -cL)));
+              float ev = ex2(z2);
+              if constexpr (decltype(masked)::value) ev = (j < nvalid) ? ev : 0.f;
+              l24[j & 3] += ev;
+              v[j] = ev;
+            }
+          };
+          if (nvalid >= 32) body(std::false_type{});
+          else body(std::true_type{});
+          l2 += (l24[0] + l24[1]) + (l24[2] + l24[3]);
+          stage_row32<BF16>(preg, e.r, piece, v);
+        }
+        fence_proxy_async_smem();
+        tc_fence_before();
+        mbar_arrive(&bar_prempty[prs]);
+        mbar_arrive(&bar_pfull[ps]);
+        mbar_arrive(&bar_sempty[ss]);
+        ++sc;
+        ++pc;
+        ++prc;
       }
-      if (row < p.N && e.wg == 0) {
-        const size_t s = (size_t)bh * p.N + row, n = (size_t)p.B * p.H * p.N;
-        p.stats[s] = m;
-        p.stats[n + s] = l;
-        p.stats[2 * n + s] = l2;
+      if constexpr (T::EW > 1) {
+        xch[2][e.wg][e.r] = l2;
+        ew_sync(T::EWT);
+        l2 = 0.f;
+#pragma unroll
+        for (int w = 0; w < T::EW; ++w) l2 += xch[2][w][e.r];
       }
+      if (ok) ok = warp_wait(&bar_ofull, it & 1, ctx);
+      tc_fence_after();
+      if (ok) {
+        const float inv_l2 = __frcp_rn(l2);
+        const long long ooff = (long long)b * p.o_str[0] + (long long)h * p.o_str[1] + (long long)row * p.o_str[2];
+#pragma unroll
+        for (int d0 = e.wg * 32; d0 < DP; d0 += 32 * T::EW) {
+          float v[32];
+          tmem_ld32(e.lane_base + C::TM_O + d0, v);
+          if (row < p.N && d0 < p.D) store_row32<BF16>(p.o, ooff, p.o_str[3], d0, p.D, v, inv_l2);
+        }
+        if (row < p.N && e.wg == 0) {
+          const size_t s = (size_t)bh * p.N + row, n = (size_t)p.B * p.H * p.N;
+          p.stats[s] = m;
+          p.stats[n + s] = l;
+          p.stats[2 * n + s] = l2;
+        }
+      }
+      tc_fence_before();  // the O reads above precede this warp's next hand-offs to the MMA warp
     }
   }
   tc_fence_before();
@@ -648,19 +687,20 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
   constexpr int NKV = C::NKV, NPR = C::NPR;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  __shared__ uint64_t bar_q, bar_kfull[2], bar_kempty[2], bar_vfull[2], bar_vempty[2], bar_sfull[2], bar_sempty[2],
+  __shared__ uint64_t bar_qfull, bar_qempty, bar_kfull[2], bar_kempty[2], bar_vfull[2], bar_vempty[2], bar_sfull[2], bar_sempty[2],
       bar_dsfull[2], bar_dsempty[2], bar_ktfull[2], bar_ktempty[2], bar_prfull[2], bar_prempty[2], bar_dqfull;
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_flag;
   __shared__ double red[8][3];
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int rb = blockIdx.x, bh = blockIdx.y, b = bh / p.H, h = bh % p.H;
   const int nchunks = (p.N + T::CH - 1) / T::CH;
+  const int ntiles = p.nrb * p.B * p.H;  // tile = (128-query row block, b*h); persistent CTAs stride over tiles
   WaitCtx ctx{&abort_flag, p.status};
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
-    mbar_init(&bar_q, 1);
+    mbar_init(&bar_qfull, 1);
+    mbar_init(&bar_qempty, 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bar_kfull[i], 1);
       mbar_init(&bar_kempty[i], 1);
@@ -695,11 +735,15 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       prefetch_tmap(&maps.v);
       prefetch_tmap(&maps.dout);
       prefetch_tmap(&maps.prior);
-      mbar_arrive_expect_tx(&bar_q, 2 * T::PL * C::Q_BYTES);
-      tma_tile<T>(smem + C::OFF_Q, &maps.q, &bar_q, kBM, rb * kBM, h, b, p.B, T::PL);
-      tma_tile<T>(smem + C::OFF_DO, &maps.dout, &bar_q, kBM, rb * kBM, h, b, p.B, T::PL);
-      int kc = 0, tc = 0, pc = 0;
+      int kc = 0, tc = 0, pc = 0, it = 0;
       bool ok = true;
+      for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++it) {
+      const int rb = tile % p.nrb, bh = tile / p.nrb, b = bh / p.H, h = bh % p.H;
+      // Q and dO of this tile once the previous tile's last S/dP MMAs have read the old ones
+      if (!(ok = mbar_wait(&bar_qempty, (it & 1) ^ 1, ctx))) break;
+      mbar_arrive_expect_tx(&bar_qfull, 2 * T::PL * C::Q_BYTES);
+      tma_tile<T>(smem + C::OFF_Q, &maps.q, &bar_qfull, kBM, rb * kBM, h, b, p.B, T::PL);
+      tma_tile<T>(smem + C::OFF_DO, &maps.dout, &bar_qfull, kBM, rb * kBM, h, b, p.B, T::PL);
       for (int sweep = 0; sweep < 2 && ok; ++sweep) {
         for (int c = 0; c < nchunks && ok; ++c) {
           // the prior tile first: it only waits for the element-wise warps, while K may wait for dQ's MMA
@@ -729,11 +773,12 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
           }
         }
       }
+      }
     }
   } else if (warp == T::MMA_WARP) {
     if (lane == 0) {
-      int kc = 0, sc = 0, dc = 0;
-      bool ok = mbar_wait(&bar_q, 0, ctx);
+      int kc = 0, sc = 0, dc = 0, it = 0;
+      bool ok = true;
       auto issue = [&](bool release_k) -> bool {
         const int ks = kc % NKV, ss = sc & 1;
         if (!mbar_wait(&bar_kfull[ks], (kc / NKV) & 1, ctx)) return false;
@@ -770,31 +815,40 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         ++dc;
         return true;
       };
-      for (int c = 0; c < nchunks && ok; ++c) ok = issue(true);
-      const int kc0 = kc;  // first K use of sweep 2
-      if (ok) ok = issue(false);
-      for (int c = 0; c < nchunks && ok; ++c) {
-        if constexpr (NKV == 2) {  // look ahead: S/dP of the next chunk overlap the element-wise work on this one
-          if (c + 1 < nchunks && !(ok = issue(false))) break;
-          if (!(ok = issue_dq(c, kc0))) break;
-        } else {                   // one K/V buffer: the next chunk's K can only arrive after this chunk's dQ
-          if (!(ok = issue_dq(c, kc0))) break;
-          if (c + 1 < nchunks && !(ok = issue(false))) break;
+      for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++it) {
+        if (!(ok = mbar_wait(&bar_qfull, it & 1, ctx))) break;
+        for (int c = 0; c < nchunks && ok; ++c) ok = issue(true);
+        const int kc0 = kc;  // first K use of sweep 2
+        if (ok) ok = issue(false);
+        if (ok && nchunks == 1) mma_commit(&bar_qempty);  // every S/dP MMA of this tile has been issued
+        for (int c = 0; c < nchunks && ok; ++c) {
+          if constexpr (NKV == 2) {  // look ahead: S/dP of the next chunk overlap the element-wise work on this one
+            if (c + 1 < nchunks && !(ok = issue(false))) break;
+            if (c + 2 == nchunks) mma_commit(&bar_qempty);
+            if (!(ok = issue_dq(c, kc0))) break;
+          } else {                   // one K/V buffer: the next chunk's K can only arrive after this chunk's dQ
+            if (!(ok = issue_dq(c, kc0))) break;
+            if (c + 1 < nchunks && !(ok = issue(false))) break;
+            if (c + 2 == nchunks) mma_commit(&bar_qempty);
+          }
         }
+        if (ok) mma_commit(&bar_dqfull);
       }
-      if (ok) mma_commit(&bar_dqfull);
     }
   } else {
     // ---------------- element-wise warps ----------------
     const Ew e = ew_id(tmem);
+    const float sc_l2 = p.scale_log2;
+    const size_t nrows_all = (size_t)p.B * p.H * p.N;
+    int sc = 0, pc = 0, dc = 0, it = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++it) {
+    const int rb = tile % p.nrb, bh = tile / p.nrb, b = bh / p.H, h = bh % p.H;
     const int row = rb * kBM + e.r;
     const bool valid = row < p.N;
     const Abg ab = load_abg(p, h);
-    const float sc_l2 = p.scale_log2;
-    const size_t nrows_all = (size_t)p.B * p.H * p.N;
     const size_t srow = (size_t)bh * p.N + (valid ? row : 0);
     float m = 0.f, inv_l1 = 0.f, inv_l2 = 0.f, d2s = 0.f;
-    bool ok = true;
     if (valid) {
       m = p.stats[srow];
       inv_l1 = __frcp_rn(p.stats[nrows_all + srow]);
@@ -804,7 +858,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
     // row's 16-byte chunks split between the warpgroups; fp32: straight from global memory.
     const long long oo = (long long)b * p.oi_str[0] + (long long)h * p.oi_str[1] + (long long)row * p.oi_str[2];
     if constexpr (BF16) {
-      ok = warp_wait(&bar_q, 0, ctx);
+      if (ok) ok = warp_wait(&bar_qfull, it & 1, ctx);
       const __nv_bfloat16* orow = reinterpret_cast<const __nv_bfloat16*>(p.o_in) + oo;
       const bool vec = p.oi_str[3] == 1 && (reinterpret_cast<uintptr_t>(orow) & 15) == 0;
       if (ok && valid) {
@@ -850,7 +904,6 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
     }
     const float aL = ab.a * kLog2e, bL = ab.b * kLog2e, gL = ab.g * kLog2e, cL = ab.c * kLog2e;
     float acc[7] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // r, a, b, c, e, f, g
-    int sc = 0, pc = 0;
     for (int c = 0; c < nchunks && ok; ++c) {
       const int ss = sc & 1, prs = pc % NPR;
       if (!(ok = warp_wait(&bar_sfull[ss], (sc >> 1) & 1, ctx))) break;
@@ -862,27 +915,36 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         uint32_t vs[32], ws[32];
         tmem_ld32_issue(e.lane_base + C::TM_S + ss * T::CH + piece * 32, vs);
         tmem_ld32_issue(e.lane_base + C::TM_DP + ss * T::CH + piece * 32, ws);
-        const int col0 = c * T::CH + piece * 32;
+        const int nvalid = p.N - (c * T::CH + piece * 32);
         float dp[32], ap[32];
         prior32_smem<BF16>(prt, e.r, piece, dp, ap);
         tmem_wait32(vs);
         tmem_pin32(ws);
+        float pa[2][7] = {};  // two interleaved partial sums per quantity (shorter dependency chains)
+        auto body = [&](auto masked) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const bool cv = col0 + j < p.N;
-          const float t = __uint_as_float(vs[j]) * sc_l2;
-          const float p1 = cv ? ex2(t - m) * inv_l1 : 0.f;
-          const float z2 = fmaf(aL, p1, fmaf(bL, dp[j], fmaf(gL, ap[j], -cL)));
-          const float p2 = cv ? ex2(z2) * inv_l2 : 0.f;
-          const float wv = p2 * (__uint_as_float(ws[j]) - d2s);
-          acc[0] += wv;
-          acc[1] = fmaf(wv, p1, acc[1]);
-          acc[2] = fmaf(p2, p1, acc[2]);
-          acc[3] = fmaf(wv, dp[j], acc[3]);
-          acc[4] = fmaf(p2, dp[j], acc[4]);
-          acc[5] = fmaf(wv, ap[j], acc[5]);
-          acc[6] = fmaf(p2, ap[j], acc[6]);
-        }
+          for (int j = 0; j < 32; ++j) {
+            const float t = __uint_as_float(vs[j]) * sc_l2;
+            float p1 = ex2(t - m) * inv_l1;
+            if constexpr (decltype(masked)::value) p1 = (j < nvalid) ? p1 : 0.f;
+            const float z2 = fmaf(aL, p1, fmaf(bL, dp[j], fmaf(gL, ap[j], -cL)));
+            float p2 = ex2(z2) * inv_l2;
+            if constexpr (decltype(masked)::value) p2 = (j < nvalid) ? p2 : 0.f;
+            const float wv = p2 * (__uint_as_float(ws[j]) - d2s);
+            float* q = pa[j & 1];
+            q[0] += wv;
+            q[1] = fmaf(wv, p1, q[1]);
+            q[2] = fmaf(p2, p1, q[2]);
+            q[3] = fmaf(wv, dp[j], q[3]);
+            q[4] = fmaf(p2, dp[j], q[4]);
+            q[5] = fmaf(wv, ap[j], q[5]);
+            q[6] = fmaf(p2, ap[j], q[6]);
+          }
+        };
+        if (nvalid >= 32) body(std::false_type{});
+        else body(std::true_type{});
+#pragma unroll
+        for (int k = 0; k < 7; ++k) acc[k] += pa[0][k] + pa[1][k];
       }
       tc_fence_before();
       mbar_arrive(&bar_prempty[prs]);
@@ -931,7 +993,6 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       out[2] = (red[0][2] + red[1][2]) + (red[2][2] + red[3][2]);
     }
     // Sweep 2
-    int dc = 0;
     for (int c = 0; c < nchunks && ok; ++c) {
       const int ss = sc & 1, ds = dc % C::NDS, prs = pc % NPR;
       if (!(ok = warp_wait(&bar_sfull[ss], (sc >> 1) & 1, ctx))) break;
@@ -945,21 +1006,25 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         uint32_t vs[32], ws[32];
         tmem_ld32_issue(e.lane_base + C::TM_S + ss * T::CH + piece * 32, vs);
         tmem_ld32_issue(e.lane_base + C::TM_DP + ss * T::CH + piece * 32, ws);
-        const int col0 = c * T::CH + piece * 32;
+        const int nvalid = p.N - (c * T::CH + piece * 32);
         float dp[32], ap[32], v[32];
         prior32_smem<BF16>(prt, e.r, piece, dp, ap);
         tmem_wait32(vs);
         tmem_pin32(ws);
+        auto body = [&](auto masked) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const bool cv = col0 + j < p.N;
-          const float t = __uint_as_float(vs[j]) * sc_l2;
-          const float p1 = cv ? ex2(t - m) * inv_l1 : 0.f;
-          const float z2 = fmaf(aL, p1, fmaf(bL, dp[j], fmaf(gL, ap[j], -cL)));
-          const float p2 = cv ? ex2(z2) * inv_l2 : 0.f;
-          const float dz = p2 * (__uint_as_float(ws[j]) - delta2);
-          v[j] = p1 * fmaf(ab.a, dz, -delta1);
-        }
+          for (int j = 0; j < 32; ++j) {
+            const float t = __uint_as_float(vs[j]) * sc_l2;
+            float p1 = ex2(t - m) * inv_l1;
+            if constexpr (decltype(masked)::value) p1 = (j < nvalid) ? p1 : 0.f;
+            const float z2 = fmaf(aL, p1, fmaf(bL, dp[j], fmaf(gL, ap[j], -cL)));
+            const float p2 = ex2(z2) * inv_l2;
+            const float dz = p2 * (__uint_as_float(ws[j]) - delta2);
+            v[j] = p1 * fmaf(ab.a, dz, -delta1);  // masked columns: p1 = 0 -> dS = 0
+          }
+        };
+        if (nvalid >= 32) body(std::false_type{});
+        else body(std::true_type{});
         stage_row32<BF16>(dreg, e.r, piece, v);
       }
       fence_proxy_async_smem();
@@ -971,7 +1036,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       ++dc;
       ++pc;
     }
-    if (ok) ok = warp_wait(&bar_dqfull, 0, ctx);
+    if (ok) ok = warp_wait(&bar_dqfull, it & 1, ctx);
     tc_fence_after();
     if (ok) {
       const long long qoff = (long long)b * p.dq_str[0] + (long long)h * p.dq_str[1] + (long long)row * p.dq_str[2];
@@ -981,6 +1046,8 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         tmem_ld32(e.lane_base + C::TM_DQ + d0, v);  // collective: every lane loads, valid rows store
         if (valid && d0 < p.D) store_row32<BF16>(p.dq, qoff, p.dq_str[3], d0, p.D, v, p.inv_sqrt_d);
       }
+    }
+    tc_fence_before();  // the dQ reads above precede this warp's next hand-offs to the MMA warp
     }
   }
   tc_fence_before();
@@ -1027,19 +1094,20 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
   constexpr int NB = C::NB, NST = C::NST, NPR = C::NPR;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  __shared__ uint64_t bar_kv, bar_qfull[2], bar_qempty[2], bar_sfull[2], bar_sempty[2], bar_tfull[2], bar_tempty[2],
+  __shared__ uint64_t bar_kvfull, bar_kvempty, bar_qfull[2], bar_qempty[2], bar_sfull[2], bar_sempty[2], bar_tfull[2], bar_tempty[2],
       bar_prfull[2], bar_prempty[2], bar_done;
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_flag;
-  __shared__ __align__(16) float rec_sh[2][T::CH][8];
+  __shared__ __align__(16) float rec_sh[2][5][T::CH];  // per query: m, 1/l1, 1/l2, delta1, delta2
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int kblk = blockIdx.x, bh = blockIdx.y, b = bh / p.H, h = bh % p.H;
   const int nchunks = (p.N + T::CH - 1) / T::CH;
+  const int ntiles = p.nrb * p.B * p.H;  // tile = (128-key block, b*h); persistent CTAs stride over tiles
   WaitCtx ctx{&abort_flag, p.status};
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
-    mbar_init(&bar_kv, 1);
+    mbar_init(&bar_kvfull, 1);
+    mbar_init(&bar_kvempty, 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bar_qfull[i], 1);
       mbar_init(&bar_qempty[i], 1);
@@ -1069,12 +1137,19 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       prefetch_tmap(&maps.k);
       prefetch_tmap(&maps.v);
       prefetch_tmap(&maps.dout);
-      mbar_arrive_expect_tx(&bar_kv, 2 * T::PL * C::K_BYTES);
-      tma_tile<T>(smem + C::OFF_K, &maps.k, &bar_kv, kBM, kblk * kBM, h, b, p.B, T::PL);
-      tma_tile<T>(smem + C::OFF_V, &maps.v, &bar_kv, kBM, kblk * kBM, h, b, p.B, T::PL);
+      bool ok = true;
+      int it = 0;
+      for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++it) {
+      const int kblk = tile % p.nrb, bh = tile / p.nrb, b = bh / p.H, h = bh % p.H;
+      // K and V blocks of this tile once the previous tile's last S^T/dP^T MMAs have read the old ones
+      if (!(ok = mbar_wait(&bar_kvempty, (it & 1) ^ 1, ctx))) break;
+      mbar_arrive_expect_tx(&bar_kvfull, 2 * T::PL * C::K_BYTES);
+      tma_tile<T>(smem + C::OFF_K, &maps.k, &bar_kvfull, kBM, kblk * kBM, h, b, p.B, T::PL);
+      tma_tile<T>(smem + C::OFF_V, &maps.v, &bar_kvfull, kBM, kblk * kBM, h, b, p.B, T::PL);
       for (int c = 0; c < nchunks; ++c) {
-        const int qs = c % NB;
-        if (!mbar_wait(&bar_qempty[qs], ((c / NB) & 1) ^ 1, ctx)) break;
+        const int gc = it * nchunks + c;  // chunk count over all tiles (buffer slots and phases)
+        const int qs = gc % NB;
+        if (!(ok = mbar_wait(&bar_qempty[qs], ((gc / NB) & 1) ^ 1, ctx))) break;
         mbar_arrive_expect_tx(&bar_qfull[qs], 2 * T::PL * C::Q_BYTES + 2 * C::QT_BYTES);
         tma_tile<T>(smem + C::OFF_Q + qs * T::PL * C::Q_BYTES, &maps.q, &bar_qfull[qs], T::CH, c * T::CH, h, b, p.B,
                     T::PL);
@@ -1085,20 +1160,22 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
           tma_tileT(smem + C::OFF_DOT + qs * C::QT_BYTES, &maps.dot, &bar_qfull[qs], c * T::CH, h, b);
         }
         if constexpr (NPR > 0) {
-          const int ps = c % NPR;
-          if (!mbar_wait(&bar_prempty[ps], ((c / NPR) & 1) ^ 1, ctx)) break;
+          const int ps = gc % NPR;
+          if (!(ok = mbar_wait(&bar_prempty[ps], ((gc / NPR) & 1) ^ 1, ctx))) break;
           mbar_arrive_expect_tx(&bar_prfull[ps], kPriorTileBytes);
           tma_prior(smem + C::OFF_PR + ps * kPriorTileBytes, &maps.prior, &bar_prfull[ps], kblk * kBM, c);
         }
       }
+      }
     }
   } else if (warp == T::MMA_WARP) {
     if (lane == 0) {
-      bool ok = mbar_wait(&bar_kv, 0, ctx);
-      auto issue_s = [&](int c) -> bool {
-        const int qs = c % NB;
-        if (!mbar_wait(&bar_qfull[qs], (c / NB) & 1, ctx)) return false;
-        if (!mbar_wait(&bar_sempty[qs], ((c / NB) & 1) ^ 1, ctx)) return false;
+      bool ok = true;
+      int it = 0;
+      auto issue_s = [&](int gc) -> bool {
+        const int qs = gc % NB;
+        if (!mbar_wait(&bar_qfull[qs], (gc / NB) & 1, ctx)) return false;
+        if (!mbar_wait(&bar_sempty[qs], ((gc / NB) & 1) ^ 1, ctx)) return false;
         tc_fence_after();
         mma_qk<T, T::CH>(tmem + C::TM_S + qs * T::CH, sbase + C::OFF_K, C::K_BYTES,
                          sbase + C::OFF_Q + qs * T::PL * C::Q_BYTES, C::Q_BYTES);
@@ -1107,11 +1184,19 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         mma_commit(&bar_sfull[qs]);
         return true;
       };
-      if (ok) ok = issue_s(0);
+      for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++it) {
+      const int g0 = it * nchunks;
+      if (!(ok = mbar_wait(&bar_kvfull, it & 1, ctx))) break;
+      if (ok) ok = issue_s(g0);
+      if (ok && nchunks == 1) mma_commit(&bar_kvempty);  // every S^T/dP^T MMA of this tile has been issued
       for (int c = 0; c < nchunks && ok; ++c) {
-        if (NB == 2 && c + 1 < nchunks && !(ok = issue_s(c + 1))) break;
-        const int qs = c % NB, ts = c % NST;
-        if (!(ok = mbar_wait(&bar_tfull[ts], (c / NST) & 1, ctx))) break;
+        const int gc = g0 + c;
+        if (NB == 2 && c + 1 < nchunks) {
+          if (!(ok = issue_s(gc + 1))) break;
+          if (c + 2 == nchunks) mma_commit(&bar_kvempty);
+        }
+        const int qs = gc % NB, ts = gc % NST;
+        if (!(ok = mbar_wait(&bar_tfull[ts], (gc / NST) & 1, ctx))) break;
         tc_fence_after();
         uint32_t dob, qb;
         if constexpr (BF16) {
@@ -1125,46 +1210,58 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         mma_pv<T>(tmem + C::TM_DK, sbase + C::OFF_DS + ts * C::ST_BYTES, qb, c > 0);
         mma_commit(&bar_tempty[ts]);
         mma_commit(&bar_qempty[qs]);
-        if (NB == 1 && c + 1 < nchunks && !(ok = issue_s(c + 1))) break;
+        if (NB == 1 && c + 1 < nchunks) {
+          if (!(ok = issue_s(gc + 1))) break;
+          if (c + 2 == nchunks) mma_commit(&bar_kvempty);
+        }
       }
       if (ok) mma_commit(&bar_done);
+      }
     }
   } else {
     // ---------------- element-wise warps: thread = key ----------------
     const Ew e = ew_id(tmem);
+    const float sc_l2 = p.scale_log2;
+    bool ok = true;
+    int it = 0;
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++it) {
+    const int kblk = tile % p.nrb, bh = tile / p.nrb, b = bh / p.H, h = bh % p.H;
     const int key = kblk * kBM + e.r;
     const Abg ab = load_abg(p, h);
-    const float sc_l2 = p.scale_log2;
     const float aL = ab.a * kLog2e, bL = ab.b * kLog2e, gL = ab.g * kLog2e, cL = ab.c * kLog2e;
     const int pkey = key < p.np ? key : 0;
     const bool kvalid = key < p.N;
-    bool ok = true;
+    (void)pkey;
     for (int c = 0; c < nchunks; ++c) {
-      const int qs = c % NB, ts = c % NST;
+      const int gc = it * nchunks + c;
+      const int qs = gc % NB, ts = gc % NST;
       // row records of this query chunk -> shared memory (double-buffered by chunk parity). The named barrier is
       // reached once per chunk by every element-wise thread, also after an abort, so it can never wait forever.
-      float(*rec)[8] = rec_sh[c & 1];
+      float(*rec)[T::CH] = rec_sh[gc & 1];
       if (threadIdx.x < T::CH) {
         const int q = c * T::CH + threadIdx.x;
         float4 a = make_float4(0.f, 0.f, 0.f, 0.f), bb = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (q < p.N) {
+        if (q < p.N) {  // rows past N get zero records: P1 = P2 = dS = 0 in their columns
           const float* src = p.rowrec + ((size_t)bh * p.N + q) * 8;
           a = *reinterpret_cast<const float4*>(src);
           bb = *reinterpret_cast<const float4*>(src + 4);
         }
-        *reinterpret_cast<float4*>(&rec[threadIdx.x][0]) = a;
-        *reinterpret_cast<float4*>(&rec[threadIdx.x][4]) = bb;
+        rec[0][threadIdx.x] = a.x;
+        rec[1][threadIdx.x] = a.y;
+        rec[2][threadIdx.x] = a.z;
+        rec[3][threadIdx.x] = a.w;
+        rec[4][threadIdx.x] = bb.x;
       }
       ew_sync(T::EWT);
       if (!ok) continue;
-      if (!(ok = warp_wait(&bar_sfull[qs], (c / NB) & 1, ctx))) continue;
-      if (!(ok = warp_wait(&bar_tempty[ts], ((c / NST) & 1) ^ 1, ctx))) continue;
+      if (!(ok = warp_wait(&bar_sfull[qs], (gc / NB) & 1, ctx))) continue;
+      if (!(ok = warp_wait(&bar_tempty[ts], ((gc / NST) & 1) ^ 1, ctx))) continue;
       if constexpr (NPR > 0)
-        if (!(ok = warp_wait(&bar_prfull[c % NPR], (c / NPR) & 1, ctx))) continue;
+        if (!(ok = warp_wait(&bar_prfull[gc % NPR], (gc / NPR) & 1, ctx))) continue;
       tc_fence_after();
       uint8_t* p2reg = smem + C::OFF_P2 + ts * C::ST_BYTES;
       uint8_t* dsreg = smem + C::OFF_DS + ts * C::ST_BYTES;
-      const uint8_t* prt = smem + C::OFF_PR + (NPR > 0 ? (c % (NPR > 0 ? NPR : 1)) : 0) * kPriorTileBytes;
+      const uint8_t* prt = smem + C::OFF_PR + (NPR > 0 ? (gc % (NPR > 0 ? NPR : 1)) : 0) * kPriorTileBytes;
 #pragma unroll 1
       for (int piece = e.wg; piece < T::PIECES; piece += T::EW) {
         uint32_t vs[32], ws[32];
@@ -1175,28 +1272,41 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         tmem_wait32(vs);
         tmem_pin32(ws);
         float v[32], w[32];
+        // keys past N (last block only) produce rows of P2^T / dS^T that only reach dK/dV rows that are never
+        // stored, so no per-key mask is needed
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const float4 ra = *reinterpret_cast<const float4*>(&rec[piece * 32 + j][0]);  // m, 1/l1, 1/l2, delta1
-          const float d2 = rec[piece * 32 + j][4];
-          const float t = __uint_as_float(vs[j]) * sc_l2;
-          const float p1 = ex2(t - ra.x) * ra.y;
-          const float z2 = fmaf(aL, p1, fmaf(bL, dp[j], fmaf(gL, ap[j], -cL)));
-          const float p2 = ex2(z2) * ra.z;
-          const float dz = p2 * (__uint_as_float(ws[j]) - d2);
-          v[j] = kvalid ? p2 : 0.f;
-          w[j] = kvalid ? p1 * fmaf(ab.a, dz, -ra.w) : 0.f;
+        for (int j4 = 0; j4 < 32; j4 += 4) {
+          const int q = piece * 32 + j4;
+          const float4 m4 = *reinterpret_cast<const float4*>(&rec[0][q]);
+          const float4 il1 = *reinterpret_cast<const float4*>(&rec[1][q]);
+          const float4 il2 = *reinterpret_cast<const float4*>(&rec[2][q]);
+          const float4 d1 = *reinterpret_cast<const float4*>(&rec[3][q]);
+          const float4 d2 = *reinterpret_cast<const float4*>(&rec[4][q]);
+          const float mm[4] = {m4.x, m4.y, m4.z, m4.w}, i1[4] = {il1.x, il1.y, il1.z, il1.w};
+          const float i2[4] = {il2.x, il2.y, il2.z, il2.w}, e1[4] = {d1.x, d1.y, d1.z, d1.w};
+          const float e2[4] = {d2.x, d2.y, d2.z, d2.w};
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const int j = j4 + k;
+            const float t = __uint_as_float(vs[j]) * sc_l2;
+            const float p1 = ex2(t - mm[k]) * i1[k];
+            const float z2 = fmaf(aL, p1, fmaf(bL, dp[j], fmaf(gL, ap[j], -cL)));
+            const float p2 = ex2(z2) * i2[k];
+            const float dz = p2 * (__uint_as_float(ws[j]) - e2[k]);
+            v[j] = p2;
+            w[j] = p1 * fmaf(ab.a, dz, -e1[k]);
+          }
         }
         stage_row32<BF16>(p2reg, e.r, piece, v);
         stage_row32<BF16>(dsreg, e.r, piece, w);
       }
       fence_proxy_async_smem();
       tc_fence_before();
-      if constexpr (NPR > 0) mbar_arrive(&bar_prempty[c % NPR]);
+      if constexpr (NPR > 0) mbar_arrive(&bar_prempty[gc % NPR]);
       mbar_arrive(&bar_tfull[ts]);
       mbar_arrive(&bar_sempty[qs]);
     }
-    if (ok) ok = warp_wait(&bar_done, 0, ctx);
+    if (ok) ok = warp_wait(&bar_done, it & 1, ctx);
     tc_fence_after();
     if (ok) {
       const long long koff = (long long)b * p.dk_str[0] + (long long)h * p.dk_str[1] + (long long)key * p.dk_str[2];
@@ -1209,6 +1319,8 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         tmem_ld32(e.lane_base + C::TM_DV + d0, v);
         if (kvalid && d0 < p.D) store_row32<BF16>(p.dv, voff, p.dv_str[3], d0, p.D, v, 1.0f);
       }
+    }
+    tc_fence_before();  // the dK/dV reads above precede this warp's next hand-offs to the MMA warp
     }
   }
   tc_fence_before();
