@@ -266,7 +266,7 @@ size_t bwd_ws(const Dims& d, uint8_t* base, BwdWs* w) {
   };
   BwdWs t{};
   t.status = reinterpret_cast<int*>(take(sizeof(int)));
-  t.rowrec = reinterpret_cast<float*>(take((size_t)d.B * d.H * d.N * 8 * 4));
+  t.rowrec = reinterpret_cast<float*>(take((size_t)d.B * d.H * d.np * 4 * 4));  // [B*H][np/CH][4][CH]
   t.part = reinterpret_cast<double*>(take((size_t)d.B * d.H * d.nrb * 3 * 8));
   if (!d.bf16) {
     const size_t nat = (size_t)2 * d.B * d.H * d.N * d.DP * 4, trn = (size_t)d.B * d.H * d.DP * d.np * 4;
@@ -343,7 +343,18 @@ KParams base_params(const Dims& d, const float* abg, int per_head, const void* p
   p.per_head = per_head;
   p.prior = prior;
   p.priorT = reinterpret_cast<const uint8_t*>(prior) + prior_table_bytes(d);
+  p.nchp = d.np / (d.bf16 ? 64 : 32);
   return p;
+}
+
+// Store map over a bf16 output [B, H, N, D] (box 64 x 128), or false when the tensor is not TMA-compatible (the
+// kernels then store rows directly).
+bool map_output(CUtensorMap* m, void* data, const long long* stride, const Dims& d) {
+  if (!d.bf16) return false;
+  GeoAttnTensor t;
+  t.data = data;
+  for (int i = 0; i < 4; ++i) t.stride[i] = stride[i];
+  return map_user_bf16(m, t, d, kBM) == GEOATTN_OK;
 }
 
 // Persistent grid: one CTA per SM (every attention kernel holds an SM's tensor memory), at most one per tile.
@@ -382,15 +393,15 @@ int run_fwd(const TileMaps& maps, const KParams& p, const Dims& d, cudaStream_t 
   return rc;
 }
 template <bool BF16, int DP>
-int run_bwd(const TileMaps& rmaps, const TileMaps& cmaps, const KParams& p, const Dims& d, cudaStream_t st,
-            void* const* ev) {
+int run_bwd(const TileMaps& rmaps, const TileMaps& cmaps, const KParams& prow, const KParams& pcol, const Dims& d,
+            cudaStream_t st, void* const* ev) {
   record(ev, 0, st);
   int rc = launch(geoattn_bwd_rows_kernel<BF16, DP>, RowsCfg<BF16, DP>::SMEM, Tile<BF16, DP>::NTHREADS,
-                  persistent_grid(d), st, rmaps, p);
+                  persistent_grid(d), st, rmaps, prow);
   if (rc) return rc;
   record(ev, 1, st);
   rc = launch(geoattn_bwd_cols_kernel<BF16, DP>, ColsCfg<BF16, DP>::SMEM, Tile<BF16, DP>::NTHREADS,
-              persistent_grid(d), st, cmaps, p);
+              persistent_grid(d), st, cmaps, pcol);
   record(ev, 2, st);
   return rc;
 }
@@ -507,6 +518,7 @@ int geoattn_fwd(const GeoAttnFwdArgs* a, void* stream) {
   for (int i = 0; i < 4; ++i) p.o_str[i] = a->o_stride[i];
   p.stats = a->stats;
   p.status = ws.status;
+  p.out_tma = map_output(&maps.out0, a->o, a->o_stride, d) ? 1 : 0;
   if (d.bf16) {
     if (d.DP == 64) return run_fwd<true, 64>(maps, p, d, st, a->events);
     if (d.DP == 128) return run_fwd<true, 128>(maps, p, d, st, a->events);
@@ -570,12 +582,16 @@ int geoattn_bwd(const GeoAttnBwdArgs* a, void* stream) {
   p.rowrec = ws.rowrec;
   p.part = ws.part;
   p.status = ws.status;
+  KParams prow = p, pcol = p;
+  prow.out_tma = map_output(&rm.out0, a->dq, a->dq_stride, d) ? 1 : 0;
+  pcol.out_tma =
+      (map_output(&cm.out0, a->dk, a->dk_stride, d) && map_output(&cm.out1, a->dv, a->dv_stride, d)) ? 1 : 0;
   if (d.bf16) {
-    if (d.DP == 64) rc = run_bwd<true, 64>(rm, cm, p, d, st, a->events);
-    else if (d.DP == 128) rc = run_bwd<true, 128>(rm, cm, p, d, st, a->events);
-    else rc = run_bwd<true, 192>(rm, cm, p, d, st, a->events);
+    if (d.DP == 64) rc = run_bwd<true, 64>(rm, cm, prow, pcol, d, st, a->events);
+    else if (d.DP == 128) rc = run_bwd<true, 128>(rm, cm, prow, pcol, d, st, a->events);
+    else rc = run_bwd<true, 192>(rm, cm, prow, pcol, d, st, a->events);
   } else {
-    rc = run_bwd<false, 64>(rm, cm, p, d, st, a->events);
+    rc = run_bwd<false, 64>(rm, cm, prow, pcol, d, st, a->events);
   }
   if (rc) return rc;
   finalize_abg_kernel<<<dim3(3, d.nabg), 256, 0, st>>>(ws.part, d.B, d.H, d.nrb, a->shape.per_head, a->dabg);

@@ -6,15 +6,17 @@
 //
 // All kernels share one CTA shape: EW element-wise warpgroups (EW = 2 for bf16, 1 for fp32; a thread of warp w owns
 // TMEM lane 32*(w%4) + lane, i.e. one row of every 128-row accumulator, and warpgroup w/4 owns every EW-th 32-column
-// piece of each chunk), then one warp that issues TMA loads and one that issues tcgen05.mma. Every MMA is M = 128
-// with fp32 accumulators in tensor memory. Shared-memory operand tiles use the 128-byte swizzle; one "region" is
-// rows x 128 bytes (64 bf16 or 32 fp32 along the contiguous dimension). The geo-prior tile of each chunk is staged
-// into shared memory by the TMA warp ahead of use (or, where shared memory is full, read from L2 directly).
+// piece of each chunk), then one warp that issues the operand TMA loads, one that issues tcgen05.mma and one that
+// stages the geo-prior tile of each chunk into shared memory (so the prior ring and the operand rings refill
+// independently). Every MMA is M = 128 with fp32 accumulators in tensor memory. Shared-memory operand tiles use the
+// 128-byte swizzle; one "region" is rows x 128 bytes (64 bf16 or 32 fp32 along the contiguous dimension). Where
+// shared memory is full the prior is read from L2 directly. bf16 outputs (O, dQ, dK, dV) leave through a swizzled
+// shared-memory tile and a TMA store; the operands of the next tile are prefetched into L2 while this one runs.
 //
-// Softmax #1 runs in log2 units: t = acc * (log2(e)/sqrt(d)) is formed by one rounded multiply, the same
-// instruction in every pass and kernel, so the backward recomputes exactly the forward's scaled scores.
-// Softmax #2 needs no running max: Z <= c = |alpha|+|beta|+|gamma| whenever dist, ang >= 0, so
-// e = 2^((Z - c) log2 e) lies in (0, 1].
+// Softmax #1 runs in log2 units: t = acc * (log2(e)/sqrt(d)) with row max m. Once the row sum l1 is known, the
+// normalised probability is one fused multiply-add and one exp2: P1 = 2^(fma(acc, log2(e)/sqrt(d), -m1)) with
+// m1 = m + log2(l1). Softmax #2 needs no running max: Z <= c = |alpha|+|beta|+|gamma| whenever dist, ang >= 0, so
+// e = 2^((Z - c) log2 e) lies in (0, 1]; with its row sum l2, P2 = 2^(Z log2 e - c2), c2 = c log2 e + log2(l2).
 #pragma once
 #include <cuda_fp16.h>
 
@@ -55,9 +57,11 @@ struct KParams {
   void* dv;
   long long dv_str[4];
   float* stats;         // forward -> backward: [3][B*H*N] = m (log2 units), l1, l2
-  float* rowrec;        // backward row records [B*H*N][8] = m, 1/l1, 1/l2, delta1, delta2
+  float* rowrec;        // backward row records [B*H][nchp][4][CH] = m1, c2, delta1, delta2 per row (chunk-blocked)
+  int nchp;             // record chunks per b*h = np / CH
   double* part;         // [B*H*nrb][3] partial d(alpha), d(beta), d(gamma)
   int* status;          // device status word (0 = ok)
+  int out_tma;          // outputs leave through TMA stores (bf16, TMA-compatible output tensors)
 };
 
 struct Abg {
@@ -254,9 +258,10 @@ struct Tile {
   static constexpr uint32_t FMT = BF16 ? 1 : 2;
   static constexpr int EW = BF16 ? 2 : 1;   // element-wise warpgroups
   static constexpr int EWT = 128 * EW;      // element-wise threads
-  static constexpr int NTHREADS = EWT + 64;
+  static constexpr int NTHREADS = EWT + 96;
   static constexpr int TMA_WARP = 4 * EW;
   static constexpr int MMA_WARP = 4 * EW + 1;
+  static constexpr int PR_WARP = 4 * EW + 2;  // geo-prior tiles
   static_assert(DP % KB == 0, "padded head dim must be a whole number of 128-byte regions");
   static_assert(PIECES % EW == 0, "each warpgroup owns whole pieces");
 };
@@ -346,7 +351,41 @@ __device__ __forceinline__ void tma_prior(uint8_t* dst, const CUtensorMap* map, 
 
 struct TileMaps {
   CUtensorMap q, k, v, dout, kt, qt, dot, prior;  // unused entries are left zero
+  CUtensorMap out0, out1;                         // bf16 output stores: fwd O; rows dQ; cols dK, dV
 };
+
+// L2 prefetch of a row block of a natural operand (boxes of `rows` rows, all NKB regions and planes).
+template <class T>
+__device__ __forceinline__ void prefetch_tile(const CUtensorMap* map, int row0, int h, int b, int B, int npl) {
+  for (int pl = 0; pl < npl; ++pl)
+    for (int kb = 0; kb < T::NKB; ++kb) tma_prefetch_4d(map, kb * T::KB, row0, h, b + pl * B);
+}
+// L2 prefetch of all rows [0, N) of a natural operand in boxes of CH rows.
+template <class T>
+__device__ __forceinline__ void prefetch_rows(const CUtensorMap* map, int N, int h, int b, int B, int npl) {
+  for (int r0 = 0; r0 < N; r0 += T::CH) prefetch_tile<T>(map, r0, h, b, B, npl);
+}
+
+// bf16 output epilogue: 32 accumulator columns [d0, d0+32) of row r, scaled and rounded, into a swizzled tile of
+// 128-row x 64-column regions (the layout a TMA store of box (64, 128) reads).
+__device__ __forceinline__ void stage_out32(uint8_t* tile, int r, int d0, float (&v)[32], float scale) {
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] *= scale;
+  stage_row32<true>(tile + (d0 / 64) * (kBM * 128), r, (d0 % 64) / 32, v);
+}
+// Stores the staged tile (row block row0 of (b, h)) once every element-wise thread has staged its row. Called by all
+// element-wise threads; thread 0 issues the stores. The caller's next rewrite of `tile` must follow a
+// bulk_wait_read0() by thread 0 and a barrier among the element-wise threads.
+template <class T>
+__device__ __forceinline__ void store_tile(const CUtensorMap* map, const uint8_t* tile, int D, int row0, int h, int b,
+                                           bool issue) {
+  fence_proxy_async_smem();
+  ew_sync(T::EWT);
+  if (threadIdx.x == 0 && issue) {
+    for (int kb = 0; kb < T::NKB && kb * 64 < D; ++kb) tma_store_4d(map, tile + kb * (kBM * 128), kb * 64, row0, h, b);
+    bulk_commit();
+  }
+}
 
 // Prior access for one chunk: staged tile in shared memory, or the table in global memory.
 template <bool F16, bool STAGED>
@@ -380,6 +419,8 @@ struct FwdCfg : Tile<BF16, DP> {
   static constexpr int TM_S = 0;
   static constexpr int TM_O = 2 * T::CH;
   static constexpr int TMEM_COLS = pow2_cols(2 * T::CH + DP);
+  // O leaves through the two P buffers (free once the tile's last P.V has run) when they hold the whole row block
+  static constexpr bool EPI_TMA = BF16 && T::NKB * kBM * 128 <= 2 * P_BYTES;
 };
 
 template <bool BF16, int DP>
@@ -388,6 +429,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
   using C = FwdCfg<BF16, DP>;
   using T = typename C::T;
   constexpr int NPR = C::NPR;
+  static_assert(!C::EPI_TMA || T::EW > 1, "the TMA epilogue relies on the warpgroup exchange barrier");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ uint64_t bar_qfull, bar_qempty, bar_kfull[2], bar_kempty[2], bar_vfull[2], bar_vempty[2], bar_sfull[2],
@@ -399,6 +441,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
   const int nchunks = (p.N + T::CH - 1) / T::CH;
   const int ntiles = p.nrb * p.B * p.H;  // tile = (128-query row block, b*h); persistent CTAs stride over tiles
   WaitCtx ctx{&abort_flag, p.status};
+  const bool epi_tma = C::EPI_TMA && p.out_tma;
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
@@ -434,8 +477,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       prefetch_tmap(&maps.q);
       prefetch_tmap(&maps.k);
       prefetch_tmap(&maps.v);
-      prefetch_tmap(&maps.prior);
-      int kc = 0, vc = 0, prc = 0, it = 0;
+      int kc = 0, vc = 0, it = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++it) {
         const int rb = tile % p.nrb, bh = tile / p.nrb, b = bh / p.H, h = bh % p.H;
@@ -444,6 +486,12 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         mbar_arrive_expect_tx(&bar_qfull, T::PL * C::Q_BYTES);
         tma_tile<T>(smem + C::OFF_Q, &maps.q, &bar_qfull, kBM, rb * kBM, h, b, p.B, T::PL);
         for (int pass = 0; pass < 2 && ok; ++pass) {
+          if (pass == 1 && tile + (int)gridDim.x < ntiles) {  // next tile's operands into L2
+            const int nt = tile + gridDim.x, nbh = nt / p.nrb, nb = nbh / p.H, nh = nbh % p.H;
+            prefetch_tile<T>(&maps.q, (nt % p.nrb) * kBM, nh, nb, p.B, T::PL);
+            prefetch_rows<T>(&maps.k, p.N, nh, nb, p.B, T::PL);
+            if constexpr (BF16) prefetch_rows<T>(&maps.v, p.N, nh, nb, p.B, 1);
+          }
           for (int c = 0; c < nchunks && ok; ++c) {
             const int ks = kc & 1;
             if (!(ok = mbar_wait(&bar_kempty[ks], ((kc >> 1) & 1) ^ 1, ctx))) break;
@@ -459,14 +507,25 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
                 tma_tile<T>(smem + C::OFF_V + vs * C::V_BYTES, &maps.v, &bar_vfull[vs], T::CH, c * T::CH, h, b, p.B, 1);
               else
                 tma_tileT(smem + C::OFF_V + vs * C::V_BYTES, &maps.v, &bar_vfull[vs], c * T::CH, h, b);
-              const int ps = prc % NPR;
-              if (!(ok = mbar_wait(&bar_prempty[ps], ((prc / NPR) & 1) ^ 1, ctx))) break;
-              mbar_arrive_expect_tx(&bar_prfull[ps], kPriorTileBytes);
-              tma_prior(smem + C::OFF_PR + ps * kPriorTileBytes, &maps.prior, &bar_prfull[ps], rb * kBM, c);
-              ++prc;
               ++vc;
             }
           }
+        }
+      }
+    }
+  } else if (warp == T::PR_WARP) {
+    if (lane == 0) {
+      prefetch_tmap(&maps.prior);
+      int prc = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+        const int rb = tile % p.nrb;
+        for (int c = 0; c < nchunks && ok; ++c) {  // pass B only
+          const int ps = prc % NPR;
+          if (!(ok = mbar_wait(&bar_prempty[ps], ((prc / NPR) & 1) ^ 1, ctx))) break;
+          mbar_arrive_expect_tx(&bar_prfull[ps], kPriorTileBytes);
+          tma_prior(smem + C::OFF_PR + ps * kPriorTileBytes, &maps.prior, &bar_prfull[ps], rb * kBM, c);
+          ++prc;
         }
       }
     }
@@ -506,7 +565,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         if (ok) mma_commit(&bar_ofull);
       }
     }
-  } else {
+  } else if (warp < T::TMA_WARP) {
     // ---------------- element-wise warps ----------------
     const Ew e = ew_id(tmem);
     const float sc_l2 = p.scale_log2;
@@ -517,7 +576,8 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       const int row = rb * kBM + e.r;
       const Abg ab = load_abg(p, h);
       float m = -INFINITY, l = 0.f;
-      // Pass A: running max and sum over this warpgroup's pieces
+      // Pass A: running max and sum over this warpgroup's pieces. The max is taken over the raw accumulators
+      // (scaling by a positive constant and rounding are monotonic), the sum from fma(acc, scale, -m).
       for (int c = 0; c < nchunks && ok; ++c) {
         const int ss = sc & 1;
         if (!(ok = warp_wait(&bar_sfull[ss], (sc >> 1) & 1, ctx))) break;
@@ -527,23 +587,20 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
           float v[32];
           tmem_ld32(e.lane_base + C::TM_S + ss * T::CH + piece * 32, v);
           const int nvalid = p.N - (c * T::CH + piece * 32);  // >= 32: no masked column in this piece
-          if (nvalid >= 32) {
+          if (nvalid < 32) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] *= sc_l2;
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = (j < nvalid) ? v[j] * sc_l2 : -INFINITY;
+            for (int j = 0; j < 32; ++j) v[j] = (j < nvalid) ? v[j] : -INFINITY;
           }
           // four independent partial maxima / sums keep the dependency chains short
           float mx4[4] = {v[0], v[1], v[2], v[3]};
 #pragma unroll
           for (int j = 4; j < 32; ++j) mx4[j & 3] = fmaxf(mx4[j & 3], v[j]);
-          const float mn = fmaxf(m, fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])));
+          const float mn = fmaxf(m, fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * sc_l2);
           // a warpgroup whose columns so far are all masked keeps m = -inf, l = 0 (never 2^(-inf - -inf))
           const float mref = (mn == -INFINITY) ? 0.f : mn;
           float s4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-          for (int j = 0; j < 32; ++j) s4[j & 3] += ex2(v[j] - mref);
+          for (int j = 0; j < 32; ++j) s4[j & 3] += ex2(fmaf(v[j], sc_l2, -mref));
           l = l * ex2(m - mref) + ((s4[0] + s4[1]) + (s4[2] + s4[3]));
           m = mn;
         }
@@ -554,6 +611,8 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       if constexpr (T::EW > 1) {  // combine the warpgroups' statistics (same order in every warpgroup)
         xch[0][e.wg][e.r] = m;
         xch[1][e.wg][e.r] = l;
+        // the previous tile's O store has finished reading the P buffers before pass B rewrites them
+        if (epi_tma && threadIdx.x == 0) bulk_wait_read0();
         ew_sync(T::EWT);
         m = xch[0][0][e.r];
 #pragma unroll
@@ -566,7 +625,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         }
         ew_sync(T::EWT);
       }
-      const float inv_l1 = __frcp_rn(l);
+      const float m1 = m + log2f(l);  // P1 = 2^(t - m1)
       const float aL = ab.a * kLog2e, bL = ab.b * kLog2e, gL = ab.g * kLog2e, cL = ab.c * kLog2e;
       float l2 = 0.f;
       // Pass B
@@ -590,8 +649,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
           auto body = [&](auto masked) {
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
-              const float t = __uint_as_float(vs[j]) * sc_l2;
-              const float p1 = ex2(t - m) * inv_l1;
+              const float p1 = ex2(fmaf(__uint_as_float(vs[j]), sc_l2, -m1));
               const float z2 = fmaf(aL, p1, fmaf(bL, dp[j], fmaf(gL, ap[j], -cL)));
               float ev = ex2(z2);
               if constexpr (decltype(masked)::value) ev = (j < nvalid) ? ev : 0.f;
@@ -622,8 +680,19 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       }
       if (ok) ok = warp_wait(&bar_ofull, it & 1, ctx);
       tc_fence_after();
-      if (ok) {
-        const float inv_l2 = __frcp_rn(l2);
+      const float inv_l2 = __frcp_rn(l2);
+      if (epi_tma) {
+        // every P.V of the tile has completed (ofull), so the P buffers hold the staged O tile
+        if (ok) {
+#pragma unroll
+          for (int d0 = e.wg * 32; d0 < DP; d0 += 32 * T::EW) {
+            float v[32];
+            tmem_ld32(e.lane_base + C::TM_O + d0, v);
+            stage_out32(smem + C::OFF_P, e.r, d0, v, inv_l2);
+          }
+        }
+        store_tile<T>(&maps.out0, smem + C::OFF_P, p.D, rb * kBM, h, b, ok);
+      } else if (ok) {
         const long long ooff = (long long)b * p.o_str[0] + (long long)h * p.o_str[1] + (long long)row * p.o_str[2];
 #pragma unroll
         for (int d0 = e.wg * 32; d0 < DP; d0 += 32 * T::EW) {
@@ -631,15 +700,16 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
           tmem_ld32(e.lane_base + C::TM_O + d0, v);
           if (row < p.N && d0 < p.D) store_row32<BF16>(p.o, ooff, p.o_str[3], d0, p.D, v, inv_l2);
         }
-        if (row < p.N && e.wg == 0) {
-          const size_t s = (size_t)bh * p.N + row, n = (size_t)p.B * p.H * p.N;
-          p.stats[s] = m;
-          p.stats[n + s] = l;
-          p.stats[2 * n + s] = l2;
-        }
+      }
+      if (ok && row < p.N && e.wg == 0) {
+        const size_t s = (size_t)bh * p.N + row, n = (size_t)p.B * p.H * p.N;
+        p.stats[s] = m;
+        p.stats[n + s] = l;
+        p.stats[2 * n + s] = l2;
       }
       tc_fence_before();  // the O reads above precede this warp's next hand-offs to the MMA warp
     }
+    if (epi_tma && threadIdx.x == 0) bulk_wait_read0();  // shared memory outlives the last store's reads
   }
   tc_fence_before();
   __syncthreads();
@@ -649,11 +719,11 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
 // ===============================================================================================================
 // Backward row pass: one CTA per (128-query row block, b*h).
 // Sweep 1 recomputes S, dP = dO V^T, P1, P2 and accumulates, per row, with the shift delta2' = dO.O:
-//   r = sum w, a = sum w P1, b = sum P2 P1, c = sum w Dp, e = sum P2 Dp, f = sum w Ap, g = sum P2 Ap,
-//   where w = P2 (dP - delta2').  Then delta2 = delta2' + r (so rowsum(dZ) vanishes, as with
-//   delta2 = rowsum(P2 dP2) recomputed from tiles), and with dZ = w - r P2:
-//   sum dZ P1 = a - r b,  sum dZ Dp = c - r e,  sum dZ Ap = f - r g,  delta1 = alpha (a - r b).
-// Sweep 2 recomputes the tiles again, forms dS = P1 (alpha dZ - delta1) and accumulates dQ += dS K.
+//   r = sum w, a = sum w P1, b = sum P2 P1,  where w = P2 (dP - delta2').
+//   Then delta2 = delta2' + r (so rowsum(dZ) vanishes, as with delta2 = rowsum(P2 dP2) recomputed from tiles), and
+//   with dZ = w - r P2: sum dZ P1 = a - r b = d(alpha) of the row, delta1 = alpha (a - r b).
+// Sweep 2 recomputes the tiles again, forms dZ, dS = P1 (alpha dZ - delta1), accumulates dQ += dS K and the row's
+// d(beta) = sum dZ Dp, d(gamma) = sum dZ Ap. The row records (m1, c2, delta1, delta2) go to the key pass.
 // ===============================================================================================================
 template <bool BF16, int DP>
 struct RowsCfg : Tile<BF16, DP> {
@@ -677,7 +747,15 @@ struct RowsCfg : Tile<BF16, DP> {
   static constexpr int TM_DP = 2 * T::CH;          // 2 buffers
   static constexpr int TM_DQ = 4 * T::CH;
   static constexpr int TMEM_COLS = pow2_cols(4 * T::CH + DP);
+  // dQ leaves through the dS buffers (free once the tile's last dQ MMA has run) when they hold the whole row block
+  static constexpr bool EPI_TMA = BF16 && T::NKB * kBM * 128 <= NDS * DS_BYTES;
 };
+
+// Row record of `row` (chunk-blocked so that the key pass can fetch one query chunk's records in one bulk copy).
+template <class T>
+__device__ __forceinline__ float* rec_ptr(const KParams& p, int bh, int row) {
+  return p.rowrec + ((size_t)bh * p.nchp + row / T::CH) * 4 * T::CH + row % T::CH;
+}
 
 template <bool BF16, int DP>
 __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
@@ -692,10 +770,12 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_flag;
   __shared__ double red[8][3];
+  __shared__ float xd2[Tile<BF16, DP>::EW][kBM];  // cross-warpgroup delta2' halves
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int nchunks = (p.N + T::CH - 1) / T::CH;
   const int ntiles = p.nrb * p.B * p.H;  // tile = (128-query row block, b*h); persistent CTAs stride over tiles
   WaitCtx ctx{&abort_flag, p.status};
+  const bool epi_tma = C::EPI_TMA && p.out_tma;
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
@@ -734,8 +814,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       prefetch_tmap(&maps.k);
       prefetch_tmap(&maps.v);
       prefetch_tmap(&maps.dout);
-      prefetch_tmap(&maps.prior);
-      int kc = 0, tc = 0, pc = 0, it = 0;
+      int kc = 0, tc = 0, it = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++it) {
       const int rb = tile % p.nrb, bh = tile / p.nrb, b = bh / p.H, h = bh % p.H;
@@ -745,13 +824,14 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       tma_tile<T>(smem + C::OFF_Q, &maps.q, &bar_qfull, kBM, rb * kBM, h, b, p.B, T::PL);
       tma_tile<T>(smem + C::OFF_DO, &maps.dout, &bar_qfull, kBM, rb * kBM, h, b, p.B, T::PL);
       for (int sweep = 0; sweep < 2 && ok; ++sweep) {
+        if (sweep == 1 && tile + (int)gridDim.x < ntiles) {  // next tile's operands into L2
+          const int nt = tile + gridDim.x, nbh = nt / p.nrb, nb = nbh / p.H, nh = nbh % p.H, nrow = (nt % p.nrb) * kBM;
+          prefetch_tile<T>(&maps.q, nrow, nh, nb, p.B, T::PL);
+          prefetch_tile<T>(&maps.dout, nrow, nh, nb, p.B, T::PL);
+          prefetch_rows<T>(&maps.k, p.N, nh, nb, p.B, T::PL);
+          prefetch_rows<T>(&maps.v, p.N, nh, nb, p.B, T::PL);
+        }
         for (int c = 0; c < nchunks && ok; ++c) {
-          // the prior tile first: it only waits for the element-wise warps, while K may wait for dQ's MMA
-          const int ps = pc % NPR;
-          if (!(ok = mbar_wait(&bar_prempty[ps], ((pc / NPR) & 1) ^ 1, ctx))) break;
-          mbar_arrive_expect_tx(&bar_prfull[ps], kPriorTileBytes);
-          tma_prior(smem + C::OFF_PR + ps * kPriorTileBytes, &maps.prior, &bar_prfull[ps], rb * kBM, c);
-          ++pc;
           const int ks = kc % NKV;
           if (!(ok = mbar_wait(&bar_kempty[ks], ((kc / NKV) & 1) ^ 1, ctx))) break;
           mbar_arrive_expect_tx(&bar_kfull[ks], T::PL * C::K_BYTES);
@@ -774,6 +854,37 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         }
       }
       }
+    }
+  } else if (warp == T::PR_WARP) {
+    prefetch_tmap(&maps.prior);
+    int pc = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+      const int rb = tile % p.nrb;
+      // the next tile's forward output rows (for delta2' = dO.O) into L2, one 128-byte line per prefetch
+      if (tile + (int)gridDim.x < ntiles) {
+        const int nt = tile + gridDim.x, nbh = nt / p.nrb, nb = nbh / p.H, nh = nbh % p.H, nrow = (nt % p.nrb) * kBM;
+        const int lines = (p.D * T::EB + 127) / 128;
+        for (int i = lane; i < kBM * lines; i += 32) {
+          const int r = nrow + i / lines;
+          if (r >= p.N) break;
+          const long long off = (long long)nb * p.oi_str[0] + (long long)nh * p.oi_str[1] + (long long)r * p.oi_str[2] +
+                                (long long)((i % lines) * (128 / T::EB)) * p.oi_str[3];
+          prefetch_l2(reinterpret_cast<const uint8_t*>(p.o_in) + off * T::EB);
+        }
+      }
+      if (lane == 0) {
+        for (int sweep = 0; sweep < 2 && ok; ++sweep) {
+          for (int c = 0; c < nchunks && ok; ++c) {
+            const int ps = pc % NPR;
+            if (!(ok = mbar_wait(&bar_prempty[ps], ((pc / NPR) & 1) ^ 1, ctx))) break;
+            mbar_arrive_expect_tx(&bar_prfull[ps], kPriorTileBytes);
+            tma_prior(smem + C::OFF_PR + ps * kPriorTileBytes, &maps.prior, &bar_prfull[ps], rb * kBM, c);
+            ++pc;
+          }
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
     }
   } else if (warp == T::MMA_WARP) {
     if (lane == 0) {
@@ -835,7 +946,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         if (ok) mma_commit(&bar_dqfull);
       }
     }
-  } else {
+  } else if (warp < T::TMA_WARP) {
     // ---------------- element-wise warps ----------------
     const Ew e = ew_id(tmem);
     const float sc_l2 = p.scale_log2;
@@ -847,53 +958,60 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
     const int row = rb * kBM + e.r;
     const bool valid = row < p.N;
     const Abg ab = load_abg(p, h);
+    const float aL = ab.a * kLog2e, bL = ab.b * kLog2e, gL = ab.g * kLog2e, cL = ab.c * kLog2e;
     const size_t srow = (size_t)bh * p.N + (valid ? row : 0);
-    float m = 0.f, inv_l1 = 0.f, inv_l2 = 0.f, d2s = 0.f;
+    // P1 = 2^(t - m1), P2 = 2^(Z log2 e - c2); rows past N get m1 = c2 = +inf (P1 = P2 = 0)
+    float m1 = INFINITY, c2 = INFINITY, d2s = 0.f;
     if (valid) {
-      m = p.stats[srow];
-      inv_l1 = __frcp_rn(p.stats[nrows_all + srow]);
-      inv_l2 = __frcp_rn(p.stats[2 * nrows_all + srow]);
+      m1 = p.stats[srow] + log2f(p.stats[nrows_all + srow]);
+      c2 = cL + log2f(p.stats[2 * nrows_all + srow]);
     }
-    // delta2' = dO . O per row. bf16: dO from the TMA-loaded tile in shared memory and O with 16-byte loads, the
-    // row's 16-byte chunks split between the warpgroups; fp32: straight from global memory.
+    // delta2' = dO . O per row. bf16: dO from the TMA-loaded tile in shared memory and O with 16-byte loads (all
+    // issued before the first use), the row's 16-byte chunks split between the warpgroups; fp32: from global memory.
     const long long oo = (long long)b * p.oi_str[0] + (long long)h * p.oi_str[1] + (long long)row * p.oi_str[2];
     if constexpr (BF16) {
       if (ok) ok = warp_wait(&bar_qfull, it & 1, ctx);
       const __nv_bfloat16* orow = reinterpret_cast<const __nv_bfloat16*>(p.o_in) + oo;
       const bool vec = p.oi_str[3] == 1 && (reinterpret_cast<uintptr_t>(orow) & 15) == 0;
+      constexpr int PER = T::NKB * 8 / T::EW;  // 16-byte chunks of a row per warpgroup
       if (ok && valid) {
-        for (int ch = e.wg; ch < T::NKB * 8; ch += T::EW) {
-          const int kb = ch >> 3, q = ch & 7, d0 = kb * 64 + q * 8;
-          if (d0 >= p.D) continue;
-          const uint4 du = *reinterpret_cast<const uint4*>(smem + C::OFF_DO + kb * (kBM * 128) + sw128(e.r, q));
-          const uint32_t dw[4] = {du.x, du.y, du.z, du.w};
-          float ov[8];
-          if (vec && d0 + 8 <= p.D) {
-            const uint4 u = *reinterpret_cast<const uint4*>(orow + d0);
-            const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+        uint4 ou[PER];
+#pragma unroll
+        for (int i = 0; i < PER; ++i) {
+          const int d0 = (e.wg + i * T::EW) * 8;
+          ou[i] = (vec && d0 + 8 <= p.D) ? *reinterpret_cast<const uint4*>(orow + d0) : make_uint4(0u, 0u, 0u, 0u);
+        }
+#pragma unroll
+        for (int i = 0; i < PER; ++i) {
+          const int ch = e.wg + i * T::EW, kb = ch >> 3, q = ch & 7, d0 = ch * 8;
+          if (d0 < p.D) {
+            const uint4 du = *reinterpret_cast<const uint4*>(smem + C::OFF_DO + kb * (kBM * 128) + sw128(e.r, q));
+            const uint32_t dw[4] = {du.x, du.y, du.z, du.w};
+            const uint32_t w[4] = {ou[i].x, ou[i].y, ou[i].z, ou[i].w};
+            float ov[8];
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
               const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[k]));
               ov[2 * k] = f.x;
               ov[2 * k + 1] = f.y;
             }
-          } else {
+            if (!(vec && d0 + 8 <= p.D)) {
 #pragma unroll
-            for (int k = 0; k < 8; ++k) ov[k] = d0 + k < p.D ? __bfloat162float(orow[(d0 + k) * p.oi_str[3]]) : 0.f;
-          }
+              for (int k = 0; k < 8; ++k) ov[k] = d0 + k < p.D ? __bfloat162float(orow[(d0 + k) * p.oi_str[3]]) : 0.f;
+            }
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&dw[k]));
-            d2s = fmaf(f.x, ov[2 * k], d2s);
-            d2s = fmaf(f.y, ov[2 * k + 1], d2s);
+            for (int k = 0; k < 4; ++k) {
+              const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&dw[k]));
+              d2s = fmaf(f.x, ov[2 * k], d2s);
+              d2s = fmaf(f.y, ov[2 * k + 1], d2s);
+            }
           }
         }
       }
       if constexpr (T::EW == 2) {
-        float* xs = reinterpret_cast<float*>(smem + C::OFF_DS) + 14 * kBM;
-        xs[e.wg * kBM + e.r] = d2s;
+        xd2[e.wg][e.r] = d2s;  // rewritten next tile, after this tile's later barriers
         ew_sync(T::EWT);
-        d2s = xs[e.r] + xs[kBM + e.r];
+        d2s = xd2[0][e.r] + xd2[1][e.r];
       }
     } else {
       if (valid) {
@@ -902,8 +1020,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
           d2s = fmaf(load_elem<BF16>(p.dout, od + d * p.do_str[3]), load_elem<BF16>(p.o_in, oo + d * p.oi_str[3]), d2s);
       }
     }
-    const float aL = ab.a * kLog2e, bL = ab.b * kLog2e, gL = ab.g * kLog2e, cL = ab.c * kLog2e;
-    float acc[7] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // r, a, b, c, e, f, g
+    float acc[3] = {0.f, 0.f, 0.f};  // r, a, b
     for (int c = 0; c < nchunks && ok; ++c) {
       const int ss = sc & 1, prs = pc % NPR;
       if (!(ok = warp_wait(&bar_sfull[ss], (sc >> 1) & 1, ctx))) break;
@@ -920,31 +1037,25 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         prior32_smem<BF16>(prt, e.r, piece, dp, ap);
         tmem_wait32(vs);
         tmem_pin32(ws);
-        float pa[2][7] = {};  // two interleaved partial sums per quantity (shorter dependency chains)
+        float pa[2][3] = {};  // two interleaved partial sums per quantity (shorter dependency chains)
         auto body = [&](auto masked) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
-            const float t = __uint_as_float(vs[j]) * sc_l2;
-            float p1 = ex2(t - m) * inv_l1;
+            float p1 = ex2(fmaf(__uint_as_float(vs[j]), sc_l2, -m1));
             if constexpr (decltype(masked)::value) p1 = (j < nvalid) ? p1 : 0.f;
-            const float z2 = fmaf(aL, p1, fmaf(bL, dp[j], fmaf(gL, ap[j], -cL)));
-            float p2 = ex2(z2) * inv_l2;
+            float p2 = ex2(fmaf(aL, p1, fmaf(bL, dp[j], fmaf(gL, ap[j], -c2))));
             if constexpr (decltype(masked)::value) p2 = (j < nvalid) ? p2 : 0.f;
             const float wv = p2 * (__uint_as_float(ws[j]) - d2s);
             float* q = pa[j & 1];
             q[0] += wv;
             q[1] = fmaf(wv, p1, q[1]);
             q[2] = fmaf(p2, p1, q[2]);
-            q[3] = fmaf(wv, dp[j], q[3]);
-            q[4] = fmaf(p2, dp[j], q[4]);
-            q[5] = fmaf(wv, ap[j], q[5]);
-            q[6] = fmaf(p2, ap[j], q[6]);
           }
         };
         if (nvalid >= 32) body(std::false_type{});
         else body(std::true_type{});
 #pragma unroll
-        for (int k = 0; k < 7; ++k) acc[k] += pa[0][k] + pa[1][k];
+        for (int k = 0; k < 3; ++k) acc[k] += pa[0][k] + pa[1][k];
       }
       tc_fence_before();
       mbar_arrive(&bar_prempty[prs]);
@@ -953,46 +1064,31 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       ++pc;
     }
     if constexpr (T::EW == 2) {
-      // combine the two warpgroups' row sums through the (still unused) dS buffer, warpgroup 0's first
+      // combine the two warpgroups' row sums through the dS buffers (unused until sweep 2), warpgroup 0's first,
+      // once the previous tile's dQ store has finished reading them
+      if (epi_tma && threadIdx.x == 0) bulk_wait_read0();
+      ew_sync(T::EWT);
       float* xs = reinterpret_cast<float*>(smem + C::OFF_DS);
 #pragma unroll
-      for (int k = 0; k < 7; ++k) xs[(e.wg * 7 + k) * kBM + e.r] = acc[k];
+      for (int k = 0; k < 3; ++k) xs[(e.wg * 3 + k) * kBM + e.r] = acc[k];
       ew_sync(T::EWT);
 #pragma unroll
-      for (int k = 0; k < 7; ++k) acc[k] = xs[k * kBM + e.r] + xs[(7 + k) * kBM + e.r];
+      for (int k = 0; k < 3; ++k) acc[k] = xs[k * kBM + e.r] + xs[(3 + k) * kBM + e.r];
       ew_sync(T::EWT);
     }
     const float sr = acc[0];
     const float delta2 = d2s + sr;
-    const float ta = fmaf(-sr, acc[2], acc[1]);
+    const float ta = fmaf(-sr, acc[2], acc[1]);  // sum dZ P1 of the row
     const float delta1 = ab.a * ta;
-    const bool mine = valid && e.wg == 0;
-    double ga = mine ? (double)ta : 0.0, gb = mine ? (double)fmaf(-sr, acc[4], acc[3]) : 0.0,
-           gg = mine ? (double)fmaf(-sr, acc[6], acc[5]) : 0.0;
-    if (mine && ok) {
-      float* rec = p.rowrec + srow * 8;
-      *reinterpret_cast<float4*>(rec) = make_float4(m, inv_l1, inv_l2, delta1);
-      *reinterpret_cast<float4*>(rec + 4) = make_float4(delta2, 0.f, 0.f, 0.f);
-    }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-      ga += __shfl_down_sync(0xffffffffu, ga, off);
-      gb += __shfl_down_sync(0xffffffffu, gb, off);
-      gg += __shfl_down_sync(0xffffffffu, gg, off);
-    }
-    if (lane == 0) {
-      red[warp][0] = ga;
-      red[warp][1] = gb;
-      red[warp][2] = gg;
-    }
-    ew_sync(T::EWT);
-    if (threadIdx.x == 0) {
-      double* out = p.part + ((size_t)bh * p.nrb + rb) * 3;
-      out[0] = (red[0][0] + red[1][0]) + (red[2][0] + red[3][0]);
-      out[1] = (red[0][1] + red[1][1]) + (red[2][1] + red[3][1]);
-      out[2] = (red[0][2] + red[1][2]) + (red[2][2] + red[3][2]);
+    if (e.wg == 0 && ok) {
+      float* rec = rec_ptr<T>(p, bh, row);
+      rec[0] = m1;
+      rec[T::CH] = c2;
+      rec[2 * T::CH] = valid ? delta1 : 0.f;
+      rec[3 * T::CH] = valid ? delta2 : 0.f;
     }
     // Sweep 2
+    float gbp[2] = {0.f, 0.f}, ggp[2] = {0.f, 0.f};  // d(beta), d(gamma) partials of the row
     for (int c = 0; c < nchunks && ok; ++c) {
       const int ss = sc & 1, ds = dc % C::NDS, prs = pc % NPR;
       if (!(ok = warp_wait(&bar_sfull[ss], (sc >> 1) & 1, ctx))) break;
@@ -1014,13 +1110,14 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         auto body = [&](auto masked) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
-            const float t = __uint_as_float(vs[j]) * sc_l2;
-            float p1 = ex2(t - m) * inv_l1;
+            float p1 = ex2(fmaf(__uint_as_float(vs[j]), sc_l2, -m1));
             if constexpr (decltype(masked)::value) p1 = (j < nvalid) ? p1 : 0.f;
-            const float z2 = fmaf(aL, p1, fmaf(bL, dp[j], fmaf(gL, ap[j], -cL)));
-            const float p2 = ex2(z2) * inv_l2;
+            float p2 = ex2(fmaf(aL, p1, fmaf(bL, dp[j], fmaf(gL, ap[j], -c2))));
+            if constexpr (decltype(masked)::value) p2 = (j < nvalid) ? p2 : 0.f;
             const float dz = p2 * (__uint_as_float(ws[j]) - delta2);
             v[j] = p1 * fmaf(ab.a, dz, -delta1);  // masked columns: p1 = 0 -> dS = 0
+            gbp[j & 1] = fmaf(dz, dp[j], gbp[j & 1]);
+            ggp[j & 1] = fmaf(dz, ap[j], ggp[j & 1]);
           }
         };
         if (nvalid >= 32) body(std::false_type{});
@@ -1036,9 +1133,46 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       ++dc;
       ++pc;
     }
+    // block partials of d(alpha) (one per row: warpgroup 0), d(beta), d(gamma) (every warpgroup's columns)
+    {
+      double ga = (valid && e.wg == 0) ? (double)ta : 0.0, gb = valid ? (double)(gbp[0] + gbp[1]) : 0.0,
+             gg = valid ? (double)(ggp[0] + ggp[1]) : 0.0;
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) {
+        ga += __shfl_down_sync(0xffffffffu, ga, off);
+        gb += __shfl_down_sync(0xffffffffu, gb, off);
+        gg += __shfl_down_sync(0xffffffffu, gg, off);
+      }
+      if (lane == 0) {
+        red[warp][0] = ga;
+        red[warp][1] = gb;
+        red[warp][2] = gg;
+      }
+      ew_sync(T::EWT);
+      if (threadIdx.x == 0) {
+        double s3[3] = {0.0, 0.0, 0.0};
+        for (int w = 0; w < 4 * T::EW; ++w)
+          for (int k = 0; k < 3; ++k) s3[k] += red[w][k];
+        double* out = p.part + ((size_t)bh * p.nrb + rb) * 3;
+        out[0] = s3[0];
+        out[1] = s3[1];
+        out[2] = s3[2];
+      }
+    }
     if (ok) ok = warp_wait(&bar_dqfull, it & 1, ctx);
     tc_fence_after();
-    if (ok) {
+    if (epi_tma) {
+      // every dQ MMA of the tile has completed (dqfull), so the dS buffers hold the staged dQ tile
+      if (ok) {
+#pragma unroll 1
+        for (int d0 = e.wg * 32; d0 < DP; d0 += 32 * T::EW) {
+          float v[32];
+          tmem_ld32(e.lane_base + C::TM_DQ + d0, v);
+          stage_out32(smem + C::OFF_DS, e.r, d0, v, p.inv_sqrt_d);
+        }
+      }
+      store_tile<T>(&maps.out0, smem + C::OFF_DS, p.D, rb * kBM, h, b, ok);
+    } else if (ok) {
       const long long qoff = (long long)b * p.dq_str[0] + (long long)h * p.dq_str[1] + (long long)row * p.dq_str[2];
 #pragma unroll 1
       for (int d0 = e.wg * 32; d0 < DP; d0 += 32 * T::EW) {
@@ -1049,6 +1183,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
     }
     tc_fence_before();  // the dQ reads above precede this warp's next hand-offs to the MMA warp
     }
+    if (epi_tma && threadIdx.x == 0) bulk_wait_read0();  // shared memory outlives the last store's reads
   }
   tc_fence_before();
   __syncthreads();
@@ -1058,6 +1193,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
 // ===============================================================================================================
 // Backward key pass: one CTA per (128-key block, b*h); keys on TMEM lanes. For each chunk of CH queries:
 //   S^T = K Q^T, dP^T = V dO^T; P1, P2, dZ, dS from the row records; dV += P2^T dO, dK += dS^T Q.
+// The chunk's row records arrive by bulk copy together with its Q / dO tiles.
 // ===============================================================================================================
 template <bool BF16, int DP>
 struct ColsCfg : Tile<BF16, DP> {
@@ -1069,6 +1205,7 @@ struct ColsCfg : Tile<BF16, DP> {
   static constexpr int Q_BYTES = T::CH * DP * T::EB;        // per plane per buffer (Q and dO chunks)
   static constexpr int QT_BYTES = BF16 ? 0 : DP * 128;      // fp32: transposed Q / dO chunk (hi)
   static constexpr int ST_BYTES = kBM * 128;                // P2^T or dS^T tile
+  static constexpr int REC_BYTES = 4 * T::CH * 4;           // row records of one query chunk: m1, c2, delta1, delta2
   static constexpr int OFF_K = 0;
   static constexpr int OFF_V = OFF_K + T::PL * K_BYTES;
   static constexpr int OFF_Q = OFF_V + T::PL * K_BYTES;
@@ -1078,12 +1215,15 @@ struct ColsCfg : Tile<BF16, DP> {
   static constexpr int OFF_P2 = OFF_DOT + NB * QT_BYTES;
   static constexpr int OFF_DS = OFF_P2 + NST * ST_BYTES;
   static constexpr int OFF_PR = OFF_DS + NST * ST_BYTES;
-  static constexpr int SMEM = OFF_PR + NPR * kPriorTileBytes + 1024;
+  static constexpr int OFF_REC = OFF_PR + NPR * kPriorTileBytes;
+  static constexpr int SMEM = OFF_REC + NB * REC_BYTES + 1024;
   static constexpr int TM_S = 0;
   static constexpr int TM_DP = NB * T::CH;
   static constexpr int TM_DK = 2 * NB * T::CH;
   static constexpr int TM_DV = TM_DK + DP;
   static constexpr int TMEM_COLS = pow2_cols(2 * NB * T::CH + 2 * DP);
+  // dK and dV leave in turn through the P2^T / dS^T buffers (contiguous, free once the tile's last MMA has run)
+  static constexpr bool EPI_TMA = BF16 && T::NKB * kBM * 128 <= 2 * NST * ST_BYTES;
 };
 
 template <bool BF16, int DP>
@@ -1098,11 +1238,11 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       bar_prfull[2], bar_prempty[2], bar_done;
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_flag;
-  __shared__ __align__(16) float rec_sh[2][5][T::CH];  // per query: m, 1/l1, 1/l2, delta1, delta2
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int nchunks = (p.N + T::CH - 1) / T::CH;
   const int ntiles = p.nrb * p.B * p.H;  // tile = (128-key block, b*h); persistent CTAs stride over tiles
   WaitCtx ctx{&abort_flag, p.status};
+  const bool epi_tma = C::EPI_TMA && p.out_tma;
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
@@ -1146,11 +1286,16 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       mbar_arrive_expect_tx(&bar_kvfull, 2 * T::PL * C::K_BYTES);
       tma_tile<T>(smem + C::OFF_K, &maps.k, &bar_kvfull, kBM, kblk * kBM, h, b, p.B, T::PL);
       tma_tile<T>(smem + C::OFF_V, &maps.v, &bar_kvfull, kBM, kblk * kBM, h, b, p.B, T::PL);
+      if (tile + (int)gridDim.x < ntiles) {  // next tile's key block into L2
+        const int nt = tile + gridDim.x, nbh = nt / p.nrb, nb = nbh / p.H, nh = nbh % p.H, nrow = (nt % p.nrb) * kBM;
+        prefetch_tile<T>(&maps.k, nrow, nh, nb, p.B, T::PL);
+        prefetch_tile<T>(&maps.v, nrow, nh, nb, p.B, T::PL);
+      }
       for (int c = 0; c < nchunks; ++c) {
         const int gc = it * nchunks + c;  // chunk count over all tiles (buffer slots and phases)
         const int qs = gc % NB;
         if (!(ok = mbar_wait(&bar_qempty[qs], ((gc / NB) & 1) ^ 1, ctx))) break;
-        mbar_arrive_expect_tx(&bar_qfull[qs], 2 * T::PL * C::Q_BYTES + 2 * C::QT_BYTES);
+        mbar_arrive_expect_tx(&bar_qfull[qs], 2 * T::PL * C::Q_BYTES + 2 * C::QT_BYTES + C::REC_BYTES);
         tma_tile<T>(smem + C::OFF_Q + qs * T::PL * C::Q_BYTES, &maps.q, &bar_qfull[qs], T::CH, c * T::CH, h, b, p.B,
                     T::PL);
         tma_tile<T>(smem + C::OFF_DO + qs * T::PL * C::Q_BYTES, &maps.dout, &bar_qfull[qs], T::CH, c * T::CH, h, b,
@@ -1159,13 +1304,26 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
           tma_tileT(smem + C::OFF_QT + qs * C::QT_BYTES, &maps.qt, &bar_qfull[qs], c * T::CH, h, b);
           tma_tileT(smem + C::OFF_DOT + qs * C::QT_BYTES, &maps.dot, &bar_qfull[qs], c * T::CH, h, b);
         }
-        if constexpr (NPR > 0) {
-          const int ps = gc % NPR;
-          if (!(ok = mbar_wait(&bar_prempty[ps], ((gc / NPR) & 1) ^ 1, ctx))) break;
-          mbar_arrive_expect_tx(&bar_prfull[ps], kPriorTileBytes);
-          tma_prior(smem + C::OFF_PR + ps * kPriorTileBytes, &maps.prior, &bar_prfull[ps], kblk * kBM, c);
-        }
+        bulk_load(smem + C::OFF_REC + qs * C::REC_BYTES, p.rowrec + ((size_t)bh * p.nchp + c) * 4 * T::CH,
+                  C::REC_BYTES, &bar_qfull[qs]);
       }
+      }
+    }
+  } else if (warp == T::PR_WARP) {
+    if constexpr (NPR > 0) {
+      if (lane == 0) {
+        prefetch_tmap(&maps.prior);
+        bool ok = true;
+        int it = 0;
+        for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++it) {
+          const int kblk = tile % p.nrb;
+          for (int c = 0; c < nchunks && ok; ++c) {
+            const int gc = it * nchunks + c, ps = gc % NPR;
+            if (!(ok = mbar_wait(&bar_prempty[ps], ((gc / NPR) & 1) ^ 1, ctx))) break;
+            mbar_arrive_expect_tx(&bar_prfull[ps], kPriorTileBytes);
+            tma_prior(smem + C::OFF_PR + ps * kPriorTileBytes, &maps.prior, &bar_prfull[ps], kblk * kBM, c);
+          }
+        }
       }
     }
   } else if (warp == T::MMA_WARP) {
@@ -1218,7 +1376,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       if (ok) mma_commit(&bar_done);
       }
     }
-  } else {
+  } else if (warp < T::TMA_WARP) {
     // ---------------- element-wise warps: thread = key ----------------
     const Ew e = ew_id(tmem);
     const float sc_l2 = p.scale_log2;
@@ -1228,37 +1386,26 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
     const int kblk = tile % p.nrb, bh = tile / p.nrb, b = bh / p.H, h = bh % p.H;
     const int key = kblk * kBM + e.r;
     const Abg ab = load_abg(p, h);
-    const float aL = ab.a * kLog2e, bL = ab.b * kLog2e, gL = ab.g * kLog2e, cL = ab.c * kLog2e;
+    const float aL = ab.a * kLog2e, bL = ab.b * kLog2e, gL = ab.g * kLog2e;
     const int pkey = key < p.np ? key : 0;
     const bool kvalid = key < p.N;
     (void)pkey;
+    if (epi_tma) {  // the previous tile's dV store has finished reading the P2^T / dS^T buffers
+      if (threadIdx.x == 0) bulk_wait_read0();
+      ew_sync(T::EWT);
+    }
     for (int c = 0; c < nchunks; ++c) {
       const int gc = it * nchunks + c;
       const int qs = gc % NB, ts = gc % NST;
-      // row records of this query chunk -> shared memory (double-buffered by chunk parity). The named barrier is
-      // reached once per chunk by every element-wise thread, also after an abort, so it can never wait forever.
-      float(*rec)[T::CH] = rec_sh[gc & 1];
-      if (threadIdx.x < T::CH) {
-        const int q = c * T::CH + threadIdx.x;
-        float4 a = make_float4(0.f, 0.f, 0.f, 0.f), bb = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (q < p.N) {  // rows past N get zero records: P1 = P2 = dS = 0 in their columns
-          const float* src = p.rowrec + ((size_t)bh * p.N + q) * 8;
-          a = *reinterpret_cast<const float4*>(src);
-          bb = *reinterpret_cast<const float4*>(src + 4);
-        }
-        rec[0][threadIdx.x] = a.x;
-        rec[1][threadIdx.x] = a.y;
-        rec[2][threadIdx.x] = a.z;
-        rec[3][threadIdx.x] = a.w;
-        rec[4][threadIdx.x] = bb.x;
-      }
-      ew_sync(T::EWT);
       if (!ok) continue;
       if (!(ok = warp_wait(&bar_sfull[qs], (gc / NB) & 1, ctx))) continue;
       if (!(ok = warp_wait(&bar_tempty[ts], ((gc / NST) & 1) ^ 1, ctx))) continue;
       if constexpr (NPR > 0)
         if (!(ok = warp_wait(&bar_prfull[gc % NPR], (gc / NPR) & 1, ctx))) continue;
+      // the chunk's row records (rows past N carry m1 = c2 = +inf: P1 = P2 = dS = 0 in their columns)
+      if (!(ok = warp_wait(&bar_qfull[qs], (gc / NB) & 1, ctx))) continue;
       tc_fence_after();
+      const float* rec = reinterpret_cast<const float*>(smem + C::OFF_REC + qs * C::REC_BYTES);
       uint8_t* p2reg = smem + C::OFF_P2 + ts * C::ST_BYTES;
       uint8_t* dsreg = smem + C::OFF_DS + ts * C::ST_BYTES;
       const uint8_t* prt = smem + C::OFF_PR + (NPR > 0 ? (gc % (NPR > 0 ? NPR : 1)) : 0) * kPriorTileBytes;
@@ -1277,21 +1424,17 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
 #pragma unroll
         for (int j4 = 0; j4 < 32; j4 += 4) {
           const int q = piece * 32 + j4;
-          const float4 m4 = *reinterpret_cast<const float4*>(&rec[0][q]);
-          const float4 il1 = *reinterpret_cast<const float4*>(&rec[1][q]);
-          const float4 il2 = *reinterpret_cast<const float4*>(&rec[2][q]);
-          const float4 d1 = *reinterpret_cast<const float4*>(&rec[3][q]);
-          const float4 d2 = *reinterpret_cast<const float4*>(&rec[4][q]);
-          const float mm[4] = {m4.x, m4.y, m4.z, m4.w}, i1[4] = {il1.x, il1.y, il1.z, il1.w};
-          const float i2[4] = {il2.x, il2.y, il2.z, il2.w}, e1[4] = {d1.x, d1.y, d1.z, d1.w};
-          const float e2[4] = {d2.x, d2.y, d2.z, d2.w};
+          const float4 m4 = *reinterpret_cast<const float4*>(rec + q);
+          const float4 c4 = *reinterpret_cast<const float4*>(rec + T::CH + q);
+          const float4 d1 = *reinterpret_cast<const float4*>(rec + 2 * T::CH + q);
+          const float4 d2 = *reinterpret_cast<const float4*>(rec + 3 * T::CH + q);
+          const float mm[4] = {m4.x, m4.y, m4.z, m4.w}, cc[4] = {c4.x, c4.y, c4.z, c4.w};
+          const float e1[4] = {d1.x, d1.y, d1.z, d1.w}, e2[4] = {d2.x, d2.y, d2.z, d2.w};
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
             const int j = j4 + k;
-            const float t = __uint_as_float(vs[j]) * sc_l2;
-            const float p1 = ex2(t - mm[k]) * i1[k];
-            const float z2 = fmaf(aL, p1, fmaf(bL, dp[j], fmaf(gL, ap[j], -cL)));
-            const float p2 = ex2(z2) * i2[k];
+            const float p1 = ex2(fmaf(__uint_as_float(vs[j]), sc_l2, -mm[k]));
+            const float p2 = ex2(fmaf(aL, p1, fmaf(bL, dp[j], fmaf(gL, ap[j], -cc[k]))));
             const float dz = p2 * (__uint_as_float(ws[j]) - e2[k]);
             v[j] = p2;
             w[j] = p1 * fmaf(ab.a, dz, -e1[k]);
@@ -1308,7 +1451,30 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
     }
     if (ok) ok = warp_wait(&bar_done, it & 1, ctx);
     tc_fence_after();
-    if (ok) {
+    if (epi_tma) {
+      // every MMA of the tile has completed (done): the P2^T / dS^T buffers take dK, then dV
+      uint8_t* stg = smem + C::OFF_P2;
+      if (ok) {
+#pragma unroll 1
+        for (int d0 = e.wg * 32; d0 < DP; d0 += 32 * T::EW) {
+          float v[32];
+          tmem_ld32(e.lane_base + C::TM_DK + d0, v);
+          stage_out32(stg, e.r, d0, v, p.inv_sqrt_d);
+        }
+      }
+      store_tile<T>(&maps.out0, stg, p.D, kblk * kBM, h, b, ok);
+      if (threadIdx.x == 0) bulk_wait_read0();
+      ew_sync(T::EWT);
+      if (ok) {
+#pragma unroll 1
+        for (int d0 = e.wg * 32; d0 < DP; d0 += 32 * T::EW) {
+          float v[32];
+          tmem_ld32(e.lane_base + C::TM_DV + d0, v);
+          stage_out32(stg, e.r, d0, v, 1.0f);
+        }
+      }
+      store_tile<T>(&maps.out1, stg, p.D, kblk * kBM, h, b, ok);
+    } else if (ok) {
       const long long koff = (long long)b * p.dk_str[0] + (long long)h * p.dk_str[1] + (long long)key * p.dk_str[2];
       const long long voff = (long long)b * p.dv_str[0] + (long long)h * p.dv_str[1] + (long long)key * p.dv_str[2];
 #pragma unroll 1
@@ -1322,6 +1488,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
     }
     tc_fence_before();  // the dK/dV reads above precede this warp's next hand-offs to the MMA warp
     }
+    if (epi_tma && threadIdx.x == 0) bulk_wait_read0();  // shared memory outlives the last store's reads
   }
   tc_fence_before();
   __syncthreads();

@@ -41,7 +41,7 @@ def test_size_queries_without_gpu(L):
     sh = _lib.Shape(32, 8, 512, 64, _lib.DTYPE_BF16, 1)
     assert L.geoattn_prior_bytes(ctypes.byref(sh)) == 2 * 512 * 512 * 4
     assert L.geoattn_stats_bytes(ctypes.byref(sh)) == 3 * 32 * 8 * 512 * 4
-    assert L.geoattn_bwd_workspace_bytes(ctypes.byref(sh)) > 32 * 8 * 512 * 32
+    assert L.geoattn_bwd_workspace_bytes(ctypes.byref(sh)) > 32 * 8 * 512 * 16   # 4 float row records per row
     bad = _lib.Shape(1, 1, 16, 256, _lib.DTYPE_BF16, 0)
     assert L.geoattn_prior_bytes(ctypes.byref(bad)) == 0
     fp = _lib.Shape(1, 1, 16, 128, _lib.DTYPE_FP32, 0)
