@@ -566,10 +566,8 @@ int geoattn_bwd(const GeoAttnBwdArgs* a, void* stream) {
       (rc = map_prior(&cm.prior, reinterpret_cast<const uint8_t*>(a->prior) + prior_table_bytes(d), d)))
     return rc;
   KParams p = base_params(d, a->abg, a->shape.per_head, a->prior);
-  p.o_in = a->o.data;
   p.dout = a->dout.data;
   for (int i = 0; i < 4; ++i) {
-    p.oi_str[i] = a->o.stride[i];
     p.do_str[i] = a->dout.stride[i];
     p.dq_str[i] = a->dq_stride[i];
     p.dk_str[i] = a->dk_stride[i];

@@ -46,8 +46,6 @@ struct KParams {
   const void* priorT;   // transposed table
   void* o;              // forward output, strides o_str
   long long o_str[4];
-  const void* o_in;     // backward: forward output (for delta2 = dO . O)
-  long long oi_str[4];
   const void* dout;     // backward: dO
   long long do_str[4];
   void* dq;
@@ -263,7 +261,7 @@ struct Tile {
   static constexpr int MMA_WARP = 4 * EW + 1;
   static constexpr int PR_WARP = 4 * EW + 2;  // geo-prior tiles
   static_assert(DP % KB == 0, "padded head dim must be a whole number of 128-byte regions");
-  static_assert(PIECES % EW == 0, "each warpgroup owns whole pieces");
+  static_assert(PIECES == EW, "each warpgroup owns exactly one piece of every chunk");
 };
 
 // Element-wise thread identity.
@@ -586,6 +584,8 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         for (int piece = e.wg; piece < T::PIECES; piece += T::EW) {
           float v[32];
           tmem_ld32(e.lane_base + C::TM_S + ss * T::CH + piece * 32, v);
+          tc_fence_before();
+          mbar_arrive(&bar_sempty[ss]);  // the scores are in registers: the MMA may refill the buffer
           const int nvalid = p.N - (c * T::CH + piece * 32);  // >= 32: no masked column in this piece
           if (nvalid < 32) {
 #pragma unroll
@@ -604,8 +604,6 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
           l = l * ex2(m - mref) + ((s4[0] + s4[1]) + (s4[2] + s4[3]));
           m = mn;
         }
-        tc_fence_before();
-        mbar_arrive(&bar_sempty[ss]);
         ++sc;
       }
       if constexpr (T::EW > 1) {  // combine the warpgroups' statistics (same order in every warpgroup)
@@ -644,6 +642,9 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
           tmem_ld32_issue(e.lane_base + C::TM_S + ss * T::CH + piece * 32, vs);
           prior32_smem<BF16>(prt, e.r, piece, dp, ap);  // overlaps the tensor-memory load
           tmem_wait32(vs);
+          tc_fence_before();
+          mbar_arrive(&bar_prempty[prs]);  // scores and prior are in registers: both buffers may be refilled
+          mbar_arrive(&bar_sempty[ss]);
           const int nvalid = p.N - (c * T::CH + piece * 32);
           float l24[4] = {0.f, 0.f, 0.f, 0.f};
           auto body = [&](auto masked) {
@@ -663,10 +664,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
           stage_row32<BF16>(preg, e.r, piece, v);
         }
         fence_proxy_async_smem();
-        tc_fence_before();
-        mbar_arrive(&bar_prempty[prs]);
         mbar_arrive(&bar_pfull[ps]);
-        mbar_arrive(&bar_sempty[ss]);
         ++sc;
         ++pc;
         ++prc;
@@ -718,10 +716,9 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
 
 // ===============================================================================================================
 // Backward row pass: one CTA per (128-query row block, b*h).
-// Sweep 1 recomputes S, dP = dO V^T, P1, P2 and accumulates, per row, with the shift delta2' = dO.O:
-//   r = sum w, a = sum w P1, b = sum P2 P1,  where w = P2 (dP - delta2').
-//   Then delta2 = delta2' + r (so rowsum(dZ) vanishes, as with delta2 = rowsum(P2 dP2) recomputed from tiles), and
-//   with dZ = w - r P2: sum dZ P1 = a - r b = d(alpha) of the row, delta1 = alpha (a - r b).
+// Sweep 1 recomputes S, dP = dO V^T, P1, P2 and accumulates, per row,
+//   delta2 = sum P2 dP,  a = sum P2 dP P1,  b = sum P2 P1,
+//   so that with dZ = P2 (dP - delta2): sum dZ P1 = a - delta2 b = d(alpha) of the row, delta1 = alpha (a - delta2 b).
 // Sweep 2 recomputes the tiles again, forms dZ, dS = P1 (alpha dZ - delta1), accumulates dQ += dS K and the row's
 // d(beta) = sum dZ Dp, d(gamma) = sum dZ Ap. The row records (m1, c2, delta1, delta2) go to the key pass.
 // ===============================================================================================================
@@ -770,7 +767,6 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_flag;
   __shared__ double red[8][3];
-  __shared__ float xd2[Tile<BF16, DP>::EW][kBM];  // cross-warpgroup delta2' halves
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int nchunks = (p.N + T::CH - 1) / T::CH;
   const int ntiles = p.nrb * p.B * p.H;  // tile = (128-query row block, b*h); persistent CTAs stride over tiles
@@ -861,18 +857,6 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
     bool ok = true;
     for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
       const int rb = tile % p.nrb;
-      // the next tile's forward output rows (for delta2' = dO.O) into L2, one 128-byte line per prefetch
-      if (tile + (int)gridDim.x < ntiles) {
-        const int nt = tile + gridDim.x, nbh = nt / p.nrb, nb = nbh / p.H, nh = nbh % p.H, nrow = (nt % p.nrb) * kBM;
-        const int lines = (p.D * T::EB + 127) / 128;
-        for (int i = lane; i < kBM * lines; i += 32) {
-          const int r = nrow + i / lines;
-          if (r >= p.N) break;
-          const long long off = (long long)nb * p.oi_str[0] + (long long)nh * p.oi_str[1] + (long long)r * p.oi_str[2] +
-                                (long long)((i % lines) * (128 / T::EB)) * p.oi_str[3];
-          prefetch_l2(reinterpret_cast<const uint8_t*>(p.o_in) + off * T::EB);
-        }
-      }
       if (lane == 0) {
         for (int sweep = 0; sweep < 2 && ok; ++sweep) {
           for (int c = 0; c < nchunks && ok; ++c) {
@@ -961,66 +945,12 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
     const float aL = ab.a * kLog2e, bL = ab.b * kLog2e, gL = ab.g * kLog2e, cL = ab.c * kLog2e;
     const size_t srow = (size_t)bh * p.N + (valid ? row : 0);
     // P1 = 2^(t - m1), P2 = 2^(Z log2 e - c2); rows past N get m1 = c2 = +inf (P1 = P2 = 0)
-    float m1 = INFINITY, c2 = INFINITY, d2s = 0.f;
+    float m1 = INFINITY, c2 = INFINITY;
     if (valid) {
       m1 = p.stats[srow] + log2f(p.stats[nrows_all + srow]);
       c2 = cL + log2f(p.stats[2 * nrows_all + srow]);
     }
-    // delta2' = dO . O per row. bf16: dO from the TMA-loaded tile in shared memory and O with 16-byte loads (all
-    // issued before the first use), the row's 16-byte chunks split between the warpgroups; fp32: from global memory.
-    const long long oo = (long long)b * p.oi_str[0] + (long long)h * p.oi_str[1] + (long long)row * p.oi_str[2];
-    if constexpr (BF16) {
-      if (ok) ok = warp_wait(&bar_qfull, it & 1, ctx);
-      const __nv_bfloat16* orow = reinterpret_cast<const __nv_bfloat16*>(p.o_in) + oo;
-      const bool vec = p.oi_str[3] == 1 && (reinterpret_cast<uintptr_t>(orow) & 15) == 0;
-      constexpr int PER = T::NKB * 8 / T::EW;  // 16-byte chunks of a row per warpgroup
-      if (ok && valid) {
-        uint4 ou[PER];
-#pragma unroll
-        for (int i = 0; i < PER; ++i) {
-          const int d0 = (e.wg + i * T::EW) * 8;
-          ou[i] = (vec && d0 + 8 <= p.D) ? *reinterpret_cast<const uint4*>(orow + d0) : make_uint4(0u, 0u, 0u, 0u);
-        }
-#pragma unroll
-        for (int i = 0; i < PER; ++i) {
-          const int ch = e.wg + i * T::EW, kb = ch >> 3, q = ch & 7, d0 = ch * 8;
-          if (d0 < p.D) {
-            const uint4 du = *reinterpret_cast<const uint4*>(smem + C::OFF_DO + kb * (kBM * 128) + sw128(e.r, q));
-            const uint32_t dw[4] = {du.x, du.y, du.z, du.w};
-            const uint32_t w[4] = {ou[i].x, ou[i].y, ou[i].z, ou[i].w};
-            float ov[8];
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[k]));
-              ov[2 * k] = f.x;
-              ov[2 * k + 1] = f.y;
-            }
-            if (!(vec && d0 + 8 <= p.D)) {
-#pragma unroll
-              for (int k = 0; k < 8; ++k) ov[k] = d0 + k < p.D ? __bfloat162float(orow[(d0 + k) * p.oi_str[3]]) : 0.f;
-            }
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&dw[k]));
-              d2s = fmaf(f.x, ov[2 * k], d2s);
-              d2s = fmaf(f.y, ov[2 * k + 1], d2s);
-            }
-          }
-        }
-      }
-      if constexpr (T::EW == 2) {
-        xd2[e.wg][e.r] = d2s;  // rewritten next tile, after this tile's later barriers
-        ew_sync(T::EWT);
-        d2s = xd2[0][e.r] + xd2[1][e.r];
-      }
-    } else {
-      if (valid) {
-        const long long od = (long long)b * p.do_str[0] + (long long)h * p.do_str[1] + (long long)row * p.do_str[2];
-        for (int d = 0; d < p.D; ++d)
-          d2s = fmaf(load_elem<BF16>(p.dout, od + d * p.do_str[3]), load_elem<BF16>(p.o_in, oo + d * p.oi_str[3]), d2s);
-      }
-    }
-    float acc[3] = {0.f, 0.f, 0.f};  // r, a, b
+    float acc[3] = {0.f, 0.f, 0.f};  // delta2, a, b
     for (int c = 0; c < nchunks && ok; ++c) {
       const int ss = sc & 1, prs = pc % NPR;
       if (!(ok = warp_wait(&bar_sfull[ss], (sc >> 1) & 1, ctx))) break;
@@ -1037,6 +967,9 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         prior32_smem<BF16>(prt, e.r, piece, dp, ap);
         tmem_wait32(vs);
         tmem_pin32(ws);
+        tc_fence_before();
+        mbar_arrive(&bar_prempty[prs]);  // scores and prior are in registers: both buffers may be refilled
+        mbar_arrive(&bar_sempty[ss]);
         float pa[2][3] = {};  // two interleaved partial sums per quantity (shorter dependency chains)
         auto body = [&](auto masked) {
 #pragma unroll
@@ -1045,7 +978,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
             if constexpr (decltype(masked)::value) p1 = (j < nvalid) ? p1 : 0.f;
             float p2 = ex2(fmaf(aL, p1, fmaf(bL, dp[j], fmaf(gL, ap[j], -c2))));
             if constexpr (decltype(masked)::value) p2 = (j < nvalid) ? p2 : 0.f;
-            const float wv = p2 * (__uint_as_float(ws[j]) - d2s);
+            const float wv = p2 * __uint_as_float(ws[j]);
             float* q = pa[j & 1];
             q[0] += wv;
             q[1] = fmaf(wv, p1, q[1]);
@@ -1057,9 +990,6 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
 #pragma unroll
         for (int k = 0; k < 3; ++k) acc[k] += pa[0][k] + pa[1][k];
       }
-      tc_fence_before();
-      mbar_arrive(&bar_prempty[prs]);
-      mbar_arrive(&bar_sempty[ss]);
       ++sc;
       ++pc;
     }
@@ -1076,9 +1006,8 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       for (int k = 0; k < 3; ++k) acc[k] = xs[k * kBM + e.r] + xs[(3 + k) * kBM + e.r];
       ew_sync(T::EWT);
     }
-    const float sr = acc[0];
-    const float delta2 = d2s + sr;
-    const float ta = fmaf(-sr, acc[2], acc[1]);  // sum dZ P1 of the row
+    const float delta2 = acc[0];
+    const float ta = fmaf(-delta2, acc[2], acc[1]);  // sum dZ P1 of the row
     const float delta1 = ab.a * ta;
     if (e.wg == 0 && ok) {
       float* rec = rec_ptr<T>(p, bh, row);
@@ -1107,6 +1036,9 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         prior32_smem<BF16>(prt, e.r, piece, dp, ap);
         tmem_wait32(vs);
         tmem_pin32(ws);
+        tc_fence_before();
+        mbar_arrive(&bar_prempty[prs]);
+        mbar_arrive(&bar_sempty[ss]);
         auto body = [&](auto masked) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
@@ -1125,10 +1057,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         stage_row32<BF16>(dreg, e.r, piece, v);
       }
       fence_proxy_async_smem();
-      tc_fence_before();
-      mbar_arrive(&bar_prempty[prs]);
       mbar_arrive(&bar_dsfull[ds]);
-      mbar_arrive(&bar_sempty[ss]);
       ++sc;
       ++dc;
       ++pc;
@@ -1418,6 +1347,9 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         prior_piece<BF16, (NPR > 0)>(prt, p.priorT, p.np, pkey, e.r, c, piece, dp, ap);
         tmem_wait32(vs);
         tmem_pin32(ws);
+        tc_fence_before();
+        if constexpr (NPR > 0) mbar_arrive(&bar_prempty[gc % NPR]);  // prior and scores are in registers
+        mbar_arrive(&bar_sempty[qs]);
         float v[32], w[32];
         // keys past N (last block only) produce rows of P2^T / dS^T that only reach dK/dV rows that are never
         // stored, so no per-key mask is needed
@@ -1444,10 +1376,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         stage_row32<BF16>(dsreg, e.r, piece, w);
       }
       fence_proxy_async_smem();
-      tc_fence_before();
-      if constexpr (NPR > 0) mbar_arrive(&bar_prempty[gc % NPR]);
       mbar_arrive(&bar_tfull[ts]);
-      mbar_arrive(&bar_sempty[qs]);
     }
     if (ok) ok = warp_wait(&bar_done, it & 1, ctx);
     tc_fence_after();

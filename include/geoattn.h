@@ -99,7 +99,7 @@ size_t geoattn_bwd_workspace_bytes(const GeoAttnShape* shape);
 
 typedef struct {
   GeoAttnShape shape;
-  GeoAttnTensor q, k, v, o, dout;
+  GeoAttnTensor q, k, v, o, dout; /* o: the forward output; checked, not read (delta2 comes from the tiles) */
   const float* abg;
   const void* prior;
   const float* stats; /* written by geoattn_fwd for the same inputs */
@@ -125,7 +125,7 @@ int geoattn_bwd(const GeoAttnBwdArgs* args, void* stream);
  * synchronise the device. Same arguments and results as geoattn_bwd, except that args->workspace is ignored: the
  * scratch comes from a static 16 MiB device array that the library holds on every device that loads it until the
  * process exits. Limits: BF16 only (GEOATTN_ERR_UNSUPPORTED for FP32); geoattn_bwd_workspace_bytes(shape) must be
- * <= 16 MiB (about B*H*N <= 500,000 rows, e.g. 32 issue dates x 16 heads x 512 stations), else
+ * <= 16 MiB (about B*H*N <= 1,000,000 rows, e.g. 64 issue dates x 16 heads x 512 stations), else
  * GEOATTN_ERR_SCRATCH before any launch. All calls share the array, so calls that overlap on the GPU race. The
  * first call on a device looks up the array's address (cudaGetSymbolAddress); make it before any stream capture.
  * It allocates nothing (no cudaMalloc/cudaFree, no allocating library call).                                  */

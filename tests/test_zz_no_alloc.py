@@ -78,7 +78,7 @@ def test_noalloc_backward_matches_workspace_backward_twice(L):
 def test_noalloc_rejects_sizes_beyond_its_buffer(L):
     from foreswe_gpu_optimization_b200 import _lib
     args = _lib.BwdArgs()
-    args.shape = _lib.Shape(256, 16, 512, 128, _lib.DTYPE_BF16, 1)      # ~67 MB of row records > 16 MiB
+    args.shape = _lib.Shape(256, 16, 512, 128, _lib.DTYPE_BF16, 1)      # ~34 MB of row records > 16 MiB
     assert L.geoattn_bwd_noalloc(ctypes.byref(args), None) == 7
     args.shape = _lib.Shape(1, 1, 64, 64, _lib.DTYPE_FP32, 0)
     assert L.geoattn_bwd_noalloc(ctypes.byref(args), None) == 2
