@@ -96,34 +96,48 @@ __device__ __forceinline__ uint32_t sw128(int r, int q) {
 }
 
 // ---------------------------------------------------------------------------------------------------------------
-// Prior loads: 32 consecutive pairs of one row.
+// Prior pieces: 32 consecutive (Dp, Ap) pairs of one row. The bf16 path keeps them packed as half2 (one register per
+// pair) and widens each pair where it is used; the fp32 path holds float pairs.
 // ---------------------------------------------------------------------------------------------------------------
 template <bool F16>
-__device__ __forceinline__ void load_prior32(const void* table, int np, int row, int col0, float (&dp)[32],
-                                             float (&ap)[32]) {
+struct Prior32 {
+  float dp[32], ap[32];
+  __device__ __forceinline__ void get(int j, float& d, float& a) const {
+    d = dp[j];
+    a = ap[j];
+  }
+};
+template <>
+struct Prior32<true> {
+  uint32_t w[32];
+  __device__ __forceinline__ void get(int j, float& d, float& a) const {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[j]));
+    d = f.x;
+    a = f.y;
+  }
+};
+
+template <bool F16>
+__device__ __forceinline__ void load_prior32(const void* table, int np, int row, int col0, Prior32<F16>& pr) {
   if constexpr (F16) {
     const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const __half2*>(table) + (size_t)row * np + col0);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      uint4 u = __ldg(src + i);
-      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        __half2 h2 = *reinterpret_cast<const __half2*>(&w[k]);
-        float2 f = __half22float2(h2);
-        dp[i * 4 + k] = f.x;
-        ap[i * 4 + k] = f.y;
-      }
+      const uint4 u = __ldg(src + i);
+      pr.w[4 * i] = u.x;
+      pr.w[4 * i + 1] = u.y;
+      pr.w[4 * i + 2] = u.z;
+      pr.w[4 * i + 3] = u.w;
     }
   } else {
     const float4* src = reinterpret_cast<const float4*>(reinterpret_cast<const float2*>(table) + (size_t)row * np + col0);
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
-      float4 f = __ldg(src + i);
-      dp[2 * i] = f.x;
-      ap[2 * i] = f.y;
-      dp[2 * i + 1] = f.z;
-      ap[2 * i + 1] = f.w;
+      const float4 f = __ldg(src + i);
+      pr.dp[2 * i] = f.x;
+      pr.ap[2 * i] = f.y;
+      pr.dp[2 * i + 1] = f.z;
+      pr.ap[2 * i + 1] = f.w;
     }
   }
 }
@@ -134,19 +148,16 @@ __device__ __forceinline__ void load_prior32(const void* table, int np, int row,
 constexpr int kPriorTileBytes = 2 * kBM * 128;
 
 template <bool F16>
-__device__ __forceinline__ void prior32_smem(const uint8_t* tile, int r, int piece, float (&dp)[32], float (&ap)[32]) {
+__device__ __forceinline__ void prior32_smem(const uint8_t* tile, int r, int piece, Prior32<F16>& pr) {
   if constexpr (F16) {
     const uint8_t* reg = tile + piece * (kBM * 128);
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
       const uint4 u = *reinterpret_cast<const uint4*>(reg + sw128(r, q));
-      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[k]));
-        dp[q * 4 + k] = f.x;
-        ap[q * 4 + k] = f.y;
-      }
+      pr.w[4 * q] = u.x;
+      pr.w[4 * q + 1] = u.y;
+      pr.w[4 * q + 2] = u.z;
+      pr.w[4 * q + 3] = u.w;
     }
   } else {
 #pragma unroll
@@ -154,10 +165,10 @@ __device__ __forceinline__ void prior32_smem(const uint8_t* tile, int r, int pie
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
         const float4 f = *reinterpret_cast<const float4*>(tile + rg * (kBM * 128) + sw128(r, q));
-        dp[rg * 16 + q * 2] = f.x;
-        ap[rg * 16 + q * 2] = f.y;
-        dp[rg * 16 + q * 2 + 1] = f.z;
-        ap[rg * 16 + q * 2 + 1] = f.w;
+        pr.dp[rg * 16 + q * 2] = f.x;
+        pr.ap[rg * 16 + q * 2] = f.y;
+        pr.dp[rg * 16 + q * 2 + 1] = f.z;
+        pr.ap[rg * 16 + q * 2 + 1] = f.w;
       }
   }
 }
@@ -388,11 +399,11 @@ __device__ __forceinline__ void store_tile(const CUtensorMap* map, const uint8_t
 // Prior access for one chunk: staged tile in shared memory, or the table in global memory.
 template <bool F16, bool STAGED>
 __device__ __forceinline__ void prior_piece(const uint8_t* tile, const void* table, int np, int row, int r, int c,
-                                            int piece, float (&dp)[32], float (&ap)[32]) {
+                                            int piece, Prior32<F16>& pr) {
   if constexpr (STAGED) {
-    prior32_smem<F16>(tile, r, piece, dp, ap);
+    prior32_smem<F16>(tile, r, piece, pr);
   } else {
-    load_prior32<F16>(table, np, row, c * (F16 ? 64 : 32) + piece * 32, dp, ap);
+    load_prior32<F16>(table, np, row, c * (F16 ? 64 : 32) + piece * 32, pr);
   }
 }
 
@@ -638,9 +649,10 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
 #pragma unroll
         for (int piece = e.wg; piece < T::PIECES; piece += T::EW) {
           uint32_t vs[32];
-          float v[32], dp[32], ap[32];
+          float v[32];
+          Prior32<BF16> pr;
           tmem_ld32_issue(e.lane_base + C::TM_S + ss * T::CH + piece * 32, vs);
-          prior32_smem<BF16>(prt, e.r, piece, dp, ap);  // overlaps the tensor-memory load
+          prior32_smem<BF16>(prt, e.r, piece, pr);  // overlaps the tensor-memory load
           tmem_wait32(vs);
           tc_fence_before();
           mbar_arrive(&bar_prempty[prs]);  // scores and prior are in registers: both buffers may be refilled
@@ -650,8 +662,10 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
           auto body = [&](auto masked) {
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
+              float dpj, apj;
+              pr.get(j, dpj, apj);
               const float p1 = ex2(fmaf(__uint_as_float(vs[j]), sc_l2, -m1));
-              const float z2 = fmaf(aL, p1, fmaf(bL, dp[j], fmaf(gL, ap[j], -cL)));
+              const float z2 = fmaf(aL, p1, fmaf(bL, dpj, fmaf(gL, apj, -cL)));
               float ev = ex2(z2);
               if constexpr (decltype(masked)::value) ev = (j < nvalid) ? ev : 0.f;
               l24[j & 3] += ev;
@@ -963,8 +977,8 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         tmem_ld32_issue(e.lane_base + C::TM_S + ss * T::CH + piece * 32, vs);
         tmem_ld32_issue(e.lane_base + C::TM_DP + ss * T::CH + piece * 32, ws);
         const int nvalid = p.N - (c * T::CH + piece * 32);
-        float dp[32], ap[32];
-        prior32_smem<BF16>(prt, e.r, piece, dp, ap);
+        Prior32<BF16> pr;
+        prior32_smem<BF16>(prt, e.r, piece, pr);
         tmem_wait32(vs);
         tmem_pin32(ws);
         tc_fence_before();
@@ -974,9 +988,11 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         auto body = [&](auto masked) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
+            float dpj, apj;
+            pr.get(j, dpj, apj);
             float p1 = ex2(fmaf(__uint_as_float(vs[j]), sc_l2, -m1));
             if constexpr (decltype(masked)::value) p1 = (j < nvalid) ? p1 : 0.f;
-            float p2 = ex2(fmaf(aL, p1, fmaf(bL, dp[j], fmaf(gL, ap[j], -c2))));
+            float p2 = ex2(fmaf(aL, p1, fmaf(bL, dpj, fmaf(gL, apj, -c2))));
             if constexpr (decltype(masked)::value) p2 = (j < nvalid) ? p2 : 0.f;
             const float wv = p2 * __uint_as_float(ws[j]);
             float* q = pa[j & 1];
@@ -1032,8 +1048,9 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         tmem_ld32_issue(e.lane_base + C::TM_S + ss * T::CH + piece * 32, vs);
         tmem_ld32_issue(e.lane_base + C::TM_DP + ss * T::CH + piece * 32, ws);
         const int nvalid = p.N - (c * T::CH + piece * 32);
-        float dp[32], ap[32], v[32];
-        prior32_smem<BF16>(prt, e.r, piece, dp, ap);
+        float v[32];
+        Prior32<BF16> pr;
+        prior32_smem<BF16>(prt, e.r, piece, pr);
         tmem_wait32(vs);
         tmem_pin32(ws);
         tc_fence_before();
@@ -1042,14 +1059,16 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         auto body = [&](auto masked) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
+            float dpj, apj;
+            pr.get(j, dpj, apj);
             float p1 = ex2(fmaf(__uint_as_float(vs[j]), sc_l2, -m1));
             if constexpr (decltype(masked)::value) p1 = (j < nvalid) ? p1 : 0.f;
-            float p2 = ex2(fmaf(aL, p1, fmaf(bL, dp[j], fmaf(gL, ap[j], -c2))));
+            float p2 = ex2(fmaf(aL, p1, fmaf(bL, dpj, fmaf(gL, apj, -c2))));
             if constexpr (decltype(masked)::value) p2 = (j < nvalid) ? p2 : 0.f;
             const float dz = p2 * (__uint_as_float(ws[j]) - delta2);
             v[j] = p1 * fmaf(ab.a, dz, -delta1);  // masked columns: p1 = 0 -> dS = 0
-            gbp[j & 1] = fmaf(dz, dp[j], gbp[j & 1]);
-            ggp[j & 1] = fmaf(dz, ap[j], ggp[j & 1]);
+            gbp[j & 1] = fmaf(dz, dpj, gbp[j & 1]);
+            ggp[j & 1] = fmaf(dz, apj, ggp[j & 1]);
           }
         };
         if (nvalid >= 32) body(std::false_type{});
@@ -1343,8 +1362,8 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         uint32_t vs[32], ws[32];
         tmem_ld32_issue(e.lane_base + C::TM_S + qs * T::CH + piece * 32, vs);
         tmem_ld32_issue(e.lane_base + C::TM_DP + qs * T::CH + piece * 32, ws);
-        float dp[32], ap[32];
-        prior_piece<BF16, (NPR > 0)>(prt, p.priorT, p.np, pkey, e.r, c, piece, dp, ap);
+        Prior32<BF16> pr;
+        prior_piece<BF16, (NPR > 0)>(prt, p.priorT, p.np, pkey, e.r, c, piece, pr);
         tmem_wait32(vs);
         tmem_pin32(ws);
         tc_fence_before();
@@ -1365,8 +1384,10 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
             const int j = j4 + k;
+            float dpj, apj;
+            pr.get(j, dpj, apj);
             const float p1 = ex2(fmaf(__uint_as_float(vs[j]), sc_l2, -mm[k]));
-            const float p2 = ex2(fmaf(aL, p1, fmaf(bL, dp[j], fmaf(gL, ap[j], -cc[k]))));
+            const float p2 = ex2(fmaf(aL, p1, fmaf(bL, dpj, fmaf(gL, apj, -cc[k]))));
             const float dz = p2 * (__uint_as_float(ws[j]) - e2[k]);
             v[j] = p2;
             w[j] = p1 * fmaf(ab.a, dz, -e1[k]);

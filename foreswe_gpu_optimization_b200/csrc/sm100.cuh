@@ -67,6 +67,24 @@ struct WaitCtx {
   int* status;               // global, first error wins
 };
 
+// try_wait that may suspend the thread until the phase completes or `hint_ns` elapses (PTX suspendTimeHint), so a
+// waiting warp stops competing for issue slots with the warps that do the work.
+__device__ __forceinline__ bool mbar_test_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
+// Longest single suspension inside a bounded wait: the abort flag and the wait limit are re-checked at least this
+// often (a completed phase wakes the thread at once).
+constexpr uint32_t kSuspendHintNs = 200000;
+
 // Wait until the barrier's phase with the given parity completes. Returns false (and raises the CTA's abort flag)
 // if the bounded wait expires or another thread of the CTA already aborted.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const WaitCtx& ctx) {
@@ -74,7 +92,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const 
   const uint64_t t0 = global_timer_ns();
   while (true) {
     if (*ctx.abort_flag) return false;
-    if (mbar_test(bar, parity)) return true;
+    if (mbar_test_sleep(bar, parity, kSuspendHintNs)) return true;
     if (global_timer_ns() - t0 > kWaitLimitNs) {
       *ctx.abort_flag = 1;
       if (ctx.status) atomicCAS(ctx.status, kDevOk, kDevWaitTimeout);
