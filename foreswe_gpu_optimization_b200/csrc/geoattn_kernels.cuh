@@ -415,13 +415,14 @@ template <bool BF16, int DP>
 struct FwdCfg : Tile<BF16, DP> {
   using T = Tile<BF16, DP>;
   static constexpr int NPR = (BF16 && DP > 128) ? 1 : 2;  // staged prior buffers
+  static constexpr int NK = (BF16 && DP <= 128) ? 3 : 2;    // K chunk buffers (pass A outruns a 2-deep ring)
   static constexpr int Q_BYTES = kBM * DP * T::EB;          // per plane
   static constexpr int K_BYTES = T::CH * DP * T::EB;        // per plane per buffer
   static constexpr int V_BYTES = T::CH * DP * T::EB;        // hi only (natural bf16 / transposed fp32)
   static constexpr int P_BYTES = kBM * 128;
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_K = OFF_Q + T::PL * Q_BYTES;
-  static constexpr int OFF_V = OFF_K + 2 * T::PL * K_BYTES;
+  static constexpr int OFF_V = OFF_K + NK * T::PL * K_BYTES;
   static constexpr int OFF_P = OFF_V + 2 * V_BYTES;
   static constexpr int OFF_PR = OFF_P + 2 * P_BYTES;
   static constexpr int SMEM = OFF_PR + NPR * kPriorTileBytes + 1024;
@@ -437,11 +438,11 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
     geoattn_fwd_kernel(const __grid_constant__ TileMaps maps, const KParams p) {
   using C = FwdCfg<BF16, DP>;
   using T = typename C::T;
-  constexpr int NPR = C::NPR;
+  constexpr int NPR = C::NPR, NK = C::NK;
   static_assert(!C::EPI_TMA || T::EW > 1, "the TMA epilogue relies on the warpgroup exchange barrier");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  __shared__ uint64_t bar_qfull, bar_qempty, bar_kfull[2], bar_kempty[2], bar_vfull[2], bar_vempty[2], bar_sfull[2],
+  __shared__ uint64_t bar_qfull, bar_qempty, bar_kfull[3], bar_kempty[3], bar_vfull[2], bar_vempty[2], bar_sfull[2],
       bar_sempty[2], bar_pfull[2], bar_pempty[2], bar_prfull[2], bar_prempty[2], bar_ofull;
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_flag;
@@ -456,9 +457,11 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
     abort_flag = 0;
     mbar_init(&bar_qfull, 1);
     mbar_init(&bar_qempty, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < 3; ++i) {
       mbar_init(&bar_kfull[i], 1);
       mbar_init(&bar_kempty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&bar_vfull[i], 1);
       mbar_init(&bar_vempty[i], 1);
       mbar_init(&bar_sfull[i], 1);
@@ -502,8 +505,8 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
             if constexpr (BF16) prefetch_rows<T>(&maps.v, p.N, nh, nb, p.B, 1);
           }
           for (int c = 0; c < nchunks && ok; ++c) {
-            const int ks = kc & 1;
-            if (!(ok = mbar_wait(&bar_kempty[ks], ((kc >> 1) & 1) ^ 1, ctx))) break;
+            const int ks = kc % NK;
+            if (!(ok = mbar_wait(&bar_kempty[ks], ((kc / NK) & 1) ^ 1, ctx))) break;
             mbar_arrive_expect_tx(&bar_kfull[ks], T::PL * C::K_BYTES);
             tma_tile<T>(smem + C::OFF_K + ks * T::PL * C::K_BYTES, &maps.k, &bar_kfull[ks], T::CH, c * T::CH, h, b,
                         p.B, T::PL);
@@ -543,8 +546,8 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       int kc = 0, sc = 0, pc = 0, it = 0;
       bool ok = true;
       auto issue_s = [&](void) -> bool {
-        const int ks = kc & 1, ss = sc & 1;
-        if (!mbar_wait(&bar_kfull[ks], (kc >> 1) & 1, ctx)) return false;
+        const int ks = kc % NK, ss = sc & 1;
+        if (!mbar_wait(&bar_kfull[ks], (kc / NK) & 1, ctx)) return false;
         if (!mbar_wait(&bar_sempty[ss], ((sc >> 1) & 1) ^ 1, ctx)) return false;
         tc_fence_after();
         mma_qk<T, T::CH>(tmem + C::TM_S + ss * T::CH, sbase + C::OFF_Q, C::Q_BYTES,
@@ -641,7 +644,6 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       for (int c = 0; c < nchunks && ok; ++c) {
         const int ss = sc & 1, ps = pc & 1, prs = prc % NPR;
         if (!(ok = warp_wait(&bar_sfull[ss], (sc >> 1) & 1, ctx))) break;
-        if (!(ok = warp_wait(&bar_pempty[ps], ((pc >> 1) & 1) ^ 1, ctx))) break;
         if (!(ok = warp_wait(&bar_prfull[prs], (prc / NPR) & 1, ctx))) break;
         tc_fence_after();
         uint8_t* preg = smem + C::OFF_P + ps * C::P_BYTES;
@@ -659,14 +661,16 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
           mbar_arrive(&bar_sempty[ss]);
           const int nvalid = p.N - (c * T::CH + piece * 32);
           float l24[4] = {0.f, 0.f, 0.f, 0.f};
+          // phase-ordered: 32 independent exp2 for P1, then the biased exp2 (more independent work per warp)
           auto body = [&](auto masked) {
+            float p1[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) p1[j] = ex2(fmaf(__uint_as_float(vs[j]), sc_l2, -m1));
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
               float dpj, apj;
               pr.get(j, dpj, apj);
-              const float p1 = ex2(fmaf(__uint_as_float(vs[j]), sc_l2, -m1));
-              const float z2 = fmaf(aL, p1, fmaf(bL, dpj, fmaf(gL, apj, -cL)));
-              float ev = ex2(z2);
+              float ev = ex2(fmaf(aL, p1[j], fmaf(bL, dpj, fmaf(gL, apj, -cL))));
               if constexpr (decltype(masked)::value) ev = (j < nvalid) ? ev : 0.f;
               l24[j & 3] += ev;
               v[j] = ev;
@@ -675,8 +679,11 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
           if (nvalid >= 32) body(std::false_type{});
           else body(std::true_type{});
           l2 += (l24[0] + l24[1]) + (l24[2] + l24[3]);
+          // the P buffer is free once the P.V two chunks back has run (waited here, after the math)
+          if (!(ok = warp_wait(&bar_pempty[ps], ((pc >> 1) & 1) ^ 1, ctx))) break;
           stage_row32<BF16>(preg, e.r, piece, v);
         }
+        if (!ok) break;
         fence_proxy_async_smem();
         mbar_arrive(&bar_pfull[ps]);
         ++sc;
@@ -986,19 +993,23 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         mbar_arrive(&bar_sempty[ss]);
         float pa[2][3] = {};  // two interleaved partial sums per quantity (shorter dependency chains)
         auto body = [&](auto masked) {
+          float p1[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            p1[j] = ex2(fmaf(__uint_as_float(vs[j]), sc_l2, -m1));
+            if constexpr (decltype(masked)::value) p1[j] = (j < nvalid) ? p1[j] : 0.f;
+          }
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             float dpj, apj;
             pr.get(j, dpj, apj);
-            float p1 = ex2(fmaf(__uint_as_float(vs[j]), sc_l2, -m1));
-            if constexpr (decltype(masked)::value) p1 = (j < nvalid) ? p1 : 0.f;
-            float p2 = ex2(fmaf(aL, p1, fmaf(bL, dpj, fmaf(gL, apj, -c2))));
+            float p2 = ex2(fmaf(aL, p1[j], fmaf(bL, dpj, fmaf(gL, apj, -c2))));
             if constexpr (decltype(masked)::value) p2 = (j < nvalid) ? p2 : 0.f;
             const float wv = p2 * __uint_as_float(ws[j]);
             float* q = pa[j & 1];
             q[0] += wv;
-            q[1] = fmaf(wv, p1, q[1]);
-            q[2] = fmaf(p2, p1, q[2]);
+            q[1] = fmaf(wv, p1[j], q[1]);
+            q[2] = fmaf(p2, p1[j], q[2]);
           }
         };
         if (nvalid >= 32) body(std::false_type{});
@@ -1037,7 +1048,6 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
     for (int c = 0; c < nchunks && ok; ++c) {
       const int ss = sc & 1, ds = dc % C::NDS, prs = pc % NPR;
       if (!(ok = warp_wait(&bar_sfull[ss], (sc >> 1) & 1, ctx))) break;
-      if (!(ok = warp_wait(&bar_dsempty[ds], ((dc / C::NDS) & 1) ^ 1, ctx))) break;
       if (!(ok = warp_wait(&bar_prfull[prs], (pc / NPR) & 1, ctx))) break;
       tc_fence_after();
       uint8_t* dreg = smem + C::OFF_DS + ds * C::DS_BYTES;
@@ -1057,24 +1067,31 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         mbar_arrive(&bar_prempty[prs]);
         mbar_arrive(&bar_sempty[ss]);
         auto body = [&](auto masked) {
+          float p1[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            p1[j] = ex2(fmaf(__uint_as_float(vs[j]), sc_l2, -m1));
+            if constexpr (decltype(masked)::value) p1[j] = (j < nvalid) ? p1[j] : 0.f;
+          }
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             float dpj, apj;
             pr.get(j, dpj, apj);
-            float p1 = ex2(fmaf(__uint_as_float(vs[j]), sc_l2, -m1));
-            if constexpr (decltype(masked)::value) p1 = (j < nvalid) ? p1 : 0.f;
-            float p2 = ex2(fmaf(aL, p1, fmaf(bL, dpj, fmaf(gL, apj, -c2))));
+            float p2 = ex2(fmaf(aL, p1[j], fmaf(bL, dpj, fmaf(gL, apj, -c2))));
             if constexpr (decltype(masked)::value) p2 = (j < nvalid) ? p2 : 0.f;
             const float dz = p2 * (__uint_as_float(ws[j]) - delta2);
-            v[j] = p1 * fmaf(ab.a, dz, -delta1);  // masked columns: p1 = 0 -> dS = 0
+            v[j] = p1[j] * fmaf(ab.a, dz, -delta1);  // masked columns: p1 = 0 -> dS = 0
             gbp[j & 1] = fmaf(dz, dpj, gbp[j & 1]);
             ggp[j & 1] = fmaf(dz, apj, ggp[j & 1]);
           }
         };
         if (nvalid >= 32) body(std::false_type{});
         else body(std::true_type{});
+        // the dS buffer is free once the dQ MMA that read it has run (waited here, after the math)
+        if (!(ok = warp_wait(&bar_dsempty[ds], ((dc / C::NDS) & 1) ^ 1, ctx))) break;
         stage_row32<BF16>(dreg, e.r, piece, v);
       }
+      if (!ok) break;
       fence_proxy_async_smem();
       mbar_arrive(&bar_dsfull[ds]);
       ++sc;
@@ -1347,7 +1364,6 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       const int qs = gc % NB, ts = gc % NST;
       if (!ok) continue;
       if (!(ok = warp_wait(&bar_sfull[qs], (gc / NB) & 1, ctx))) continue;
-      if (!(ok = warp_wait(&bar_tempty[ts], ((gc / NST) & 1) ^ 1, ctx))) continue;
       if constexpr (NPR > 0)
         if (!(ok = warp_wait(&bar_prfull[gc % NPR], (gc / NPR) & 1, ctx))) continue;
       // the chunk's row records (rows past N carry m1 = c2 = +inf: P1 = P2 = dS = 0 in their columns)
@@ -1393,9 +1409,12 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
             w[j] = p1 * fmaf(ab.a, dz, -e1[k]);
           }
         }
+        // the staging tiles are free once the previous chunk's dV/dK MMAs have run (waited here, after the math)
+        if (!(ok = warp_wait(&bar_tempty[ts], ((gc / NST) & 1) ^ 1, ctx))) break;
         stage_row32<BF16>(p2reg, e.r, piece, v);
         stage_row32<BF16>(dsreg, e.r, piece, w);
       }
+      if (!ok) continue;
       fence_proxy_async_smem();
       mbar_arrive(&bar_tfull[ts]);
     }
