@@ -32,6 +32,7 @@ sys.path.insert(0, REPO)
 METRIC = "geo-attn fwd+bwd TFLOPS & % tensor peak at 1/2/4/8 B200 vs eager; ms/step"
 UNIT = "TFLOP/s"
 B_TOTAL, H, N, D = 256, 16, 512, 128
+E2E_SLICES = 8   # issue-date slices of the end-to-end step (host copies of one overlap compute of the previous)
 
 
 def flops(b):
@@ -310,23 +311,17 @@ def main():
     # end to end through the public API: pinned host inputs copied in every step, bias gradients read back
     e2e = None
     if not args.no_e2e:
+        from foreswe_gpu_optimization_b200.streaming import HostBatchPipeline
         hq, hk, hv, hd = (t.pin_memory() for t in (qh, kh, vh, doh))
-        dq_, dk_, dv_, dd_ = (torch.empty_like(t) for t in (q, k, v, do))
         out = torch.empty(3 * H, dtype=torch.float32).pin_memory()
+        pipe = HostBatchPipeline(qh.shape, q.dtype, dev, slices=E2E_SLICES)
 
         def e2e_step():
-            for dst, src in ((dq_, hq), (dk_, hk), (dv_, hv), (dd_, hd)):
-                dst.copy_(src, non_blocking=True)
-            xs = [t.requires_grad_(True) for t in (dq_, dk_, dv_)]
             for t in params:
                 t.grad = None
-            o = g.geo_attention(xs[0], xs[1], xs[2], geom, *params)
-            o.backward(dd_)
+            pipe.step(hq, hk, hv, hd, geom, *params)   # copies of slice i+1 overlap fwd+bwd of slice i
             allreduce_bias_grads()
             out.copy_(torch.cat([p.grad for p in params]), non_blocking=True)
-            for t in xs:
-                t.grad = None
-                t.requires_grad_(False)
         for _ in range(args.warmup):
             e2e_step()
         torch.cuda.synchronize()
@@ -344,8 +339,10 @@ def main():
             tdist.all_reduce(tt, op=tdist.ReduceOp.MAX)
             ems = tt.item()
         e2e = {"value": flops(B_TOTAL) / (ems * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": ems,
-               "h2d_bytes_per_step": 4 * q.numel() * 2, "d2h_bytes_per_step": 3 * H * 4}
-        del hq, hk, hv, hd, dq_, dk_, dv_, dd_
+               "h2d_bytes_per_step": 4 * q.numel() * 2, "d2h_bytes_per_step": 3 * H * 4,
+               "pipeline": "HostBatchPipeline: %d slices of issue dates, pinned H2D copies overlapped with fwd+bwd"
+                           % E2E_SLICES}
+        del hq, hk, hv, hd, pipe
 
     eager = None
     if not args.no_eager and rank == 0:

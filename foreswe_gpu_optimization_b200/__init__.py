@@ -6,6 +6,7 @@ tcgen05/TMA kernels with fp32 accumulators in tensor memory, forward and backwar
 from .geo_attention_v2 import (CFG, PRESETS, FusedGeoAttentionV2, fused_geo_attention_v2, geo_attention,
                                patch_model, use_preset)
 from .geometry import StationGeometry, prior_from_dense
+from .streaming import HostBatchPipeline
 
 __all__ = ["CFG", "PRESETS", "FusedGeoAttentionV2", "fused_geo_attention_v2", "geo_attention", "patch_model",
-           "use_preset", "StationGeometry", "prior_from_dense"]
+           "use_preset", "StationGeometry", "prior_from_dense", "HostBatchPipeline"]
