@@ -277,7 +277,7 @@ def main():
         for e in evs:
             e.record()
         return evs
-    ev_sets = [(mk(2), mk(3)) for _ in range(args.steps)]
+    ev_sets = [(mk(2), mk(4)) for _ in range(args.steps)]
     torch.cuda.synchronize()
 
     clocks = ClockSampler(range(world) if world > 1 else [local])
@@ -300,7 +300,8 @@ def main():
     ms = t0.elapsed_time(t1) / args.steps
     kt = {"geoattn_fwd_kernel": statistics.mean(f[0].elapsed_time(f[1]) for f, _ in ev_sets),
           "geoattn_bwd_rows_kernel": statistics.mean(bw[0].elapsed_time(bw[1]) for _, bw in ev_sets),
-          "geoattn_bwd_cols_kernel": statistics.mean(bw[1].elapsed_time(bw[2]) for _, bw in ev_sets)}
+          "geoattn_bwd_cols_kernel": statistics.mean(bw[1].elapsed_time(bw[2]) for _, bw in ev_sets),
+          "geoattn_bwd_dq_kernel": statistics.mean(bw[2].elapsed_time(bw[3]) for _, bw in ev_sets)}
     if dist_on:
         tt = torch.tensor([ms] + list(kt.values()), device=dev, dtype=torch.float64)
         tdist.all_reduce(tt, op=tdist.ReduceOp.MAX)
@@ -362,7 +363,11 @@ def main():
 
     if rank == 0:
         dom = max(kt, key=kt.get)
-        per_launch = 4.0 * b * H * N * N * D        # each kernel carries one third of the algorithmic flops
+        # algorithmic flops per launch (recompute not counted): fwd QK^T + PV; row pass dP; key pass dV + dK; dQ GEMM
+        unit = 2.0 * b * H * N * N * D
+        kflops = {"geoattn_fwd_kernel": 2 * unit, "geoattn_bwd_rows_kernel": unit, "geoattn_bwd_cols_kernel": 2 * unit,
+                  "geoattn_bwd_dq_kernel": unit}
+        per_launch = kflops[dom]
         ach = per_launch / (kt[dom] * 1e-3) / 1e12
         pk, pk_src = peaks()
         roof = {"bound": "tensor", "kernel": dom, "achieved": ach, "peak": pk, "unit": "TFLOP/s", "frac": ach / pk,
@@ -372,7 +377,7 @@ def main():
                 "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
                 "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": config(world),
                 "tensor_peak_frac": value / world / pk, "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
-                "gpu_eager": eager, "gpu_launches": 4 * args.steps, "clocks": clk}
+                "gpu_eager": eager, "gpu_launches": 5 * args.steps, "clocks": clk}
         print(json.dumps(line), flush=True)
     if dist_on:
         tdist.barrier()

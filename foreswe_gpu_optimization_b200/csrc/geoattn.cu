@@ -256,8 +256,10 @@ struct BwdWs {
   float* rowrec;
   double* part;
   float *qn, *kn, *vn, *don, *kt, *qt, *dot;
+  void* dsT;  // bf16 dS^T scratch [B*H][N_pad keys][N_pad queries] (dS-scratch backward only)
 };
-size_t bwd_ws(const Dims& d, uint8_t* base, BwdWs* w) {
+// The BF16 backward with a caller-provided workspace keeps dS in a scratch (`with_ds`): key pass -> dQ GEMM.
+size_t bwd_ws(const Dims& d, uint8_t* base, BwdWs* w, bool with_ds) {
   size_t off = 0;
   auto take = [&](size_t bytes) -> uint8_t* {
     uint8_t* p = base ? base + off : nullptr;
@@ -278,8 +280,17 @@ size_t bwd_ws(const Dims& d, uint8_t* base, BwdWs* w) {
     t.qt = reinterpret_cast<float*>(take(trn));
     t.dot = reinterpret_cast<float*>(take(trn));
   }
+  if (with_ds && d.bf16) t.dsT = take((size_t)d.B * d.H * d.np * d.np * 2);
   if (w) *w = t;
   return off;
+}
+
+// TMA map over the bf16 dS^T scratch, viewed as 3-D (query, key, b*h); box: 64 queries x `keys` keys.
+int map_dsT(CUtensorMap* m, void* base, const Dims& d, int keys) {
+  const uint64_t dims[3] = {(uint64_t)d.np, (uint64_t)d.np, (uint64_t)d.B * d.H};
+  const uint64_t str[2] = {(uint64_t)d.np * 2, (uint64_t)d.np * d.np * 2};
+  const uint32_t box[3] = {64, (uint32_t)keys, 1};
+  return make_tmap(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, base, dims, str, box) ? GEOATTN_OK : GEOATTN_ERR_TMA;
 }
 
 // TMA map over a user bf16 tensor [B, H, N, D] (box: 64 x rows).
@@ -392,17 +403,38 @@ int run_fwd(const TileMaps& maps, const KParams& p, const Dims& d, cudaStream_t 
   record(ev, 1, st);
   return rc;
 }
+// Backward launches. Events (optional): before the row pass, between the row and key passes, after the key pass,
+// after the dQ GEMM (equal to the third when there is none).
 template <bool BF16, int DP>
 int run_bwd(const TileMaps& rmaps, const TileMaps& cmaps, const KParams& prow, const KParams& pcol, const Dims& d,
             cudaStream_t st, void* const* ev) {
   record(ev, 0, st);
-  int rc = launch(geoattn_bwd_rows_kernel<BF16, DP>, RowsCfg<BF16, DP>::SMEM, Tile<BF16, DP>::NTHREADS,
+  int rc = launch(geoattn_bwd_rows_kernel<BF16, DP, true>, RowsCfg<BF16, DP, true>::SMEM, Tile<BF16, DP>::NTHREADS,
                   persistent_grid(d), st, rmaps, prow);
   if (rc) return rc;
   record(ev, 1, st);
-  rc = launch(geoattn_bwd_cols_kernel<BF16, DP>, ColsCfg<BF16, DP>::SMEM, Tile<BF16, DP>::NTHREADS,
+  rc = launch(geoattn_bwd_cols_kernel<BF16, DP, false>, ColsCfg<BF16, DP>::SMEM, Tile<BF16, DP>::NTHREADS,
               persistent_grid(d), st, cmaps, pcol);
   record(ev, 2, st);
+  record(ev, 3, st);
+  return rc;
+}
+// BF16 with the dS scratch: row pass (one sweep: records, d(alpha)), key pass (dK, dV, dS^T, d(beta), d(gamma)),
+// dQ GEMM.
+template <int DP>
+int run_bwd_ds(const TileMaps& rmaps, const TileMaps& cmaps, const TileMaps& qmaps, const KParams& prow,
+               const KParams& pcol, const KParams& pdq, const Dims& d, cudaStream_t st, void* const* ev) {
+  record(ev, 0, st);
+  int rc = launch(geoattn_bwd_rows_kernel<true, DP, false>, RowsCfg<true, DP, false>::SMEM,
+                  Tile<true, DP>::NTHREADS, persistent_grid(d), st, rmaps, prow);
+  if (rc) return rc;
+  record(ev, 1, st);
+  rc = launch(geoattn_bwd_cols_kernel<true, DP, true>, ColsCfg<true, DP>::SMEM, Tile<true, DP>::NTHREADS,
+              persistent_grid(d), st, cmaps, pcol);
+  if (rc) return rc;
+  record(ev, 2, st);
+  rc = launch(geoattn_bwd_dq_kernel<DP>, DqCfg<DP>::SMEM, DqCfg<DP>::NTHREADS, persistent_grid(d), st, qmaps, pdq);
+  record(ev, 3, st);
   return rc;
 }
 
@@ -482,7 +514,7 @@ size_t geoattn_fwd_workspace_bytes(const GeoAttnShape* shape) {
 size_t geoattn_bwd_workspace_bytes(const GeoAttnShape* shape) {
   Dims d;
   if (check_shape(shape, d)) return 0;
-  return bwd_ws(d, nullptr, nullptr);
+  return bwd_ws(d, nullptr, nullptr, true);
 }
 
 int geoattn_fwd(const GeoAttnFwdArgs* a, void* stream) {
@@ -527,7 +559,13 @@ int geoattn_fwd(const GeoAttnFwdArgs* a, void* stream) {
   return run_fwd<false, 64>(maps, p, d, st, a->events);
 }
 
-int geoattn_bwd(const GeoAttnBwdArgs* a, void* stream) {
+}  // extern "C"
+
+namespace geoattn {
+namespace {
+// `with_ds`: the workspace holds the dS scratch (geoattn_bwd); without it (geoattn_bwd_noalloc, whose scratch is
+// small) the BF16 backward forms dQ in the row pass's second sweep, as the FP32 path always does.
+int backward(const GeoAttnBwdArgs* a, void* stream, bool with_ds) {
   if (!a) return GEOATTN_ERR_INVALID;
   Dims d;
   if (int rc = check_shape(&a->shape, d)) return rc;
@@ -538,7 +576,8 @@ int geoattn_bwd(const GeoAttnBwdArgs* a, void* stream) {
   if ((reinterpret_cast<uintptr_t>(a->workspace) & (kAlign - 1)) != 0) return GEOATTN_ERR_ALIGNMENT;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   BwdWs ws;
-  bwd_ws(d, reinterpret_cast<uint8_t*>(a->workspace), &ws);
+  with_ds = with_ds && d.bf16;
+  bwd_ws(d, reinterpret_cast<uint8_t*>(a->workspace), &ws, with_ds);
   if (cudaMemsetAsync(ws.status, 0, sizeof(int), st) != cudaSuccess) return GEOATTN_ERR_LAUNCH;
   TileMaps rm, cm;
   std::memset(&rm, 0, sizeof(rm));
@@ -584,7 +623,18 @@ int geoattn_bwd(const GeoAttnBwdArgs* a, void* stream) {
   prow.out_tma = map_output(&rm.out0, a->dq, a->dq_stride, d) ? 1 : 0;
   pcol.out_tma =
       (map_output(&cm.out0, a->dk, a->dk_stride, d) && map_output(&cm.out1, a->dv, a->dv_stride, d)) ? 1 : 0;
-  if (d.bf16) {
+  if (with_ds) {
+    TileMaps qm;
+    std::memset(&qm, 0, sizeof(qm));
+    if ((rc = map_dsT(&cm.dsT, ws.dsT, d, kBM)) || (rc = map_dsT(&qm.dsT, ws.dsT, d, 64)) ||
+        (rc = map_user_bf16(&qm.k, a->k, d, 64)))
+      return rc;
+    KParams pdq = prow;  // dQ output map and strides
+    qm.out0 = rm.out0;
+    if (d.DP == 64) rc = run_bwd_ds<64>(rm, cm, qm, prow, pcol, pdq, d, st, a->events);
+    else if (d.DP == 128) rc = run_bwd_ds<128>(rm, cm, qm, prow, pcol, pdq, d, st, a->events);
+    else rc = run_bwd_ds<192>(rm, cm, qm, prow, pcol, pdq, d, st, a->events);
+  } else if (d.bf16) {
     if (d.DP == 64) rc = run_bwd<true, 64>(rm, cm, prow, pcol, d, st, a->events);
     else if (d.DP == 128) rc = run_bwd<true, 128>(rm, cm, prow, pcol, d, st, a->events);
     else rc = run_bwd<true, 192>(rm, cm, prow, pcol, d, st, a->events);
@@ -595,6 +645,12 @@ int geoattn_bwd(const GeoAttnBwdArgs* a, void* stream) {
   finalize_abg_kernel<<<dim3(3, d.nabg), 256, 0, st>>>(ws.part, d.B, d.H, d.nrb, a->shape.per_head, a->dabg);
   return cudaGetLastError() == cudaSuccess ? GEOATTN_OK : GEOATTN_ERR_LAUNCH;
 }
+}  // namespace
+}  // namespace geoattn
+
+extern "C" {
+
+int geoattn_bwd(const GeoAttnBwdArgs* a, void* stream) { return backward(a, stream, true); }
 
 int geoattn_read_status(const void* workspace, int* status, void* stream) {
   if (!dev_ptr(workspace) || !status) return GEOATTN_ERR_INVALID;
@@ -651,10 +707,10 @@ extern "C" int geoattn_bwd_noalloc(const GeoAttnBwdArgs* a, void* stream) {
   Dims d;
   if (int rc = check_shape(&a->shape, d)) return rc;
   if (!d.bf16) return GEOATTN_ERR_UNSUPPORTED;  // the FP32 path's operand planes do not fit a modest static buffer
-  if (bwd_ws(d, nullptr, nullptr) > kNoAllocScratchBytes) return GEOATTN_ERR_SCRATCH;
+  if (bwd_ws(d, nullptr, nullptr, false) > kNoAllocScratchBytes) return GEOATTN_ERR_SCRATCH;
   void* scratch = nullptr;
   if (int rc = noalloc_scratch(&scratch)) return rc;
   GeoAttnBwdArgs b = *a;
   b.workspace = scratch;
-  return geoattn_bwd(&b, stream);
+  return backward(&b, stream, false);
 }

@@ -360,7 +360,8 @@ __device__ __forceinline__ void tma_prior(uint8_t* dst, const CUtensorMap* map, 
 
 struct TileMaps {
   CUtensorMap q, k, v, dout, kt, qt, dot, prior;  // unused entries are left zero
-  CUtensorMap out0, out1;                         // bf16 output stores: fwd O; rows dQ; cols dK, dV
+  CUtensorMap out0, out1;                         // bf16 output stores: fwd O; rows / dQ GEMM dQ; cols dK, dV
+  CUtensorMap dsT;                                // dS^T scratch [b*h][key][query]: cols stores, dQ GEMM loads
 };
 
 // L2 prefetch of a row block of a natural operand (boxes of `rows` rows, all NKB regions and planes).
@@ -740,10 +741,12 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
 // Sweep 1 recomputes S, dP = dO V^T, P1, P2 and accumulates, per row,
 //   delta2 = sum P2 dP,  a = sum P2 dP P1,  b = sum P2 P1,
 //   so that with dZ = P2 (dP - delta2): sum dZ P1 = a - delta2 b = d(alpha) of the row, delta1 = alpha (a - delta2 b).
-// Sweep 2 recomputes the tiles again, forms dZ, dS = P1 (alpha dZ - delta1), accumulates dQ += dS K and the row's
-// d(beta) = sum dZ Dp, d(gamma) = sum dZ Ap. The row records (m1, c2, delta1, delta2) go to the key pass.
+// With DQ, sweep 2 recomputes the tiles again, forms dZ, dS = P1 (alpha dZ - delta1), accumulates dQ += dS K and
+// the row's d(beta) = sum dZ Dp, d(gamma) = sum dZ Ap. Without DQ (bf16 with a dS scratch), the kernel stops after
+// sweep 1: the key pass stores dS and the bias gradients of beta and gamma, and a GEMM forms dQ.
+// The row records (m1, c2, delta1, delta2) go to the key pass.
 // ===============================================================================================================
-template <bool BF16, int DP>
+template <bool BF16, int DP, bool DQ = true>
 struct RowsCfg : Tile<BF16, DP> {
   using T = Tile<BF16, DP>;
   static constexpr int NKV = (!BF16 || DP > 128) ? 1 : 2;  // K/V chunk buffers
@@ -752,21 +755,23 @@ struct RowsCfg : Tile<BF16, DP> {
   static constexpr int K_BYTES = T::CH * DP * T::EB;  // per plane per buffer (K and V chunks)
   static constexpr int KT_BYTES = BF16 ? 0 : DP * 128;  // fp32: transposed K chunk (hi) for dQ
   static constexpr int DS_BYTES = kBM * 128;
-  static constexpr int NDS = BF16 ? 2 : 1;            // dS / K^T buffers
+  static constexpr int NDS = BF16 ? 2 : 1;            // dS / K^T buffers (ring size)
+  static constexpr int NDS_ALLOC = DQ ? NDS : 0;      // allocated only with DQ
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_DO = OFF_Q + T::PL * Q_BYTES;
   static constexpr int OFF_K = OFF_DO + T::PL * Q_BYTES;
   static constexpr int OFF_V = OFF_K + NKV * T::PL * K_BYTES;
   static constexpr int OFF_KT = OFF_V + NKV * T::PL * K_BYTES;
-  static constexpr int OFF_DS = OFF_KT + NDS * KT_BYTES;
-  static constexpr int OFF_PR = OFF_DS + NDS * DS_BYTES;
-  static constexpr int SMEM = OFF_PR + NPR * kPriorTileBytes + 1024;
+  static constexpr int OFF_DS = OFF_KT + NDS_ALLOC * KT_BYTES;
+  static constexpr int OFF_PR = OFF_DS + NDS_ALLOC * DS_BYTES;
+  static constexpr int OFF_XS = OFF_PR + NPR * kPriorTileBytes;  // without DQ: the warpgroups' row-sum exchange
+  static constexpr int SMEM = OFF_XS + (DQ ? 0 : 6 * kBM * 4) + 1024;
   static constexpr int TM_S = 0;                   // 2 buffers
   static constexpr int TM_DP = 2 * T::CH;          // 2 buffers
   static constexpr int TM_DQ = 4 * T::CH;
-  static constexpr int TMEM_COLS = pow2_cols(4 * T::CH + DP);
+  static constexpr int TMEM_COLS = pow2_cols(4 * T::CH + (DQ ? DP : 0));
   // dQ leaves through the dS buffers (free once the tile's last dQ MMA has run) when they hold the whole row block
-  static constexpr bool EPI_TMA = BF16 && T::NKB * kBM * 128 <= NDS * DS_BYTES;
+  static constexpr bool EPI_TMA = DQ && BF16 && T::NKB * kBM * 128 <= NDS * DS_BYTES;
 };
 
 // Row record of `row` (chunk-blocked so that the key pass can fetch one query chunk's records in one bulk copy).
@@ -775,10 +780,11 @@ __device__ __forceinline__ float* rec_ptr(const KParams& p, int bh, int row) {
   return p.rowrec + ((size_t)bh * p.nchp + row / T::CH) * 4 * T::CH + row % T::CH;
 }
 
-template <bool BF16, int DP>
+template <bool BF16, int DP, bool DQ>
 __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
     geoattn_bwd_rows_kernel(const __grid_constant__ TileMaps maps, const KParams p) {
-  using C = RowsCfg<BF16, DP>;
+  static_assert(DQ || BF16, "the dS-scratch backward is bf16 only");
+  using C = RowsCfg<BF16, DP, DQ>;
   using T = typename C::T;
   constexpr int NKV = C::NKV, NPR = C::NPR;
   extern __shared__ uint8_t smem_raw[];
@@ -792,7 +798,8 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
   const int nchunks = (p.N + T::CH - 1) / T::CH;
   const int ntiles = p.nrb * p.B * p.H;  // tile = (128-query row block, b*h); persistent CTAs stride over tiles
   WaitCtx ctx{&abort_flag, p.status};
-  const bool epi_tma = C::EPI_TMA && p.out_tma;
+  const bool epi_tma = DQ && C::EPI_TMA && p.out_tma;
+  constexpr int SWEEPS = DQ ? 2 : 1;
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
@@ -840,8 +847,8 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       mbar_arrive_expect_tx(&bar_qfull, 2 * T::PL * C::Q_BYTES);
       tma_tile<T>(smem + C::OFF_Q, &maps.q, &bar_qfull, kBM, rb * kBM, h, b, p.B, T::PL);
       tma_tile<T>(smem + C::OFF_DO, &maps.dout, &bar_qfull, kBM, rb * kBM, h, b, p.B, T::PL);
-      for (int sweep = 0; sweep < 2 && ok; ++sweep) {
-        if (sweep == 1 && tile + (int)gridDim.x < ntiles) {  // next tile's operands into L2
+      for (int sweep = 0; sweep < SWEEPS && ok; ++sweep) {
+        if (sweep == SWEEPS - 1 && tile + (int)gridDim.x < ntiles) {  // next tile's operands into L2
           const int nt = tile + gridDim.x, nbh = nt / p.nrb, nb = nbh / p.H, nh = nbh % p.H, nrow = (nt % p.nrb) * kBM;
           prefetch_tile<T>(&maps.q, nrow, nh, nb, p.B, T::PL);
           prefetch_tile<T>(&maps.dout, nrow, nh, nb, p.B, T::PL);
@@ -879,7 +886,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
     for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
       const int rb = tile % p.nrb;
       if (lane == 0) {
-        for (int sweep = 0; sweep < 2 && ok; ++sweep) {
+        for (int sweep = 0; sweep < SWEEPS && ok; ++sweep) {
           for (int c = 0; c < nchunks && ok; ++c) {
             const int ps = pc % NPR;
             if (!(ok = mbar_wait(&bar_prempty[ps], ((pc / NPR) & 1) ^ 1, ctx))) break;
@@ -934,6 +941,10 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++it) {
         if (!(ok = mbar_wait(&bar_qfull, it & 1, ctx))) break;
         for (int c = 0; c < nchunks && ok; ++c) ok = issue(true);
+        if constexpr (!DQ) {
+          if (ok) mma_commit(&bar_qempty);  // every S/dP MMA of this tile has been issued
+          continue;
+        }
         const int kc0 = kc;  // first K use of sweep 2
         if (ok) ok = issue(false);
         if (ok && nchunks == 1) mma_commit(&bar_qempty);  // every S/dP MMA of this tile has been issued
@@ -1021,11 +1032,11 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       ++pc;
     }
     if constexpr (T::EW == 2) {
-      // combine the two warpgroups' row sums through the dS buffers (unused until sweep 2), warpgroup 0's first,
-      // once the previous tile's dQ store has finished reading them
+      // combine the two warpgroups' row sums, warpgroup 0's first: through the dS buffers (unused until sweep 2) once
+      // the previous tile's dQ store has finished reading them, or (without DQ) through a small exchange region
       if (epi_tma && threadIdx.x == 0) bulk_wait_read0();
       ew_sync(T::EWT);
-      float* xs = reinterpret_cast<float*>(smem + C::OFF_DS);
+      float* xs = reinterpret_cast<float*>(smem + (DQ ? C::OFF_DS : C::OFF_XS));
 #pragma unroll
       for (int k = 0; k < 3; ++k) xs[(e.wg * 3 + k) * kBM + e.r] = acc[k];
       ew_sync(T::EWT);
@@ -1045,6 +1056,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
     }
     // Sweep 2
     float gbp[2] = {0.f, 0.f}, ggp[2] = {0.f, 0.f};  // d(beta), d(gamma) partials of the row
+    if constexpr (DQ) {
     for (int c = 0; c < nchunks && ok; ++c) {
       const int ss = sc & 1, ds = dc % C::NDS, prs = pc % NPR;
       if (!(ok = warp_wait(&bar_sfull[ss], (sc >> 1) & 1, ctx))) break;
@@ -1098,7 +1110,9 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       ++dc;
       ++pc;
     }
-    // block partials of d(alpha) (one per row: warpgroup 0), d(beta), d(gamma) (every warpgroup's columns)
+    }
+    // block partials of d(alpha) (one per row: warpgroup 0), d(beta), d(gamma) (every warpgroup's columns; without
+    // DQ the key pass writes those two)
     {
       double ga = (valid && e.wg == 0) ? (double)ta : 0.0, gb = valid ? (double)(gbp[0] + gbp[1]) : 0.0,
              gg = valid ? (double)(ggp[0] + ggp[1]) : 0.0;
@@ -1120,13 +1134,16 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
           for (int k = 0; k < 3; ++k) s3[k] += red[w][k];
         double* out = p.part + ((size_t)bh * p.nrb + rb) * 3;
         out[0] = s3[0];
-        out[1] = s3[1];
-        out[2] = s3[2];
+        if constexpr (DQ) {
+          out[1] = s3[1];
+          out[2] = s3[2];
+        }
       }
     }
-    if (ok) ok = warp_wait(&bar_dqfull, it & 1, ctx);
+    if (DQ && ok) ok = warp_wait(&bar_dqfull, it & 1, ctx);
     tc_fence_after();
-    if (epi_tma) {
+    if constexpr (!DQ) {
+    } else if (epi_tma) {
       // every dQ MMA of the tile has completed (dqfull), so the dS buffers hold the staged dQ tile
       if (ok) {
 #pragma unroll 1
@@ -1158,7 +1175,9 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
 // ===============================================================================================================
 // Backward key pass: one CTA per (128-key block, b*h); keys on TMEM lanes. For each chunk of CH queries:
 //   S^T = K Q^T, dP^T = V dO^T; P1, P2, dZ, dS from the row records; dV += P2^T dO, dK += dS^T Q.
-// The chunk's row records arrive by bulk copy together with its Q / dO tiles.
+// The chunk's row records arrive by bulk copy together with its Q / dO tiles. With SDS (bf16 with a dS scratch) the
+// TMA warp also stores each staged dS^T tile to the scratch (for the dQ GEMM) and the element-wise warps accumulate
+// the key block's d(beta) = sum dZ Dp and d(gamma) = sum dZ Ap.
 // ===============================================================================================================
 template <bool BF16, int DP>
 struct ColsCfg : Tile<BF16, DP> {
@@ -1191,9 +1210,10 @@ struct ColsCfg : Tile<BF16, DP> {
   static constexpr bool EPI_TMA = BF16 && T::NKB * kBM * 128 <= 2 * NST * ST_BYTES;
 };
 
-template <bool BF16, int DP>
+template <bool BF16, int DP, bool SDS>
 __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
     geoattn_bwd_cols_kernel(const __grid_constant__ TileMaps maps, const KParams p) {
+  static_assert(!SDS || BF16, "the dS-scratch backward is bf16 only");
   using C = ColsCfg<BF16, DP>;
   using T = typename C::T;
   constexpr int NB = C::NB, NST = C::NST, NPR = C::NPR;
@@ -1203,6 +1223,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       bar_prfull[2], bar_prempty[2], bar_done;
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_flag;
+  __shared__ double redc[8][2];
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int nchunks = (p.N + T::CH - 1) / T::CH;
   const int ntiles = p.nrb * p.B * p.H;  // tile = (128-key block, b*h); persistent CTAs stride over tiles
@@ -1219,7 +1240,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       mbar_init(&bar_sfull[i], 1);
       mbar_init(&bar_sempty[i], T::EWT);
       mbar_init(&bar_tfull[i], T::EWT);
-      mbar_init(&bar_tempty[i], 1);
+      mbar_init(&bar_tempty[i], SDS ? 2 : 1);  // the MMAs that read the tile (and, with SDS, its store)
       mbar_init(&bar_prfull[i], 1);
       mbar_init(&bar_prempty[i], T::EWT);
     }
@@ -1246,6 +1267,17 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       int it = 0;
       for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++it) {
       const int kblk = tile % p.nrb, bh = tile / p.nrb, b = bh / p.H, h = bh % p.H;
+      // dS^T tile of chunk c (use g of its staging slot) to the scratch once the element-wise warps staged it; the
+      // slot is handed back (second arrival on its empty barrier) once the store has read it
+      auto store_ds = [&](int g, int c) -> bool {
+        const int ts = g % NST;
+        if (!mbar_wait(&bar_tfull[ts], (g / NST) & 1, ctx)) return false;
+        tma_store_3d(&maps.dsT, smem + C::OFF_DS + ts * C::ST_BYTES, c * T::CH, kblk * kBM, bh);
+        bulk_commit();
+        bulk_wait_read0();
+        mbar_arrive(&bar_tempty[ts]);
+        return true;
+      };
       // K and V blocks of this tile once the previous tile's last S^T/dP^T MMAs have read the old ones
       if (!(ok = mbar_wait(&bar_kvempty, (it & 1) ^ 1, ctx))) break;
       mbar_arrive_expect_tx(&bar_kvfull, 2 * T::PL * C::K_BYTES);
@@ -1271,7 +1303,11 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         }
         bulk_load(smem + C::OFF_REC + qs * C::REC_BYTES, p.rowrec + ((size_t)bh * p.nchp + c) * 4 * T::CH,
                   C::REC_BYTES, &bar_qfull[qs]);
+        if constexpr (SDS)
+          if (c > 0 && !(ok = store_ds(gc - 1, c - 1))) break;
       }
+      if constexpr (SDS)
+        if (ok) ok = store_ds(it * nchunks + nchunks - 1, nchunks - 1);
       }
     }
   } else if (warp == T::PR_WARP) {
@@ -1359,6 +1395,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       if (threadIdx.x == 0) bulk_wait_read0();
       ew_sync(T::EWT);
     }
+    float gbp[2] = {0.f, 0.f}, ggp[2] = {0.f, 0.f};  // with SDS: this key's d(beta), d(gamma) partials
     for (int c = 0; c < nchunks; ++c) {
       const int gc = it * nchunks + c;
       const int qs = gc % NB, ts = gc % NST;
@@ -1407,6 +1444,10 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
             const float dz = p2 * (__uint_as_float(ws[j]) - e2[k]);
             v[j] = p2;
             w[j] = p1 * fmaf(ab.a, dz, -e1[k]);
+            if constexpr (SDS) {
+              gbp[k & 1] = fmaf(dz, dpj, gbp[k & 1]);
+              ggp[k & 1] = fmaf(dz, apj, ggp[k & 1]);
+            }
           }
         }
         // the staging tiles are free once the previous chunk's dV/dK MMAs have run (waited here, after the math)
@@ -1418,7 +1459,37 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       fence_proxy_async_smem();
       mbar_arrive(&bar_tfull[ts]);
     }
+    if constexpr (SDS) {  // block partials of d(beta), d(gamma) (keys past N excluded)
+      double gb = kvalid ? (double)(gbp[0] + gbp[1]) : 0.0, gg = kvalid ? (double)(ggp[0] + ggp[1]) : 0.0;
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) {
+        gb += __shfl_down_sync(0xffffffffu, gb, off);
+        gg += __shfl_down_sync(0xffffffffu, gg, off);
+      }
+      if (lane == 0) {
+        redc[warp][0] = gb;
+        redc[warp][1] = gg;
+      }
+      ew_sync(T::EWT);
+      if (threadIdx.x == 0) {
+        double s2[2] = {0.0, 0.0};
+        for (int w = 0; w < 4 * T::EW; ++w) {
+          s2[0] += redc[w][0];
+          s2[1] += redc[w][1];
+        }
+        double* out = p.part + ((size_t)bh * p.nrb + kblk) * 3;
+        out[1] = s2[0];
+        out[2] = s2[1];
+      }
+    }
     if (ok) ok = warp_wait(&bar_done, it & 1, ctx);
+    // with SDS the staging tiles are also read by the dS stores: wait for the last ones before the epilogue
+    if constexpr (SDS) {
+      for (int k = 0; k < NST && k < nchunks && ok; ++k) {
+        const int g = it * nchunks + nchunks - 1 - k;
+        ok = warp_wait(&bar_tempty[g % NST], (g / NST) & 1, ctx);
+      }
+    }
     tc_fence_after();
     if (epi_tma) {
       // every MMA of the tile has completed (done): the P2^T / dS^T buffers take dK, then dV
@@ -1458,6 +1529,166 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
     tc_fence_before();  // the dK/dV reads above precede this warp's next hand-offs to the MMA warp
     }
     if (epi_tma && threadIdx.x == 0) bulk_wait_read0();  // shared memory outlives the last store's reads
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, C::TMEM_COLS);
+}
+
+// ===============================================================================================================
+// dQ = dS K / sqrt(d) (bf16), from the dS^T tiles [b*h][key][query] the key pass stored. One CTA per (128-query
+// block, b*h), persistent; it loops over 64-key chunks: acc[128 x DP] += dS[128 x 64] . K[64 x DP], dS read as an
+// MN-major A operand (queries contiguous) and K as an MN-major B operand (head dim contiguous), the accumulator
+// double-buffered in tensor memory so that one tile's epilogue overlaps the next tile's MMAs.
+// Warps: 4 epilogue warps (thread = TMEM lane = query row), 1 TMA warp, 1 MMA warp.
+// ===============================================================================================================
+template <int DP>
+struct DqCfg {
+  using T = Tile<true, DP>;
+  static constexpr int NSTAGE = 4;
+  static constexpr int A_BYTES = 2 * 64 * 128;            // dS: two 64-query halves x 64 keys x 128 B
+  static constexpr int B_BYTES = T::NKB * 64 * 128;       // K chunk: NKB regions of 64 keys x 128 B
+  static constexpr int STAGE = A_BYTES + B_BYTES;
+  static constexpr int OFF_OUT = NSTAGE * STAGE;          // epilogue staging: NKB regions of 128 rows x 128 B
+  static constexpr int SMEM = OFF_OUT + T::NKB * kBM * 128 + 1024;
+  static constexpr int TMEM_COLS = pow2_cols(2 * DP);
+  static constexpr int NTHREADS = 128 + 64;
+  static constexpr int TMA_WARP = 4, MMA_WARP = 5;
+};
+
+template <int DP>
+__device__ __forceinline__ void mma_dq(uint32_t tmem_acc, uint32_t a_base, uint32_t b_base, bool accumulate) {
+  constexpr uint32_t idesc = instr_desc(1, 1, 1, 128, DP);  // bf16, A and B MN-major
+#pragma unroll
+  for (int s = 0; s < 4; ++s) {                            // K = 16 keys per MMA
+    const uint64_t ad = smem_desc_sw128(a_base + s * 16 * 128, 64 * 128, 1024);
+    const uint64_t bd = smem_desc_sw128(b_base + s * 16 * 128, 64 * 128, 1024);
+    mma_ss<Kind::kF16>(tmem_acc, ad, bd, idesc, (accumulate || s > 0) ? 1u : 0u);
+  }
+}
+
+template <int DP>
+__global__ void __launch_bounds__(DqCfg<DP>::NTHREADS, 1)
+    geoattn_bwd_dq_kernel(const __grid_constant__ TileMaps maps, const KParams p) {
+  using C = DqCfg<DP>;
+  using T = typename C::T;
+  constexpr int NS = C::NSTAGE;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ uint64_t bar_full[NS], bar_empty[NS], bar_accfull[2], bar_accempty[2];
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ int abort_flag;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int nchunks = (p.N + 63) / 64;  // key chunks (keys past N meet zero-filled K rows)
+  const int ntiles = p.nrb * p.B * p.H;
+  WaitCtx ctx{&abort_flag, p.status};
+  const bool epi_tma = p.out_tma != 0;
+
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&bar_full[i], 1);
+      mbar_init(&bar_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bar_accfull[i], 1);
+      mbar_init(&bar_accempty[i], 128);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(&tmem_base_sh, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base_sh;
+  const uint32_t sbase = smem_u32(smem);
+
+  if (warp == C::TMA_WARP) {
+    if (lane == 0) {
+      prefetch_tmap(&maps.dsT);
+      prefetch_tmap(&maps.k);
+      int sc = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+        const int rb = tile % p.nrb, bh = tile / p.nrb, b = bh / p.H, h = bh % p.H;
+        for (int c = 0; c < nchunks && ok; ++c, ++sc) {
+          const int st = sc % NS;
+          if (!(ok = mbar_wait(&bar_empty[st], ((sc / NS) & 1) ^ 1, ctx))) break;
+          uint8_t* dst = smem + st * C::STAGE;
+          mbar_arrive_expect_tx(&bar_full[st], C::STAGE);
+          tma_load_3d(dst, &maps.dsT, &bar_full[st], rb * kBM, c * 64, bh);
+          tma_load_3d(dst + 64 * 128, &maps.dsT, &bar_full[st], rb * kBM + 64, c * 64, bh);
+          tma_tile<T>(dst + C::A_BYTES, &maps.k, &bar_full[st], 64, c * 64, h, b, p.B, 1);
+        }
+      }
+    }
+  } else if (warp == C::MMA_WARP) {
+    if (lane == 0) {
+      int sc = 0, it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++it) {
+        const int ab = it & 1;
+        if (!(ok = mbar_wait(&bar_accempty[ab], ((it >> 1) & 1) ^ 1, ctx))) break;
+        tc_fence_after();
+        for (int c = 0; c < nchunks && ok; ++c, ++sc) {
+          const int st = sc % NS;
+          if (!(ok = mbar_wait(&bar_full[st], (sc / NS) & 1, ctx))) break;
+          tc_fence_after();
+          mma_dq<DP>(tmem + ab * DP, sbase + st * C::STAGE, sbase + st * C::STAGE + C::A_BYTES, c > 0);
+          mma_commit(&bar_empty[st]);
+        }
+        if (ok) mma_commit(&bar_accfull[ab]);
+      }
+    }
+  } else {
+    // ---------------- epilogue warps ----------------
+    const int r = (warp & 3) * 32 + lane;
+    const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+    int it = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++it) {
+      const int rb = tile % p.nrb, bh = tile / p.nrb, b = bh / p.H, h = bh % p.H;
+      const int row = rb * kBM + r, ab = it & 1;
+      if (ok) ok = warp_wait(&bar_accfull[ab], (it >> 1) & 1, ctx);
+      tc_fence_after();
+      if (epi_tma) {
+        if (threadIdx.x == 0) bulk_wait_read0();  // the previous tile's store has read the staging tile
+        ew_sync(128);
+        if (ok) {
+#pragma unroll 1
+          for (int d0 = 0; d0 < DP; d0 += 32) {
+            float v[32];
+            tmem_ld32(lane_base + ab * DP + d0, v);
+            stage_out32(smem + C::OFF_OUT, r, d0, v, p.inv_sqrt_d);
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&bar_accempty[ab]);
+        fence_proxy_async_smem();
+        ew_sync(128);
+        if (threadIdx.x == 0 && ok) {
+          for (int kb = 0; kb < T::NKB && kb * 64 < p.D; ++kb)
+            tma_store_4d(&maps.out0, smem + C::OFF_OUT + kb * (kBM * 128), kb * 64, rb * kBM, h, b);
+          bulk_commit();
+        }
+      } else {
+        const long long qoff = (long long)b * p.dq_str[0] + (long long)h * p.dq_str[1] + (long long)row * p.dq_str[2];
+        if (ok) {
+#pragma unroll 1
+          for (int d0 = 0; d0 < DP; d0 += 32) {
+            float v[32];
+            tmem_ld32(lane_base + ab * DP + d0, v);
+            if (row < p.N && d0 < p.D) store_row32<true>(p.dq, qoff, p.dq_str[3], d0, p.D, v, p.inv_sqrt_d);
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&bar_accempty[ab]);
+      }
+    }
+    if (epi_tma && threadIdx.x == 0) bulk_wait_read0();
   }
   tc_fence_before();
   __syncthreads();

@@ -24,7 +24,7 @@ from . import _lib
 from .geometry import StationGeometry, prior_from_dense
 
 # Optional per-kernel timing hook: lists of torch.cuda.Event (already recorded once, so their handles exist) that
-# the library records around its kernels on the launching stream -- {"fwd": [2 events], "bwd": [3 events]}.
+# the library records around its kernels on the launching stream -- {"fwd": [2 events], "bwd": [4 events]}.
 TIMING_EVENTS = {"fwd": None, "bwd": None}
 
 PRESETS = {"accurate_experimental": dict(precision="auto"), "accurate_x3_experimental": dict(precision="auto"),

@@ -24,7 +24,7 @@
 extern "C" {
 #endif
 
-#define GEOATTN_VERSION 1
+#define GEOATTN_VERSION 2
 
 enum {
   GEOATTN_OK = 0,
@@ -111,12 +111,15 @@ typedef struct {
   long long dv_stride[4];
   float* dabg;        /* fp32 [3 * nabg]: d alpha..., d beta..., d gamma... (summed over batch, rows) */
   void* workspace;    /* geoattn_bwd_workspace_bytes, 256-byte aligned */
-  void* const* events; /* optional (NULL = none): 3 cudaEvent_t recorded on `stream` before the row-pass kernel,
-                          between the row-pass and key-pass kernels, and after the key-pass kernel */
+  void* const* events; /* optional (NULL = none): 4 cudaEvent_t recorded on `stream` before the row-pass kernel,
+                          between the row-pass and key-pass kernels, after the key-pass kernel and after the dQ
+                          GEMM (the last two coincide when dQ comes from the row pass) */
 } GeoAttnBwdArgs;
 
 /* dQ, dK, dV and the bias-parameter gradients; replaces FusedGeoAttentionV2.backward
- * (geo_attention_v2.py:428-461). Deterministic: no atomics, fixed reduction order. */
+ * (geo_attention_v2.py:428-461). Deterministic: no atomics, fixed reduction order. BF16: the workspace holds a
+ * bf16 dS scratch of B*H*N_pad^2 elements (N_pad = N rounded up to 128), which the key pass writes and a dQ GEMM
+ * reads; FP32: dQ comes from a second sweep of the row pass. */
 int geoattn_bwd(const GeoAttnBwdArgs* args, void* stream);
 
 /* Allocation-free backward (no counterpart in the reference, which always allocates through PyTorch).

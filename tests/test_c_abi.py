@@ -31,7 +31,7 @@ def test_every_declared_symbol_is_exported(L):
 
 
 def test_version_and_error_strings(L):
-    assert L.geoattn_version() == 1
+    assert L.geoattn_version() == 2
     for code in range(7):
         assert L.geoattn_error_string(code)
     assert b"unknown" in L.geoattn_error_string(99)
