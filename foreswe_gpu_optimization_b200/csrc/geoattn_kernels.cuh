@@ -27,6 +27,18 @@
 namespace geoattn {
 
 constexpr int kBM = 128;        // rows per tile (TMEM lanes)
+
+// Dynamic shared memory of every attention kernel. The 1024-byte alignment (what the 128-byte-swizzled TMA and MMA
+// tiles need) is part of the declaration: the compiler pads the static shared data in front of it to a multiple of
+// 1024 bytes, so no slack is allocated for aligning by hand. A kernel that finds it misaligned anyway reports an
+// error instead of running (smem_misaligned).
+extern __shared__ __align__(1024) uint8_t smem_raw[];
+
+__device__ __forceinline__ bool smem_misaligned(int* status) {
+  if ((smem_u32(smem_raw) & 1023u) == 0) return false;
+  if (threadIdx.x == 0 && status) atomicCAS(status, kDevOk, kDevSmemMisaligned);
+  return true;
+}
 constexpr float kLog2e = 1.4426950408889634f;
 
 __host__ __device__ constexpr int pow2_cols(int n) { return n <= 32 ? 32 : n <= 64 ? 64 : n <= 128 ? 128 : n <= 256 ? 256 : 512; }
@@ -426,7 +438,7 @@ struct FwdCfg : Tile<BF16, DP> {
   static constexpr int OFF_V = OFF_K + NK * T::PL * K_BYTES;
   static constexpr int OFF_P = OFF_V + 2 * V_BYTES;
   static constexpr int OFF_PR = OFF_P + 2 * P_BYTES;
-  static constexpr int SMEM = OFF_PR + NPR * kPriorTileBytes + 1024;
+  static constexpr int SMEM = OFF_PR + NPR * kPriorTileBytes;
   static constexpr int TM_S = 0;
   static constexpr int TM_O = 2 * T::CH;
   static constexpr int TMEM_COLS = pow2_cols(2 * T::CH + DP);
@@ -441,8 +453,8 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
   using T = typename C::T;
   constexpr int NPR = C::NPR, NK = C::NK;
   static_assert(!C::EPI_TMA || T::EW > 1, "the TMA epilogue relies on the warpgroup exchange barrier");
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  if (smem_misaligned(p.status)) return;  // uniform over the CTA, before any barrier or allocation
+  uint8_t* smem = smem_raw;
   __shared__ uint64_t bar_qfull, bar_qempty, bar_kfull[3], bar_kempty[3], bar_vfull[2], bar_vempty[2], bar_sfull[2],
       bar_sempty[2], bar_pfull[2], bar_pempty[2], bar_prfull[2], bar_prempty[2], bar_ofull;
   __shared__ uint32_t tmem_base_sh;
@@ -765,7 +777,7 @@ struct RowsCfg : Tile<BF16, DP> {
   static constexpr int OFF_DS = OFF_KT + NDS_ALLOC * KT_BYTES;
   static constexpr int OFF_PR = OFF_DS + NDS_ALLOC * DS_BYTES;
   static constexpr int OFF_XS = OFF_PR + NPR * kPriorTileBytes;  // without DQ: the warpgroups' row-sum exchange
-  static constexpr int SMEM = OFF_XS + (DQ ? 0 : 6 * kBM * 4) + 1024;
+  static constexpr int SMEM = OFF_XS + (DQ ? 0 : 6 * kBM * 4);
   static constexpr int TM_S = 0;                   // 2 buffers
   static constexpr int TM_DP = 2 * T::CH;          // 2 buffers
   static constexpr int TM_DQ = 4 * T::CH;
@@ -787,8 +799,8 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
   using C = RowsCfg<BF16, DP, DQ>;
   using T = typename C::T;
   constexpr int NKV = C::NKV, NPR = C::NPR;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  if (smem_misaligned(p.status)) return;  // uniform over the CTA, before any barrier or allocation
+  uint8_t* smem = smem_raw;
   __shared__ uint64_t bar_qfull, bar_qempty, bar_kfull[2], bar_kempty[2], bar_vfull[2], bar_vempty[2], bar_sfull[2], bar_sempty[2],
       bar_dsfull[2], bar_dsempty[2], bar_ktfull[2], bar_ktempty[2], bar_prfull[2], bar_prempty[2], bar_dqfull;
   __shared__ uint32_t tmem_base_sh;
@@ -1183,7 +1195,7 @@ template <bool BF16, int DP>
 struct ColsCfg : Tile<BF16, DP> {
   using T = Tile<BF16, DP>;
   static constexpr int NB = (BF16 && DP <= 128) ? 2 : 1;   // buffers for query chunks and S^T / dP^T
-  static constexpr int NST = (BF16 && DP <= 64) ? 2 : 1;   // buffers for the staged P2^T / dS^T tiles
+  static constexpr int NST = (BF16 && DP <= 128) ? 2 : 1;  // buffers for the staged P2^T / dS^T tiles
   static constexpr int NPR = !BF16 ? 0 : (DP <= 64 ? 2 : 1);  // staged prior buffers (0: read from L2)
   static constexpr int K_BYTES = kBM * DP * T::EB;          // per plane (K and V blocks)
   static constexpr int Q_BYTES = T::CH * DP * T::EB;        // per plane per buffer (Q and dO chunks)
@@ -1200,7 +1212,7 @@ struct ColsCfg : Tile<BF16, DP> {
   static constexpr int OFF_DS = OFF_P2 + NST * ST_BYTES;
   static constexpr int OFF_PR = OFF_DS + NST * ST_BYTES;
   static constexpr int OFF_REC = OFF_PR + NPR * kPriorTileBytes;
-  static constexpr int SMEM = OFF_REC + NB * REC_BYTES + 1024;
+  static constexpr int SMEM = OFF_REC + NB * REC_BYTES;
   static constexpr int TM_S = 0;
   static constexpr int TM_DP = NB * T::CH;
   static constexpr int TM_DK = 2 * NB * T::CH;
@@ -1217,8 +1229,8 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
   using C = ColsCfg<BF16, DP>;
   using T = typename C::T;
   constexpr int NB = C::NB, NST = C::NST, NPR = C::NPR;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  if (smem_misaligned(p.status)) return;  // uniform over the CTA, before any barrier or allocation
+  uint8_t* smem = smem_raw;
   __shared__ uint64_t bar_kvfull, bar_kvempty, bar_qfull[2], bar_qempty[2], bar_sfull[2], bar_sempty[2], bar_tfull[2], bar_tempty[2],
       bar_prfull[2], bar_prempty[2], bar_done;
   __shared__ uint32_t tmem_base_sh;
@@ -1550,7 +1562,7 @@ struct DqCfg {
   static constexpr int B_BYTES = T::NKB * 64 * 128;       // K chunk: NKB regions of 64 keys x 128 B
   static constexpr int STAGE = A_BYTES + B_BYTES;
   static constexpr int OFF_OUT = NSTAGE * STAGE;          // epilogue staging: NKB regions of 128 rows x 128 B
-  static constexpr int SMEM = OFF_OUT + T::NKB * kBM * 128 + 1024;
+  static constexpr int SMEM = OFF_OUT + T::NKB * kBM * 128;
   static constexpr int TMEM_COLS = pow2_cols(2 * DP);
   static constexpr int NTHREADS = 128 + 64;
   static constexpr int TMA_WARP = 4, MMA_WARP = 5;
@@ -1573,8 +1585,8 @@ __global__ void __launch_bounds__(DqCfg<DP>::NTHREADS, 1)
   using C = DqCfg<DP>;
   using T = typename C::T;
   constexpr int NS = C::NSTAGE;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  if (smem_misaligned(p.status)) return;  // uniform over the CTA, before any barrier or allocation
+  uint8_t* smem = smem_raw;
   __shared__ uint64_t bar_full[NS], bar_empty[NS], bar_accfull[2], bar_accempty[2];
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_flag;

@@ -16,7 +16,7 @@ namespace geoattn {
 // the launch's status word and the CTA abandons its work (all later waits return immediately), so a lost
 // arrival becomes a host-visible error instead of a hung GPU.
 // ----------------------------------------------------------------------------------------------------------
-enum DeviceStatus : int { kDevOk = 0, kDevWaitTimeout = 1 };
+enum DeviceStatus : int { kDevOk = 0, kDevWaitTimeout = 1, kDevSmemMisaligned = 2 };
 
 // 2^31 ns ~ 2.1 s per wait: far above any legitimate wait in these kernels (a whole launch takes milliseconds).
 constexpr uint64_t kWaitLimitNs = 1ull << 31;

@@ -135,7 +135,8 @@ int geoattn_bwd(const GeoAttnBwdArgs* args, void* stream);
 int geoattn_bwd_noalloc(const GeoAttnBwdArgs* args, void* stream);
 
 /* ---- diagnostics --------------------------------------------------------------------------------------- */
-/* Copies the device status word of a workspace (0 = ok, 1 = a bounded wait expired) to *status. Synchronises
+/* Copies the device status word of a workspace (0 = ok, 1 = a bounded wait expired, 2 = a kernel found its shared
+ * memory misaligned and did nothing) to *status. Synchronises
  * the stream; for tests and debugging only. */
 int geoattn_read_status(const void* workspace, int* status, void* stream);
 const char* geoattn_error_string(int code);
