@@ -670,8 +670,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
           prior32_smem<BF16>(prt, e.r, piece, pr);  // overlaps the tensor-memory load
           tmem_wait32(vs);
           tc_fence_before();
-          mbar_arrive(&bar_prempty[prs]);  // scores and prior are in registers: both buffers may be refilled
-          mbar_arrive(&bar_sempty[ss]);
+          mbar_arrive(&bar_sempty[ss]);  // the scores are in registers: the MMA may refill the buffer
           const int nvalid = p.N - (c * T::CH + piece * 32);
           float l24[4] = {0.f, 0.f, 0.f, 0.f};
           // phase-ordered: 32 independent exp2 for P1, then the biased exp2 (more independent work per warp)
@@ -692,6 +691,8 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
           if (nvalid >= 32) body(std::false_type{});
           else body(std::true_type{});
           l2 += (l24[0] + l24[1]) + (l24[2] + l24[3]);
+          // the prior tile is released once every value read from it has been used (not when the loads are issued)
+          mbar_arrive(&bar_prempty[prs]);
           // the P buffer is free once the P.V two chunks back has run (waited here, after the math)
           if (!(ok = warp_wait(&bar_pempty[ps], ((pc >> 1) & 1) ^ 1, ctx))) break;
           stage_row32<BF16>(preg, e.r, piece, v);
@@ -981,18 +982,31 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
     const size_t nrows_all = (size_t)p.B * p.H * p.N;
     int sc = 0, pc = 0, dc = 0, it = 0;
     bool ok = true;
+    // the forward's row statistics (m, l1, l2) of a tile are loaded one tile ahead, so their latency is hidden
+    auto load_stats = [&](int t, float (&st3)[3]) {
+      const int r_ = (t % p.nrb) * kBM + e.r;
+      if (t < ntiles && r_ < p.N) {
+        const size_t sr = (size_t)(t / p.nrb) * p.N + r_;
+        st3[0] = p.stats[sr];
+        st3[1] = p.stats[nrows_all + sr];
+        st3[2] = p.stats[2 * nrows_all + sr];
+      }
+    };
+    float nst[3] = {0.f, 1.f, 1.f};
+    load_stats(blockIdx.x, nst);
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++it) {
     const int rb = tile % p.nrb, bh = tile / p.nrb, b = bh / p.H, h = bh % p.H;
     const int row = rb * kBM + e.r;
     const bool valid = row < p.N;
+    const float cst[3] = {nst[0], nst[1], nst[2]};
+    load_stats(tile + gridDim.x, nst);
     const Abg ab = load_abg(p, h);
     const float aL = ab.a * kLog2e, bL = ab.b * kLog2e, gL = ab.g * kLog2e, cL = ab.c * kLog2e;
-    const size_t srow = (size_t)bh * p.N + (valid ? row : 0);
     // P1 = 2^(t - m1), P2 = 2^(Z log2 e - c2); rows past N get m1 = c2 = +inf (P1 = P2 = 0)
     float m1 = INFINITY, c2 = INFINITY;
     if (valid) {
-      m1 = p.stats[srow] + log2f(p.stats[nrows_all + srow]);
-      c2 = cL + log2f(p.stats[2 * nrows_all + srow]);
+      m1 = cst[0] + log2f(cst[1]);
+      c2 = cL + log2f(cst[2]);
     }
     float acc[3] = {0.f, 0.f, 0.f};  // delta2, a, b
     for (int c = 0; c < nchunks && ok; ++c) {
@@ -1012,8 +1026,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         tmem_wait32(vs);
         tmem_pin32(ws);
         tc_fence_before();
-        mbar_arrive(&bar_prempty[prs]);  // scores and prior are in registers: both buffers may be refilled
-        mbar_arrive(&bar_sempty[ss]);
+        mbar_arrive(&bar_sempty[ss]);  // the scores are in registers: the MMA may refill the buffer
         float pa[2][3] = {};  // two interleaved partial sums per quantity (shorter dependency chains)
         auto body = [&](auto masked) {
           float p1[32];
@@ -1039,6 +1052,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         else body(std::true_type{});
 #pragma unroll
         for (int k = 0; k < 3; ++k) acc[k] += pa[0][k] + pa[1][k];
+        mbar_arrive(&bar_prempty[prs]);  // every value read from the prior tile has been used
       }
       ++sc;
       ++pc;
@@ -1088,7 +1102,6 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         tmem_wait32(vs);
         tmem_pin32(ws);
         tc_fence_before();
-        mbar_arrive(&bar_prempty[prs]);
         mbar_arrive(&bar_sempty[ss]);
         auto body = [&](auto masked) {
           float p1[32];
@@ -1111,6 +1124,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         };
         if (nvalid >= 32) body(std::false_type{});
         else body(std::true_type{});
+        mbar_arrive(&bar_prempty[prs]);  // every value read from the prior tile has been used
         // the dS buffer is free once the dQ MMA that read it has run (waited here, after the math)
         if (!(ok = warp_wait(&bar_dsempty[ds], ((dc / C::NDS) & 1) ^ 1, ctx))) break;
         stage_row32<BF16>(dreg, e.r, piece, v);
@@ -1194,8 +1208,10 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
 template <bool BF16, int DP>
 struct ColsCfg : Tile<BF16, DP> {
   using T = Tile<BF16, DP>;
-  static constexpr int NB = (BF16 && DP <= 128) ? 2 : 1;   // buffers for query chunks and S^T / dP^T
-  static constexpr int NST = (BF16 && DP <= 128) ? 2 : 1;  // buffers for the staged P2^T / dS^T tiles
+  static constexpr int NQ = (BF16 && DP <= 128) ? 3 : 1;   // query-chunk (Q, dO) buffers
+  static constexpr int NSB = (BF16 && DP <= 128) ? 2 : 1;  // S^T / dP^T accumulator buffers in tensor memory
+  static constexpr int NR = 2;                             // row-record buffers
+  static constexpr int NST = (BF16 && DP <= 64) ? 2 : 1;   // buffers for the staged P2^T / dS^T tiles
   static constexpr int NPR = !BF16 ? 0 : (DP <= 64 ? 2 : 1);  // staged prior buffers (0: read from L2)
   static constexpr int K_BYTES = kBM * DP * T::EB;          // per plane (K and V blocks)
   static constexpr int Q_BYTES = T::CH * DP * T::EB;        // per plane per buffer (Q and dO chunks)
@@ -1205,19 +1221,19 @@ struct ColsCfg : Tile<BF16, DP> {
   static constexpr int OFF_K = 0;
   static constexpr int OFF_V = OFF_K + T::PL * K_BYTES;
   static constexpr int OFF_Q = OFF_V + T::PL * K_BYTES;
-  static constexpr int OFF_DO = OFF_Q + NB * T::PL * Q_BYTES;
-  static constexpr int OFF_QT = OFF_DO + NB * T::PL * Q_BYTES;
-  static constexpr int OFF_DOT = OFF_QT + NB * QT_BYTES;
-  static constexpr int OFF_P2 = OFF_DOT + NB * QT_BYTES;
+  static constexpr int OFF_DO = OFF_Q + NQ * T::PL * Q_BYTES;
+  static constexpr int OFF_QT = OFF_DO + NQ * T::PL * Q_BYTES;
+  static constexpr int OFF_DOT = OFF_QT + NQ * QT_BYTES;
+  static constexpr int OFF_P2 = OFF_DOT + NQ * QT_BYTES;
   static constexpr int OFF_DS = OFF_P2 + NST * ST_BYTES;
   static constexpr int OFF_PR = OFF_DS + NST * ST_BYTES;
   static constexpr int OFF_REC = OFF_PR + NPR * kPriorTileBytes;
-  static constexpr int SMEM = OFF_REC + NB * REC_BYTES;
+  static constexpr int SMEM = OFF_REC + NR * REC_BYTES;
   static constexpr int TM_S = 0;
-  static constexpr int TM_DP = NB * T::CH;
-  static constexpr int TM_DK = 2 * NB * T::CH;
+  static constexpr int TM_DP = NSB * T::CH;
+  static constexpr int TM_DK = 2 * NSB * T::CH;
   static constexpr int TM_DV = TM_DK + DP;
-  static constexpr int TMEM_COLS = pow2_cols(2 * NB * T::CH + 2 * DP);
+  static constexpr int TMEM_COLS = pow2_cols(2 * NSB * T::CH + 2 * DP);
   // dK and dV leave in turn through the P2^T / dS^T buffers (contiguous, free once the tile's last MMA has run)
   static constexpr bool EPI_TMA = BF16 && T::NKB * kBM * 128 <= 2 * NST * ST_BYTES;
 };
@@ -1228,11 +1244,11 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
   static_assert(!SDS || BF16, "the dS-scratch backward is bf16 only");
   using C = ColsCfg<BF16, DP>;
   using T = typename C::T;
-  constexpr int NB = C::NB, NST = C::NST, NPR = C::NPR;
+  constexpr int NQ = C::NQ, NSB = C::NSB, NR = C::NR, NST = C::NST, NPR = C::NPR;
   if (smem_misaligned(p.status)) return;  // uniform over the CTA, before any barrier or allocation
   uint8_t* smem = smem_raw;
-  __shared__ uint64_t bar_kvfull, bar_kvempty, bar_qfull[2], bar_qempty[2], bar_sfull[2], bar_sempty[2], bar_tfull[2], bar_tempty[2],
-      bar_prfull[2], bar_prempty[2], bar_done;
+  __shared__ uint64_t bar_kvfull, bar_kvempty, bar_qfull[3], bar_qempty[3], bar_sfull[2], bar_sempty[2], bar_tfull[2],
+      bar_tempty[2], bar_prfull[2], bar_prempty[2], bar_recfull[2], bar_recempty[2], bar_done;
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_flag;
   __shared__ double redc[8][2];
@@ -1246,9 +1262,13 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
     abort_flag = 0;
     mbar_init(&bar_kvfull, 1);
     mbar_init(&bar_kvempty, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < 3; ++i) {
       mbar_init(&bar_qfull[i], 1);
       mbar_init(&bar_qempty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bar_recfull[i], 1);
+      mbar_init(&bar_recempty[i], T::EWT);
       mbar_init(&bar_sfull[i], 1);
       mbar_init(&bar_sempty[i], T::EWT);
       mbar_init(&bar_tfull[i], T::EWT);
@@ -1302,9 +1322,9 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       }
       for (int c = 0; c < nchunks; ++c) {
         const int gc = it * nchunks + c;  // chunk count over all tiles (buffer slots and phases)
-        const int qs = gc % NB;
-        if (!(ok = mbar_wait(&bar_qempty[qs], ((gc / NB) & 1) ^ 1, ctx))) break;
-        mbar_arrive_expect_tx(&bar_qfull[qs], 2 * T::PL * C::Q_BYTES + 2 * C::QT_BYTES + C::REC_BYTES);
+        const int qs = gc % NQ;
+        if (!(ok = mbar_wait(&bar_qempty[qs], ((gc / NQ) & 1) ^ 1, ctx))) break;
+        mbar_arrive_expect_tx(&bar_qfull[qs], 2 * T::PL * C::Q_BYTES + 2 * C::QT_BYTES);
         tma_tile<T>(smem + C::OFF_Q + qs * T::PL * C::Q_BYTES, &maps.q, &bar_qfull[qs], T::CH, c * T::CH, h, b, p.B,
                     T::PL);
         tma_tile<T>(smem + C::OFF_DO + qs * T::PL * C::Q_BYTES, &maps.dout, &bar_qfull[qs], T::CH, c * T::CH, h, b,
@@ -1313,8 +1333,11 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
           tma_tileT(smem + C::OFF_QT + qs * C::QT_BYTES, &maps.qt, &bar_qfull[qs], c * T::CH, h, b);
           tma_tileT(smem + C::OFF_DOT + qs * C::QT_BYTES, &maps.dot, &bar_qfull[qs], c * T::CH, h, b);
         }
-        bulk_load(smem + C::OFF_REC + qs * C::REC_BYTES, p.rowrec + ((size_t)bh * p.nchp + c) * 4 * T::CH,
-                  C::REC_BYTES, &bar_qfull[qs]);
+        const int rs = gc % NR;  // the chunk's row records, on their own ring
+        if (!(ok = mbar_wait(&bar_recempty[rs], ((gc / NR) & 1) ^ 1, ctx))) break;
+        mbar_arrive_expect_tx(&bar_recfull[rs], C::REC_BYTES);
+        bulk_load(smem + C::OFF_REC + rs * C::REC_BYTES, p.rowrec + ((size_t)bh * p.nchp + c) * 4 * T::CH,
+                  C::REC_BYTES, &bar_recfull[rs]);
         if constexpr (SDS)
           if (c > 0 && !(ok = store_ds(gc - 1, c - 1))) break;
       }
@@ -1344,15 +1367,15 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       bool ok = true;
       int it = 0;
       auto issue_s = [&](int gc) -> bool {
-        const int qs = gc % NB;
-        if (!mbar_wait(&bar_qfull[qs], (gc / NB) & 1, ctx)) return false;
-        if (!mbar_wait(&bar_sempty[qs], ((gc / NB) & 1) ^ 1, ctx)) return false;
+        const int qs = gc % NQ, ss = gc % NSB;
+        if (!mbar_wait(&bar_qfull[qs], (gc / NQ) & 1, ctx)) return false;
+        if (!mbar_wait(&bar_sempty[ss], ((gc / NSB) & 1) ^ 1, ctx)) return false;
         tc_fence_after();
-        mma_qk<T, T::CH>(tmem + C::TM_S + qs * T::CH, sbase + C::OFF_K, C::K_BYTES,
+        mma_qk<T, T::CH>(tmem + C::TM_S + ss * T::CH, sbase + C::OFF_K, C::K_BYTES,
                          sbase + C::OFF_Q + qs * T::PL * C::Q_BYTES, C::Q_BYTES);
-        mma_qk<T, T::CH>(tmem + C::TM_DP + qs * T::CH, sbase + C::OFF_V, C::K_BYTES,
+        mma_qk<T, T::CH>(tmem + C::TM_DP + ss * T::CH, sbase + C::OFF_V, C::K_BYTES,
                          sbase + C::OFF_DO + qs * T::PL * C::Q_BYTES, C::Q_BYTES);
-        mma_commit(&bar_sfull[qs]);
+        mma_commit(&bar_sfull[ss]);
         return true;
       };
       for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++it) {
@@ -1362,11 +1385,11 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       if (ok && nchunks == 1) mma_commit(&bar_kvempty);  // every S^T/dP^T MMA of this tile has been issued
       for (int c = 0; c < nchunks && ok; ++c) {
         const int gc = g0 + c;
-        if (NB == 2 && c + 1 < nchunks) {
+        if (NSB == 2 && c + 1 < nchunks) {
           if (!(ok = issue_s(gc + 1))) break;
           if (c + 2 == nchunks) mma_commit(&bar_kvempty);
         }
-        const int qs = gc % NB, ts = gc % NST;
+        const int qs = gc % NQ, ts = gc % NST;
         if (!(ok = mbar_wait(&bar_tfull[ts], (gc / NST) & 1, ctx))) break;
         tc_fence_after();
         uint32_t dob, qb;
@@ -1381,7 +1404,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         mma_pv<T>(tmem + C::TM_DK, sbase + C::OFF_DS + ts * C::ST_BYTES, qb, c > 0);
         mma_commit(&bar_tempty[ts]);
         mma_commit(&bar_qempty[qs]);
-        if (NB == 1 && c + 1 < nchunks) {
+        if (NSB == 1 && c + 1 < nchunks) {
           if (!(ok = issue_s(gc + 1))) break;
           if (c + 2 == nchunks) mma_commit(&bar_kvempty);
         }
@@ -1410,30 +1433,29 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
     float gbp[2] = {0.f, 0.f}, ggp[2] = {0.f, 0.f};  // with SDS: this key's d(beta), d(gamma) partials
     for (int c = 0; c < nchunks; ++c) {
       const int gc = it * nchunks + c;
-      const int qs = gc % NB, ts = gc % NST;
+      const int ss = gc % NSB, rs = gc % NR, ts = gc % NST;
       if (!ok) continue;
-      if (!(ok = warp_wait(&bar_sfull[qs], (gc / NB) & 1, ctx))) continue;
+      if (!(ok = warp_wait(&bar_sfull[ss], (gc / NSB) & 1, ctx))) continue;
       if constexpr (NPR > 0)
         if (!(ok = warp_wait(&bar_prfull[gc % NPR], (gc / NPR) & 1, ctx))) continue;
       // the chunk's row records (rows past N carry m1 = c2 = +inf: P1 = P2 = dS = 0 in their columns)
-      if (!(ok = warp_wait(&bar_qfull[qs], (gc / NB) & 1, ctx))) continue;
+      if (!(ok = warp_wait(&bar_recfull[rs], (gc / NR) & 1, ctx))) continue;
       tc_fence_after();
-      const float* rec = reinterpret_cast<const float*>(smem + C::OFF_REC + qs * C::REC_BYTES);
+      const float* rec = reinterpret_cast<const float*>(smem + C::OFF_REC + rs * C::REC_BYTES);
       uint8_t* p2reg = smem + C::OFF_P2 + ts * C::ST_BYTES;
       uint8_t* dsreg = smem + C::OFF_DS + ts * C::ST_BYTES;
       const uint8_t* prt = smem + C::OFF_PR + (NPR > 0 ? (gc % (NPR > 0 ? NPR : 1)) : 0) * kPriorTileBytes;
 #pragma unroll 1
       for (int piece = e.wg; piece < T::PIECES; piece += T::EW) {
         uint32_t vs[32], ws[32];
-        tmem_ld32_issue(e.lane_base + C::TM_S + qs * T::CH + piece * 32, vs);
-        tmem_ld32_issue(e.lane_base + C::TM_DP + qs * T::CH + piece * 32, ws);
+        tmem_ld32_issue(e.lane_base + C::TM_S + ss * T::CH + piece * 32, vs);
+        tmem_ld32_issue(e.lane_base + C::TM_DP + ss * T::CH + piece * 32, ws);
         Prior32<BF16> pr;
         prior_piece<BF16, (NPR > 0)>(prt, p.priorT, p.np, pkey, e.r, c, piece, pr);
         tmem_wait32(vs);
         tmem_pin32(ws);
         tc_fence_before();
-        if constexpr (NPR > 0) mbar_arrive(&bar_prempty[gc % NPR]);  // prior and scores are in registers
-        mbar_arrive(&bar_sempty[qs]);
+        mbar_arrive(&bar_sempty[ss]);  // the scores are in registers: the MMA may refill the buffer
         float v[32], w[32];
         // keys past N (last block only) produce rows of P2^T / dS^T that only reach dK/dV rows that are never
         // stored, so no per-key mask is needed
@@ -1462,6 +1484,8 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
             }
           }
         }
+        mbar_arrive(&bar_recempty[rs]);  // the records and the prior tile are read and used
+        if constexpr (NPR > 0) mbar_arrive(&bar_prempty[gc % NPR]);
         // the staging tiles are free once the previous chunk's dV/dK MMAs have run (waited here, after the math)
         if (!(ok = warp_wait(&bar_tempty[ts], ((gc / NST) & 1) ^ 1, ctx))) break;
         stage_row32<BF16>(p2reg, e.r, piece, v);
