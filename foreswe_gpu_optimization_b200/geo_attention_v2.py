@@ -78,35 +78,68 @@ def _shape(q, per_head):
     return _lib.Shape(B, H, N, D, _lib.DTYPE_BF16 if q.dtype == torch.bfloat16 else _lib.DTYPE_FP32, per_head)
 
 
+def _forward(q, k, v, prior, abg, per_head):
+    """geoattn_fwd on torch tensors: returns (o, stats). q, k, v [B, H, N, D] bf16 or fp32 on one CUDA device."""
+    if q.dim() != 4 or k.shape != q.shape or v.shape != q.shape:
+        raise ValueError("q, k, v must be [B, H, N, D] with equal shapes")
+    if q.dtype not in (torch.bfloat16, torch.float32) or k.dtype != q.dtype or v.dtype != q.dtype:
+        raise TypeError("q, k, v must all be bf16 or all be fp32")
+    if not q.is_cuda:
+        raise RuntimeError("geo attention runs on CUDA tensors only (no CPU path)")
+    if prior.device != q.device:
+        raise ValueError("the geo prior lives on %s, q on %s" % (prior.device, q.device))
+    q, k, v = _tma_ready(q), _tma_ready(k), _tma_ready(v)
+    sh = _shape(q, per_head)
+    L = _lib.lib()
+    # O takes q's layout: for split_heads views of a [B, N, H*D] projection it is [B, N, H, D] in memory, so the
+    # caller's combine_heads (transpose(1, 2).contiguous()) needs no copy and dO comes back as a strided view
+    o = torch.empty_like(q)
+    stats = torch.empty(L.geoattn_stats_bytes(ctypes.byref(sh)) // 4, dtype=torch.float32, device=q.device)
+    ws = torch.empty(L.geoattn_fwd_workspace_bytes(ctypes.byref(sh)), dtype=torch.uint8, device=q.device)
+    args = _lib.FwdArgs(sh, _lib.tensor_arg(q), _lib.tensor_arg(k), _lib.tensor_arg(v),
+                        ctypes.c_void_p(abg.data_ptr()), ctypes.c_void_p(prior.data_ptr()),
+                        ctypes.c_void_p(o.data_ptr()), _lib.c_ll4(*o.stride()),
+                        ctypes.c_void_p(stats.data_ptr()), ctypes.c_void_p(ws.data_ptr()))
+    ev = _events("fwd")
+    if ev:
+        args.events = ev[0]
+    _lib.check(L.geoattn_fwd(ctypes.byref(args), _stream()))
+    return o, stats
+
+
+def _backward(q, k, v, o, do, prior, abg, stats, per_head):
+    """geoattn_bwd on torch tensors: returns (dq, dk, dv, dabg); dq/dk/dv keep the strides of q/k/v."""
+    B, H, N, D = q.shape
+    q, k, v = _tma_ready(q), _tma_ready(k), _tma_ready(v)
+    do = _tma_ready(do.to(q.dtype))
+    sh = _shape(q, per_head)
+    L = _lib.lib()
+    dq = torch.empty_strided(q.shape, q.stride(), dtype=q.dtype, device=q.device)
+    dk = torch.empty_strided(k.shape, k.stride(), dtype=k.dtype, device=k.device)
+    dv = torch.empty_strided(v.shape, v.stride(), dtype=v.dtype, device=v.device)
+    nabg = H if per_head else 1
+    dabg = torch.empty(3 * nabg, dtype=torch.float32, device=q.device)
+    ws = torch.empty(L.geoattn_bwd_workspace_bytes(ctypes.byref(sh)), dtype=torch.uint8, device=q.device)
+    args = _lib.BwdArgs(sh, _lib.tensor_arg(q), _lib.tensor_arg(k), _lib.tensor_arg(v), _lib.tensor_arg(o),
+                        _lib.tensor_arg(do), ctypes.c_void_p(abg.data_ptr()), ctypes.c_void_p(prior.data_ptr()),
+                        ctypes.c_void_p(stats.data_ptr()), ctypes.c_void_p(dq.data_ptr()),
+                        _lib.c_ll4(*dq.stride()), ctypes.c_void_p(dk.data_ptr()), _lib.c_ll4(*dk.stride()),
+                        ctypes.c_void_p(dv.data_ptr()), _lib.c_ll4(*dv.stride()),
+                        ctypes.c_void_p(dabg.data_ptr()), ctypes.c_void_p(ws.data_ptr()))
+    ev = _events("bwd")
+    if ev:
+        args.events = ev[0]
+    _lib.check(L.geoattn_bwd(ctypes.byref(args), _stream()))
+    return dq, dk, dv, dabg
+
+
 class FusedGeoAttentionV2(torch.autograd.Function):
     """O = softmax(alpha*softmax(QK^T/sqrt d) + beta*Dp + gamma*Ap) V on libgeoattn (fwd + bwd)."""
 
     @staticmethod
     def forward(ctx, q, k, v, prior, alpha, beta, gamma):
-        if q.dim() != 4 or k.shape != q.shape or v.shape != q.shape:
-            raise ValueError("q, k, v must be [B, H, N, D] with equal shapes")
-        if q.dtype not in (torch.bfloat16, torch.float32) or k.dtype != q.dtype or v.dtype != q.dtype:
-            raise TypeError("q, k, v must all be bf16 or all be fp32")
-        if not q.is_cuda:
-            raise RuntimeError("geo attention runs on CUDA tensors only (no CPU path)")
-        B, H, N, D = q.shape
-        if prior.device != q.device:
-            raise ValueError("the geo prior lives on %s, q on %s" % (prior.device, q.device))
-        abg, per_head = _abg(alpha, beta, gamma, H, q.device)
-        q, k, v = _tma_ready(q), _tma_ready(k), _tma_ready(v)
-        sh = _shape(q, per_head)
-        L = _lib.lib()
-        o = torch.empty(B, H, N, D, dtype=q.dtype, device=q.device)
-        stats = torch.empty(L.geoattn_stats_bytes(ctypes.byref(sh)) // 4, dtype=torch.float32, device=q.device)
-        ws = torch.empty(L.geoattn_fwd_workspace_bytes(ctypes.byref(sh)), dtype=torch.uint8, device=q.device)
-        args = _lib.FwdArgs(sh, _lib.tensor_arg(q), _lib.tensor_arg(k), _lib.tensor_arg(v),
-                            ctypes.c_void_p(abg.data_ptr()), ctypes.c_void_p(prior.data_ptr()),
-                            ctypes.c_void_p(o.data_ptr()), _lib.c_ll4(*o.stride()),
-                            ctypes.c_void_p(stats.data_ptr()), ctypes.c_void_p(ws.data_ptr()))
-        ev = _events("fwd")
-        if ev:
-            args.events = ev[0]
-        _lib.check(L.geoattn_fwd(ctypes.byref(args), _stream()))
+        abg, per_head = _abg(alpha, beta, gamma, q.shape[1], q.device)
+        o, stats = _forward(q, k, v, prior, abg, per_head)
         ctx.save_for_backward(q, k, v, o, prior, abg, stats)
         ctx.per_head = per_head
         ctx.abg_meta = [(t.shape, t.dtype) for t in (alpha, beta, gamma)]
@@ -115,26 +148,8 @@ class FusedGeoAttentionV2(torch.autograd.Function):
     @staticmethod
     def backward(ctx, do):
         q, k, v, o, prior, abg, stats = ctx.saved_tensors
-        B, H, N, D = q.shape
-        do = _tma_ready(do.to(q.dtype))
-        sh = _shape(q, ctx.per_head)
-        L = _lib.lib()
-        dq = torch.empty_strided(q.shape, q.stride(), dtype=q.dtype, device=q.device)
-        dk = torch.empty_strided(k.shape, k.stride(), dtype=k.dtype, device=k.device)
-        dv = torch.empty_strided(v.shape, v.stride(), dtype=v.dtype, device=v.device)
-        nabg = H if ctx.per_head else 1
-        dabg = torch.empty(3 * nabg, dtype=torch.float32, device=q.device)
-        ws = torch.empty(L.geoattn_bwd_workspace_bytes(ctypes.byref(sh)), dtype=torch.uint8, device=q.device)
-        args = _lib.BwdArgs(sh, _lib.tensor_arg(q), _lib.tensor_arg(k), _lib.tensor_arg(v), _lib.tensor_arg(o),
-                            _lib.tensor_arg(do), ctypes.c_void_p(abg.data_ptr()), ctypes.c_void_p(prior.data_ptr()),
-                            ctypes.c_void_p(stats.data_ptr()), ctypes.c_void_p(dq.data_ptr()),
-                            _lib.c_ll4(*dq.stride()), ctypes.c_void_p(dk.data_ptr()), _lib.c_ll4(*dk.stride()),
-                            ctypes.c_void_p(dv.data_ptr()), _lib.c_ll4(*dv.stride()),
-                            ctypes.c_void_p(dabg.data_ptr()), ctypes.c_void_p(ws.data_ptr()))
-        ev = _events("bwd")
-        if ev:
-            args.events = ev[0]
-        _lib.check(L.geoattn_bwd(ctypes.byref(args), _stream()))
+        dq, dk, dv, dabg = _backward(q, k, v, o, do, prior, abg, stats, ctx.per_head)
+        nabg = q.shape[1] if ctx.per_head else 1
         grads = []
         for i, (shape, dtype) in enumerate(ctx.abg_meta):
             grads.append(dabg[i * nabg:(i + 1) * nabg].reshape(shape).to(dtype))

@@ -132,6 +132,8 @@ def test_split_heads_strided_views(ops):
     o.backward(do)
     for x in views:
         assert x.grad.stride() == x.stride()
+    # O has q's layout, so the call site's combine_heads (transpose(1, 2).contiguous()) copies nothing
+    assert o.stride() == views[0].stride() and o.transpose(1, 2).is_contiguous()
     ref = oga.grads(*(t.detach().double().cpu() for t in views), dist.cpu().double(), ang.cpu().double(),
                     a.detach().cpu(), b.detach().cpu(), c.detach().cpu(), do.double().cpu())
     res = dict(output=o.detach().cpu(), dQ=views[0].grad.cpu(), dK=views[1].grad.cpu(), dV=views[2].grad.cpu(),
