@@ -5,7 +5,7 @@ head dim 128, bf16; per-head alpha/beta/gamma; geo prior from synthetic station 
 (lat ~ U(35,49), lon ~ U(-124,-104), elevation ~ U(500,3500) m). One step = forward + backward of the attention
 on this rank's issue dates followed by an NCCL all-reduce of the bias-parameter gradients (N > 1).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload c5|c4]
 
 Prints ONE JSON line on rank 0. ``value`` is whole-job algorithmic TFLOP/s, 12*B*H*N^2*D per fwd+bwd (recompute not
 counted), over the max-over-ranks device time of K steps. ``e2e`` is the same metric through the public API with
@@ -211,6 +211,126 @@ def run_reference(args):
     return 0
 
 
+def run_c4(args):
+    """Full training step of a random-init geo-attention encoder (12 pre-LN layers, d_model 2048, 16 x 128 heads,
+    FFN 8192) on 24 weekly timesteps x 512 stations of one issue date, bf16 autocast, MSE loss, fused AdamW; every
+    layer's spatial attention is the geo-attention kernel. Prints one JSON line (ms per training step)."""
+    import torch.nn as nn
+    import foreswe_gpu_optimization_b200 as g
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    torch.manual_seed(0)
+    layers, dm, heads, dh, dff, weeks, feats = 12, 2048, 16, 128, 8192, 24, 15
+    geom = g.StationGeometry(*stations(0), device=dev)
+    dmat, amat = geom.distance_and_angularity()
+    eager = [False]
+
+    class Layer(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.n1, self.n2 = nn.LayerNorm(dm), nn.LayerNorm(dm)
+            self.W_q, self.W_k, self.W_v, self.W_o = (nn.Linear(dm, dm) for _ in range(4))
+            self.fc1, self.fc2 = nn.Linear(dm, dff), nn.Linear(dff, dm)
+            self.alpha = nn.Parameter(torch.rand(heads) * 0.9 + 0.1)
+            self.beta = nn.Parameter(torch.randn(heads) * 0.5)
+            self.gamma = nn.Parameter(torch.randn(heads) * 0.5)
+
+        def forward(self, x):                      # x [weeks, stations, d_model]
+            h = self.n1(x)
+            q, k, v = (w(h).view(weeks, N, heads, dh).transpose(1, 2) for w in (self.W_q, self.W_k, self.W_v))
+            if eager[0]:                           # the production method (custom_encoder_model.py:25-39)
+                s_ = torch.softmax(torch.matmul(q, k.transpose(-2, -1)) / math.sqrt(dh), dim=-1)
+                z = (self.alpha.view(-1, 1, 1) * s_ + self.beta.view(-1, 1, 1) / (1 + dmat)
+                     + self.gamma.view(-1, 1, 1) / (1 + amat))
+                a = torch.matmul(torch.softmax(z, dim=-1), v)
+            else:
+                a = g.geo_attention(q, k, v, geom, self.alpha, self.beta, self.gamma)
+            x = x + self.W_o(a.transpose(1, 2).contiguous().view(weeks, N, dm))
+            return x + self.fc2(torch.relu(self.fc1(self.n2(x))))
+
+    class Encoder(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.embed = nn.Linear(feats, dm)
+            self.layers = nn.ModuleList(Layer() for _ in range(layers))
+            self.norm = nn.LayerNorm(dm)
+            self.head = nn.Linear(dm, 1)
+
+        def forward(self, f):
+            x = self.embed(f)
+            for layer in self.layers:
+                x = layer(x)
+            return self.head(self.norm(x))
+
+    model = Encoder().to(dev)
+    nparams = sum(p.numel() for p in model.parameters())
+    opt = torch.optim.AdamW(model.parameters(), lr=1e-4, fused=True)
+    gen = torch.Generator(device=dev).manual_seed(1)
+    feat = torch.randn(weeks, N, feats, device=dev, generator=gen)
+    target = torch.rand(weeks, N, 1, device=dev, generator=gen)
+
+    def train_step():
+        opt.zero_grad(set_to_none=True)
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            loss = torch.nn.functional.mse_loss(model(feat).float(), target)
+        loss.backward()
+        opt.step()
+        return loss
+
+    def time_steps():
+        for _ in range(args.warmup):
+            train_step()
+        torch.cuda.synchronize()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for _ in range(args.steps):
+            ls = train_step()
+        t1.record()
+        torch.cuda.synchronize()
+        return t0.elapsed_time(t1) / args.steps, ls
+
+    eager_ms = None
+    if not args.no_eager:
+        eager[0] = True
+        eager_ms, _ = time_steps()
+        eager[0] = False
+    ms, loss = time_steps()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    # the attention alone at the step's shape (12 layers' fwd+bwd), to report its share of the step
+    (qa, ka, va, doa), (a0, b0, c0) = inputs(weeks, 3, "cpu")
+    qa, ka, va, doa = (t.to(dev) for t in (qa, ka, va, doa))
+    pa = [t.to(dev).requires_grad_(True) for t in (a0, b0, c0)]
+    xs = [t.detach().requires_grad_(True) for t in (qa, ka, va)]
+    for _ in range(args.warmup):
+        g.geo_attention(*xs, geom, *pa).backward(doa)
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(args.steps * layers):
+        g.geo_attention(*xs, geom, *pa).backward(doa)
+    e1.record()
+    torch.cuda.synchronize()
+    attn_ms = e0.elapsed_time(e1) / args.steps
+    attn_flops = layers * flops(weeks)
+    dense_flops = 6.0 * nparams * weeks * N
+    pk, pk_src = peaks()
+    line = {"metric": "geo-attention encoder training step (fwd+bwd+fused AdamW), ms/step", "value": ms,
+            "unit": "ms/step", "higher_is_better": False, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "dtype": "bf16 autocast (fp32 master weights)", "data": "synthetic",
+            "config": {"workload": "12-layer pre-LN encoder, d_model 2048, 16 heads x 128, FFN 8192, 24 weeks x 512 "
+                                   "stations x 15 features, MSE vs U(0,1) targets, fused AdamW, random init",
+                       "params": nparams, "tokens_per_step": weeks * N, "attention_batch": weeks},
+            "eager_attention_ms_per_step": eager_ms,
+            "attention_ms_per_step": attn_ms, "attention_share": attn_ms / ms,
+            "attention_tflops": attn_flops / (attn_ms * 1e-3) / 1e12,
+            "model_tflops": (dense_flops + attn_flops) / (ms * 1e-3) / 1e12,
+            "model_tensor_frac": (dense_flops + attn_flops) / (ms * 1e-3) / 1e12 / pk, "peak_source": pk_src,
+            "loss": float(loss.item())}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -221,6 +341,8 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-eager", action="store_true")
     ap.add_argument("--batch", type=int, default=None, help="override the global batch (small cases for profiling)")
+    ap.add_argument("--workload", default="c5", choices=("c5", "c4"),
+                    help="c5: the attention scaling configuration (the headline line); c4: a full encoder training step")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     if args.batch:
@@ -228,6 +350,8 @@ def main():
         B_TOTAL = args.batch
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload == "c4":
+        return run_c4(args)
 
     import foreswe_gpu_optimization_b200 as g
     from foreswe_gpu_optimization_b200 import geo_attention_v2 as gv2
