@@ -762,7 +762,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
 template <bool BF16, int DP, bool DQ = true>
 struct RowsCfg : Tile<BF16, DP> {
   using T = Tile<BF16, DP>;
-  static constexpr int NKV = (!BF16 || DP > 128) ? 1 : 2;  // K/V chunk buffers
+  static constexpr int NKV = (!BF16 || DP > 128) ? 1 : (DQ ? 2 : 3);  // K/V chunk buffers
   static constexpr int NPR = (BF16 && DP <= 128) ? 2 : 1;   // staged prior buffers
   static constexpr int Q_BYTES = kBM * DP * T::EB;    // per plane (Q and dO)
   static constexpr int K_BYTES = T::CH * DP * T::EB;  // per plane per buffer (K and V chunks)
@@ -777,8 +777,8 @@ struct RowsCfg : Tile<BF16, DP> {
   static constexpr int OFF_KT = OFF_V + NKV * T::PL * K_BYTES;
   static constexpr int OFF_DS = OFF_KT + NDS_ALLOC * KT_BYTES;
   static constexpr int OFF_PR = OFF_DS + NDS_ALLOC * DS_BYTES;
-  static constexpr int OFF_XS = OFF_PR + NPR * kPriorTileBytes;  // without DQ: the warpgroups' row-sum exchange
-  static constexpr int SMEM = OFF_XS + (DQ ? 0 : 6 * kBM * 4);
+  static constexpr int OFF_XS = OFF_PR + NPR * kPriorTileBytes;  // without DQ: warpgroup 1's row sums
+  static constexpr int SMEM = OFF_XS + (DQ ? 0 : 3 * kBM * 4);
   static constexpr int TM_S = 0;                   // 2 buffers
   static constexpr int TM_DP = 2 * T::CH;          // 2 buffers
   static constexpr int TM_DQ = 4 * T::CH;
@@ -802,8 +802,8 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
   constexpr int NKV = C::NKV, NPR = C::NPR;
   if (smem_misaligned(p.status)) return;  // uniform over the CTA, before any barrier or allocation
   uint8_t* smem = smem_raw;
-  __shared__ uint64_t bar_qfull, bar_qempty, bar_kfull[2], bar_kempty[2], bar_vfull[2], bar_vempty[2], bar_sfull[2], bar_sempty[2],
-      bar_dsfull[2], bar_dsempty[2], bar_ktfull[2], bar_ktempty[2], bar_prfull[2], bar_prempty[2], bar_dqfull;
+  __shared__ uint64_t bar_qfull, bar_qempty, bar_kfull[3], bar_kempty[3], bar_vfull[3], bar_vempty[3], bar_sfull[2],
+      bar_sempty[2], bar_dsfull[2], bar_dsempty[2], bar_ktfull[2], bar_ktempty[2], bar_prfull[2], bar_prempty[2], bar_dqfull;
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_flag;
   __shared__ double red[8][3];
@@ -818,11 +818,13 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
     abort_flag = 0;
     mbar_init(&bar_qfull, 1);
     mbar_init(&bar_qempty, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < 3; ++i) {
       mbar_init(&bar_kfull[i], 1);
       mbar_init(&bar_kempty[i], 1);
       mbar_init(&bar_vfull[i], 1);
       mbar_init(&bar_vempty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&bar_sfull[i], 1);
       mbar_init(&bar_sempty[i], T::EWT);
       mbar_init(&bar_dsfull[i], T::EWT);
@@ -1058,17 +1060,32 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       ++pc;
     }
     if constexpr (T::EW == 2) {
-      // combine the two warpgroups' row sums, warpgroup 0's first: through the dS buffers (unused until sweep 2) once
-      // the previous tile's dQ store has finished reading them, or (without DQ) through a small exchange region
-      if (epi_tma && threadIdx.x == 0) bulk_wait_read0();
-      ew_sync(T::EWT);
-      float* xs = reinterpret_cast<float*>(smem + (DQ ? C::OFF_DS : C::OFF_XS));
+      if constexpr (DQ) {
+        // combine the two warpgroups' row sums (warpgroup 0's first) through the dS buffers, unused until sweep 2,
+        // once the previous tile's dQ store has finished reading them; both warpgroups need them for sweep 2
+        if (epi_tma && threadIdx.x == 0) bulk_wait_read0();
+        ew_sync(T::EWT);
+        float* xs = reinterpret_cast<float*>(smem + C::OFF_DS);
 #pragma unroll
-      for (int k = 0; k < 3; ++k) xs[(e.wg * 3 + k) * kBM + e.r] = acc[k];
-      ew_sync(T::EWT);
+        for (int k = 0; k < 3; ++k) xs[(e.wg * 3 + k) * kBM + e.r] = acc[k];
+        ew_sync(T::EWT);
 #pragma unroll
-      for (int k = 0; k < 3; ++k) acc[k] = xs[k * kBM + e.r] + xs[(3 + k) * kBM + e.r];
-      ew_sync(T::EWT);
+        for (int k = 0; k < 3; ++k) acc[k] = xs[k * kBM + e.r] + xs[(3 + k) * kBM + e.r];
+        ew_sync(T::EWT);
+      } else {
+        // only warpgroup 0 uses the combined sums (records, d(alpha)): warpgroup 1 hands its sums over. The region
+        // is rewritten only after the next tile's sweep, past this tile's partials barrier.
+        float* xs = reinterpret_cast<float*>(smem + C::OFF_XS);
+        if (e.wg == 1) {
+#pragma unroll
+          for (int k = 0; k < 3; ++k) xs[k * kBM + e.r] = acc[k];
+        }
+        ew_sync(T::EWT);
+        if (e.wg == 0) {
+#pragma unroll
+          for (int k = 0; k < 3; ++k) acc[k] += xs[k * kBM + e.r];
+        }
+      }
     }
     const float delta2 = acc[0];
     const float ta = fmaf(-delta2, acc[2], acc[1]);  // sum dZ P1 of the row
@@ -1245,6 +1262,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
   using C = ColsCfg<BF16, DP>;
   using T = typename C::T;
   constexpr int NQ = C::NQ, NSB = C::NSB, NR = C::NR, NST = C::NST, NPR = C::NPR;
+  constexpr int SLAG = NQ > 1 ? NQ - 1 : 1;  // chunks by which the dS stores trail the query-chunk loads
   if (smem_misaligned(p.status)) return;  // uniform over the CTA, before any barrier or allocation
   uint8_t* smem = smem_raw;
   __shared__ uint64_t bar_kvfull, bar_kvempty, bar_qfull[3], bar_qempty[3], bar_sfull[2], bar_sempty[2], bar_tfull[2],
@@ -1338,11 +1356,14 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         mbar_arrive_expect_tx(&bar_recfull[rs], C::REC_BYTES);
         bulk_load(smem + C::OFF_REC + rs * C::REC_BYTES, p.rowrec + ((size_t)bh * p.nchp + c) * 4 * T::CH,
                   C::REC_BYTES, &bar_recfull[rs]);
+        // the dS stores trail the loads by LAG chunks, so a store's wait for its tile never holds back the loads
+        // the MMAs need next (LAG < NQ keeps the dependency chain acyclic)
         if constexpr (SDS)
-          if (c > 0 && !(ok = store_ds(gc - 1, c - 1))) break;
+          if (c >= SLAG && !(ok = store_ds(gc - SLAG, c - SLAG))) break;
       }
       if constexpr (SDS)
-        if (ok) ok = store_ds(it * nchunks + nchunks - 1, nchunks - 1);
+        for (int c2 = nchunks - SLAG < 0 ? 0 : nchunks - SLAG; c2 < nchunks && ok; ++c2)
+          ok = store_ds(it * nchunks + c2, c2);
       }
     }
   } else if (warp == T::PR_WARP) {
