@@ -395,6 +395,25 @@ __device__ __forceinline__ void stage_out32(uint8_t* tile, int r, int d0, float 
   for (int j = 0; j < 32; ++j) v[j] *= scale;
   stage_row32<true>(tile + (d0 / 64) * (kBM * 128), r, (d0 % 64) / 32, v);
 }
+// Loads NP 32-column pieces of this thread's accumulator row (TMEM columns c0, c0 + step, ...; also the output
+// columns) with a single wait, then stages them scaled and rounded into the swizzled output tile.
+template <int NP>
+__device__ __forceinline__ void stage_acc(uint32_t tbase, int c0, int step, uint8_t* tile, int r, float scale) {
+  uint32_t v[NP][32];
+#pragma unroll
+  for (int i = 0; i < NP; ++i) tmem_ld32_issue(tbase + c0 + i * step, v[i]);
+  tmem_wait32(v[0]);
+#pragma unroll
+  for (int i = 1; i < NP; ++i) tmem_pin32(v[i]);
+#pragma unroll
+  for (int i = 0; i < NP; ++i) {
+    float f[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[i][j]);
+    stage_out32(tile, r, c0 + i * step, f, scale);
+  }
+}
+
 // Stores the staged tile (row block row0 of (b, h)) once every element-wise thread has staged its row. Called by all
 // element-wise threads; thread 0 issues the stores. The caller's next rewrite of `tile` must follow a
 // bulk_wait_read0() by thread 0 and a barrier among the element-wise threads.
@@ -716,14 +735,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       const float inv_l2 = __frcp_rn(l2);
       if (epi_tma) {
         // every P.V of the tile has completed (ofull), so the P buffers hold the staged O tile
-        if (ok) {
-#pragma unroll
-          for (int d0 = e.wg * 32; d0 < DP; d0 += 32 * T::EW) {
-            float v[32];
-            tmem_ld32(e.lane_base + C::TM_O + d0, v);
-            stage_out32(smem + C::OFF_P, e.r, d0, v, inv_l2);
-          }
-        }
+        if (ok) stage_acc<DP / (32 * T::EW)>(e.lane_base + C::TM_O, e.wg * 32, 32 * T::EW, smem + C::OFF_P, e.r, inv_l2);
         store_tile<T>(&maps.out0, smem + C::OFF_P, p.D, rb * kBM, h, b, ok);
       } else if (ok) {
         const long long ooff = (long long)b * p.o_str[0] + (long long)h * p.o_str[1] + (long long)row * p.o_str[2];
@@ -1188,14 +1200,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
     if constexpr (!DQ) {
     } else if (epi_tma) {
       // every dQ MMA of the tile has completed (dqfull), so the dS buffers hold the staged dQ tile
-      if (ok) {
-#pragma unroll 1
-        for (int d0 = e.wg * 32; d0 < DP; d0 += 32 * T::EW) {
-          float v[32];
-          tmem_ld32(e.lane_base + C::TM_DQ + d0, v);
-          stage_out32(smem + C::OFF_DS, e.r, d0, v, p.inv_sqrt_d);
-        }
-      }
+      if (ok) stage_acc<DP / (32 * T::EW)>(e.lane_base + C::TM_DQ, e.wg * 32, 32 * T::EW, smem + C::OFF_DS, e.r, p.inv_sqrt_d);
       store_tile<T>(&maps.out0, smem + C::OFF_DS, p.D, rb * kBM, h, b, ok);
     } else if (ok) {
       const long long qoff = (long long)b * p.dq_str[0] + (long long)h * p.dq_str[1] + (long long)row * p.dq_str[2];
@@ -1551,25 +1556,11 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
     if (epi_tma) {
       // every MMA of the tile has completed (done): the P2^T / dS^T buffers take dK, then dV
       uint8_t* stg = smem + C::OFF_P2;
-      if (ok) {
-#pragma unroll 1
-        for (int d0 = e.wg * 32; d0 < DP; d0 += 32 * T::EW) {
-          float v[32];
-          tmem_ld32(e.lane_base + C::TM_DK + d0, v);
-          stage_out32(stg, e.r, d0, v, p.inv_sqrt_d);
-        }
-      }
+      if (ok) stage_acc<DP / (32 * T::EW)>(e.lane_base + C::TM_DK, e.wg * 32, 32 * T::EW, stg, e.r, p.inv_sqrt_d);
       store_tile<T>(&maps.out0, stg, p.D, kblk * kBM, h, b, ok);
       if (threadIdx.x == 0) bulk_wait_read0();
       ew_sync(T::EWT);
-      if (ok) {
-#pragma unroll 1
-        for (int d0 = e.wg * 32; d0 < DP; d0 += 32 * T::EW) {
-          float v[32];
-          tmem_ld32(e.lane_base + C::TM_DV + d0, v);
-          stage_out32(stg, e.r, d0, v, 1.0f);
-        }
-      }
+      if (ok) stage_acc<DP / (32 * T::EW)>(e.lane_base + C::TM_DV, e.wg * 32, 32 * T::EW, stg, e.r, 1.0f);
       store_tile<T>(&maps.out1, stg, p.D, kblk * kBM, h, b, ok);
     } else if (ok) {
       const long long koff = (long long)b * p.dk_str[0] + (long long)h * p.dk_str[1] + (long long)key * p.dk_str[2];
@@ -1716,11 +1707,8 @@ __global__ void __launch_bounds__(DqCfg<DP>::NTHREADS, 1)
         ew_sync(128);
         if (ok) {
 #pragma unroll 1
-          for (int d0 = 0; d0 < DP; d0 += 32) {
-            float v[32];
-            tmem_ld32(lane_base + ab * DP + d0, v);
-            stage_out32(smem + C::OFF_OUT, r, d0, v, p.inv_sqrt_d);
-          }
+          for (int d0 = 0; d0 < DP; d0 += 64)  // two 32-column pieces per TMEM wait
+            stage_acc<2>(lane_base + ab * DP, d0, 32, smem + C::OFF_OUT, r, p.inv_sqrt_d);
         }
         tc_fence_before();
         mbar_arrive(&bar_accempty[ab]);
