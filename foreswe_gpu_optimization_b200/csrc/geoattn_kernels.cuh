@@ -621,36 +621,94 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       const Abg ab = load_abg(p, h);
       float m = -INFINITY, l = 0.f;
       // Pass A: running max and sum over this warpgroup's pieces. The max is taken over the raw accumulators
-      // (scaling by a positive constant and rounding are monotonic), the sum from fma(acc, scale, -m).
-      for (int c = 0; c < nchunks && ok; ++c) {
-        const int ss = sc & 1;
-        if (!(ok = warp_wait(&bar_sfull[ss], (sc >> 1) & 1, ctx))) break;
-        tc_fence_after();
+      // (scaling by a positive constant and rounding are monotonic), the sum from fma(acc, scale, -m). The next
+      // chunk's scores are loaded from tensor memory while this chunk's are reduced (two register sets).
+      const int piece = e.wg;
+      auto reduce_a = [&](uint32_t (&u)[32], int c) {
+        float v[32];
 #pragma unroll
-        for (int piece = e.wg; piece < T::PIECES; piece += T::EW) {
-          float v[32];
-          tmem_ld32(e.lane_base + C::TM_S + ss * T::CH + piece * 32, v);
-          tc_fence_before();
-          mbar_arrive(&bar_sempty[ss]);  // the scores are in registers: the MMA may refill the buffer
-          const int nvalid = p.N - (c * T::CH + piece * 32);  // >= 32: no masked column in this piece
-          if (nvalid < 32) {
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(u[j]);
+        const int nvalid = p.N - (c * T::CH + piece * 32);  // >= 32: no masked column in this piece
+        if (nvalid < 32) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = (j < nvalid) ? v[j] : -INFINITY;
-          }
-          // four independent partial maxima / sums keep the dependency chains short
-          float mx4[4] = {v[0], v[1], v[2], v[3]};
-#pragma unroll
-          for (int j = 4; j < 32; ++j) mx4[j & 3] = fmaxf(mx4[j & 3], v[j]);
-          const float mn = fmaxf(m, fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * sc_l2);
-          // a warpgroup whose columns so far are all masked keeps m = -inf, l = 0 (never 2^(-inf - -inf))
-          const float mref = (mn == -INFINITY) ? 0.f : mn;
-          float s4[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-          for (int j = 0; j < 32; ++j) s4[j & 3] += ex2(fmaf(v[j], sc_l2, -mref));
-          l = l * ex2(m - mref) + ((s4[0] + s4[1]) + (s4[2] + s4[3]));
-          m = mn;
+          for (int j = 0; j < 32; ++j) v[j] = (j < nvalid) ? v[j] : -INFINITY;
         }
-        ++sc;
+        // four independent partial maxima / sums keep the dependency chains short
+        float mx4[4] = {v[0], v[1], v[2], v[3]};
+#pragma unroll
+        for (int j = 4; j < 32; ++j) mx4[j & 3] = fmaxf(mx4[j & 3], v[j]);
+        const float mn = fmaxf(m, fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * sc_l2);
+        // a warpgroup whose columns so far are all masked keeps m = -inf, l = 0 (never 2^(-inf - -inf))
+        const float mref = (mn == -INFINITY) ? 0.f : mn;
+        float s4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int j = 0; j < 32; ++j) s4[j & 3] += ex2(fmaf(v[j], sc_l2, -mref));
+        l = l * ex2(m - mref) + ((s4[0] + s4[1]) + (s4[2] + s4[3]));
+        m = mn;
+      };
+      // two chunks' scores (c, c + 1) reduced together: one max over 64 values, then 64 independent exp2
+      auto reduce_pair = [&](uint32_t (&u0)[32], uint32_t (&u1)[32], int c) {
+        float v[64];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          v[j] = __uint_as_float(u0[j]);
+          v[32 + j] = __uint_as_float(u1[j]);
+        }
+        const int nv0 = p.N - (c * T::CH + piece * 32), nv1 = nv0 - T::CH;
+        if (nv1 < 32) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            v[j] = (j < nv0) ? v[j] : -INFINITY;
+            v[32 + j] = (j < nv1) ? v[32 + j] : -INFINITY;
+          }
+        }
+        float mx8[8] = {v[0], v[1], v[2], v[3], v[4], v[5], v[6], v[7]};
+#pragma unroll
+        for (int j = 8; j < 64; ++j) mx8[j & 7] = fmaxf(mx8[j & 7], v[j]);
+        const float mxa = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                                fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+        const float mn = fmaxf(m, mxa * sc_l2);
+        const float mref = (mn == -INFINITY) ? 0.f : mn;
+        float s8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int j = 0; j < 64; ++j) s8[j & 7] += ex2(fmaf(v[j], sc_l2, -mref));
+        l = l * ex2(m - mref) + (((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7])));
+        m = mn;
+      };
+      // waits for chunk c's scores (global count g) and issues their load into u
+      // waits for chunk c's scores (global count g) and issues their load into u
+      auto load_s = [&](int g, uint32_t (&u)[32]) -> bool {
+        if (!warp_wait(&bar_sfull[g & 1], (g >> 1) & 1, ctx)) return false;
+        tc_fence_after();
+        tmem_ld32_issue(e.lane_base + C::TM_S + (g & 1) * T::CH + piece * 32, u);
+        return true;
+      };
+      // the loaded scores are in registers: the MMA may refill their buffer
+      auto release_s = [&](int g, uint32_t (&u)[32]) {
+        tmem_wait32(u);
+        tc_fence_before();
+        mbar_arrive(&bar_sempty[g & 1]);
+      };
+      {
+        // chunks in pairs: both chunks' scores are loaded, then reduced together (64 independent values per thread)
+        uint32_t ua[32], ub[32];
+        const int g0 = sc;
+        for (int c = 0; c < nchunks && ok; c += 2) {
+          const bool two = c + 1 < nchunks;
+          if (!(ok = load_s(g0 + c, ua))) break;
+          if (two && !(ok = load_s(g0 + c + 1, ub))) break;
+          release_s(g0 + c, ua);
+          if (two) {
+            tc_fence_before();
+            mbar_arrive(&bar_sempty[(g0 + c + 1) & 1]);
+            tmem_pin32(ub);
+            reduce_pair(ua, ub, c);
+          } else {
+            reduce_a(ua, c);
+          }
+        }
+        tmem_wait_all();  // no load stays in flight past the loop (aborted paths included)
+        sc += nchunks;
       }
       if constexpr (T::EW > 1) {  // combine the warpgroups' statistics (same order in every warpgroup)
         xch[0][e.wg][e.r] = m;
@@ -680,8 +738,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         tc_fence_after();
         uint8_t* preg = smem + C::OFF_P + ps * C::P_BYTES;
         const uint8_t* prt = smem + C::OFF_PR + prs * kPriorTileBytes;
-#pragma unroll
-        for (int piece = e.wg; piece < T::PIECES; piece += T::EW) {
+        {
           uint32_t vs[32];
           float v[32];
           Prior32<BF16> pr;
@@ -716,7 +773,6 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
           if (!(ok = warp_wait(&bar_pempty[ps], ((pc >> 1) & 1) ^ 1, ctx))) break;
           stage_row32<BF16>(preg, e.r, piece, v);
         }
-        if (!ok) break;
         fence_proxy_async_smem();
         mbar_arrive(&bar_pfull[ps]);
         ++sc;

@@ -236,6 +236,9 @@ __device__ __forceinline__ void tmem_wait32(uint32_t (&r)[32]) {
                :
                : "memory");
 }
+// Waits for every outstanding TMEM load of this thread (no values pinned).
+__device__ __forceinline__ void tmem_wait_all() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
 // Pin values loaded by an earlier tmem_ld32_issue behind a wait that has already been issued (no instruction).
 __device__ __forceinline__ void tmem_pin32(uint32_t (&r)[32]) {
   asm volatile(""
