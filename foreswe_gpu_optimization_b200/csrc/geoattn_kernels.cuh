@@ -458,9 +458,12 @@ struct FwdCfg : Tile<BF16, DP> {
   static constexpr int OFF_P = OFF_V + 2 * V_BYTES;
   static constexpr int OFF_PR = OFF_P + 2 * P_BYTES;
   static constexpr int SMEM = OFF_PR + NPR * kPriorTileBytes;
+  // 4 score buffers in tensor memory: the MMA warp runs up to 3 chunks ahead of the element-wise warps, and the
+  // last score MMA of a tile (which frees Q for the next tile) issues ~3 chunks before the tile ends
+  static constexpr int NSB = 4;
   static constexpr int TM_S = 0;
-  static constexpr int TM_O = 2 * T::CH;
-  static constexpr int TMEM_COLS = pow2_cols(2 * T::CH + DP);
+  static constexpr int TM_O = NSB * T::CH;
+  static constexpr int TMEM_COLS = pow2_cols(NSB * T::CH + DP);
   // O leaves through the two P buffers (free once the tile's last P.V has run) when they hold the whole row block
   static constexpr bool EPI_TMA = BF16 && T::NKB * kBM * 128 <= 2 * P_BYTES;
 };
@@ -470,12 +473,12 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
     geoattn_fwd_kernel(const __grid_constant__ TileMaps maps, const KParams p) {
   using C = FwdCfg<BF16, DP>;
   using T = typename C::T;
-  constexpr int NPR = C::NPR, NK = C::NK;
+  constexpr int NPR = C::NPR, NK = C::NK, NSB = C::NSB;
   static_assert(!C::EPI_TMA || T::EW > 1, "the TMA epilogue relies on the warpgroup exchange barrier");
   if (smem_misaligned(p.status)) return;  // uniform over the CTA, before any barrier or allocation
   uint8_t* smem = smem_raw;
-  __shared__ uint64_t bar_qfull, bar_qempty, bar_kfull[3], bar_kempty[3], bar_vfull[2], bar_vempty[2], bar_sfull[2],
-      bar_sempty[2], bar_pfull[2], bar_pempty[2], bar_prfull[2], bar_prempty[2], bar_ofull;
+  __shared__ uint64_t bar_qfull, bar_qempty, bar_kfull[3], bar_kempty[3], bar_vfull[2], bar_vempty[2], bar_sfull[4],
+      bar_sempty[4], bar_pfull[2], bar_pempty[2], bar_prfull[2], bar_prempty[2], bar_ofull;
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_flag;
   __shared__ float xch[3][Tile<BF16, DP>::EW][kBM];  // cross-warpgroup row statistics: m, l1, l2
@@ -493,11 +496,13 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       mbar_init(&bar_kfull[i], 1);
       mbar_init(&bar_kempty[i], 1);
     }
+    for (int i = 0; i < 4; ++i) {
+      mbar_init(&bar_sfull[i], 1);
+      mbar_init(&bar_sempty[i], T::EWT);
+    }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bar_vfull[i], 1);
       mbar_init(&bar_vempty[i], 1);
-      mbar_init(&bar_sfull[i], 1);
-      mbar_init(&bar_sempty[i], T::EWT);
       mbar_init(&bar_pfull[i], T::EWT);
       mbar_init(&bar_pempty[i], 1);
       mbar_init(&bar_prfull[i], 1);
@@ -536,6 +541,19 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
             prefetch_rows<T>(&maps.k, p.N, nh, nb, p.B, T::PL);
             if constexpr (BF16) prefetch_rows<T>(&maps.v, p.N, nh, nb, p.B, 1);
           }
+          // pass B in the MMA warp's order: K of chunk c, then V of chunk c - (NSB - 1), whose P.V MMA follows
+          // the score MMA of chunk c
+          auto load_v = [&](int cv) -> bool {
+            const int vs = vc & 1;
+            if (!mbar_wait(&bar_vempty[vs], ((vc >> 1) & 1) ^ 1, ctx)) return false;
+            mbar_arrive_expect_tx(&bar_vfull[vs], C::V_BYTES);
+            if constexpr (BF16)
+              tma_tile<T>(smem + C::OFF_V + vs * C::V_BYTES, &maps.v, &bar_vfull[vs], T::CH, cv * T::CH, h, b, p.B, 1);
+            else
+              tma_tileT(smem + C::OFF_V + vs * C::V_BYTES, &maps.v, &bar_vfull[vs], cv * T::CH, h, b);
+            ++vc;
+            return true;
+          };
           for (int c = 0; c < nchunks && ok; ++c) {
             const int ks = kc % NK;
             if (!(ok = mbar_wait(&bar_kempty[ks], ((kc / NK) & 1) ^ 1, ctx))) break;
@@ -543,17 +561,11 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
             tma_tile<T>(smem + C::OFF_K + ks * T::PL * C::K_BYTES, &maps.k, &bar_kfull[ks], T::CH, c * T::CH, h, b,
                         p.B, T::PL);
             ++kc;
-            if (pass == 1) {
-              const int vs = vc & 1;
-              if (!(ok = mbar_wait(&bar_vempty[vs], ((vc >> 1) & 1) ^ 1, ctx))) break;
-              mbar_arrive_expect_tx(&bar_vfull[vs], C::V_BYTES);
-              if constexpr (BF16)
-                tma_tile<T>(smem + C::OFF_V + vs * C::V_BYTES, &maps.v, &bar_vfull[vs], T::CH, c * T::CH, h, b, p.B, 1);
-              else
-                tma_tileT(smem + C::OFF_V + vs * C::V_BYTES, &maps.v, &bar_vfull[vs], c * T::CH, h, b);
-              ++vc;
-            }
+            if (pass == 1 && c >= C::NSB - 1) ok = load_v(c - (C::NSB - 1));
           }
+          if (pass == 1)
+            for (int cv = nchunks - (C::NSB - 1); cv < nchunks && ok; ++cv)
+              if (cv >= 0) ok = load_v(cv);
         }
       }
     }
@@ -578,9 +590,9 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       int kc = 0, sc = 0, pc = 0, it = 0;
       bool ok = true;
       auto issue_s = [&](void) -> bool {
-        const int ks = kc % NK, ss = sc & 1;
+        const int ks = kc % NK, ss = sc % NSB;
         if (!mbar_wait(&bar_kfull[ks], (kc / NK) & 1, ctx)) return false;
-        if (!mbar_wait(&bar_sempty[ss], ((sc >> 1) & 1) ^ 1, ctx)) return false;
+        if (!mbar_wait(&bar_sempty[ss], ((sc / NSB) & 1) ^ 1, ctx)) return false;
         tc_fence_after();
         mma_qk<T, T::CH>(tmem + C::TM_S + ss * T::CH, sbase + C::OFF_Q, C::Q_BYTES,
                          sbase + C::OFF_K + ks * T::PL * C::K_BYTES, C::K_BYTES);
@@ -592,11 +604,18 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       };
       for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++it) {
         if (!(ok = mbar_wait(&bar_qfull, it & 1, ctx))) break;
-        for (int c = 0; c < nchunks && ok; ++c) ok = issue_s();
-        if (ok) ok = issue_s();
+        for (int c = 0; c < nchunks && ok; ++c) ok = issue_s();  // pass A
+        int nb = 0;  // pass-B score MMAs issued
+        // keeps the pass-B scores up to NSB - 1 chunks ahead; Q is released once the tile's last one is issued
+        auto top_up = [&](int upto) -> bool {
+          for (; nb < nchunks && nb < upto; ++nb) {
+            if (!issue_s()) return false;
+            if (nb + 1 == nchunks) mma_commit(&bar_qempty);
+          }
+          return true;
+        };
         for (int c = 0; c < nchunks && ok; ++c) {
-          if (c + 1 < nchunks && !(ok = issue_s())) break;
-          if (c + 1 == nchunks) mma_commit(&bar_qempty);  // every score MMA of this tile has been issued
+          if (!(ok = top_up(c + NSB))) break;
           const int ps = pc & 1;
           if (!(ok = mbar_wait(&bar_pfull[ps], (pc >> 1) & 1, ctx))) break;
           if (!(ok = mbar_wait(&bar_vfull[ps], (pc >> 1) & 1, ctx))) break;
@@ -678,16 +697,16 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       // waits for chunk c's scores (global count g) and issues their load into u
       // waits for chunk c's scores (global count g) and issues their load into u
       auto load_s = [&](int g, uint32_t (&u)[32]) -> bool {
-        if (!warp_wait(&bar_sfull[g & 1], (g >> 1) & 1, ctx)) return false;
+        if (!warp_wait(&bar_sfull[g % NSB], (g / NSB) & 1, ctx)) return false;
         tc_fence_after();
-        tmem_ld32_issue(e.lane_base + C::TM_S + (g & 1) * T::CH + piece * 32, u);
+        tmem_ld32_issue(e.lane_base + C::TM_S + (g % NSB) * T::CH + piece * 32, u);
         return true;
       };
       // the loaded scores are in registers: the MMA may refill their buffer
       auto release_s = [&](int g, uint32_t (&u)[32]) {
         tmem_wait32(u);
         tc_fence_before();
-        mbar_arrive(&bar_sempty[g & 1]);
+        mbar_arrive(&bar_sempty[g % NSB]);
       };
       {
         // chunks in pairs: both chunks' scores are loaded, then reduced together (64 independent values per thread)
@@ -700,7 +719,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
           release_s(g0 + c, ua);
           if (two) {
             tc_fence_before();
-            mbar_arrive(&bar_sempty[(g0 + c + 1) & 1]);
+            mbar_arrive(&bar_sempty[(g0 + c + 1) % NSB]);
             tmem_pin32(ub);
             reduce_pair(ua, ub, c);
           } else {
@@ -732,8 +751,8 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       float l2 = 0.f;
       // Pass B
       for (int c = 0; c < nchunks && ok; ++c) {
-        const int ss = sc & 1, ps = pc & 1, prs = prc % NPR;
-        if (!(ok = warp_wait(&bar_sfull[ss], (sc >> 1) & 1, ctx))) break;
+        const int ss = sc % NSB, ps = pc & 1, prs = prc % NPR;
+        if (!(ok = warp_wait(&bar_sfull[ss], (sc / NSB) & 1, ctx))) break;
         if (!(ok = warp_wait(&bar_prfull[prs], (prc / NPR) & 1, ctx))) break;
         tc_fence_after();
         uint8_t* preg = smem + C::OFF_P + ps * C::P_BYTES;
@@ -847,10 +866,13 @@ struct RowsCfg : Tile<BF16, DP> {
   static constexpr int OFF_PR = OFF_DS + NDS_ALLOC * DS_BYTES;
   static constexpr int OFF_XS = OFF_PR + NPR * kPriorTileBytes;  // without DQ: warpgroup 1's row sums
   static constexpr int SMEM = OFF_XS + (DQ ? 0 : 3 * kBM * 4);
-  static constexpr int TM_S = 0;                   // 2 buffers
-  static constexpr int TM_DP = 2 * T::CH;          // 2 buffers
-  static constexpr int TM_DQ = 4 * T::CH;
-  static constexpr int TMEM_COLS = pow2_cols(4 * T::CH + (DQ ? DP : 0));
+  // S / dP accumulator buffers in tensor memory: 4 without the dQ accumulator, so the MMA warp runs ~3 chunks ahead
+  // and frees Q / dO for the next tile early enough to hide its reload
+  static constexpr int NSB = DQ ? 2 : 4;
+  static constexpr int TM_S = 0;
+  static constexpr int TM_DP = NSB * T::CH;
+  static constexpr int TM_DQ = 2 * NSB * T::CH;
+  static constexpr int TMEM_COLS = pow2_cols(2 * NSB * T::CH + (DQ ? DP : 0));
   // dQ leaves through the dS buffers (free once the tile's last dQ MMA has run) when they hold the whole row block
   static constexpr bool EPI_TMA = DQ && BF16 && T::NKB * kBM * 128 <= NDS * DS_BYTES;
 };
@@ -867,11 +889,11 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
   static_assert(DQ || BF16, "the dS-scratch backward is bf16 only");
   using C = RowsCfg<BF16, DP, DQ>;
   using T = typename C::T;
-  constexpr int NKV = C::NKV, NPR = C::NPR;
+  constexpr int NKV = C::NKV, NPR = C::NPR, NSB = C::NSB;
   if (smem_misaligned(p.status)) return;  // uniform over the CTA, before any barrier or allocation
   uint8_t* smem = smem_raw;
-  __shared__ uint64_t bar_qfull, bar_qempty, bar_kfull[3], bar_kempty[3], bar_vfull[3], bar_vempty[3], bar_sfull[2],
-      bar_sempty[2], bar_dsfull[2], bar_dsempty[2], bar_ktfull[2], bar_ktempty[2], bar_prfull[2], bar_prempty[2], bar_dqfull;
+  __shared__ uint64_t bar_qfull, bar_qempty, bar_kfull[3], bar_kempty[3], bar_vfull[3], bar_vempty[3], bar_sfull[4],
+      bar_sempty[4], bar_dsfull[2], bar_dsempty[2], bar_ktfull[2], bar_ktempty[2], bar_prfull[2], bar_prempty[2], bar_dqfull;
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_flag;
   __shared__ double red[8][3];
@@ -892,9 +914,11 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       mbar_init(&bar_vfull[i], 1);
       mbar_init(&bar_vempty[i], 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < 4; ++i) {
       mbar_init(&bar_sfull[i], 1);
       mbar_init(&bar_sempty[i], T::EWT);
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&bar_dsfull[i], T::EWT);
       mbar_init(&bar_dsempty[i], 1);
       mbar_init(&bar_ktfull[i], 1);
@@ -986,10 +1010,10 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       int kc = 0, sc = 0, dc = 0, it = 0;
       bool ok = true;
       auto issue = [&](bool release_k) -> bool {
-        const int ks = kc % NKV, ss = sc & 1;
+        const int ks = kc % NKV, ss = sc % NSB;
         if (!mbar_wait(&bar_kfull[ks], (kc / NKV) & 1, ctx)) return false;
         if (!mbar_wait(&bar_vfull[ks], (kc / NKV) & 1, ctx)) return false;
-        if (!mbar_wait(&bar_sempty[ss], ((sc >> 1) & 1) ^ 1, ctx)) return false;
+        if (!mbar_wait(&bar_sempty[ss], ((sc / NSB) & 1) ^ 1, ctx)) return false;
         tc_fence_after();
         const uint32_t kb = sbase + C::OFF_K + ks * T::PL * C::K_BYTES;
         const uint32_t vb = sbase + C::OFF_V + ks * T::PL * C::K_BYTES;
@@ -1080,8 +1104,8 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
     }
     float acc[3] = {0.f, 0.f, 0.f};  // delta2, a, b
     for (int c = 0; c < nchunks && ok; ++c) {
-      const int ss = sc & 1, prs = pc % NPR;
-      if (!(ok = warp_wait(&bar_sfull[ss], (sc >> 1) & 1, ctx))) break;
+      const int ss = sc % NSB, prs = pc % NPR;
+      if (!(ok = warp_wait(&bar_sfull[ss], (sc / NSB) & 1, ctx))) break;
       if (!(ok = warp_wait(&bar_prfull[prs], (pc / NPR) & 1, ctx))) break;
       tc_fence_after();
       const uint8_t* prt = smem + C::OFF_PR + prs * kPriorTileBytes;
@@ -1169,8 +1193,8 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
     float gbp[2] = {0.f, 0.f}, ggp[2] = {0.f, 0.f};  // d(beta), d(gamma) partials of the row
     if constexpr (DQ) {
     for (int c = 0; c < nchunks && ok; ++c) {
-      const int ss = sc & 1, ds = dc % C::NDS, prs = pc % NPR;
-      if (!(ok = warp_wait(&bar_sfull[ss], (sc >> 1) & 1, ctx))) break;
+      const int ss = sc % NSB, ds = dc % C::NDS, prs = pc % NPR;
+      if (!(ok = warp_wait(&bar_sfull[ss], (sc / NSB) & 1, ctx))) break;
       if (!(ok = warp_wait(&bar_prfull[prs], (pc / NPR) & 1, ctx))) break;
       tc_fence_after();
       uint8_t* dreg = smem + C::OFF_DS + ds * C::DS_BYTES;
