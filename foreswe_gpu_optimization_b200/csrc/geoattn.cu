@@ -214,13 +214,8 @@ int check_shape(const GeoAttnShape* s, Dims& d) {
   d.nrb = (d.N + kBM - 1) / kBM;
   d.np = d.nrb * kBM;
   d.nabg = s->per_head ? d.H : 1;
-  if (d.bf16) {
-    if (d.D > 192) return GEOATTN_ERR_UNSUPPORTED;
-    d.DP = d.D <= 64 ? 64 : d.D <= 128 ? 128 : 192;
-  } else {
-    if (d.D > 64) return GEOATTN_ERR_UNSUPPORTED;
-    d.DP = 64;
-  }
+  if (d.D > 192) return GEOATTN_ERR_UNSUPPORTED;
+  d.DP = d.D <= 64 ? 64 : d.D <= 128 ? 128 : 192;
   if ((long long)d.nrb * d.B * d.H > (1ll << 30)) return GEOATTN_ERR_UNSUPPORTED;  // tile index fits an int
   return GEOATTN_OK;
 }
@@ -451,7 +446,7 @@ const char* geoattn_error_string(int code) {
   switch (code) {
     case GEOATTN_OK: return "ok";
     case GEOATTN_ERR_INVALID: return "invalid argument (null pointer, non-positive size or unknown enum)";
-    case GEOATTN_ERR_UNSUPPORTED: return "unsupported shape/dtype (bf16: head_dim <= 192, fp32: head_dim <= 64)";
+    case GEOATTN_ERR_UNSUPPORTED: return "unsupported shape/dtype (head_dim <= 192)";
     case GEOATTN_ERR_ALIGNMENT: return "tensor not TMA-compatible (head dim must be contiguous, base and strides 16-byte aligned)";
     case GEOATTN_ERR_TMA: return "TMA descriptor encoding failed";
     case GEOATTN_ERR_LAUNCH: return "CUDA kernel launch failed";
@@ -556,7 +551,9 @@ int geoattn_fwd(const GeoAttnFwdArgs* a, void* stream) {
     if (d.DP == 128) return run_fwd<true, 128>(maps, p, d, st, a->events);
     return run_fwd<true, 192>(maps, p, d, st, a->events);
   }
-  return run_fwd<false, 64>(maps, p, d, st, a->events);
+  if (d.DP == 64) return run_fwd<false, 64>(maps, p, d, st, a->events);
+  if (d.DP == 128) return run_fwd<false, 128>(maps, p, d, st, a->events);
+  return run_fwd<false, 192>(maps, p, d, st, a->events);
 }
 
 }  // extern "C"
@@ -639,7 +636,9 @@ int backward(const GeoAttnBwdArgs* a, void* stream, bool with_ds) {
     else if (d.DP == 128) rc = run_bwd<true, 128>(rm, cm, prow, pcol, d, st, a->events);
     else rc = run_bwd<true, 192>(rm, cm, prow, pcol, d, st, a->events);
   } else {
-    rc = run_bwd<false, 64>(rm, cm, prow, pcol, d, st, a->events);
+    if (d.DP == 64) rc = run_bwd<false, 64>(rm, cm, prow, pcol, d, st, a->events);
+    else if (d.DP == 128) rc = run_bwd<false, 128>(rm, cm, prow, pcol, d, st, a->events);
+    else rc = run_bwd<false, 192>(rm, cm, prow, pcol, d, st, a->events);
   }
   if (rc) return rc;
   finalize_abg_kernel<<<dim3(3, d.nabg), 256, 0, st>>>(ws.part, d.B, d.H, d.nrb, a->shape.per_head, a->dabg);

@@ -27,6 +27,7 @@
 namespace geoattn {
 
 constexpr int kBM = 128;        // rows per tile (TMEM lanes)
+constexpr int kSmemPerBlock = 227 * 1024;  // opt-in shared memory per block (static + dynamic)
 
 // Dynamic shared memory of every attention kernel. The 1024-byte alignment (what the 128-byte-swizzled TMA and MMA
 // tiles need) is part of the declaration: the compiler pads the static shared data in front of it to a multiple of
@@ -302,14 +303,15 @@ __device__ __forceinline__ Ew ew_id(uint32_t tmem) {
   return e;
 }
 
-// Issue acc[128 x NB] (+)= A[128 x DP] . B[NB x DP]^T, both K-major, regions of 128 x 128 B (A) and NB x 128 B (B).
-// With NTERM == 3 the product is hi*hi + hi*lo + lo*hi (planes 0/1 at a_plane/b_plane byte strides).
-template <class T, int NB>
+// Issue acc[128 x NB] (+)= A[128 x KD] . B[NB x KD]^T, both K-major, regions of 128 x 128 B (A) and NB x 128 B (B);
+// KD = DP (the whole head dimension) or KB (one 128-byte head-dim chunk, added to the accumulator when
+// `accumulate`). With NTERM == 3 the product is hi*hi + hi*lo + lo*hi (planes 0/1 at a_plane/b_plane byte strides).
+template <class T, int NB, int KD = T::DP>
 __device__ __forceinline__ void mma_qk(uint32_t tmem_acc, uint32_t a_base, uint32_t a_plane, uint32_t b_base,
-                                       uint32_t b_plane) {
+                                       uint32_t b_plane, bool accumulate = false) {
   constexpr uint32_t idesc = instr_desc(T::FMT, 0, 0, 128, NB);
-  constexpr int STEPS = T::DP / T::KS;
-  int first = 1;
+  constexpr int STEPS = KD / T::KS;
+  int first = accumulate ? 0 : 1;
 #pragma unroll
   for (int term = 0; term < T::NTERM; ++term) {
     const uint32_t ap = (term == 2) ? a_plane : 0;  // (hi,hi), (hi,lo), (lo,hi)
@@ -359,6 +361,23 @@ __device__ __forceinline__ void tma_tile(uint8_t* dst, const CUtensorMap* map, u
   for (int pl = 0; pl < npl; ++pl)
     for (int kb = 0; kb < T::NKB; ++kb)
       tma_load_4d(dst + (size_t)(pl * T::NKB + kb) * nrows * 128, map, bar, kb * T::KB, row0, h, b + pl * B);
+}
+// fp32 head dims above 64 ("wide"): the score-shaped products stream their operands through a ring of slots, each
+// holding one 32-wide head-dim chunk dc of a 128-row A tile and of a CH-row B chunk, hi and lo planes:
+// [plane 0: A (128 x 128 B) | B (CH x 128 B)][plane 1: A | B]. The MMA accumulates the chunks' products.
+constexpr int kSlotPlaneBytes = (kBM + 32) * 128;
+template <class T>
+__device__ __forceinline__ void tma_slot(uint8_t* slot, uint64_t* bar, const CUtensorMap* amap, int arow0,
+                                         const CUtensorMap* bmap, int brow0, int dc, int h, int b, int B) {
+  for (int pl = 0; pl < 2; ++pl) {
+    tma_load_4d(slot + pl * kSlotPlaneBytes, amap, bar, dc * T::KB, arow0, h, b + pl * B);
+    tma_load_4d(slot + pl * kSlotPlaneBytes + kBM * 128, bmap, bar, dc * T::KB, brow0, h, b + pl * B);
+  }
+}
+template <class T>
+__device__ __forceinline__ void mma_slot(uint32_t tmem_acc, uint32_t slot, bool accumulate) {
+  static_assert(!T::kBF16 && T::CH == 32, "slots carry fp32 planes with 32-row B chunks");
+  mma_qk<T, T::CH, T::KB>(tmem_acc, slot, kSlotPlaneBytes, slot + kBM * 128, kSlotPlaneBytes, accumulate);
 }
 // Transposed fp32 plane chunk: DP rows (d) x 32 columns (n) starting at column n0 -> one region of DP x 128 B.
 __device__ __forceinline__ void tma_tileT(uint8_t* dst, const CUtensorMap* map, uint64_t* bar, int n0, int h, int b) {
@@ -446,10 +465,13 @@ __device__ __forceinline__ void prior_piece(const uint8_t* tile, const void* tab
 template <bool BF16, int DP>
 struct FwdCfg : Tile<BF16, DP> {
   using T = Tile<BF16, DP>;
-  static constexpr int NPR = (BF16 && DP > 128) ? 1 : 2;  // staged prior buffers
-  static constexpr int NK = (BF16 && DP <= 128) ? 3 : 2;    // K chunk buffers (pass A outruns a 2-deep ring)
-  static constexpr int Q_BYTES = kBM * DP * T::EB;          // per plane
-  static constexpr int K_BYTES = T::CH * DP * T::EB;        // per plane per buffer
+  // fp32 beyond 64: no resident Q; Q and K reach the score MMA in head-dim chunks through the K ring's slots
+  static constexpr bool WIDE = !BF16 && DP > 64;
+  static constexpr int NDC = WIDE ? DP / T::KB : 1;                    // head-dim chunks per score MMA
+  static constexpr int NPR = (WIDE || (BF16 && DP > 128)) ? 1 : 2;   // staged prior buffers
+  static constexpr int NK = ((WIDE && DP <= 128) || (BF16 && DP <= 128)) ? 3 : 2;  // K ring slots
+  static constexpr int Q_BYTES = WIDE ? 0 : kBM * DP * T::EB;          // per plane
+  static constexpr int K_BYTES = WIDE ? kSlotPlaneBytes : T::CH * DP * T::EB;  // per plane per ring slot
   static constexpr int V_BYTES = T::CH * DP * T::EB;        // hi only (natural bf16 / transposed fp32)
   static constexpr int P_BYTES = kBM * 128;
   static constexpr int OFF_Q = 0;
@@ -458,6 +480,7 @@ struct FwdCfg : Tile<BF16, DP> {
   static constexpr int OFF_P = OFF_V + 2 * V_BYTES;
   static constexpr int OFF_PR = OFF_P + 2 * P_BYTES;
   static constexpr int SMEM = OFF_PR + NPR * kPriorTileBytes;
+  static_assert(SMEM + 4096 <= kSmemPerBlock, "forward: dynamic + static shared memory above the per-block limit");
   // 4 score buffers in tensor memory: the MMA warp runs up to 3 chunks ahead of the element-wise warps, and the
   // last score MMA of a tile (which frees Q for the next tile) issues ~3 chunks before the tile ends
   static constexpr int NSB = 4;
@@ -530,10 +553,11 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       bool ok = true;
       for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++it) {
         const int rb = tile % p.nrb, bh = tile / p.nrb, b = bh / p.H, h = bh % p.H;
-        // Q of this tile once the previous tile's last score MMA has read the old one
-        if (!(ok = mbar_wait(&bar_qempty, (it & 1) ^ 1, ctx))) break;
-        mbar_arrive_expect_tx(&bar_qfull, T::PL * C::Q_BYTES);
-        tma_tile<T>(smem + C::OFF_Q, &maps.q, &bar_qfull, kBM, rb * kBM, h, b, p.B, T::PL);
+        if constexpr (!C::WIDE) {  // Q of this tile once the previous tile's last score MMA has read the old one
+          if (!(ok = mbar_wait(&bar_qempty, (it & 1) ^ 1, ctx))) break;
+          mbar_arrive_expect_tx(&bar_qfull, T::PL * C::Q_BYTES);
+          tma_tile<T>(smem + C::OFF_Q, &maps.q, &bar_qfull, kBM, rb * kBM, h, b, p.B, T::PL);
+        }
         for (int pass = 0; pass < 2 && ok; ++pass) {
           if (pass == 1 && tile + (int)gridDim.x < ntiles) {  // next tile's operands into L2
             const int nt = tile + gridDim.x, nbh = nt / p.nrb, nb = nbh / p.H, nh = nbh % p.H;
@@ -555,13 +579,18 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
             return true;
           };
           for (int c = 0; c < nchunks && ok; ++c) {
-            const int ks = kc % NK;
-            if (!(ok = mbar_wait(&bar_kempty[ks], ((kc / NK) & 1) ^ 1, ctx))) break;
-            mbar_arrive_expect_tx(&bar_kfull[ks], T::PL * C::K_BYTES);
-            tma_tile<T>(smem + C::OFF_K + ks * T::PL * C::K_BYTES, &maps.k, &bar_kfull[ks], T::CH, c * T::CH, h, b,
-                        p.B, T::PL);
-            ++kc;
-            if (pass == 1 && c >= C::NSB - 1) ok = load_v(c - (C::NSB - 1));
+            for (int dc = 0; dc < C::NDC && ok; ++dc) {
+              const int ks = kc % NK;
+              if (!(ok = mbar_wait(&bar_kempty[ks], ((kc / NK) & 1) ^ 1, ctx))) break;
+              mbar_arrive_expect_tx(&bar_kfull[ks], T::PL * C::K_BYTES);
+              uint8_t* slot = smem + C::OFF_K + ks * T::PL * C::K_BYTES;
+              if constexpr (C::WIDE)
+                tma_slot<T>(slot, &bar_kfull[ks], &maps.q, rb * kBM, &maps.k, c * T::CH, dc, h, b, p.B);
+              else
+                tma_tile<T>(slot, &maps.k, &bar_kfull[ks], T::CH, c * T::CH, h, b, p.B, T::PL);
+              ++kc;
+            }
+            if (ok && pass == 1 && c >= C::NSB - 1) ok = load_v(c - (C::NSB - 1));
           }
           if (pass == 1)
             for (int cv = nchunks - (C::NSB - 1); cv < nchunks && ok; ++cv)
@@ -590,27 +619,41 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       int kc = 0, sc = 0, pc = 0, it = 0;
       bool ok = true;
       auto issue_s = [&](void) -> bool {
-        const int ks = kc % NK, ss = sc % NSB;
-        if (!mbar_wait(&bar_kfull[ks], (kc / NK) & 1, ctx)) return false;
-        if (!mbar_wait(&bar_sempty[ss], ((sc / NSB) & 1) ^ 1, ctx)) return false;
-        tc_fence_after();
-        mma_qk<T, T::CH>(tmem + C::TM_S + ss * T::CH, sbase + C::OFF_Q, C::Q_BYTES,
-                         sbase + C::OFF_K + ks * T::PL * C::K_BYTES, C::K_BYTES);
+        const int ss = sc % NSB;
+        if constexpr (C::WIDE) {
+          if (!mbar_wait(&bar_sempty[ss], ((sc / NSB) & 1) ^ 1, ctx)) return false;
+          for (int dc = 0; dc < C::NDC; ++dc) {
+            const int ks = kc % NK;
+            if (!mbar_wait(&bar_kfull[ks], (kc / NK) & 1, ctx)) return false;
+            tc_fence_after();
+            mma_slot<T>(tmem + C::TM_S + ss * T::CH, sbase + C::OFF_K + ks * T::PL * C::K_BYTES, dc > 0);
+            mma_commit(&bar_kempty[ks]);
+            ++kc;
+          }
+        } else {
+          const int ks = kc % NK;
+          if (!mbar_wait(&bar_kfull[ks], (kc / NK) & 1, ctx)) return false;
+          if (!mbar_wait(&bar_sempty[ss], ((sc / NSB) & 1) ^ 1, ctx)) return false;
+          tc_fence_after();
+          mma_qk<T, T::CH>(tmem + C::TM_S + ss * T::CH, sbase + C::OFF_Q, C::Q_BYTES,
+                           sbase + C::OFF_K + ks * T::PL * C::K_BYTES, C::K_BYTES);
+          mma_commit(&bar_kempty[ks]);
+          ++kc;
+        }
         mma_commit(&bar_sfull[ss]);
-        mma_commit(&bar_kempty[ks]);
-        ++kc;
         ++sc;
         return true;
       };
       for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++it) {
-        if (!(ok = mbar_wait(&bar_qfull, it & 1, ctx))) break;
+        if constexpr (!C::WIDE)
+          if (!(ok = mbar_wait(&bar_qfull, it & 1, ctx))) break;
         for (int c = 0; c < nchunks && ok; ++c) ok = issue_s();  // pass A
         int nb = 0;  // pass-B score MMAs issued
         // keeps the pass-B scores up to NSB - 1 chunks ahead; Q is released once the tile's last one is issued
         auto top_up = [&](int upto) -> bool {
           for (; nb < nchunks && nb < upto; ++nb) {
             if (!issue_s()) return false;
-            if (nb + 1 == nchunks) mma_commit(&bar_qempty);
+            if (!C::WIDE && nb + 1 == nchunks) mma_commit(&bar_qempty);
           }
           return true;
         };
@@ -694,7 +737,6 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         l = l * ex2(m - mref) + (((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7])));
         m = mn;
       };
-      // waits for chunk c's scores (global count g) and issues their load into u
       // waits for chunk c's scores (global count g) and issues their load into u
       auto load_s = [&](int g, uint32_t (&u)[32]) -> bool {
         if (!warp_wait(&bar_sfull[g % NSB], (g / NSB) & 1, ctx)) return false;
@@ -849,10 +891,14 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
 template <bool BF16, int DP, bool DQ = true>
 struct RowsCfg : Tile<BF16, DP> {
   using T = Tile<BF16, DP>;
-  static constexpr int NKV = (!BF16 || DP > 128) ? 1 : (DQ ? 2 : 3);  // K/V chunk buffers
+  // fp32 beyond 64: no resident Q / dO; (Q, K) and (dO, V) reach the S and dP MMAs in head-dim chunks through the
+  // K ring's slots (the V ring is unused)
+  static constexpr bool WIDE = !BF16 && DP > 64;
+  static constexpr int NDC = WIDE ? DP / T::KB : 1;
+  static constexpr int NKV = WIDE ? 3 : (!BF16 || DP > 128) ? 1 : (DQ ? 2 : 3);  // K/V chunk buffers / ring slots
   static constexpr int NPR = (BF16 && DP <= 128) ? 2 : 1;   // staged prior buffers
-  static constexpr int Q_BYTES = kBM * DP * T::EB;    // per plane (Q and dO)
-  static constexpr int K_BYTES = T::CH * DP * T::EB;  // per plane per buffer (K and V chunks)
+  static constexpr int Q_BYTES = WIDE ? 0 : kBM * DP * T::EB;                   // per plane (Q and dO)
+  static constexpr int K_BYTES = WIDE ? kSlotPlaneBytes : T::CH * DP * T::EB;  // per plane per buffer / slot
   static constexpr int KT_BYTES = BF16 ? 0 : DP * 128;  // fp32: transposed K chunk (hi) for dQ
   static constexpr int DS_BYTES = kBM * 128;
   static constexpr int NDS = BF16 ? 2 : 1;            // dS / K^T buffers (ring size)
@@ -861,11 +907,12 @@ struct RowsCfg : Tile<BF16, DP> {
   static constexpr int OFF_DO = OFF_Q + T::PL * Q_BYTES;
   static constexpr int OFF_K = OFF_DO + T::PL * Q_BYTES;
   static constexpr int OFF_V = OFF_K + NKV * T::PL * K_BYTES;
-  static constexpr int OFF_KT = OFF_V + NKV * T::PL * K_BYTES;
+  static constexpr int OFF_KT = OFF_V + (WIDE ? 0 : NKV * T::PL * K_BYTES);
   static constexpr int OFF_DS = OFF_KT + NDS_ALLOC * KT_BYTES;
   static constexpr int OFF_PR = OFF_DS + NDS_ALLOC * DS_BYTES;
   static constexpr int OFF_XS = OFF_PR + NPR * kPriorTileBytes;  // without DQ: warpgroup 1's row sums
   static constexpr int SMEM = OFF_XS + (DQ ? 0 : 3 * kBM * 4);
+  static_assert(SMEM + 1024 <= kSmemPerBlock, "row pass: dynamic + static shared memory above the per-block limit");
   // S / dP accumulator buffers in tensor memory: 4 without the dQ accumulator, so the MMA warp runs ~3 chunks ahead
   // and frees Q / dO for the next tile early enough to hide its reload
   static constexpr int NSB = DQ ? 2 : 4;
@@ -949,11 +996,12 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       bool ok = true;
       for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++it) {
       const int rb = tile % p.nrb, bh = tile / p.nrb, b = bh / p.H, h = bh % p.H;
-      // Q and dO of this tile once the previous tile's last S/dP MMAs have read the old ones
-      if (!(ok = mbar_wait(&bar_qempty, (it & 1) ^ 1, ctx))) break;
-      mbar_arrive_expect_tx(&bar_qfull, 2 * T::PL * C::Q_BYTES);
-      tma_tile<T>(smem + C::OFF_Q, &maps.q, &bar_qfull, kBM, rb * kBM, h, b, p.B, T::PL);
-      tma_tile<T>(smem + C::OFF_DO, &maps.dout, &bar_qfull, kBM, rb * kBM, h, b, p.B, T::PL);
+      if constexpr (!C::WIDE) {  // Q and dO of this tile once the previous tile's last S/dP MMAs have read the old ones
+        if (!(ok = mbar_wait(&bar_qempty, (it & 1) ^ 1, ctx))) break;
+        mbar_arrive_expect_tx(&bar_qfull, 2 * T::PL * C::Q_BYTES);
+        tma_tile<T>(smem + C::OFF_Q, &maps.q, &bar_qfull, kBM, rb * kBM, h, b, p.B, T::PL);
+        tma_tile<T>(smem + C::OFF_DO, &maps.dout, &bar_qfull, kBM, rb * kBM, h, b, p.B, T::PL);
+      }
       for (int sweep = 0; sweep < SWEEPS && ok; ++sweep) {
         if (sweep == SWEEPS - 1 && tile + (int)gridDim.x < ntiles) {  // next tile's operands into L2
           const int nt = tile + gridDim.x, nbh = nt / p.nrb, nb = nbh / p.H, nh = nbh % p.H, nrow = (nt % p.nrb) * kBM;
@@ -963,16 +1011,31 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
           prefetch_rows<T>(&maps.v, p.N, nh, nb, p.B, T::PL);
         }
         for (int c = 0; c < nchunks && ok; ++c) {
-          const int ks = kc % NKV;
-          if (!(ok = mbar_wait(&bar_kempty[ks], ((kc / NKV) & 1) ^ 1, ctx))) break;
-          mbar_arrive_expect_tx(&bar_kfull[ks], T::PL * C::K_BYTES);
-          tma_tile<T>(smem + C::OFF_K + ks * T::PL * C::K_BYTES, &maps.k, &bar_kfull[ks], T::CH, c * T::CH, h, b, p.B,
-                      T::PL);
-          if (!(ok = mbar_wait(&bar_vempty[ks], ((kc / NKV) & 1) ^ 1, ctx))) break;
-          mbar_arrive_expect_tx(&bar_vfull[ks], T::PL * C::K_BYTES);
-          tma_tile<T>(smem + C::OFF_V + ks * T::PL * C::K_BYTES, &maps.v, &bar_vfull[ks], T::CH, c * T::CH, h, b, p.B,
-                      T::PL);
-          ++kc;
+          if constexpr (C::WIDE) {  // (Q, K) head-dim chunks for S, then (dO, V) chunks for dP
+            for (int j = 0; j < 2 * C::NDC && ok; ++j) {
+              const int ks = kc % NKV, dc = j % C::NDC;
+              if (!(ok = mbar_wait(&bar_kempty[ks], ((kc / NKV) & 1) ^ 1, ctx))) break;
+              mbar_arrive_expect_tx(&bar_kfull[ks], T::PL * C::K_BYTES);
+              uint8_t* slot = smem + C::OFF_K + ks * T::PL * C::K_BYTES;
+              if (j < C::NDC)
+                tma_slot<T>(slot, &bar_kfull[ks], &maps.q, rb * kBM, &maps.k, c * T::CH, dc, h, b, p.B);
+              else
+                tma_slot<T>(slot, &bar_kfull[ks], &maps.dout, rb * kBM, &maps.v, c * T::CH, dc, h, b, p.B);
+              ++kc;
+            }
+            if (!ok) break;
+          } else {
+            const int ks = kc % NKV;
+            if (!(ok = mbar_wait(&bar_kempty[ks], ((kc / NKV) & 1) ^ 1, ctx))) break;
+            mbar_arrive_expect_tx(&bar_kfull[ks], T::PL * C::K_BYTES);
+            tma_tile<T>(smem + C::OFF_K + ks * T::PL * C::K_BYTES, &maps.k, &bar_kfull[ks], T::CH, c * T::CH, h, b,
+                        p.B, T::PL);
+            if (!(ok = mbar_wait(&bar_vempty[ks], ((kc / NKV) & 1) ^ 1, ctx))) break;
+            mbar_arrive_expect_tx(&bar_vfull[ks], T::PL * C::K_BYTES);
+            tma_tile<T>(smem + C::OFF_V + ks * T::PL * C::K_BYTES, &maps.v, &bar_vfull[ks], T::CH, c * T::CH, h, b,
+                        p.B, T::PL);
+            ++kc;
+          }
           if constexpr (!BF16) {
             if (sweep == 1) {
               const int ts = tc % C::NDS;
@@ -1010,6 +1073,22 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       int kc = 0, sc = 0, dc = 0, it = 0;
       bool ok = true;
       auto issue = [&](bool release_k) -> bool {
+        if constexpr (C::WIDE) {  // S then dP, each accumulated over the head-dim chunks of its slots
+          const int ss = sc % NSB;
+          if (!mbar_wait(&bar_sempty[ss], ((sc / NSB) & 1) ^ 1, ctx)) return false;
+          for (int j = 0; j < 2 * C::NDC; ++j) {
+            const int ks = kc % NKV, dc = j % C::NDC;
+            if (!mbar_wait(&bar_kfull[ks], (kc / NKV) & 1, ctx)) return false;
+            tc_fence_after();
+            mma_slot<T>(tmem + (j < C::NDC ? C::TM_S : C::TM_DP) + ss * T::CH,
+                        sbase + C::OFF_K + ks * T::PL * C::K_BYTES, dc > 0);
+            mma_commit(&bar_kempty[ks]);
+            ++kc;
+          }
+          mma_commit(&bar_sfull[ss]);
+          ++sc;
+          return true;
+        }
         const int ks = kc % NKV, ss = sc % NSB;
         if (!mbar_wait(&bar_kfull[ks], (kc / NKV) & 1, ctx)) return false;
         if (!mbar_wait(&bar_vfull[ks], (kc / NKV) & 1, ctx)) return false;
@@ -1041,12 +1120,13 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         mma_pv<T>(tmem + C::TM_DQ, sbase + C::OFF_DS + ds * C::DS_BYTES, bsrc, c > 0);
         mma_commit(&bar_dsempty[ds]);
         if constexpr (!BF16) mma_commit(&bar_ktempty[ds]);
-        mma_commit(&bar_kempty[ks]);
+        if constexpr (!C::WIDE) mma_commit(&bar_kempty[ks]);  // wide: the slots were released by their MMAs
         ++dc;
         return true;
       };
       for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++it) {
-        if (!(ok = mbar_wait(&bar_qfull, it & 1, ctx))) break;
+        if constexpr (!C::WIDE)
+          if (!(ok = mbar_wait(&bar_qfull, it & 1, ctx))) break;
         for (int c = 0; c < nchunks && ok; ++c) ok = issue(true);
         if constexpr (!DQ) {
           if (ok) mma_commit(&bar_qempty);  // every S/dP MMA of this tile has been issued
@@ -1056,7 +1136,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         if (ok) ok = issue(false);
         if (ok && nchunks == 1) mma_commit(&bar_qempty);  // every S/dP MMA of this tile has been issued
         for (int c = 0; c < nchunks && ok; ++c) {
-          if constexpr (NKV == 2) {  // look ahead: S/dP of the next chunk overlap the element-wise work on this one
+          if constexpr (NKV == 2 || C::WIDE) {  // look ahead: S/dP of the next chunk overlap the element-wise work
             if (c + 1 < nchunks && !(ok = issue(false))) break;
             if (c + 2 == nchunks) mma_commit(&bar_qempty);
             if (!(ok = issue_dq(c, kc0))) break;
@@ -1189,8 +1269,12 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       rec[2 * T::CH] = valid ? delta1 : 0.f;
       rec[3 * T::CH] = valid ? delta2 : 0.f;
     }
-    // Sweep 2
-    float gbp[2] = {0.f, 0.f}, ggp[2] = {0.f, 0.f};  // d(beta), d(gamma) partials of the row
+    // Sweep 2. d(alpha) of the row is summed again here from the explicit dZ, as sum dZ (P1 - b) with b = sum P2 P1:
+    // sum dZ is 0 in exact arithmetic, but the recomputed P2 sum to 1 + eps (fp32 rounding of c2, exp2), which
+    // leaves sum dZ = -eps delta2; with P1 near uniform that bias dominates sum dZ P1 (and a - delta2 b cancels to
+    // a few ulps of delta2). Subtracting b sum dZ removes it to O(eps^2) for any P1.
+    const float pb = acc[2];
+    float gap[2] = {0.f, 0.f}, gbp[2] = {0.f, 0.f}, ggp[2] = {0.f, 0.f};  // d(alpha), d(beta), d(gamma) of the row
     if constexpr (DQ) {
     for (int c = 0; c < nchunks && ok; ++c) {
       const int ss = sc % NSB, ds = dc % C::NDS, prs = pc % NPR;
@@ -1227,6 +1311,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
             if constexpr (decltype(masked)::value) p2 = (j < nvalid) ? p2 : 0.f;
             const float dz = p2 * (__uint_as_float(ws[j]) - delta2);
             v[j] = p1[j] * fmaf(ab.a, dz, -delta1);  // masked columns: p1 = 0 -> dS = 0
+            gap[j & 1] = fmaf(dz, p1[j] - pb, gap[j & 1]);
             gbp[j & 1] = fmaf(dz, dpj, gbp[j & 1]);
             ggp[j & 1] = fmaf(dz, apj, ggp[j & 1]);
           }
@@ -1246,10 +1331,11 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       ++pc;
     }
     }
-    // block partials of d(alpha) (one per row: warpgroup 0), d(beta), d(gamma) (every warpgroup's columns; without
-    // DQ the key pass writes those two)
+    // block partials of d(alpha) (without DQ: one per row from sweep 1, warpgroup 0), d(beta), d(gamma) (every
+    // warpgroup's columns; without DQ the key pass writes those two)
     {
-      double ga = (valid && e.wg == 0) ? (double)ta : 0.0, gb = valid ? (double)(gbp[0] + gbp[1]) : 0.0,
+      double ga = DQ ? (valid ? (double)(gap[0] + gap[1]) : 0.0) : ((valid && e.wg == 0) ? (double)ta : 0.0);
+      double gb = valid ? (double)(gbp[0] + gbp[1]) : 0.0,
              gg = valid ? (double)(ggp[0] + ggp[1]) : 0.0;
 #pragma unroll
       for (int off = 16; off > 0; off >>= 1) {
@@ -1310,17 +1396,23 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
 template <bool BF16, int DP>
 struct ColsCfg : Tile<BF16, DP> {
   using T = Tile<BF16, DP>;
+  // fp32 beyond 64: no resident K / V blocks; (K, Q) and (V, dO) reach the S^T and dP^T MMAs in head-dim chunks
+  // through a ring of NRS slots (the transposed Q / dO chunks for dK, dV still arrive per query chunk)
+  static constexpr bool WIDE = !BF16 && DP > 64;
+  static constexpr int NDC = WIDE ? DP / T::KB : 1;
+  static constexpr int NRS = WIDE ? 3 : 0;
   static constexpr int NQ = (BF16 && DP <= 128) ? 3 : 1;   // query-chunk (Q, dO) buffers
   static constexpr int NSB = (BF16 && DP <= 128) ? 2 : 1;  // S^T / dP^T accumulator buffers in tensor memory
   static constexpr int NR = 2;                             // row-record buffers
   static constexpr int NST = (BF16 && DP <= 64) ? 2 : 1;   // buffers for the staged P2^T / dS^T tiles
   static constexpr int NPR = !BF16 ? 0 : (DP <= 64 ? 2 : 1);  // staged prior buffers (0: read from L2)
-  static constexpr int K_BYTES = kBM * DP * T::EB;          // per plane (K and V blocks)
-  static constexpr int Q_BYTES = T::CH * DP * T::EB;        // per plane per buffer (Q and dO chunks)
+  static constexpr int K_BYTES = WIDE ? 0 : kBM * DP * T::EB;    // per plane (K and V blocks)
+  static constexpr int Q_BYTES = WIDE ? 0 : T::CH * DP * T::EB;  // per plane per buffer (Q and dO chunks)
   static constexpr int QT_BYTES = BF16 ? 0 : DP * 128;      // fp32: transposed Q / dO chunk (hi)
   static constexpr int ST_BYTES = kBM * 128;                // P2^T or dS^T tile
   static constexpr int REC_BYTES = 4 * T::CH * 4;           // row records of one query chunk: m1, c2, delta1, delta2
-  static constexpr int OFF_K = 0;
+  static constexpr int OFF_RS = 0;
+  static constexpr int OFF_K = OFF_RS + NRS * 2 * kSlotPlaneBytes;
   static constexpr int OFF_V = OFF_K + T::PL * K_BYTES;
   static constexpr int OFF_Q = OFF_V + T::PL * K_BYTES;
   static constexpr int OFF_DO = OFF_Q + NQ * T::PL * Q_BYTES;
@@ -1331,6 +1423,7 @@ struct ColsCfg : Tile<BF16, DP> {
   static constexpr int OFF_PR = OFF_DS + NST * ST_BYTES;
   static constexpr int OFF_REC = OFF_PR + NPR * kPriorTileBytes;
   static constexpr int SMEM = OFF_REC + NR * REC_BYTES;
+  static_assert(SMEM + 1024 <= kSmemPerBlock, "key pass: dynamic + static shared memory above the per-block limit");
   static constexpr int TM_S = 0;
   static constexpr int TM_DP = NSB * T::CH;
   static constexpr int TM_DK = 2 * NSB * T::CH;
@@ -1351,7 +1444,8 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
   if (smem_misaligned(p.status)) return;  // uniform over the CTA, before any barrier or allocation
   uint8_t* smem = smem_raw;
   __shared__ uint64_t bar_kvfull, bar_kvempty, bar_qfull[3], bar_qempty[3], bar_sfull[2], bar_sempty[2], bar_tfull[2],
-      bar_tempty[2], bar_prfull[2], bar_prempty[2], bar_recfull[2], bar_recempty[2], bar_done;
+      bar_tempty[2], bar_prfull[2], bar_prempty[2], bar_recfull[2], bar_recempty[2], bar_done, bar_rsfull[3],
+      bar_rsempty[3];
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_flag;
   __shared__ double redc[8][2];
@@ -1368,6 +1462,8 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
     for (int i = 0; i < 3; ++i) {
       mbar_init(&bar_qfull[i], 1);
       mbar_init(&bar_qempty[i], 1);
+      mbar_init(&bar_rsfull[i], 1);
+      mbar_init(&bar_rsempty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bar_recfull[i], 1);
@@ -1399,7 +1495,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       prefetch_tmap(&maps.v);
       prefetch_tmap(&maps.dout);
       bool ok = true;
-      int it = 0;
+      int it = 0, rc = 0;
       for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++it) {
       const int kblk = tile % p.nrb, bh = tile / p.nrb, b = bh / p.H, h = bh % p.H;
       // dS^T tile of chunk c (use g of its staging slot) to the scratch once the element-wise warps staged it; the
@@ -1413,11 +1509,12 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         mbar_arrive(&bar_tempty[ts]);
         return true;
       };
-      // K and V blocks of this tile once the previous tile's last S^T/dP^T MMAs have read the old ones
-      if (!(ok = mbar_wait(&bar_kvempty, (it & 1) ^ 1, ctx))) break;
-      mbar_arrive_expect_tx(&bar_kvfull, 2 * T::PL * C::K_BYTES);
-      tma_tile<T>(smem + C::OFF_K, &maps.k, &bar_kvfull, kBM, kblk * kBM, h, b, p.B, T::PL);
-      tma_tile<T>(smem + C::OFF_V, &maps.v, &bar_kvfull, kBM, kblk * kBM, h, b, p.B, T::PL);
+      if constexpr (!C::WIDE) {  // K and V blocks once the previous tile's last S^T/dP^T MMAs have read the old ones
+        if (!(ok = mbar_wait(&bar_kvempty, (it & 1) ^ 1, ctx))) break;
+        mbar_arrive_expect_tx(&bar_kvfull, 2 * T::PL * C::K_BYTES);
+        tma_tile<T>(smem + C::OFF_K, &maps.k, &bar_kvfull, kBM, kblk * kBM, h, b, p.B, T::PL);
+        tma_tile<T>(smem + C::OFF_V, &maps.v, &bar_kvfull, kBM, kblk * kBM, h, b, p.B, T::PL);
+      }
       if (tile + (int)gridDim.x < ntiles) {  // next tile's key block into L2
         const int nt = tile + gridDim.x, nbh = nt / p.nrb, nb = nbh / p.H, nh = nbh % p.H, nrow = (nt % p.nrb) * kBM;
         prefetch_tile<T>(&maps.k, nrow, nh, nb, p.B, T::PL);
@@ -1428,10 +1525,12 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         const int qs = gc % NQ;
         if (!(ok = mbar_wait(&bar_qempty[qs], ((gc / NQ) & 1) ^ 1, ctx))) break;
         mbar_arrive_expect_tx(&bar_qfull[qs], 2 * T::PL * C::Q_BYTES + 2 * C::QT_BYTES);
-        tma_tile<T>(smem + C::OFF_Q + qs * T::PL * C::Q_BYTES, &maps.q, &bar_qfull[qs], T::CH, c * T::CH, h, b, p.B,
-                    T::PL);
-        tma_tile<T>(smem + C::OFF_DO + qs * T::PL * C::Q_BYTES, &maps.dout, &bar_qfull[qs], T::CH, c * T::CH, h, b,
-                    p.B, T::PL);
+        if constexpr (!C::WIDE) {
+          tma_tile<T>(smem + C::OFF_Q + qs * T::PL * C::Q_BYTES, &maps.q, &bar_qfull[qs], T::CH, c * T::CH, h, b,
+                      p.B, T::PL);
+          tma_tile<T>(smem + C::OFF_DO + qs * T::PL * C::Q_BYTES, &maps.dout, &bar_qfull[qs], T::CH, c * T::CH, h, b,
+                      p.B, T::PL);
+        }
         if constexpr (!BF16) {
           tma_tileT(smem + C::OFF_QT + qs * C::QT_BYTES, &maps.qt, &bar_qfull[qs], c * T::CH, h, b);
           tma_tileT(smem + C::OFF_DOT + qs * C::QT_BYTES, &maps.dot, &bar_qfull[qs], c * T::CH, h, b);
@@ -1441,6 +1540,20 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         mbar_arrive_expect_tx(&bar_recfull[rs], C::REC_BYTES);
         bulk_load(smem + C::OFF_REC + rs * C::REC_BYTES, p.rowrec + ((size_t)bh * p.nchp + c) * 4 * T::CH,
                   C::REC_BYTES, &bar_recfull[rs]);
+        if constexpr (C::WIDE) {  // (K, Q) head-dim chunks for S^T, then (V, dO) chunks for dP^T
+          for (int j = 0; j < 2 * C::NDC && ok; ++j) {
+            const int ss = rc % C::NRS, dc = j % C::NDC;
+            if (!(ok = mbar_wait(&bar_rsempty[ss], ((rc / C::NRS) & 1) ^ 1, ctx))) break;
+            mbar_arrive_expect_tx(&bar_rsfull[ss], 2 * kSlotPlaneBytes);
+            uint8_t* slot = smem + C::OFF_RS + ss * 2 * kSlotPlaneBytes;
+            if (j < C::NDC)
+              tma_slot<T>(slot, &bar_rsfull[ss], &maps.k, kblk * kBM, &maps.q, c * T::CH, dc, h, b, p.B);
+            else
+              tma_slot<T>(slot, &bar_rsfull[ss], &maps.v, kblk * kBM, &maps.dout, c * T::CH, dc, h, b, p.B);
+            ++rc;
+          }
+          if (!ok) break;
+        }
         // the dS stores trail the loads by LAG chunks, so a store's wait for its tile never holds back the loads
         // the MMAs need next (LAG < NQ keeps the dependency chain acyclic)
         if constexpr (SDS)
@@ -1471,8 +1584,23 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
   } else if (warp == T::MMA_WARP) {
     if (lane == 0) {
       bool ok = true;
-      int it = 0;
+      int it = 0, rc = 0;
       auto issue_s = [&](int gc) -> bool {
+        if constexpr (C::WIDE) {
+          const int ss = gc % NSB;
+          if (!mbar_wait(&bar_sempty[ss], ((gc / NSB) & 1) ^ 1, ctx)) return false;
+          for (int j = 0; j < 2 * C::NDC; ++j) {
+            const int rs = rc % C::NRS, dc = j % C::NDC;
+            if (!mbar_wait(&bar_rsfull[rs], (rc / C::NRS) & 1, ctx)) return false;
+            tc_fence_after();
+            mma_slot<T>(tmem + (j < C::NDC ? C::TM_S : C::TM_DP) + ss * T::CH,
+                        sbase + C::OFF_RS + rs * 2 * kSlotPlaneBytes, dc > 0);
+            mma_commit(&bar_rsempty[rs]);
+            ++rc;
+          }
+          mma_commit(&bar_sfull[ss]);
+          return true;
+        }
         const int qs = gc % NQ, ss = gc % NSB;
         if (!mbar_wait(&bar_qfull[qs], (gc / NQ) & 1, ctx)) return false;
         if (!mbar_wait(&bar_sempty[ss], ((gc / NSB) & 1) ^ 1, ctx)) return false;
@@ -1486,7 +1614,8 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       };
       for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++it) {
       const int g0 = it * nchunks;
-      if (!(ok = mbar_wait(&bar_kvfull, it & 1, ctx))) break;
+      if constexpr (!C::WIDE)
+        if (!(ok = mbar_wait(&bar_kvfull, it & 1, ctx))) break;
       if (ok) ok = issue_s(g0);
       if (ok && nchunks == 1) mma_commit(&bar_kvempty);  // every S^T/dP^T MMA of this tile has been issued
       for (int c = 0; c < nchunks && ok; ++c) {
@@ -1497,6 +1626,8 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         }
         const int qs = gc % NQ, ts = gc % NST;
         if (!(ok = mbar_wait(&bar_tfull[ts], (gc / NST) & 1, ctx))) break;
+        if constexpr (C::WIDE)  // the transposed Q / dO chunks (the slots carried the score operands)
+          if (!(ok = mbar_wait(&bar_qfull[qs], (gc / NQ) & 1, ctx))) break;
         tc_fence_after();
         uint32_t dob, qb;
         if constexpr (BF16) {

@@ -43,7 +43,7 @@ enum { GEOATTN_DTYPE_BF16 = 0, GEOATTN_DTYPE_FP32 = 1 };
  *   BF16 -> bf16 tensor-core path (kind::f16), geo prior kept as fp16 pairs;
  *   FP32 -> TF32 tensor-core path (kind::tf32) with 3-term split products for QK^T and dO V^T
  *           (round-to-nearest hi/lo operands), 1-term for the rest; geo prior kept in fp32.
- * Supported head_dim: BF16 1..192, FP32 1..64. n >= 1 (any size).                                        */
+ * Supported head_dim: 1..192 (BF16 and FP32). n >= 1 (any size).                                          */
 typedef struct {
   int batch, heads, n, head_dim;
   int dtype;

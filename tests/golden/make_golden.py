@@ -9,6 +9,7 @@ It writes tests/golden/*.npz. What each file holds and which reference code prod
 * attn_<case>.npz   foreswe_bench.attn_check.case_inputs(..., device="cpu") draws the inputs (the reference's
                     own seeded generator); foreswe_bench.geo_attention.eager_geo_attention with torch autograd in
                     float64 gives output, dQ, dK, dV, dalpha, dbeta, dgamma for a fixed dO.
+* attn_moderate_d192.npz  one "moderate" instance at the reference's default head dim D = 192.
 * attn_perhead.npz  the same operator with per-head alpha/beta/gamma of shape [1, H, 1, 1] (reference broadcasting).
 * attn_stations.npz real station geometry (below) as dist/ang, cast to fp32 as foreswe_bench/data.py:58-59 does.
 * geometry.npz      the first 48 stations of data/snotel_location_info_2.csv (lat, lon, elevation in feet) and
@@ -74,6 +75,11 @@ def main():
         inp = case_inputs(case, B=B, H=H, N=N, D=D, seed=seed, device="cpu")
         g = torch.Generator().manual_seed(1234 + seed)
         save_attn("attn_" + case, inp, torch.randn(inp[0].shape, generator=g))
+
+    # the reference's default head dim (case_inputs' D = 192), one small instance
+    inp = case_inputs("moderate", B=1, H=1, N=40, D=192, seed=8, device="cpu")
+    g = torch.Generator().manual_seed(1242)
+    save_attn("attn_moderate_d192", inp, torch.randn(inp[0].shape, generator=g))
 
     # per-head bias parameters, broadcast by the reference operator itself
     inp = case_inputs("moderate", B=2, H=3, N=17, D=8, seed=7, device="cpu")

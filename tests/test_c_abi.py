@@ -44,8 +44,11 @@ def test_size_queries_without_gpu(L):
     assert L.geoattn_bwd_workspace_bytes(ctypes.byref(sh)) > 32 * 8 * 512 * 16   # 4 float row records per row
     bad = _lib.Shape(1, 1, 16, 256, _lib.DTYPE_BF16, 0)
     assert L.geoattn_prior_bytes(ctypes.byref(bad)) == 0
+    # fp32 head_dim 128: status word, hi/lo planes of q and k ([2][N][DP]), transposed v ([DP][N padded to 128])
     fp = _lib.Shape(1, 1, 16, 128, _lib.DTYPE_FP32, 0)
-    assert L.geoattn_fwd_workspace_bytes(ctypes.byref(fp)) == 0
+    assert L.geoattn_fwd_workspace_bytes(ctypes.byref(fp)) == 256 + 2 * (2 * 16 * 128 * 4) + 128 * 128 * 4
+    for dtype in (_lib.DTYPE_FP32, _lib.DTYPE_BF16):  # head_dim above 192 has no kernel
+        assert L.geoattn_fwd_workspace_bytes(ctypes.byref(_lib.Shape(1, 1, 16, 200, dtype, 0))) == 0
 
 
 def test_invalid_arguments_rejected_before_any_launch(L):

@@ -78,6 +78,57 @@ def test_bf16_wide_heads(ops, D):
     _check(res, _oracle(q, k, v, dist, ang, a, b, c, do), TOL[torch.bfloat16], "D=%d" % D)
 
 
+@pytest.mark.parametrize("D", [128, 192, 96, 160])
+def test_tf32_wide_heads(ops, D):
+    """fp32 head dims above 64 (Q/K and dO/V streamed through the score MMAs in 32-wide head-dim chunks), up to the
+    production d_k = 192, per-head parameters, coordinate prior, N not a multiple of the tiles."""
+    B, H, N = 1, 2, 300
+    q, k, v, a, b, c, do = attn_inputs(B, H, N, D, seed=D + 1, qscale=2.0, dtype=torch.float32)
+    lat, lon, el = stations(N, seed=D)
+    geom = ops.StationGeometry(lat, lon, el)
+    res = run_device(lambda *x: ops.geo_attention(x[0], x[1], x[2], geom, *x[3:]), q, k, v, a, b, c, do)
+    dist, ang = dense_geometry(lat, lon, el)
+    _check(res, _oracle(q, k, v, dist, ang, a, b, c, do), TOL[torch.float32], "tf32 D=%d" % D)
+
+
+def _regime(ops, case, B, H, N, D):
+    inp = acceptance.case_inputs(case, B=B, H=H, N=N, D=D, seed=0)
+    do = acceptance.grad_seed_do(inp[0].shape)
+    q, k, v, dist, ang, a, b, c = inp
+    res = run_device(lambda *x: ops.fused_geo_attention_v2(x[0], x[1], x[2], dist.cuda(), ang.cuda(), *x[3:]),
+                     q, k, v, a, b, c, do)
+    for key in KEYS:
+        assert torch.isfinite(res[key]).all(), (case, key)
+    ev = acceptance.evaluate(res, inp, do, "tf32", ref=acceptance.reference(inp, do))
+    bad = {k: (r["candidate"]["max_abs"], r["bound"]) for k, r in ev.items() if not r["passed"]}
+    assert not bad, "%s %s: above 10x eager TF32: %s" % (case, (B, H, N, D), bad)
+
+
+@pytest.mark.parametrize("case", acceptance.CASES)
+def test_reference_regimes_tf32_d192(ops, case):
+    """The reference's acceptance test (tests/test_gpu_geo_attention_v2.py:32-50): its six synthetic regimes at its
+    own shape (1, 2, 100, 192), fp32 storage, within 10x eager TF32's max-abs error of the float64 operator."""
+    _regime(ops, case, 1, 2, 100, 192)
+
+
+def test_reference_regime_tf32_full_d192(ops):
+    """The reference's full-size acceptance shape (1, 16, 512, 192) in its hardest regime (score std ~ 400)."""
+    _regime(ops, "near_one_hot", 1, 16, 512, 192)
+
+
+def test_tf32_wide_repeat_bitwise(ops):
+    """The streamed fp32 path is deterministic: two runs give bitwise-equal outputs and gradients."""
+    B, H, N, D = 2, 2, 260, 192
+    q, k, v, a, b, c, do = attn_inputs(B, H, N, D, seed=9, qscale=3.0, dtype=torch.float32)
+    lat, lon, el = stations(N, seed=9)
+    geom = ops.StationGeometry(lat, lon, el)
+    fn = lambda *x: ops.geo_attention(x[0], x[1], x[2], geom, *x[3:])  # noqa: E731
+    r1 = run_device(fn, q, k, v, a, b, c, do)
+    r2 = run_device(fn, q, k, v, a, b, c, do)
+    for key in KEYS:
+        assert torch.equal(r1[key], r2[key]), key
+
+
 @pytest.mark.parametrize("case", acceptance.CASES)
 def test_reference_regimes_tf32(ops, case):
     """The reference's six synthetic regimes (foreswe_bench/attn_check.py:20-45) at D = 64 on the TF32 path:
@@ -249,7 +300,7 @@ def test_status_word_clean_and_errors_raise(ops):
     from foreswe_gpu_optimization_b200.geo_attention_v2 import read_status
     assert read_status(ws) == 0
     with pytest.raises(_lib.GeoAttnError):
-        x = torch.randn(1, 1, 16, 80, device="cuda")
+        x = torch.randn(1, 1, 16, 200, device="cuda")  # head_dim above 192
         ops.fused_geo_attention_v2(x, x, x, dist[:16, :16], ang[:16, :16], a.cuda(), b.cuda(), c.cuda())
     # a host pointer where the library expects device memory is rejected before any launch
     bad = _lib.FwdArgs(sh, _lib.tensor_arg(qd), _lib.tensor_arg(kd), _lib.tensor_arg(vd),
