@@ -5,7 +5,7 @@ head dim 128, bf16; per-head alpha/beta/gamma; geo prior from synthetic station 
 (lat ~ U(35,49), lon ~ U(-124,-104), elevation ~ U(500,3500) m). One step = forward + backward of the attention
 on this rank's issue dates followed by an NCCL all-reduce of the bias-parameter gradients (N > 1).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload c5|c4]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload c5|c4|configs]
 
 Prints ONE JSON line on rank 0. ``value`` is whole-job algorithmic TFLOP/s, 12*B*H*N^2*D per fwd+bwd (recompute not
 counted), over the max-over-ranks device time of K steps. ``e2e`` is the same metric through the public API with
@@ -331,6 +331,98 @@ def run_c4(args):
     return 0
 
 
+# (name, issue dates B, heads H, stations N, head dim D, storage dtype, logit scale on q)
+CONFIGS = (("c2_tf32", 32, 8, 512, 64, torch.float32, 1.0),
+           ("c2_tf32_saturated_x30", 32, 8, 512, 64, torch.float32, 30.0),
+           ("c3_bf16", 384, 16, 512, 64, torch.bfloat16, 1.0),
+           ("reference_shape_tf32_d192", 1, 16, 512, 192, torch.float32, 1.0),
+           ("production_heads_tf32_d192_b32", 32, 16, 512, 192, torch.float32, 1.0),
+           ("production_heads_bf16_d192_b32", 32, 16, 512, 192, torch.bfloat16, 1.0))
+# the reference's published fwd / bwd / fwd+bwd times (ms) at its production shape [1, 16, 512, 192], TF32, A100
+REFERENCE_A100_D192 = {"triton_v2_accurate": [0.491, 1.930, 2.191], "eager_tf32": [0.332, 0.564, 0.857]}
+
+
+def run_configs(args):
+    """The other configurations of the path, one JSON line each: fwd, bwd and fwd+bwd ms of the kernels (coordinate
+    prior, per-head alpha/beta/gamma, q/k/v ~ N(0,1) D^-1/4, dO ~ N(0,1)) and of eager PyTorch on the same GPU and
+    inputs (TF32 matmuls for fp32 storage, as the reference's eager TF32 baseline), CUDA events, after warm-up."""
+    import foreswe_gpu_optimization_b200 as g
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    torch.backends.cuda.matmul.allow_tf32 = True
+    pk_bf16, pk_src = peaks()
+    for name, b, h, n, d, dtype, qscale in CONFIGS:
+        gen = torch.Generator().manual_seed(11)
+        s = d ** -0.25
+        q, k, v = (torch.randn(b, h, n, d, generator=gen) * s for _ in range(3))
+        q = q * qscale
+        do = torch.randn(b, h, n, d, generator=gen)
+        q, k, v, do = (t.to(dev, dtype) for t in (q, k, v, do))
+        gp = torch.Generator().manual_seed(7)
+        params = [(torch.rand(h, generator=gp) * 0.9 + 0.1), torch.randn(h, generator=gp) * 0.5,
+                  torch.randn(h, generator=gp) * 0.5]
+        params = [t.to(dev).requires_grad_(True) for t in params]
+        rng = np.random.default_rng(0)
+        geom = g.StationGeometry(rng.uniform(35.0, 49.0, n), rng.uniform(-124.0, -104.0, n),
+                                 rng.uniform(500.0, 3500.0, n) / 0.3048, device=dev)
+        dmat, amat = geom.distance_and_angularity()
+        x = [t.detach().requires_grad_(True) for t in (q, k, v)]
+
+        def ours():
+            return g.geo_attention(x[0], x[1], x[2], geom, *params)
+
+        def eager():
+            s_ = torch.softmax(torch.matmul(x[0], x[1].transpose(-2, -1)) / math.sqrt(d), dim=-1)
+            z = (params[0].view(-1, 1, 1) * s_ + params[1].view(-1, 1, 1) / (1 + dmat)
+                 + params[2].view(-1, 1, 1) / (1 + amat))
+            return torch.matmul(torch.softmax(z, dim=-1).to(dtype), x[2])
+
+        def timed(fn, backward):
+            def once():
+                for t in x + params:
+                    t.grad = None
+                o = fn()
+                if backward:
+                    o.backward(do)
+            for _ in range(args.warmup):
+                once()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(args.steps):
+                once()
+            e1.record()
+            torch.cuda.synchronize()
+            return e0.elapsed_time(e1) / args.steps
+
+        def triple(fn):
+            try:
+                f, fb = timed(fn, False), timed(fn, True)
+                return {"fwd": f, "bwd": fb - f, "fwd_bwd": fb}
+            except torch.OutOfMemoryError:
+                torch.cuda.empty_cache()
+                return None
+
+        mine = triple(ours)
+        ref = triple(eager)
+        fl = 12.0 * b * h * n * n * d
+        line = {"workload": name, "shape_bhnd": [b, h, n, d], "dtype": "bf16" if dtype == torch.bfloat16 else "fp32 (tf32)",
+                "steps": args.steps, "warmup": args.warmup, "ms": mine, "eager_ms": ref,
+                "tflops": fl / (mine["fwd_bwd"] * 1e-3) / 1e12,
+                "speedup_vs_eager": (ref["fwd_bwd"] / mine["fwd_bwd"]) if ref else None,
+                "l2": "inputs %s L2 (q,k,v,dO = %.0f MB)" % ("larger than" if 4 * q.numel() * q.element_size() > 126e6
+                                                            else "within", 4 * q.numel() * q.element_size() / 1e6)}
+        if dtype == torch.bfloat16:
+            line["tensor_frac_of_sustained_bf16"] = line["tflops"] / pk_bf16
+            line["peak_source"] = pk_src
+        if name == "reference_shape_tf32_d192":
+            line["reference_a100_ms_fwd_bwd_fwdbwd"] = REFERENCE_A100_D192
+        print(json.dumps(line), flush=True)
+        del q, k, v, do, x, geom, dmat, amat
+        torch.cuda.empty_cache()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -341,8 +433,9 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-eager", action="store_true")
     ap.add_argument("--batch", type=int, default=None, help="override the global batch (small cases for profiling)")
-    ap.add_argument("--workload", default="c5", choices=("c5", "c4"),
-                    help="c5: the attention scaling configuration (the headline line); c4: a full encoder training step")
+    ap.add_argument("--workload", default="c5", choices=("c5", "c4", "configs"),
+                    help="c5: the attention scaling configuration (the headline line); c4: a full encoder training "
+                         "step; configs: the other shapes (C2, C3, the reference's published shape), one line each")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     if args.batch:
@@ -352,6 +445,8 @@ def main():
         return run_reference(args)
     if args.workload == "c4":
         return run_c4(args)
+    if args.workload == "configs":
+        return run_configs(args)
 
     import foreswe_gpu_optimization_b200 as g
     from foreswe_gpu_optimization_b200 import geo_attention_v2 as gv2

@@ -500,8 +500,9 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
   static_assert(!C::EPI_TMA || T::EW > 1, "the TMA epilogue relies on the warpgroup exchange barrier");
   if (smem_misaligned(p.status)) return;  // uniform over the CTA, before any barrier or allocation
   uint8_t* smem = smem_raw;
-  __shared__ uint64_t bar_qfull, bar_qempty, bar_kfull[3], bar_kempty[3], bar_vfull[2], bar_vempty[2], bar_sfull[4],
+  __shared__ uint64_t bar_qfull, bar_qempty, bar_kfull[4], bar_kempty[4], bar_vfull[2], bar_vempty[2], bar_sfull[4],
       bar_sempty[4], bar_pfull[2], bar_pempty[2], bar_prfull[2], bar_prempty[2], bar_ofull;
+  static_assert(NK <= 4 && NSB <= 4 && NPR <= 2, "ring deeper than its barrier array");
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_flag;
   __shared__ float xch[3][Tile<BF16, DP>::EW][kBM];  // cross-warpgroup row statistics: m, l1, l2
@@ -515,11 +516,9 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
     abort_flag = 0;
     mbar_init(&bar_qfull, 1);
     mbar_init(&bar_qempty, 1);
-    for (int i = 0; i < 3; ++i) {
+    for (int i = 0; i < 4; ++i) {
       mbar_init(&bar_kfull[i], 1);
       mbar_init(&bar_kempty[i], 1);
-    }
-    for (int i = 0; i < 4; ++i) {
       mbar_init(&bar_sfull[i], 1);
       mbar_init(&bar_sempty[i], T::EWT);
     }
@@ -941,6 +940,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
   uint8_t* smem = smem_raw;
   __shared__ uint64_t bar_qfull, bar_qempty, bar_kfull[3], bar_kempty[3], bar_vfull[3], bar_vempty[3], bar_sfull[4],
       bar_sempty[4], bar_dsfull[2], bar_dsempty[2], bar_ktfull[2], bar_ktempty[2], bar_prfull[2], bar_prempty[2], bar_dqfull;
+  static_assert(NKV <= 3 && NSB <= 4 && C::NDS <= 2 && NPR <= 2, "ring deeper than its barrier array");
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_flag;
   __shared__ double red[8][3];
@@ -1446,6 +1446,8 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
   __shared__ uint64_t bar_kvfull, bar_kvempty, bar_qfull[3], bar_qempty[3], bar_sfull[2], bar_sempty[2], bar_tfull[2],
       bar_tempty[2], bar_prfull[2], bar_prempty[2], bar_recfull[2], bar_recempty[2], bar_done, bar_rsfull[3],
       bar_rsempty[3];
+  static_assert(NQ <= 3 && NSB <= 2 && NST <= 2 && NPR <= 2 && NR <= 2 && C::NRS <= 3,
+                "ring deeper than its barrier array");
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_flag;
   __shared__ double redc[8][2];
