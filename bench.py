@@ -352,6 +352,10 @@ def run_configs(args):
     torch.backends.cuda.matmul.allow_tf32 = True
     pk_bf16, pk_src = peaks()
     for name, b, h, n, d, dtype, qscale in CONFIGS:
+        if args.only and name != args.only:
+            continue
+        if args.batch:
+            b = args.batch
         gen = torch.Generator().manual_seed(11)
         s = d ** -0.25
         q, k, v = (torch.randn(b, h, n, d, generator=gen) * s for _ in range(3))
@@ -404,7 +408,7 @@ def run_configs(args):
                 return None
 
         mine = triple(ours)
-        ref = triple(eager)
+        ref = None if args.no_eager else triple(eager)
         fl = 12.0 * b * h * n * n * d
         line = {"workload": name, "shape_bhnd": [b, h, n, d], "dtype": "bf16" if dtype == torch.bfloat16 else "fp32 (tf32)",
                 "steps": args.steps, "warmup": args.warmup, "ms": mine, "eager_ms": ref,
@@ -433,12 +437,14 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-eager", action="store_true")
     ap.add_argument("--batch", type=int, default=None, help="override the global batch (small cases for profiling)")
+    ap.add_argument("--only", default=None, choices=[c[0] for c in CONFIGS],
+                    help="with --workload configs: run this configuration only")
     ap.add_argument("--workload", default="c5", choices=("c5", "c4", "configs"),
                     help="c5: the attention scaling configuration (the headline line); c4: a full encoder training "
                          "step; configs: the other shapes (C2, C3, the reference's published shape), one line each")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
-    if args.batch:
+    if args.batch and args.workload != "configs":
         global B_TOTAL
         B_TOTAL = args.batch
     if args.impl == "reference":
