@@ -8,7 +8,8 @@ on this rank's issue dates followed by an NCCL all-reduce of the bias-parameter 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload c5|c4|configs]
 
 Prints ONE JSON line on rank 0. ``value`` is whole-job algorithmic TFLOP/s, 12*B*H*N^2*D per fwd+bwd (recompute not
-counted), over the max-over-ranks device time of K steps. ``e2e`` is the same metric through the public API with
+counted), over the max-over-ranks device time of K steps (replays of the step captured as one CUDA graph, so host-side
+launch work does not pace the GPU at small shards). ``e2e`` is the same metric through the public API with
 the step's inputs copied from pinned host memory and the bias gradients read back, every step. ``roofline``
 describes the dominant kernel timed live with CUDA events on its launching stream. ``--impl reference`` times the
 reference's operator on the host CPU cores (the oracle's restatement of the eager PyTorch op, all threads) on a
@@ -92,7 +93,7 @@ def traffic_per_launch(kernel):
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+    """nvidia-smi clocks / throttle reasons sampled every 50 ms around the timed region (under the same load)."""
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
          "clocks_event_reasons.sw_power_cap")
@@ -106,7 +107,7 @@ class ClockSampler:
         try:
             self.f = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", "--query-gpu=" + self.Q, "--format=csv,noheader,nounits",
-                                          "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+                                          "-lms", "50"], stdout=self.f, stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
 
@@ -496,7 +497,73 @@ def main():
         step(x[0], x[1], x[2], do)
     torch.cuda.synchronize()
 
-    # per-kernel timing events (one set per step), recorded by the library on the launching stream
+    # The step (fwd + bwd and, for N > 1, the bias-gradient all-reduce) captured as one CUDA graph: the timed region
+    # replays it, so host-side launch work (autograd, argument packing) does not pace the GPU at small shards.
+    graph = None
+    try:
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(2):
+                step(x[0], x[1], x[2], do)
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        for t in x + params:
+            t.grad = None
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            o_g = g.geo_attention(x[0], x[1], x[2], geom, *params)
+            o_g.backward(do)
+            allreduce_bias_grads()
+        del o_g
+    except RuntimeError as exc:  # capture unavailable: time eager steps instead
+        print("bench: CUDA graph capture failed (%s); timing eager steps" % str(exc).splitlines()[0], file=sys.stderr)
+        graph = None
+    use_graph = graph is not None
+    if dist_on:  # every rank takes the same path
+        flag = torch.tensor([1 if use_graph else 0], device=dev)
+        tdist.all_reduce(flag, op=tdist.ReduceOp.MIN)
+        use_graph = bool(flag.item())
+
+    def run_step():
+        if use_graph:
+            graph.replay()
+        else:
+            step(x[0], x[1], x[2], do)
+
+    for _ in range(args.warmup):
+        run_step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(3):
+        run_step()
+    e1.record()
+    torch.cuda.synchronize()
+    est_ms = max(e0.elapsed_time(e1) / 3, 0.05)
+
+    # clocks are sampled from a busy pre-roll of ~0.3 s through the timed region and the per-kernel pass below,
+    # all the same workload, so even a short timed region has samples under load
+    clocks = ClockSampler(range(world) if world > 1 else [local])
+    if rank == 0:
+        clocks.start()
+    for _ in range(int(300.0 / est_ms) + 1):
+        run_step()
+    if dist_on:
+        tdist.barrier()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for i in range(args.steps):
+        run_step()
+    t1.record()
+    torch.cuda.synchronize()
+    if dist_on:
+        tdist.barrier()
+    ms = t0.elapsed_time(t1) / args.steps
+
+    # per-kernel times for the roofline: the same K steps run eagerly, with events the library records around each
+    # kernel on its launching stream (one set per step)
     def mk(n):
         evs = [torch.cuda.Event(enable_timing=True) for _ in range(n)]
         for e in evs:
@@ -504,25 +571,13 @@ def main():
         return evs
     ev_sets = [(mk(2), mk(4)) for _ in range(args.steps)]
     torch.cuda.synchronize()
-
-    clocks = ClockSampler(range(world) if world > 1 else [local])
-    if rank == 0:
-        clocks.start()
-    if dist_on:
-        tdist.barrier()
-    torch.cuda.synchronize()
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    t0.record()
     for i in range(args.steps):
         gv2.TIMING_EVENTS["fwd"], gv2.TIMING_EVENTS["bwd"] = ev_sets[i]
         step(x[0], x[1], x[2], do)
-    t1.record()
     torch.cuda.synchronize()
     gv2.TIMING_EVENTS["fwd"] = gv2.TIMING_EVENTS["bwd"] = None
-    if dist_on:
-        tdist.barrier()
     clk = clocks.stop() if rank == 0 else None
-    ms = t0.elapsed_time(t1) / args.steps
+    del graph
     kt = {"geoattn_fwd_kernel": statistics.mean(f[0].elapsed_time(f[1]) for f, _ in ev_sets),
           "geoattn_bwd_rows_kernel": statistics.mean(bw[0].elapsed_time(bw[1]) for _, bw in ev_sets),
           "geoattn_bwd_cols_kernel": statistics.mean(bw[1].elapsed_time(bw[2]) for _, bw in ev_sets),
@@ -600,6 +655,8 @@ def main():
                 "kernel_ms": kt, "flops_per_launch": per_launch}
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+                "timing": ("K replays of the step captured as one CUDA graph" if use_graph else "K eager steps")
+                          + "; per-kernel times from K eager steps with library events",
                 "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": config(world),
                 "tensor_peak_frac": value / world / pk, "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
                 "gpu_eager": eager, "gpu_launches": 5 * args.steps, "clocks": clk}
