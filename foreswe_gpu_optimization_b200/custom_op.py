@@ -73,6 +73,9 @@ def geo_attention_op(q, k, v, prior, alpha, beta, gamma):
     return o
 
 
-def geo_attention_compiled(q, k, v, geometry: StationGeometry, alpha, beta, gamma):
-    """Coordinate form of geo_attention_op (the prior comes from `geometry`)."""
-    return geo_attention_op(q, k, v, geometry.prior(q.dtype), alpha, beta, gamma)
+def geo_attention_compiled(q, k, v, geometry: StationGeometry, alpha, beta, gamma, *, precision=None):
+    """Coordinate form of geo_attention_op (the prior comes from `geometry`); `precision` as in geo_attention."""
+    cd = _gv2._compute_dtype(q, precision, "reference")
+    qc, kc, vc = (t if t.dtype == cd else t.to(cd) for t in (q, k, v))
+    o = geo_attention_op(qc, kc, vc, geometry.prior(cd), alpha, beta, gamma)
+    return o if o.dtype == q.dtype else o.to(q.dtype)

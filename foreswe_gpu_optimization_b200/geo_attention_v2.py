@@ -11,10 +11,15 @@ plus the coordinate form ``geo_attention(q, k, v, geometry, alpha, beta, gamma)`
 Semantics follow the reference: q/k/v are [B, H, N, D] (any strides, e.g. the transposed split_heads views,
 custom_encoder_model.py:41-43); gradients are returned with the inputs' strides; alpha/beta/gamma are [1]
 (reference) or [H] (per head); ``mask`` must be None (the reference asserts the same, :475). Unlike the reference,
-the output dtype is the input dtype: bf16 inputs run the BF16 tensor-core path (bf16 output), fp32 inputs run the
-TF32 path (fp32 output). The numerics presets of the reference are accepted for compatibility; the kernels always
-use the accurate formulation (correctly repeated scaled scores, delta2 consistent with the recomputed tiles,
-round-to-nearest TF32 operands, split 3-term TF32 for the score-shaped products).
+the output dtype is the input dtype.
+
+``precision`` selects the kernels: "auto" (default) follows the input dtype (bf16 inputs run the BF16 tensor-core
+path, fp32 inputs the TF32 path); "bf16" runs the BF16 kernels on fp32 inputs too (inputs rounded to bf16, output
+and gradients returned in the input dtype); "tf32" runs the TF32 kernels on bf16 inputs (widened to fp32). ``mode``
+is "reference" (the operator above, the only one the reference has). The numerics presets of the reference are
+accepted for compatibility; the kernels always use the accurate formulation (correctly repeated scaled scores,
+delta2 consistent with the recomputed tiles, round-to-nearest TF32 operands, split 3-term TF32 for the
+score-shaped products).
 """
 import ctypes
 
@@ -31,6 +36,33 @@ PRESETS = {"accurate_experimental": dict(precision="auto"), "accurate_x3_experim
            "fast_experimental": dict(precision="auto")}
 CFG = dict(PRESETS["accurate_experimental"])
 LAUNCH_INFO = {}
+PRECISIONS = ("auto", "bf16", "tf32")
+MODES = ("reference",)
+
+
+def _compute_dtype(q, precision, mode):
+    """Storage dtype the kernels run in for `precision` ("auto" / None: q's dtype)."""
+    if mode != "reference":
+        raise NotImplementedError("mode=%r: only the reference operator (mode='reference') is implemented" % (mode,))
+    precision = precision or CFG.get("precision", "auto")
+    if precision not in PRECISIONS:
+        raise ValueError("precision must be one of %s, got %r" % (PRECISIONS, precision))
+    if precision == "bf16":
+        return torch.bfloat16
+    if precision == "tf32":
+        return torch.float32
+    if q.dtype not in (torch.bfloat16, torch.float32):
+        raise TypeError("q, k, v must be bf16 or fp32 (or pass precision='bf16' / 'tf32')")
+    return q.dtype
+
+
+def _run(q, k, v, prior_fn, alpha, beta, gamma, precision, mode):
+    """The autograd op in the kernels' dtype, with inputs converted and the output returned in q's dtype (the
+    conversions are differentiable, so the gradients come back in the inputs' dtypes)."""
+    cd = _compute_dtype(q, precision, mode)
+    qc, kc, vc = (t if t.dtype == cd else t.to(cd) for t in (q, k, v))
+    o = FusedGeoAttentionV2.apply(qc, kc, vc, prior_fn(cd), alpha, beta, gamma)
+    return o if o.dtype == q.dtype else o.to(q.dtype)
 
 
 def use_preset(name):
@@ -156,27 +188,32 @@ class FusedGeoAttentionV2(torch.autograd.Function):
         return dq, dk, dv, None, grads[0], grads[1], grads[2]
 
 
-def fused_geo_attention_v2(q, k, v, dist, ang, alpha, beta, gamma):
+def fused_geo_attention_v2(q, k, v, dist, ang, alpha, beta, gamma, *, precision=None, mode="reference"):
     """The reference's call (dense [N, N] dist/ang): prior built on the device for this call."""
-    prior = prior_from_dense(dist, ang, q.dtype)
-    return FusedGeoAttentionV2.apply(q, k, v, prior, alpha, beta, gamma)
+    return _run(q, k, v, lambda cd: prior_from_dense(dist, ang, cd), alpha, beta, gamma, precision, mode)
 
 
-def geo_attention(q, k, v, geometry, alpha, beta, gamma):
+def geo_attention(q, k, v, geometry, alpha, beta, gamma, *, precision=None, mode="reference"):
     """Coordinate form: the prior comes from ``geometry`` (a StationGeometry), built once and cached."""
     if not isinstance(geometry, StationGeometry):
         raise TypeError("geometry must be a StationGeometry")
     if geometry.n != q.shape[2]:
         raise ValueError("geometry has %d stations, q has N = %d" % (geometry.n, q.shape[2]))
-    return FusedGeoAttentionV2.apply(q, k, v, geometry.prior(q.dtype), alpha, beta, gamma)
+    return _run(q, k, v, geometry.prior, alpha, beta, gamma, precision, mode)
 
 
-def patch_model(model, preset="accurate_experimental", geometry=None):
+def patch_model(model, preset="accurate_experimental", geometry=None, precision=None, mode="reference"):
     """Swap every encoder layer's attention core for the B200 kernels (foreswe_bench/geo_attention_v2.py:468-478).
 
     With ``geometry`` (a StationGeometry) the layers ignore the dense (distances, angularities) arguments and use
-    the coordinate prior; otherwise the prior is built from the dense arguments at each call. ``preset="eager"``
-    restores the production method (foreswe_bench/geo_attention.py:326-328)."""
+    the coordinate prior; otherwise the prior is built from the dense arguments at each call. ``precision`` and
+    ``mode`` are passed to every call (module docstring). ``preset="eager"`` restores the production method
+    (foreswe_bench/geo_attention.py:326-328)."""
+    if preset != "eager":
+        if precision is not None and precision not in PRECISIONS:
+            raise ValueError("precision must be one of %s, got %r" % (PRECISIONS, precision))
+        if mode not in MODES:
+            raise NotImplementedError("mode=%r: only the reference operator (mode='reference') is implemented" % (mode,))
     for layer in model.encoder_layers:
         att = layer.self_attn
         if preset == "eager":
@@ -187,8 +224,10 @@ def patch_model(model, preset="accurate_experimental", geometry=None):
         def core(Q, K, V, distances, angularities, mask=None, _att=att):
             assert mask is None, "ForeSWE never passes a mask"
             if geometry is not None:
-                return geo_attention(Q, K, V, geometry, _att.alpha, _att.beta, _att.gamma)
-            return fused_geo_attention_v2(Q, K, V, distances, angularities, _att.alpha, _att.beta, _att.gamma)
+                return geo_attention(Q, K, V, geometry, _att.alpha, _att.beta, _att.gamma, precision=precision,
+                                     mode=mode)
+            return fused_geo_attention_v2(Q, K, V, distances, angularities, _att.alpha, _att.beta, _att.gamma,
+                                          precision=precision, mode=mode)
         att.scaled_dot_product_attention = core
     return model
 

@@ -78,6 +78,24 @@ def test_bf16_wide_heads(ops, D):
     _check(res, _oracle(q, k, v, dist, ang, a, b, c, do), TOL[torch.bfloat16], "D=%d" % D)
 
 
+@pytest.mark.parametrize("precision,dtype", [("bf16", torch.float32), ("tf32", torch.bfloat16)])
+def test_precision_override(ops, precision, dtype):
+    """precision='bf16' runs fp32 inputs through the BF16 kernels, precision='tf32' bf16 inputs through the TF32
+    kernels; output and gradients come back in the inputs' dtype, within the BF16 tolerance of the oracle evaluated
+    on the values the kernels saw (inputs and dO rounded to bf16 where the kernels or the output are bf16)."""
+    B, H, N, D = 2, 4, 200, 64
+    q, k, v, a, b, c, do = attn_inputs(B, H, N, D, seed=21, qscale=2.0, dtype=dtype)
+    lat, lon, el = stations(N, seed=22)
+    geom = ops.StationGeometry(lat, lon, el)
+    res = run_device(lambda *x: ops.geo_attention(x[0], x[1], x[2], geom, *x[3:], precision=precision),
+                     q, k, v, a, b, c, do)
+    for key in ("output", "dQ", "dK", "dV"):
+        assert res[key].dtype == dtype, (key, res[key].dtype)
+    qr, kr, vr, dor = (t.to(torch.bfloat16).float() for t in (q, k, v, do))
+    dist, ang = dense_geometry(lat, lon, el)
+    _check(res, _oracle(qr, kr, vr, dist, ang, a, b, c, dor), TOL[torch.bfloat16], "precision=%s" % precision)
+
+
 @pytest.mark.parametrize("D", [128, 192, 96, 160])
 def test_tf32_wide_heads(ops, D):
     """fp32 head dims above 64 (Q/K and dO/V streamed through the score MMAs in 32-wide head-dim chunks), up to the
