@@ -332,6 +332,98 @@ def run_c4(args):
     return 0
 
 
+def run_c5step(args):
+    """The scaling configuration's whole step: x [B/world, N, 2048] -> W_qkv -> geo-attention (16 heads x 128, the
+    kernels on strided views of the fused projection) -> W_o -> loss, forward and backward under bf16 autocast with
+    fp32 weights, and the NCCL all-reduce of dW_qkv, dW_o (67 MB fp32) and d(alpha, beta, gamma), bucketed by DDP and
+    overlapped with the backward. Prints one JSON line (ms per step, whole-step and attention TFLOP/s)."""
+    import datetime
+    import torch.nn as nn
+    import foreswe_gpu_optimization_b200 as g
+    from foreswe_gpu_optimization_b200.dp import shard
+
+    rank, world = int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist_on = world > 1
+    if dist_on:
+        import torch.distributed as tdist
+        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    dm = H * D
+    s0, s1 = shard(B_TOTAL, world, rank)
+    b = s1 - s0
+    geom = g.StationGeometry(*stations(0), device=dev)
+
+    class Step(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.W_qkv = nn.Linear(dm, 3 * dm, bias=False)
+            self.W_o = nn.Linear(dm, dm, bias=False)
+            gp = torch.Generator().manual_seed(7)
+            self.alpha = nn.Parameter(torch.rand(H, generator=gp) * 0.9 + 0.1)
+            self.beta = nn.Parameter(torch.randn(H, generator=gp) * 0.5)
+            self.gamma = nn.Parameter(torch.randn(H, generator=gp) * 0.5)
+
+        def forward(self, x):                   # x [b, N, dm]
+            qkv = self.W_qkv(x).view(b, N, 3, H, D)
+            q, k, v = (qkv[:, :, i].transpose(1, 2) for i in range(3))   # [b, H, N, D] strided views
+            o = g.geo_attention(q, k, v, geom, self.alpha, self.beta, self.gamma)
+            return self.W_o(o.transpose(1, 2).reshape(b, N, dm))
+
+    torch.manual_seed(0)
+    model = Step().to(dev)
+    if dist_on:
+        model = nn.parallel.DistributedDataParallel(model, device_ids=[local], bucket_cap_mb=25)
+    gen = torch.Generator(device=dev).manual_seed(100 + rank)
+    x = torch.randn(b, N, dm, device=dev, generator=gen)
+    target = torch.randn(b, N, dm, device=dev, generator=gen)
+
+    def step():
+        model.zero_grad(set_to_none=True)
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            y = model(x)
+        loss = torch.nn.functional.mse_loss(y.float(), target)
+        loss.backward()
+        return loss
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if dist_on:
+        tdist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        loss = step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    if dist_on:
+        tt = torch.tensor([ms], device=dev, dtype=torch.float64)
+        tdist.all_reduce(tt, op=tdist.ReduceOp.MAX)
+        ms = tt.item()
+    attn_flops = flops(B_TOTAL)
+    proj_flops = 24.0 * B_TOTAL * N * dm * dm          # W_qkv and W_o: forward 8 B N dm^2, backward twice that
+    if rank == 0:
+        line = {"metric": "geo-attention scaling step (W_qkv -> geo-attn -> W_o fwd+bwd + gradient all-reduce), ms/step",
+                "value": ms, "unit": "ms/step", "higher_is_better": False, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "dtype": "bf16 autocast (fp32 weights)", "data": "synthetic",
+                "config": {"workload": "%d issue dates sharded over %d GPU(s) x %d stations, d_model %d, %d heads x %d; "
+                                       "all-reduce of dW_qkv, dW_o (%.0f MB fp32) and d(alpha, beta, gamma) by DDP"
+                                       % (B_TOTAL, world, N, dm, H, D, 4 * dm * dm * 4 / 1e6), "per_gpu_batch": b},
+                "step_tflops": (attn_flops + proj_flops) / (ms * 1e-3) / 1e12,
+                "attention_tflop_per_step": attn_flops / 1e12, "projection_tflop_per_step": proj_flops / 1e12,
+                "loss": float(loss.item())}
+        print(json.dumps(line), flush=True)
+    if dist_on:
+        tdist.barrier()
+        del model
+        tdist.destroy_process_group()
+    return 0
+
+
 # (name, issue dates B, heads H, stations N, head dim D, storage dtype, logit scale on q)
 CONFIGS = (("c2_tf32", 32, 8, 512, 64, torch.float32, 1.0),
            ("c2_tf32_saturated_x30", 32, 8, 512, 64, torch.float32, 30.0),
@@ -440,12 +532,13 @@ def main():
     ap.add_argument("--batch", type=int, default=None, help="override the global batch (small cases for profiling)")
     ap.add_argument("--only", default=None, choices=[c[0] for c in CONFIGS],
                     help="with --workload configs: run this configuration only")
-    ap.add_argument("--workload", default="c5", choices=("c5", "c4", "configs"),
-                    help="c5: the attention scaling configuration (the headline line); c4: a full encoder training "
-                         "step; configs: the other shapes (C2, C3, the reference's published shape), one line each")
+    ap.add_argument("--workload", default="c5", choices=("c5", "c5step", "c4", "configs"),
+                    help="c5: the attention scaling configuration (the headline line); c5step: its whole step with the "
+                         "W_qkv / W_o projections and their gradient all-reduce; c4: a full encoder training step; "
+                         "configs: the other shapes (C2, C3, the reference's published shape), one line each")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
-    if args.batch and args.workload != "configs":
+    if args.batch and args.workload not in ("configs",):
         global B_TOTAL
         B_TOTAL = args.batch
     if args.impl == "reference":
@@ -454,6 +547,8 @@ def main():
         return run_c4(args)
     if args.workload == "configs":
         return run_configs(args)
+    if args.workload == "c5step":
+        return run_c5step(args)
 
     import foreswe_gpu_optimization_b200 as g
     from foreswe_gpu_optimization_b200 import geo_attention_v2 as gv2
