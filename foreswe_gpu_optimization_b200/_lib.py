@@ -8,6 +8,7 @@ import os
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libgeoattn.so")
+ABI_VERSION = 2  # GEOATTN_VERSION of include/geoattn.h that these ctypes structures mirror
 
 GEOATTN_OK = 0
 DTYPE_BF16, DTYPE_FP32 = 0, 1
@@ -83,6 +84,9 @@ def lib():
         L.geoattn_bwd_noalloc.argtypes = [ctypes.POINTER(BwdArgs), ctypes.c_void_p]
         L.geoattn_read_status.restype = ctypes.c_int
         L.geoattn_read_status.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int), ctypes.c_void_p]
+        if L.geoattn_version() != ABI_VERSION:  # argument structs of another layout: refuse before any call
+            raise RuntimeError("%s has ABI version %d, this binding expects %d; rebuild it"
+                               % (LIB_PATH, L.geoattn_version(), ABI_VERSION))
         _LIB = L
     return _LIB
 

@@ -2,6 +2,7 @@
 // (geometry prologue, TF32 operand split, deterministic bias-gradient reduction).
 #include <cuda_fp16.h>
 
+#include <atomic>
 #include <cmath>
 #include <cstdint>
 #include <cstring>
@@ -365,17 +366,18 @@ bool map_output(CUtensorMap* m, void* data, const long long* stride, const Dims&
 
 // Persistent grid: one CTA per SM (every attention kernel holds an SM's tensor memory), at most one per tile.
 dim3 persistent_grid(const Dims& d) {
-  static int sms[64] = {};
+  // SM count per device, looked up once; host threads that race here store the same value
+  static std::atomic<int> sms[64];
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) dev = 0;
-  if (!sms[dev]) {
-    int n = 0;
+  const bool cached = dev >= 0 && dev < 64;
+  int n = cached ? sms[dev].load(std::memory_order_relaxed) : 0;
+  if (n <= 0) {
     if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
-    sms[dev] = n;
+    if (cached) sms[dev].store(n, std::memory_order_relaxed);
   }
   const long long tiles = (long long)d.nrb * d.B * d.H;
-  return dim3((unsigned)(tiles < sms[dev] ? tiles : sms[dev]));
+  return dim3((unsigned)(tiles < n ? tiles : n));
 }
 
 template <class K>
