@@ -61,7 +61,8 @@ def _run(q, k, v, prior_fn, alpha, beta, gamma, precision, mode):
     conversions are differentiable, so the gradients come back in the inputs' dtypes)."""
     cd = _compute_dtype(q, precision, mode)
     qc, kc, vc = (t if t.dtype == cd else t.to(cd) for t in (q, k, v))
-    o = FusedGeoAttentionV2.apply(qc, kc, vc, prior_fn(cd), alpha, beta, gamma)
+    prior = prior_fn(cd) if q.numel() else torch.empty(0, dtype=torch.uint8, device=q.device)
+    o = FusedGeoAttentionV2.apply(qc, kc, vc, prior, alpha, beta, gamma)
     return o if o.dtype == q.dtype else o.to(q.dtype)
 
 
@@ -120,6 +121,8 @@ def _forward(q, k, v, prior, abg, per_head):
         raise RuntimeError("geo attention runs on CUDA tensors only (no CPU path)")
     if prior.device != q.device:
         raise ValueError("the geo prior lives on %s, q on %s" % (prior.device, q.device))
+    if q.numel() == 0:  # an empty batch, head or station set: nothing to launch
+        return torch.empty_like(q), torch.empty(0, dtype=torch.float32, device=q.device)
     q, k, v = _tma_ready(q), _tma_ready(k), _tma_ready(v)
     sh = _shape(q, per_head)
     L = _lib.lib()
@@ -142,6 +145,9 @@ def _forward(q, k, v, prior, abg, per_head):
 def _backward(q, k, v, o, do, prior, abg, stats, per_head):
     """geoattn_bwd on torch tensors: returns (dq, dk, dv, dabg); dq/dk/dv keep the strides of q/k/v."""
     B, H, N, D = q.shape
+    if q.numel() == 0:  # empty input: empty gradients, and the bias-parameter gradients are empty sums
+        return (torch.empty_like(q), torch.empty_like(k), torch.empty_like(v),
+                torch.zeros(3 * (H if per_head else 1), dtype=torch.float32, device=q.device))
     q, k, v = _tma_ready(q), _tma_ready(k), _tma_ready(v)
     do = _tma_ready(do.to(q.dtype))
     sh = _shape(q, per_head)

@@ -96,6 +96,36 @@ def test_precision_override(ops, precision, dtype):
     _check(res, _oracle(qr, kr, vr, dist, ang, a, b, c, dor), TOL[torch.bfloat16], "precision=%s" % precision)
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32], ids=["bf16", "tf32"])
+@pytest.mark.parametrize("shape", [(0, 2, 64, 64), (2, 0, 64, 64), (1, 2, 0, 64)], ids=["B0", "H0", "N0"])
+def test_empty_inputs(ops, dtype, shape):
+    """An empty batch, head set or station set returns empty outputs and gradients and zero bias gradients, as the
+    eager operator does, without launching."""
+    B, H, N, D = shape
+    x = [torch.randn(B, H, N, D, device="cuda").to(dtype).requires_grad_(True) for _ in range(3)]
+    p = [torch.tensor([v], device="cuda", requires_grad=True) for v in (0.5, -0.2, 0.3)]
+    dist = torch.zeros(N, N, device="cuda")
+    o = ops.fused_geo_attention_v2(*x, dist, dist, *p)
+    assert o.shape == (B, H, N, D) and o.dtype == dtype
+    o.sum().backward()
+    for t in x:
+        assert t.grad.shape == t.shape
+    for t in p:
+        assert t.grad is not None and t.grad.item() == 0.0
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32], ids=["bf16", "tf32"])
+def test_many_chunks_per_row(ops, dtype):
+    """N = 1500 stations (24 bf16 / 47 fp32 key chunks per row, 12 row blocks, ragged last chunk and block)."""
+    B, H, N, D = 1, 2, 1500, 64
+    q, k, v, a, b, c, do = attn_inputs(B, H, N, D, seed=31, qscale=2.0, dtype=dtype)
+    lat, lon, el = stations(N, seed=32)
+    geom = ops.StationGeometry(lat, lon, el)
+    res = run_device(lambda *x: ops.geo_attention(x[0], x[1], x[2], geom, *x[3:]), q, k, v, a, b, c, do)
+    dist, ang = dense_geometry(lat, lon, el)
+    _check(res, _oracle(q, k, v, dist, ang, a, b, c, do), TOL[dtype], "N=1500 %s" % dtype)
+
+
 @pytest.mark.parametrize("D", [128, 192, 96, 160])
 def test_tf32_wide_heads(ops, D):
     """fp32 head dims above 64 (Q/K and dO/V streamed through the score MMAs in 32-wide head-dim chunks), up to the
