@@ -8,7 +8,7 @@ Restates foreswe_bench/attn_check.py:
     against the float64 oracle must be <= 10 x eager's max-abs error (same precision, same dO) + 1e-7*max|ref|;
   * ``err``          (:57-65) -- max-abs, rel-L2 and cosine against the reference.
 
-The north-star tolerances (rel-L2 vs the FP32 operator: 5e-4 for TF32, 8e-3 for BF16) are ``REL_L2_TOL``.
+The path's stated tolerances (rel-L2 vs the FP32 operator: 5e-4 for TF32, 8e-3 for BF16) are ``REL_L2_TOL``.
 Eager's own error is computed here on the CPU: fp32 directly, TF32 with operands rounded to TF32
 (``geo_attention.tf32_matmul``), which is the error model of cuBLAS TF32.
 """

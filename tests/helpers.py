@@ -4,7 +4,7 @@ import torch
 
 from oracle import geometry as ogeo
 
-TOL = {torch.bfloat16: 8e-3, torch.float32: 5e-4}   # rel-L2 vs the FP32 operator
+TOL = {torch.bfloat16: 8e-3, torch.float32: 5e-4}   # rel-L2 vs the FP32 operator (the path's stated tolerances)
 KEYS = ("output", "dQ", "dK", "dV", "dalpha", "dbeta", "dgamma")
 
 

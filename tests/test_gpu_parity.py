@@ -42,7 +42,7 @@ def _check(res, ref, tol, label):
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32], ids=["bf16", "tf32"])
 @pytest.mark.parametrize("qscale", [1.0, 30.0], ids=["plain", "saturated_x30"])
 def test_c2_shape_coordinate_geometry(ops, dtype, qscale):
-    """N = 512 stations, D = 64, per-head parameters, prior from coordinates (the north-star call)."""
+    """N = 512 stations, D = 64, per-head parameters, prior from coordinates (the coordinate call form)."""
     B, H, N, D = 2, 4, 512, 64
     q, k, v, a, b, c, do = attn_inputs(B, H, N, D, seed=1, qscale=qscale, dtype=dtype)
     lat, lon, el = stations(N, seed=2)
