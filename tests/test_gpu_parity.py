@@ -216,18 +216,20 @@ def test_reference_golden_vectors_tf32(ops, path):
         assert e <= 5e-4 or ev[key]["passed"], (key, e, ev[key]["candidate"]["max_abs"], ev[key]["bound"])
 
 
-def test_split_heads_strided_views(ops):
+@pytest.mark.parametrize("dtype,D", [(torch.bfloat16, 64), (torch.float32, 64), (torch.float32, 192)],
+                         ids=["bf16-d64", "tf32-d64", "tf32-d192"])
+def test_split_heads_strided_views(ops, dtype, D):
     """Q/K/V as the transposed split_heads views of [B, N, H*D] (custom_encoder_model.py:41-43); gradients keep
     the input strides."""
-    B, N, H, D = 2, 160, 4, 64
+    B, N, H = 2, 160, 4
     g = torch.Generator().manual_seed(5)
-    base = [torch.randn(B, N, H * D, generator=g).cuda().to(torch.bfloat16) * 0.4 for _ in range(3)]
+    base = [torch.randn(B, N, H * D, generator=g).cuda().to(dtype) * 0.4 for _ in range(3)]
     views = [t.view(B, N, H, D).transpose(1, 2).detach().requires_grad_(True) for t in base]
     a, b, c = (torch.tensor([x], device="cuda", requires_grad=True) for x in (0.5, -0.3, 0.2))
     dist = torch.rand(N, N, generator=g).cuda() * 900
     ang = torch.rand(N, N, generator=g).cuda() * 12
     o = ops.fused_geo_attention_v2(*views, dist, ang, a, b, c)
-    do = torch.randn(o.shape, generator=g).cuda().to(torch.bfloat16)
+    do = torch.randn(o.shape, generator=g).cuda().to(dtype)
     o.backward(do)
     for x in views:
         assert x.grad.stride() == x.stride()
@@ -237,7 +239,7 @@ def test_split_heads_strided_views(ops):
                     a.detach().cpu(), b.detach().cpu(), c.detach().cpu(), do.double().cpu())
     res = dict(output=o.detach().cpu(), dQ=views[0].grad.cpu(), dK=views[1].grad.cpu(), dV=views[2].grad.cpu(),
                dalpha=a.grad.cpu(), dbeta=b.grad.cpu(), dgamma=c.grad.cpu())
-    _check(res, ref, TOL[torch.bfloat16], "strided")
+    _check(res, ref, TOL[dtype], "strided %s D=%d" % (dtype, D))
 
 
 def test_device_geometry_matches_oracle(ops):
