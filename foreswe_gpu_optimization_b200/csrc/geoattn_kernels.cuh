@@ -447,17 +447,6 @@ __device__ __forceinline__ void store_tile(const CUtensorMap* map, const uint8_t
   }
 }
 
-// Prior access for one chunk: staged tile in shared memory, or the table in global memory.
-template <bool F16, bool STAGED>
-__device__ __forceinline__ void prior_piece(const uint8_t* tile, const void* table, int np, int row, int r, int c,
-                                            int piece, Prior32<F16>& pr) {
-  if constexpr (STAGED) {
-    prior32_smem<F16>(tile, r, piece, pr);
-  } else {
-    load_prior32<F16>(table, np, row, c * (F16 ? 64 : 32) + piece * 32, pr);
-  }
-}
-
 // ===============================================================================================================
 // Forward: one CTA per (128-query row block, b*h). Pass A: row max / sum of softmax #1 over all key chunks.
 // Pass B: recompute S, form P1, Z and e = 2^((Z-c) log2 e), accumulate O += e V and l2 = sum e.
@@ -1674,6 +1663,13 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       const int gc = it * nchunks + c;
       const int ss = gc % NSB, rs = gc % NR, ts = gc % NST;
       if (!ok) continue;
+      Prior32<BF16> pr;
+      // prior from L2 (no staged tile, fp32 only: one piece per chunk): loads issued before the waits, so that their
+      // latency overlaps the wait for the chunk's scores instead of following it
+      if constexpr (NPR == 0) {
+        static_assert(T::PIECES == 1 && T::EW == 1, "prior read from L2 in one piece per chunk");
+        load_prior32<BF16>(p.priorT, p.np, pkey, c * T::CH, pr);
+      }
       if (!(ok = warp_wait(&bar_sfull[ss], (gc / NSB) & 1, ctx))) continue;
       if constexpr (NPR > 0)
         if (!(ok = warp_wait(&bar_prfull[gc % NPR], (gc / NPR) & 1, ctx))) continue;
@@ -1689,8 +1685,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         uint32_t vs[32], ws[32];
         tmem_ld32_issue(e.lane_base + C::TM_S + ss * T::CH + piece * 32, vs);
         tmem_ld32_issue(e.lane_base + C::TM_DP + ss * T::CH + piece * 32, ws);
-        Prior32<BF16> pr;
-        prior_piece<BF16, (NPR > 0)>(prt, p.priorT, p.np, pkey, e.r, c, piece, pr);
+        if constexpr (NPR > 0) prior32_smem<BF16>(prt, e.r, piece, pr);
         tmem_wait32(vs);
         tmem_pin32(ws);
         tc_fence_before();
