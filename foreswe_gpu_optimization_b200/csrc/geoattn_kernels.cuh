@@ -883,8 +883,10 @@ struct RowsCfg : Tile<BF16, DP> {
   // K ring's slots (the V ring is unused)
   static constexpr bool WIDE = !BF16 && DP > 64;
   static constexpr int NDC = WIDE ? DP / T::KB : 1;
-  static constexpr int NKV = WIDE ? 3 : (!BF16 || DP > 128) ? 1 : (DQ ? 2 : 3);  // K/V chunk buffers / ring slots
-  static constexpr int NPR = (BF16 && DP <= 128) ? 2 : 1;   // staged prior buffers
+  // fp32 at head dim 64: the prior is read from L2 (loads issued before each chunk's wait, as in the key pass), and
+  // the shared memory a staged prior tile would take holds a second K/V buffer instead
+  static constexpr int NKV = WIDE ? 3 : (DP > 128) ? 1 : (!BF16 || DQ) ? 2 : 3;  // K/V chunk buffers / ring slots
+  static constexpr int NPR = (BF16 && DP <= 128) ? 2 : (!BF16 && !WIDE) ? 0 : 1;  // staged prior buffers (0: L2)
   static constexpr int Q_BYTES = WIDE ? 0 : kBM * DP * T::EB;                   // per plane (Q and dO)
   static constexpr int K_BYTES = WIDE ? kSlotPlaneBytes : T::CH * DP * T::EB;  // per plane per buffer / slot
   static constexpr int KT_BYTES = BF16 ? 0 : DP * 128;  // fp32: transposed K chunk (hi) for dQ
@@ -925,6 +927,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
   using C = RowsCfg<BF16, DP, DQ>;
   using T = typename C::T;
   constexpr int NKV = C::NKV, NPR = C::NPR, NSB = C::NSB;
+  constexpr int PRB = NPR > 0 ? NPR : 1;  // prior-ring modulus (unused when the prior is read from L2)
   if (smem_misaligned(p.status)) return;  // uniform over the CTA, before any barrier or allocation
   uint8_t* smem = smem_raw;
   __shared__ uint64_t bar_qfull, bar_qempty, bar_kfull[3], bar_kempty[3], bar_vfull[3], bar_vempty[3], bar_sfull[4],
@@ -1039,6 +1042,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       }
     }
   } else if (warp == T::PR_WARP) {
+    if constexpr (NPR > 0) {
     prefetch_tmap(&maps.prior);
     int pc = 0;
     bool ok = true;
@@ -1056,6 +1060,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         }
       }
       ok = __shfl_sync(0xffffffffu, ok, 0);
+    }
     }
   } else if (warp == T::MMA_WARP) {
     if (lane == 0) {
@@ -1173,9 +1178,12 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
     }
     float acc[3] = {0.f, 0.f, 0.f};  // delta2, a, b
     for (int c = 0; c < nchunks && ok; ++c) {
-      const int ss = sc % NSB, prs = pc % NPR;
+      const int ss = sc % NSB, prs = pc % PRB;
+      Prior32<BF16> pr;
+      if constexpr (NPR == 0) load_prior32<BF16>(p.prior, p.np, row, c * T::CH, pr);  // before the waits
       if (!(ok = warp_wait(&bar_sfull[ss], (sc / NSB) & 1, ctx))) break;
-      if (!(ok = warp_wait(&bar_prfull[prs], (pc / NPR) & 1, ctx))) break;
+      if constexpr (NPR > 0)
+        if (!(ok = warp_wait(&bar_prfull[prs], (pc / PRB) & 1, ctx))) break;
       tc_fence_after();
       const uint8_t* prt = smem + C::OFF_PR + prs * kPriorTileBytes;
 #pragma unroll 1
@@ -1184,8 +1192,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         tmem_ld32_issue(e.lane_base + C::TM_S + ss * T::CH + piece * 32, vs);
         tmem_ld32_issue(e.lane_base + C::TM_DP + ss * T::CH + piece * 32, ws);
         const int nvalid = p.N - (c * T::CH + piece * 32);
-        Prior32<BF16> pr;
-        prior32_smem<BF16>(prt, e.r, piece, pr);
+        if constexpr (NPR > 0) prior32_smem<BF16>(prt, e.r, piece, pr);
         tmem_wait32(vs);
         tmem_pin32(ws);
         tc_fence_before();
@@ -1215,7 +1222,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         else body(std::true_type{});
 #pragma unroll
         for (int k = 0; k < 3; ++k) acc[k] += pa[0][k] + pa[1][k];
-        mbar_arrive(&bar_prempty[prs]);  // every value read from the prior tile has been used
+        if constexpr (NPR > 0) mbar_arrive(&bar_prempty[prs]);  // every value read from the prior tile has been used
       }
       ++sc;
       ++pc;
@@ -1266,9 +1273,12 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
     float gap[2] = {0.f, 0.f}, gbp[2] = {0.f, 0.f}, ggp[2] = {0.f, 0.f};  // d(alpha), d(beta), d(gamma) of the row
     if constexpr (DQ) {
     for (int c = 0; c < nchunks && ok; ++c) {
-      const int ss = sc % NSB, ds = dc % C::NDS, prs = pc % NPR;
+      const int ss = sc % NSB, ds = dc % C::NDS, prs = pc % PRB;
+      Prior32<BF16> pr;
+      if constexpr (NPR == 0) load_prior32<BF16>(p.prior, p.np, row, c * T::CH, pr);  // before the waits
       if (!(ok = warp_wait(&bar_sfull[ss], (sc / NSB) & 1, ctx))) break;
-      if (!(ok = warp_wait(&bar_prfull[prs], (pc / NPR) & 1, ctx))) break;
+      if constexpr (NPR > 0)
+        if (!(ok = warp_wait(&bar_prfull[prs], (pc / PRB) & 1, ctx))) break;
       tc_fence_after();
       uint8_t* dreg = smem + C::OFF_DS + ds * C::DS_BYTES;
       const uint8_t* prt = smem + C::OFF_PR + prs * kPriorTileBytes;
@@ -1279,8 +1289,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         tmem_ld32_issue(e.lane_base + C::TM_DP + ss * T::CH + piece * 32, ws);
         const int nvalid = p.N - (c * T::CH + piece * 32);
         float v[32];
-        Prior32<BF16> pr;
-        prior32_smem<BF16>(prt, e.r, piece, pr);
+        if constexpr (NPR > 0) prior32_smem<BF16>(prt, e.r, piece, pr);
         tmem_wait32(vs);
         tmem_pin32(ws);
         tc_fence_before();
@@ -1307,7 +1316,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         };
         if (nvalid >= 32) body(std::false_type{});
         else body(std::true_type{});
-        mbar_arrive(&bar_prempty[prs]);  // every value read from the prior tile has been used
+        if constexpr (NPR > 0) mbar_arrive(&bar_prempty[prs]);  // every value read from the prior tile has been used
         // the dS buffer is free once the dQ MMA that read it has run (waited here, after the math)
         if (!(ok = warp_wait(&bar_dsempty[ds], ((dc / C::NDS) & 1) ^ 1, ctx))) break;
         stage_row32<BF16>(dreg, e.r, piece, v);
