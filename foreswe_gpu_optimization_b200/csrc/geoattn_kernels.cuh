@@ -457,8 +457,10 @@ struct FwdCfg : Tile<BF16, DP> {
   // fp32 beyond 64: no resident Q; Q and K reach the score MMA in head-dim chunks through the K ring's slots
   static constexpr bool WIDE = !BF16 && DP > 64;
   static constexpr int NDC = WIDE ? DP / T::KB : 1;                    // head-dim chunks per score MMA
-  static constexpr int NPR = (WIDE || (BF16 && DP > 128)) ? 1 : 2;   // staged prior buffers
-  static constexpr int NK = ((WIDE && DP <= 128) || (BF16 && DP <= 128)) ? 3 : 2;  // K ring slots
+  // wide fp32: the prior is read from L2 (loads issued before each chunk's wait) instead of a single staged buffer,
+  // and the shared memory goes to a third K ring slot at every head dim
+  static constexpr int NPR = WIDE ? 0 : (BF16 && DP > 128) ? 1 : 2;  // staged prior buffers (0: L2)
+  static constexpr int NK = (WIDE || (BF16 && DP <= 128)) ? 3 : 2;  // K ring slots
   static constexpr int Q_BYTES = WIDE ? 0 : kBM * DP * T::EB;          // per plane
   static constexpr int K_BYTES = WIDE ? kSlotPlaneBytes : T::CH * DP * T::EB;  // per plane per ring slot
   static constexpr int V_BYTES = T::CH * DP * T::EB;        // hi only (natural bf16 / transposed fp32)
@@ -486,6 +488,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
   using C = FwdCfg<BF16, DP>;
   using T = typename C::T;
   constexpr int NPR = C::NPR, NK = C::NK, NSB = C::NSB;
+  constexpr int PRB = NPR > 0 ? NPR : 1;  // prior-ring modulus (unused when the prior is read from L2)
   static_assert(!C::EPI_TMA || T::EW > 1, "the TMA epilogue relies on the warpgroup exchange barrier");
   if (smem_misaligned(p.status)) return;  // uniform over the CTA, before any barrier or allocation
   uint8_t* smem = smem_raw;
@@ -587,15 +590,15 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       }
     }
   } else if (warp == T::PR_WARP) {
-    if (lane == 0) {
+    if (NPR > 0 && lane == 0) {
       prefetch_tmap(&maps.prior);
       int prc = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
         const int rb = tile % p.nrb;
         for (int c = 0; c < nchunks && ok; ++c) {  // pass B only
-          const int ps = prc % NPR;
-          if (!(ok = mbar_wait(&bar_prempty[ps], ((prc / NPR) & 1) ^ 1, ctx))) break;
+          const int ps = prc % PRB;
+          if (!(ok = mbar_wait(&bar_prempty[ps], ((prc / PRB) & 1) ^ 1, ctx))) break;
           mbar_arrive_expect_tx(&bar_prfull[ps], kPriorTileBytes);
           tma_prior(smem + C::OFF_PR + ps * kPriorTileBytes, &maps.prior, &bar_prfull[ps], rb * kBM, c);
           ++prc;
@@ -781,18 +784,23 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       float l2 = 0.f;
       // Pass B
       for (int c = 0; c < nchunks && ok; ++c) {
-        const int ss = sc % NSB, ps = pc & 1, prs = prc % NPR;
+        const int ss = sc % NSB, ps = pc & 1, prs = prc % PRB;
+        Prior32<BF16> pr;
+        if constexpr (NPR == 0) {  // from L2, issued before the waits (one piece per chunk)
+          static_assert(T::PIECES == 1 && T::EW == 1, "prior read from L2 in one piece per chunk");
+          load_prior32<BF16>(p.prior, p.np, row, c * T::CH, pr);
+        }
         if (!(ok = warp_wait(&bar_sfull[ss], (sc / NSB) & 1, ctx))) break;
-        if (!(ok = warp_wait(&bar_prfull[prs], (prc / NPR) & 1, ctx))) break;
+        if constexpr (NPR > 0)
+          if (!(ok = warp_wait(&bar_prfull[prs], (prc / PRB) & 1, ctx))) break;
         tc_fence_after();
         uint8_t* preg = smem + C::OFF_P + ps * C::P_BYTES;
         const uint8_t* prt = smem + C::OFF_PR + prs * kPriorTileBytes;
         {
           uint32_t vs[32];
           float v[32];
-          Prior32<BF16> pr;
           tmem_ld32_issue(e.lane_base + C::TM_S + ss * T::CH + piece * 32, vs);
-          prior32_smem<BF16>(prt, e.r, piece, pr);  // overlaps the tensor-memory load
+          if constexpr (NPR > 0) prior32_smem<BF16>(prt, e.r, piece, pr);  // overlaps the tensor-memory load
           tmem_wait32(vs);
           tc_fence_before();
           mbar_arrive(&bar_sempty[ss]);  // the scores are in registers: the MMA may refill the buffer
@@ -817,7 +825,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
           else body(std::true_type{});
           l2 += (l24[0] + l24[1]) + (l24[2] + l24[3]);
           // the prior tile is released once every value read from it has been used (not when the loads are issued)
-          mbar_arrive(&bar_prempty[prs]);
+          if constexpr (NPR > 0) mbar_arrive(&bar_prempty[prs]);
           // the P buffer is free once the P.V two chunks back has run (waited here, after the math)
           if (!(ok = warp_wait(&bar_pempty[ps], ((pc >> 1) & 1) ^ 1, ctx))) break;
           stage_row32<BF16>(preg, e.r, piece, v);
@@ -883,10 +891,10 @@ struct RowsCfg : Tile<BF16, DP> {
   // K ring's slots (the V ring is unused)
   static constexpr bool WIDE = !BF16 && DP > 64;
   static constexpr int NDC = WIDE ? DP / T::KB : 1;
-  // fp32 at head dim 64: the prior is read from L2 (loads issued before each chunk's wait, as in the key pass), and
-  // the shared memory a staged prior tile would take holds a second K/V buffer instead
+  // fp32: the prior is read from L2 (loads issued before each chunk's wait, as in the key pass); at head dim 64 the
+  // shared memory a staged prior tile would take holds a second K/V buffer instead
   static constexpr int NKV = WIDE ? 3 : (DP > 128) ? 1 : (!BF16 || DQ) ? 2 : 3;  // K/V chunk buffers / ring slots
-  static constexpr int NPR = (BF16 && DP <= 128) ? 2 : (!BF16 && !WIDE) ? 0 : 1;  // staged prior buffers (0: L2)
+  static constexpr int NPR = (BF16 && DP <= 128) ? 2 : !BF16 ? 0 : 1;  // staged prior buffers (0: L2)
   static constexpr int Q_BYTES = WIDE ? 0 : kBM * DP * T::EB;                   // per plane (Q and dO)
   static constexpr int K_BYTES = WIDE ? kSlotPlaneBytes : T::CH * DP * T::EB;  // per plane per buffer / slot
   static constexpr int KT_BYTES = BF16 ? 0 : DP * 128;  // fp32: transposed K chunk (hi) for dQ
