@@ -328,6 +328,50 @@ __device__ __forceinline__ void mma_qk(uint32_t tmem_acc, uint32_t a_base, uint3
   }
 }
 
+// Tensor-memory columns of a 128-row operand held as an MMA A operand: DP elements per plane, 32 bits per column.
+template <class T>
+constexpr int kAColsPerPlane = T::DP * T::EB / 4;
+
+// Copies a resident 128-row K-major operand (planes hi[, lo] at a_plane byte strides, NKB swizzled regions each)
+// from shared memory into tensor memory as an A operand: plane pl, head-dim element d -> lane = row, column
+// tmem_a + pl * kAColsPerPlane + d * EB / 4. One 128x256b copy per MMA K step. Every MMA that read the previous
+// contents of these columns must have completed before this is issued (copies after MMAs are not ordered).
+template <class T>
+__device__ __forceinline__ void cp_operand_tmem(uint32_t tmem_a, uint32_t a_base, uint32_t a_plane) {
+  constexpr int STEPS = T::DP / T::KS;
+  static_assert(T::KS * T::EB == 32, "one MMA K step is 256 bits");
+#pragma unroll
+  for (int pl = 0; pl < T::PL; ++pl)
+#pragma unroll
+    for (int s = 0; s < STEPS; ++s) {
+      const int kb = (s * T::KS) / T::KB;
+      const uint32_t w = (uint32_t)((s * T::KS) % T::KB) * T::EB;
+      tmem_cp_128x256b(tmem_a + pl * kAColsPerPlane<T> + s * 8,
+                       smem_desc_sw128(a_base + pl * a_plane + kb * (128 * 128) + w, 16, 1024));
+    }
+}
+
+// mma_qk with A = the whole head dimension of a tensor-memory operand copied by cp_operand_tmem, B in shared memory.
+template <class T, int NB>
+__device__ __forceinline__ void mma_qk_ts(uint32_t tmem_acc, uint32_t tmem_a, uint32_t b_base, uint32_t b_plane) {
+  constexpr uint32_t idesc = instr_desc(T::FMT, 0, 0, 128, NB);
+  constexpr int STEPS = T::DP / T::KS;
+  int first = 1;
+#pragma unroll
+  for (int term = 0; term < T::NTERM; ++term) {
+    const uint32_t ap = (term == 2) ? kAColsPerPlane<T> : 0;  // (hi,hi), (hi,lo), (lo,hi)
+    const uint32_t bp = (term == 1) ? b_plane : 0;
+#pragma unroll
+    for (int s = 0; s < STEPS; ++s) {
+      const int kb = (s * T::KS) / T::KB;
+      const uint32_t w = (uint32_t)((s * T::KS) % T::KB) * T::EB;
+      const uint64_t bd = smem_desc_sw128(b_base + bp + kb * (NB * 128) + w, 16, 1024);
+      mma_ts<T::KIND>(tmem_acc, tmem_a + ap + s * 8, bd, idesc, first ? 0u : 1u);
+      first = 0;
+    }
+  }
+}
+
 // Issue acc[128 x DP] (+)= P[128 x CH] . V where P is one K-major region (128 x 128 B) and V is either
 //   bf16: the natural chunk [CH rows x DP] (MN-major B: regions per 64-wide D block of CH x 128 B), or
 //   fp32: the transposed chunk [DP rows x CH] (K-major B: one region of DP x 128 B).
@@ -1407,10 +1451,17 @@ struct ColsCfg : Tile<BF16, DP> {
   static constexpr bool WIDE = !BF16 && DP > 64;
   static constexpr int NDC = WIDE ? DP / T::KB : 1;
   static constexpr int NRS = WIDE ? 3 : 0;
-  static constexpr int NQ = (BF16 && DP <= 128) ? 3 : 1;   // query-chunk (Q, dO) buffers
-  static constexpr int NSB = (BF16 && DP <= 128) ? 2 : 1;  // S^T / dP^T accumulator buffers in tensor memory
+  // fp32 at head dim 64 ("pooled"): the K and V blocks (hi/lo planes) are the tensor-memory A operands of the S^T and
+  // dP^T MMAs. They land by TMA in a shared-memory pool that, once copied into tensor memory, holds the query-chunk
+  // ring for the rest of the tile: the landing takes the ring's next NQ positions, so the ring's order and phases
+  // carry the hand-over both ways.
+  static constexpr bool POOL = !BF16 && !WIDE;
+  static constexpr int NQ = (BF16 && DP <= 128) ? 3 : POOL ? 2 : 1;   // query-chunk (Q, dO) buffers
+  static constexpr int NSB = ((BF16 && DP <= 128) || POOL) ? 2 : 1;  // S^T / dP^T accumulator buffers in TMEM
+  static constexpr int LAND = POOL ? NQ : 0;               // ring positions the K/V landing takes per tile
+  static_assert(LAND == 0 || LAND == NQ, "a landing takes every slot of the ring once");
   static constexpr int NR = 2;                             // row-record buffers
-  static constexpr int NST = (BF16 && DP <= 64) ? 2 : 1;   // buffers for the staged P2^T / dS^T tiles
+  static constexpr int NST = ((BF16 && DP <= 64) || POOL) ? 2 : 1;  // buffers for the staged P2^T / dS^T tiles
   static constexpr int NPR = !BF16 ? 0 : (DP <= 64 ? 2 : 1);  // staged prior buffers (0: read from L2)
   static constexpr int K_BYTES = WIDE ? 0 : kBM * DP * T::EB;    // per plane (K and V blocks)
   static constexpr int Q_BYTES = WIDE ? 0 : T::CH * DP * T::EB;  // per plane per buffer (Q and dO chunks)
@@ -1420,11 +1471,14 @@ struct ColsCfg : Tile<BF16, DP> {
   static constexpr int OFF_RS = 0;
   static constexpr int OFF_K = OFF_RS + NRS * 2 * kSlotPlaneBytes;
   static constexpr int OFF_V = OFF_K + T::PL * K_BYTES;
-  static constexpr int OFF_Q = OFF_V + T::PL * K_BYTES;
+  static constexpr int KV_END = OFF_V + T::PL * K_BYTES;
+  static constexpr int OFF_Q = POOL ? OFF_K : KV_END;
   static constexpr int OFF_DO = OFF_Q + NQ * T::PL * Q_BYTES;
   static constexpr int OFF_QT = OFF_DO + NQ * T::PL * Q_BYTES;
   static constexpr int OFF_DOT = OFF_QT + NQ * QT_BYTES;
-  static constexpr int OFF_P2 = OFF_DOT + NQ * QT_BYTES;
+  static constexpr int RING_END = OFF_DOT + NQ * QT_BYTES;
+  static_assert(!POOL || RING_END <= KV_END, "the query-chunk ring lies inside the K/V pool");
+  static constexpr int OFF_P2 = POOL ? KV_END : RING_END;
   static constexpr int OFF_DS = OFF_P2 + NST * ST_BYTES;
   static constexpr int OFF_PR = OFF_DS + NST * ST_BYTES;
   static constexpr int OFF_REC = OFF_PR + NPR * kPriorTileBytes;
@@ -1434,7 +1488,11 @@ struct ColsCfg : Tile<BF16, DP> {
   static constexpr int TM_DP = NSB * T::CH;
   static constexpr int TM_DK = 2 * NSB * T::CH;
   static constexpr int TM_DV = TM_DK + DP;
-  static constexpr int TMEM_COLS = pow2_cols(2 * NSB * T::CH + 2 * DP);
+  static constexpr int TM_KA = TM_DV + DP;                                      // pooled: K (hi, lo) as A operand
+  static constexpr int TM_VA = TM_KA + (POOL ? T::PL * kAColsPerPlane<T> : 0);  // pooled: V (hi, lo)
+  static constexpr int TMEM_NEED = TM_VA + (POOL ? T::PL * kAColsPerPlane<T> : 0);
+  static_assert(TMEM_NEED <= 512, "key pass: tensor-memory columns above 512");
+  static constexpr int TMEM_COLS = pow2_cols(TMEM_NEED);
   // dK and dV leave in turn through the P2^T / dS^T buffers (contiguous, free once the tile's last MMA has run)
   static constexpr bool EPI_TMA = BF16 && T::NKB * kBM * 128 <= 2 * NST * ST_BYTES;
 };
@@ -1517,7 +1575,14 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         mbar_arrive(&bar_tempty[ts]);
         return true;
       };
-      if constexpr (!C::WIDE) {  // K and V blocks once the previous tile's last S^T/dP^T MMAs have read the old ones
+      const int q0 = it * (nchunks + C::LAND) + C::LAND;  // query-chunk ring position of chunk 0
+      if constexpr (C::POOL) {  // K and V into the pool once its ring positions are free (the previous tile's MMAs ran)
+        for (int s = q0 - C::LAND; s < q0 && ok; ++s) ok = mbar_wait(&bar_qempty[s % NQ], ((s / NQ) & 1) ^ 1, ctx);
+        if (!ok) break;
+        mbar_arrive_expect_tx(&bar_kvfull, 2 * T::PL * C::K_BYTES);
+        tma_tile<T>(smem + C::OFF_K, &maps.k, &bar_kvfull, kBM, kblk * kBM, h, b, p.B, T::PL);
+        tma_tile<T>(smem + C::OFF_V, &maps.v, &bar_kvfull, kBM, kblk * kBM, h, b, p.B, T::PL);
+      } else if constexpr (!C::WIDE) {  // K and V blocks once the previous tile's last S^T/dP^T MMAs read the old ones
         if (!(ok = mbar_wait(&bar_kvempty, (it & 1) ^ 1, ctx))) break;
         mbar_arrive_expect_tx(&bar_kvfull, 2 * T::PL * C::K_BYTES);
         tma_tile<T>(smem + C::OFF_K, &maps.k, &bar_kvfull, kBM, kblk * kBM, h, b, p.B, T::PL);
@@ -1530,8 +1595,9 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       }
       for (int c = 0; c < nchunks; ++c) {
         const int gc = it * nchunks + c;  // chunk count over all tiles (buffer slots and phases)
-        const int qs = gc % NQ;
-        if (!(ok = mbar_wait(&bar_qempty[qs], ((gc / NQ) & 1) ^ 1, ctx))) break;
+        const int gq = q0 + c;            // query-chunk ring position
+        const int qs = gq % NQ;
+        if (!(ok = mbar_wait(&bar_qempty[qs], ((gq / NQ) & 1) ^ 1, ctx))) break;
         mbar_arrive_expect_tx(&bar_qfull[qs], 2 * T::PL * C::Q_BYTES + 2 * C::QT_BYTES);
         if constexpr (!C::WIDE) {
           tma_tile<T>(smem + C::OFF_Q + qs * T::PL * C::Q_BYTES, &maps.q, &bar_qfull[qs], T::CH, c * T::CH, h, b,
@@ -1593,6 +1659,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
     if (lane == 0) {
       bool ok = true;
       int it = 0, rc = 0;
+      int qoff = 0;  // query-chunk ring position minus chunk count (the pooled K/V landings take ring positions)
       auto issue_s = [&](int gc) -> bool {
         if constexpr (C::WIDE) {
           const int ss = gc % NSB;
@@ -1609,33 +1676,54 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
           mma_commit(&bar_sfull[ss]);
           return true;
         }
-        const int qs = gc % NQ, ss = gc % NSB;
-        if (!mbar_wait(&bar_qfull[qs], (gc / NQ) & 1, ctx)) return false;
+        const int gq = gc + qoff, qs = gq % NQ, ss = gc % NSB;
+        // phases of bar_qfull[qs] count only query-chunk loads; the pooled landings (one per slot per tile, this
+        // tile's included) complete no phase of it
+        const int qpar = ((gq / NQ) - (C::POOL ? it + 1 : 0)) & 1;
+        if (!mbar_wait(&bar_qfull[qs], qpar, ctx)) return false;
         if (!mbar_wait(&bar_sempty[ss], ((gc / NSB) & 1) ^ 1, ctx)) return false;
         tc_fence_after();
-        mma_qk<T, T::CH>(tmem + C::TM_S + ss * T::CH, sbase + C::OFF_K, C::K_BYTES,
-                         sbase + C::OFF_Q + qs * T::PL * C::Q_BYTES, C::Q_BYTES);
-        mma_qk<T, T::CH>(tmem + C::TM_DP + ss * T::CH, sbase + C::OFF_V, C::K_BYTES,
-                         sbase + C::OFF_DO + qs * T::PL * C::Q_BYTES, C::Q_BYTES);
+        if constexpr (C::POOL) {
+          mma_qk_ts<T, T::CH>(tmem + C::TM_S + ss * T::CH, tmem + C::TM_KA,
+                              sbase + C::OFF_Q + qs * T::PL * C::Q_BYTES, C::Q_BYTES);
+          mma_qk_ts<T, T::CH>(tmem + C::TM_DP + ss * T::CH, tmem + C::TM_VA,
+                              sbase + C::OFF_DO + qs * T::PL * C::Q_BYTES, C::Q_BYTES);
+        } else {
+          mma_qk<T, T::CH>(tmem + C::TM_S + ss * T::CH, sbase + C::OFF_K, C::K_BYTES,
+                           sbase + C::OFF_Q + qs * T::PL * C::Q_BYTES, C::Q_BYTES);
+          mma_qk<T, T::CH>(tmem + C::TM_DP + ss * T::CH, sbase + C::OFF_V, C::K_BYTES,
+                           sbase + C::OFF_DO + qs * T::PL * C::Q_BYTES, C::Q_BYTES);
+        }
         mma_commit(&bar_sfull[ss]);
         return true;
       };
       for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++it) {
-      const int g0 = it * nchunks;
+      const int g0 = it * nchunks, q0 = it * (nchunks + C::LAND) + C::LAND;
+      qoff = q0 - g0;
       if constexpr (!C::WIDE)
         if (!(ok = mbar_wait(&bar_kvfull, it & 1, ctx))) break;
+      if constexpr (C::POOL) {
+        // K and V into tensor memory. The previous tile's S^T/dP^T MMAs, the last readers of these columns, completed
+        // before its last query chunks' ring positions were released, and the TMA warp loaded this K/V only after
+        // that. The landing's ring positions are released once the copies have read the pool.
+        tc_fence_after();
+        cp_operand_tmem<T>(tmem + C::TM_KA, sbase + C::OFF_K, C::K_BYTES);
+        cp_operand_tmem<T>(tmem + C::TM_VA, sbase + C::OFF_V, C::K_BYTES);
+        for (int s = q0 - C::LAND; s < q0; ++s) mma_commit(&bar_qempty[s % NQ]);
+      }
       if (ok) ok = issue_s(g0);
-      if (ok && nchunks == 1) mma_commit(&bar_kvempty);  // every S^T/dP^T MMA of this tile has been issued
+      // every S^T/dP^T MMA of this tile has been issued: the K/V buffers may take the next tile's blocks
+      if (!C::POOL && ok && nchunks == 1) mma_commit(&bar_kvempty);
       for (int c = 0; c < nchunks && ok; ++c) {
         const int gc = g0 + c;
         if (NSB == 2 && c + 1 < nchunks) {
           if (!(ok = issue_s(gc + 1))) break;
-          if (c + 2 == nchunks) mma_commit(&bar_kvempty);
+          if (!C::POOL && c + 2 == nchunks) mma_commit(&bar_kvempty);
         }
-        const int qs = gc % NQ, ts = gc % NST;
+        const int gq = gc + qoff, qs = gq % NQ, ts = gc % NST;
         if (!(ok = mbar_wait(&bar_tfull[ts], (gc / NST) & 1, ctx))) break;
         if constexpr (C::WIDE)  // the transposed Q / dO chunks (the slots carried the score operands)
-          if (!(ok = mbar_wait(&bar_qfull[qs], (gc / NQ) & 1, ctx))) break;
+          if (!(ok = mbar_wait(&bar_qfull[qs], (gq / NQ) & 1, ctx))) break;
         tc_fence_after();
         uint32_t dob, qb;
         if constexpr (BF16) {
