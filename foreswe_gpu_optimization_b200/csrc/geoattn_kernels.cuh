@@ -1456,7 +1456,7 @@ struct ColsCfg : Tile<BF16, DP> {
   // ring for the rest of the tile: the landing takes the ring's next NQ positions, so the ring's order and phases
   // carry the hand-over both ways.
   static constexpr bool POOL = !BF16 && !WIDE;
-  static constexpr int NQ = (BF16 && DP <= 128) ? 3 : POOL ? 2 : 1;   // query-chunk (Q, dO) buffers
+  static constexpr int NQ = ((BF16 && DP <= 128) || POOL) ? 3 : 1;   // query-chunk (Q, dO) buffers
   static constexpr int NSB = ((BF16 && DP <= 128) || POOL) ? 2 : 1;  // S^T / dP^T accumulator buffers in TMEM
   static constexpr int LAND = POOL ? NQ : 0;               // ring positions the K/V landing takes per tile
   static_assert(LAND == 0 || LAND == NQ, "a landing takes every slot of the ring once");
@@ -1477,8 +1477,7 @@ struct ColsCfg : Tile<BF16, DP> {
   static constexpr int OFF_QT = OFF_DO + NQ * T::PL * Q_BYTES;
   static constexpr int OFF_DOT = OFF_QT + NQ * QT_BYTES;
   static constexpr int RING_END = OFF_DOT + NQ * QT_BYTES;
-  static_assert(!POOL || RING_END <= KV_END, "the query-chunk ring lies inside the K/V pool");
-  static constexpr int OFF_P2 = POOL ? KV_END : RING_END;
+  static constexpr int OFF_P2 = (POOL && KV_END > RING_END) ? KV_END : RING_END;  // pooled: past the larger use
   static constexpr int OFF_DS = OFF_P2 + NST * ST_BYTES;
   static constexpr int OFF_PR = OFF_DS + NST * ST_BYTES;
   static constexpr int OFF_REC = OFF_PR + NPR * kPriorTileBytes;
