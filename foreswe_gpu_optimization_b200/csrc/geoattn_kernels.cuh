@@ -937,19 +937,26 @@ struct RowsCfg : Tile<BF16, DP> {
   static constexpr int NDC = WIDE ? DP / T::KB : 1;
   // fp32: the prior is read from L2 (loads issued before each chunk's wait, as in the key pass); at head dim 64 the
   // shared memory a staged prior tile would take holds a second K/V buffer instead
-  static constexpr int NKV = WIDE ? 3 : (DP > 128) ? 1 : (!BF16 || DQ) ? 2 : 3;  // K/V chunk buffers / ring slots
+  // fp32 at head dim 64 ("pooled"): Q and dO (hi/lo planes) are the tensor-memory A operands of the S and dP MMAs.
+  // They land by TMA in a shared-memory pool that, once copied into tensor memory, holds the K and V rings for the
+  // rest of the tile: the landing takes the rings' next NKV positions, so their order and phases carry the hand-over.
+  static constexpr bool POOL = !BF16 && !WIDE;
+  static constexpr int NKV = WIDE ? 3 : POOL ? 4 : (DP > 128) ? 1 : DQ ? 2 : 3;  // K/V chunk buffers / ring slots
+  static constexpr int LAND = POOL ? NKV : 0;  // ring positions the Q/dO landing takes per tile
   static constexpr int NPR = (BF16 && DP <= 128) ? 2 : !BF16 ? 0 : 1;  // staged prior buffers (0: L2)
   static constexpr int Q_BYTES = WIDE ? 0 : kBM * DP * T::EB;                   // per plane (Q and dO)
   static constexpr int K_BYTES = WIDE ? kSlotPlaneBytes : T::CH * DP * T::EB;  // per plane per buffer / slot
   static constexpr int KT_BYTES = BF16 ? 0 : DP * 128;  // fp32: transposed K chunk (hi) for dQ
   static constexpr int DS_BYTES = kBM * 128;
-  static constexpr int NDS = BF16 ? 2 : 1;            // dS / K^T buffers (ring size)
+  static constexpr int NDS = (BF16 || POOL) ? 2 : 1;  // dS / K^T buffers (ring size)
   static constexpr int NDS_ALLOC = DQ ? NDS : 0;      // allocated only with DQ
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_DO = OFF_Q + T::PL * Q_BYTES;
-  static constexpr int OFF_K = OFF_DO + T::PL * Q_BYTES;
+  static constexpr int QD_END = OFF_DO + T::PL * Q_BYTES;
+  static constexpr int OFF_K = POOL ? 0 : QD_END;
   static constexpr int OFF_V = OFF_K + NKV * T::PL * K_BYTES;
-  static constexpr int OFF_KT = OFF_V + (WIDE ? 0 : NKV * T::PL * K_BYTES);
+  static constexpr int KV_END = OFF_V + (WIDE ? 0 : NKV * T::PL * K_BYTES);
+  static constexpr int OFF_KT = (POOL && QD_END > KV_END) ? QD_END : KV_END;  // pooled: past the larger use
   static constexpr int OFF_DS = OFF_KT + NDS_ALLOC * KT_BYTES;
   static constexpr int OFF_PR = OFF_DS + NDS_ALLOC * DS_BYTES;
   static constexpr int OFF_XS = OFF_PR + NPR * kPriorTileBytes;  // without DQ: warpgroup 1's row sums
@@ -961,7 +968,11 @@ struct RowsCfg : Tile<BF16, DP> {
   static constexpr int TM_S = 0;
   static constexpr int TM_DP = NSB * T::CH;
   static constexpr int TM_DQ = 2 * NSB * T::CH;
-  static constexpr int TMEM_COLS = pow2_cols(2 * NSB * T::CH + (DQ ? DP : 0));
+  static constexpr int TM_QA = TM_DQ + (DQ ? DP : 0);                              // pooled: Q (hi, lo)
+  static constexpr int TM_DOA = TM_QA + (POOL ? T::PL * kAColsPerPlane<T> : 0);    // pooled: dO (hi, lo)
+  static constexpr int TMEM_NEED = TM_DOA + (POOL ? T::PL * kAColsPerPlane<T> : 0);
+  static_assert(TMEM_NEED <= 512, "row pass: tensor-memory columns above 512");
+  static constexpr int TMEM_COLS = pow2_cols(TMEM_NEED);
   // dQ leaves through the dS buffers (free once the tile's last dQ MMA has run) when they hold the whole row block
   static constexpr bool EPI_TMA = DQ && BF16 && T::NKB * kBM * 128 <= NDS * DS_BYTES;
 };
@@ -982,9 +993,10 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
   constexpr int PRB = NPR > 0 ? NPR : 1;  // prior-ring modulus (unused when the prior is read from L2)
   if (smem_misaligned(p.status)) return;  // uniform over the CTA, before any barrier or allocation
   uint8_t* smem = smem_raw;
-  __shared__ uint64_t bar_qfull, bar_qempty, bar_kfull[3], bar_kempty[3], bar_vfull[3], bar_vempty[3], bar_sfull[4],
+  __shared__ uint64_t bar_qfull, bar_qempty, bar_kfull[4], bar_kempty[4], bar_vfull[4], bar_vempty[4], bar_sfull[4],
       bar_sempty[4], bar_dsfull[2], bar_dsempty[2], bar_ktfull[2], bar_ktempty[2], bar_prfull[2], bar_prempty[2], bar_dqfull;
-  static_assert(NKV <= 3 && NSB <= 4 && C::NDS <= 2 && NPR <= 2, "ring deeper than its barrier array");
+  static_assert(NKV <= 4 && NSB <= 4 && C::NDS <= 2 && NPR <= 2, "ring deeper than its barrier array");
+  static_assert(C::LAND == 0 || C::LAND == NKV, "a landing takes every slot of the K/V rings once");
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_flag;
   __shared__ double red[8][3];
@@ -999,7 +1011,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
     abort_flag = 0;
     mbar_init(&bar_qfull, 1);
     mbar_init(&bar_qempty, 1);
-    for (int i = 0; i < 3; ++i) {
+    for (int i = 0; i < 4; ++i) {
       mbar_init(&bar_kfull[i], 1);
       mbar_init(&bar_kempty[i], 1);
       mbar_init(&bar_vfull[i], 1);
@@ -1040,7 +1052,16 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       bool ok = true;
       for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++it) {
       const int rb = tile % p.nrb, bh = tile / p.nrb, b = bh / p.H, h = bh % p.H;
-      if constexpr (!C::WIDE) {  // Q and dO of this tile once the previous tile's last S/dP MMAs have read the old ones
+      if constexpr (C::POOL) {  // Q and dO into the pool once its K/V ring positions are free
+        for (int s = 0; s < C::LAND && ok; ++s, ++kc) {
+          const int ks = kc % NKV, par = ((kc / NKV) & 1) ^ 1;
+          ok = mbar_wait(&bar_kempty[ks], par, ctx) && mbar_wait(&bar_vempty[ks], par, ctx);
+        }
+        if (!ok) break;
+        mbar_arrive_expect_tx(&bar_qfull, 2 * T::PL * C::Q_BYTES);
+        tma_tile<T>(smem + C::OFF_Q, &maps.q, &bar_qfull, kBM, rb * kBM, h, b, p.B, T::PL);
+        tma_tile<T>(smem + C::OFF_DO, &maps.dout, &bar_qfull, kBM, rb * kBM, h, b, p.B, T::PL);
+      } else if constexpr (!C::WIDE) {  // Q and dO once the previous tile's last S/dP MMAs have read the old ones
         if (!(ok = mbar_wait(&bar_qempty, (it & 1) ^ 1, ctx))) break;
         mbar_arrive_expect_tx(&bar_qfull, 2 * T::PL * C::Q_BYTES);
         tma_tile<T>(smem + C::OFF_Q, &maps.q, &bar_qfull, kBM, rb * kBM, h, b, p.B, T::PL);
@@ -1136,14 +1157,22 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
           return true;
         }
         const int ks = kc % NKV, ss = sc % NSB;
-        if (!mbar_wait(&bar_kfull[ks], (kc / NKV) & 1, ctx)) return false;
-        if (!mbar_wait(&bar_vfull[ks], (kc / NKV) & 1, ctx)) return false;
+        // phases of the full barriers count only chunk loads; the pooled landings (one per slot per tile, this
+        // tile's included) complete none
+        const int kpar = ((kc / NKV) - (C::POOL ? it + 1 : 0)) & 1;
+        if (!mbar_wait(&bar_kfull[ks], kpar, ctx)) return false;
+        if (!mbar_wait(&bar_vfull[ks], kpar, ctx)) return false;
         if (!mbar_wait(&bar_sempty[ss], ((sc / NSB) & 1) ^ 1, ctx)) return false;
         tc_fence_after();
         const uint32_t kb = sbase + C::OFF_K + ks * T::PL * C::K_BYTES;
         const uint32_t vb = sbase + C::OFF_V + ks * T::PL * C::K_BYTES;
-        mma_qk<T, T::CH>(tmem + C::TM_S + ss * T::CH, sbase + C::OFF_Q, C::Q_BYTES, kb, C::K_BYTES);
-        mma_qk<T, T::CH>(tmem + C::TM_DP + ss * T::CH, sbase + C::OFF_DO, C::Q_BYTES, vb, C::K_BYTES);
+        if constexpr (C::POOL) {
+          mma_qk_ts<T, T::CH>(tmem + C::TM_S + ss * T::CH, tmem + C::TM_QA, kb, C::K_BYTES);
+          mma_qk_ts<T, T::CH>(tmem + C::TM_DP + ss * T::CH, tmem + C::TM_DOA, vb, C::K_BYTES);
+        } else {
+          mma_qk<T, T::CH>(tmem + C::TM_S + ss * T::CH, sbase + C::OFF_Q, C::Q_BYTES, kb, C::K_BYTES);
+          mma_qk<T, T::CH>(tmem + C::TM_DP + ss * T::CH, sbase + C::OFF_DO, C::Q_BYTES, vb, C::K_BYTES);
+        }
         mma_commit(&bar_sfull[ss]);
         mma_commit(&bar_vempty[ks]);
         if (release_k) mma_commit(&bar_kempty[ks]);
@@ -1173,6 +1202,18 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++it) {
         if constexpr (!C::WIDE)
           if (!(ok = mbar_wait(&bar_qfull, it & 1, ctx))) break;
+        if constexpr (C::POOL) {
+          // Q and dO into tensor memory. The previous tile's S/dP MMAs, the last readers of these columns, completed
+          // before its last K/V ring positions were released, and the TMA warp loaded this Q/dO only after that.
+          // The landing's ring positions are released once the copies have read the pool.
+          tc_fence_after();
+          cp_operand_tmem<T>(tmem + C::TM_QA, sbase + C::OFF_Q, C::Q_BYTES);
+          cp_operand_tmem<T>(tmem + C::TM_DOA, sbase + C::OFF_DO, C::Q_BYTES);
+          for (int s = 0; s < C::LAND; ++s, ++kc) {
+            mma_commit(&bar_kempty[kc % NKV]);
+            mma_commit(&bar_vempty[kc % NKV]);
+          }
+        }
         for (int c = 0; c < nchunks && ok; ++c) ok = issue(true);
         if constexpr (!DQ) {
           if (ok) mma_commit(&bar_qempty);  // every S/dP MMA of this tile has been issued
@@ -1180,11 +1221,12 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         }
         const int kc0 = kc;  // first K use of sweep 2
         if (ok) ok = issue(false);
-        if (ok && nchunks == 1) mma_commit(&bar_qempty);  // every S/dP MMA of this tile has been issued
+        // every S/dP MMA of this tile has been issued: Q and dO may take the next tile's (pooled: no separate buffer)
+        if (!C::POOL && ok && nchunks == 1) mma_commit(&bar_qempty);
         for (int c = 0; c < nchunks && ok; ++c) {
-          if constexpr (NKV == 2 || C::WIDE) {  // look ahead: S/dP of the next chunk overlap the element-wise work
+          if constexpr (NKV >= 2 || C::WIDE) {  // look ahead: S/dP of the next chunk overlap the element-wise work
             if (c + 1 < nchunks && !(ok = issue(false))) break;
-            if (c + 2 == nchunks) mma_commit(&bar_qempty);
+            if (!C::POOL && c + 2 == nchunks) mma_commit(&bar_qempty);
             if (!(ok = issue_dq(c, kc0))) break;
           } else {                   // one K/V buffer: the next chunk's K can only arrive after this chunk's dQ
             if (!(ok = issue_dq(c, kc0))) break;
