@@ -423,6 +423,17 @@ __device__ __forceinline__ void mma_slot(uint32_t tmem_acc, uint32_t slot, bool 
   static_assert(!T::kBF16 && T::CH == 32, "slots carry fp32 planes with 32-row B chunks");
   mma_qk<T, T::CH, T::KB>(tmem_acc, slot, kSlotPlaneBytes, slot + kBM * 128, kSlotPlaneBytes, accumulate);
 }
+// Two consecutive chunks (rows c*CH .. c*CH + 2*CH) of a natural operand, hi[/lo] planes, into one ring slot laid out
+// [plane][region][2*CH rows x 128 B], so that the slot is a 2*CH-row K-major B operand.
+template <class T>
+__device__ __forceinline__ void tma_pair(uint8_t* slot, const CUtensorMap* map, uint64_t* bar, int c, int h, int b,
+                                         int B) {
+  for (int pl = 0; pl < T::PL; ++pl)
+    for (int kb = 0; kb < T::NKB; ++kb)
+      for (int half = 0; half < 2; ++half)
+        tma_load_4d(slot + ((pl * T::NKB + kb) * 2 + half) * (T::CH * 128), map, bar, kb * T::KB,
+                    (c + half) * T::CH, h, b + pl * B);
+}
 // Transposed fp32 plane chunk: DP rows (d) x 32 columns (n) starting at column n0 -> one region of DP x 128 B.
 __device__ __forceinline__ void tma_tileT(uint8_t* dst, const CUtensorMap* map, uint64_t* bar, int n0, int h, int b) {
   tma_load_4d(dst, map, bar, n0, 0, h, b);
@@ -504,14 +515,22 @@ struct FwdCfg : Tile<BF16, DP> {
   // wide fp32: the prior is read from L2 (loads issued before each chunk's wait) instead of a single staged buffer,
   // and the shared memory goes to a third K ring slot at every head dim
   static constexpr int NPR = WIDE ? 0 : (BF16 && DP > 128) ? 1 : 2;  // staged prior buffers (0: L2)
-  static constexpr int NK = (WIDE || (BF16 && DP <= 128)) ? 3 : 2;  // K ring slots
+  // fp32 at head dim 64 ("pooled"): Q (hi/lo planes) is the tensor-memory A operand of the score MMAs, each of which
+  // covers a pair of 32-key chunks (N = 64: half the instructions). Q lands by TMA in a shared-memory pool that,
+  // once copied into tensor memory, holds the ring of K chunk pairs; the landing takes the ring's next NK positions.
+  static constexpr bool POOL = !BF16 && !WIDE;
+  static constexpr int PAIR = POOL ? 2 : 1;                           // chunks per score MMA / K ring slot
+  static constexpr int NK = (WIDE || POOL || (BF16 && DP <= 128)) ? 3 : 2;  // K ring slots
+  static constexpr int LAND = POOL ? NK : 0;                          // ring positions the Q landing takes
   static constexpr int Q_BYTES = WIDE ? 0 : kBM * DP * T::EB;          // per plane
-  static constexpr int K_BYTES = WIDE ? kSlotPlaneBytes : T::CH * DP * T::EB;  // per plane per ring slot
+  static constexpr int K_BYTES = WIDE ? kSlotPlaneBytes : PAIR * T::CH * DP * T::EB;  // per plane per ring slot
   static constexpr int V_BYTES = T::CH * DP * T::EB;        // hi only (natural bf16 / transposed fp32)
   static constexpr int P_BYTES = kBM * 128;
   static constexpr int OFF_Q = 0;
-  static constexpr int OFF_K = OFF_Q + T::PL * Q_BYTES;
-  static constexpr int OFF_V = OFF_K + NK * T::PL * K_BYTES;
+  static constexpr int Q_END = OFF_Q + T::PL * Q_BYTES;
+  static constexpr int OFF_K = POOL ? 0 : Q_END;
+  static constexpr int K_END = OFF_K + NK * T::PL * K_BYTES;
+  static constexpr int OFF_V = (POOL && Q_END > K_END) ? Q_END : K_END;  // pooled: past the larger use
   static constexpr int OFF_P = OFF_V + 2 * V_BYTES;
   static constexpr int OFF_PR = OFF_P + 2 * P_BYTES;
   static constexpr int SMEM = OFF_PR + NPR * kPriorTileBytes;
@@ -519,9 +538,13 @@ struct FwdCfg : Tile<BF16, DP> {
   // 4 score buffers in tensor memory: the MMA warp runs up to 3 chunks ahead of the element-wise warps, and the
   // last score MMA of a tile (which frees Q for the next tile) issues ~3 chunks before the tile ends
   static constexpr int NSB = 4;
+  static_assert(NSB % PAIR == 0, "chunk pairs take aligned score buffers");
   static constexpr int TM_S = 0;
   static constexpr int TM_O = NSB * T::CH;
-  static constexpr int TMEM_COLS = pow2_cols(NSB * T::CH + DP);
+  static constexpr int TM_QA = TM_O + DP;  // pooled: Q (hi, lo)
+  static constexpr int TMEM_NEED = TM_QA + (POOL ? T::PL * kAColsPerPlane<T> : 0);
+  static_assert(TMEM_NEED <= 512, "forward: tensor-memory columns above 512");
+  static constexpr int TMEM_COLS = pow2_cols(TMEM_NEED);
   // O leaves through the two P buffers (free once the tile's last P.V has run) when they hold the whole row block
   static constexpr bool EPI_TMA = BF16 && T::NKB * kBM * 128 <= 2 * P_BYTES;
 };
@@ -543,7 +566,9 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
   __shared__ int abort_flag;
   __shared__ float xch[3][Tile<BF16, DP>::EW][kBM];  // cross-warpgroup row statistics: m, l1, l2
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int nchunks = (p.N + T::CH - 1) / T::CH;
+  // chunks every role iterates; pooled: whole pairs (an extra chunk past N is masked like a ragged one)
+  const int nch = C::POOL ? (((p.N + T::CH - 1) / T::CH + 1) & ~1) : (p.N + T::CH - 1) / T::CH;
+  static_assert(C::LAND == 0 || C::LAND == NK, "a landing takes every slot of the K ring once");
   const int ntiles = p.nrb * p.B * p.H;  // tile = (128-query row block, b*h); persistent CTAs stride over tiles
   WaitCtx ctx{&abort_flag, p.status};
   const bool epi_tma = C::EPI_TMA && p.out_tma;
@@ -588,7 +613,12 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       bool ok = true;
       for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++it) {
         const int rb = tile % p.nrb, bh = tile / p.nrb, b = bh / p.H, h = bh % p.H;
-        if constexpr (!C::WIDE) {  // Q of this tile once the previous tile's last score MMA has read the old one
+        if constexpr (C::POOL) {  // Q into the pool once its K ring positions are free
+          for (int s = 0; s < C::LAND && ok; ++s, ++kc) ok = mbar_wait(&bar_kempty[kc % NK], ((kc / NK) & 1) ^ 1, ctx);
+          if (!ok) break;
+          mbar_arrive_expect_tx(&bar_qfull, T::PL * C::Q_BYTES);
+          tma_tile<T>(smem + C::OFF_Q, &maps.q, &bar_qfull, kBM, rb * kBM, h, b, p.B, T::PL);
+        } else if constexpr (!C::WIDE) {  // Q once the previous tile's last score MMA has read the old one
           if (!(ok = mbar_wait(&bar_qempty, (it & 1) ^ 1, ctx))) break;
           mbar_arrive_expect_tx(&bar_qfull, T::PL * C::Q_BYTES);
           tma_tile<T>(smem + C::OFF_Q, &maps.q, &bar_qfull, kBM, rb * kBM, h, b, p.B, T::PL);
@@ -613,7 +643,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
             ++vc;
             return true;
           };
-          for (int c = 0; c < nchunks && ok; ++c) {
+          for (int c = 0; c < nch && ok; c += C::PAIR) {
             for (int dc = 0; dc < C::NDC && ok; ++dc) {
               const int ks = kc % NK;
               if (!(ok = mbar_wait(&bar_kempty[ks], ((kc / NK) & 1) ^ 1, ctx))) break;
@@ -621,14 +651,17 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
               uint8_t* slot = smem + C::OFF_K + ks * T::PL * C::K_BYTES;
               if constexpr (C::WIDE)
                 tma_slot<T>(slot, &bar_kfull[ks], &maps.q, rb * kBM, &maps.k, c * T::CH, dc, h, b, p.B);
+              else if constexpr (C::POOL)
+                tma_pair<T>(slot, &maps.k, &bar_kfull[ks], c, h, b, p.B);
               else
                 tma_tile<T>(slot, &maps.k, &bar_kfull[ks], T::CH, c * T::CH, h, b, p.B, T::PL);
               ++kc;
             }
-            if (ok && pass == 1 && c >= C::NSB - 1) ok = load_v(c - (C::NSB - 1));
+            for (int cc = c; cc < c + C::PAIR && ok; ++cc)
+              if (pass == 1 && cc >= C::NSB - 1) ok = load_v(cc - (C::NSB - 1));
           }
           if (pass == 1)
-            for (int cv = nchunks - (C::NSB - 1); cv < nchunks && ok; ++cv)
+            for (int cv = nch - (C::NSB - 1); cv < nch && ok; ++cv)
               if (cv >= 0) ok = load_v(cv);
         }
       }
@@ -640,7 +673,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       bool ok = true;
       for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
         const int rb = tile % p.nrb;
-        for (int c = 0; c < nchunks && ok; ++c) {  // pass B only
+        for (int c = 0; c < nch && ok; ++c) {  // pass B only
           const int ps = prc % PRB;
           if (!(ok = mbar_wait(&bar_prempty[ps], ((prc / PRB) & 1) ^ 1, ctx))) break;
           mbar_arrive_expect_tx(&bar_prfull[ps], kPriorTileBytes);
@@ -665,6 +698,22 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
             mma_commit(&bar_kempty[ks]);
             ++kc;
           }
+        } else if constexpr (C::POOL) {  // one N = 64 MMA for a chunk pair into two adjacent score buffers
+          const int ks = kc % NK;
+          // phases of the full barriers count only K loads; the Q landings (one per slot per tile, this tile's
+          // included) complete none
+          if (!mbar_wait(&bar_kfull[ks], ((kc / NK) - (it + 1)) & 1, ctx)) return false;
+          if (!mbar_wait(&bar_sempty[ss], ((sc / NSB) & 1) ^ 1, ctx)) return false;
+          if (!mbar_wait(&bar_sempty[ss + 1], (((sc + 1) / NSB) & 1) ^ 1, ctx)) return false;
+          tc_fence_after();
+          mma_qk_ts<T, C::PAIR * T::CH>(tmem + C::TM_S + ss * T::CH, tmem + C::TM_QA,
+                                        sbase + C::OFF_K + ks * T::PL * C::K_BYTES, C::K_BYTES);
+          mma_commit(&bar_kempty[ks]);
+          ++kc;
+          mma_commit(&bar_sfull[ss]);
+          mma_commit(&bar_sfull[ss + 1]);
+          sc += 2;
+          return true;
         } else {
           const int ks = kc % NK;
           if (!mbar_wait(&bar_kfull[ks], (kc / NK) & 1, ctx)) return false;
@@ -682,17 +731,25 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++it) {
         if constexpr (!C::WIDE)
           if (!(ok = mbar_wait(&bar_qfull, it & 1, ctx))) break;
-        for (int c = 0; c < nchunks && ok; ++c) ok = issue_s();  // pass A
-        int nb = 0;  // pass-B score MMAs issued
+        if constexpr (C::POOL) {
+          // Q into tensor memory. The previous tile's score MMAs, the last readers of these columns, completed before
+          // its last K ring positions were released, and the TMA warp loaded this Q only after that. The landing's
+          // ring positions are released once the copies have read the pool.
+          tc_fence_after();
+          cp_operand_tmem<T>(tmem + C::TM_QA, sbase + C::OFF_Q, C::Q_BYTES);
+          for (int s = 0; s < C::LAND; ++s, ++kc) mma_commit(&bar_kempty[kc % NK]);
+        }
+        for (int c = 0; c < nch && ok; c += C::PAIR) ok = issue_s();  // pass A
+        int nb = 0;  // pass-B chunks whose score MMAs are issued
         // keeps the pass-B scores up to NSB - 1 chunks ahead; Q is released once the tile's last one is issued
         auto top_up = [&](int upto) -> bool {
-          for (; nb < nchunks && nb < upto; ++nb) {
+          for (; nb < nch && nb + C::PAIR - 1 < upto; nb += C::PAIR) {
             if (!issue_s()) return false;
-            if (!C::WIDE && nb + 1 == nchunks) mma_commit(&bar_qempty);
+            if (!C::WIDE && !C::POOL && nb + 1 == nch) mma_commit(&bar_qempty);
           }
           return true;
         };
-        for (int c = 0; c < nchunks && ok; ++c) {
+        for (int c = 0; c < nch && ok; ++c) {
           if (!(ok = top_up(c + NSB))) break;
           const int ps = pc & 1;
           if (!(ok = mbar_wait(&bar_pfull[ps], (pc >> 1) & 1, ctx))) break;
@@ -789,8 +846,8 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         // chunks in pairs: both chunks' scores are loaded, then reduced together (64 independent values per thread)
         uint32_t ua[32], ub[32];
         const int g0 = sc;
-        for (int c = 0; c < nchunks && ok; c += 2) {
-          const bool two = c + 1 < nchunks;
+        for (int c = 0; c < nch && ok; c += 2) {
+          const bool two = c + 1 < nch;
           if (!(ok = load_s(g0 + c, ua))) break;
           if (two && !(ok = load_s(g0 + c + 1, ub))) break;
           release_s(g0 + c, ua);
@@ -804,7 +861,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
           }
         }
         tmem_wait_all();  // no load stays in flight past the loop (aborted paths included)
-        sc += nchunks;
+        sc += nch;
       }
       if constexpr (T::EW > 1) {  // combine the warpgroups' statistics (same order in every warpgroup)
         xch[0][e.wg][e.r] = m;
@@ -827,7 +884,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       const float aL = ab.a * kLog2e, bL = ab.b * kLog2e, gL = ab.g * kLog2e, cL = ab.c * kLog2e;
       float l2 = 0.f;
       // Pass B
-      for (int c = 0; c < nchunks && ok; ++c) {
+      for (int c = 0; c < nch && ok; ++c) {
         const int ss = sc % NSB, ps = pc & 1, prs = prc % PRB;
         Prior32<BF16> pr;
         if constexpr (NPR == 0) {  // from L2, issued before the waits (one piece per chunk)
