@@ -351,6 +351,22 @@ __device__ __forceinline__ void cp_operand_tmem(uint32_t tmem_a, uint32_t a_base
     }
 }
 
+// The shared-memory source of tcgen05.cp copies may be rewritten only once the copies have read it. A commit issued
+// right after the copies does not wait for them, and neither does an MMA that reads only the last copied columns
+// (measured: repeated runs differed where the next chunk's TMA overwrote a copied plane). This issues one MMA per
+// copied 8-column block of an operand (each ordered after the copy it reads) into 32 scratch accumulator columns
+// `acc`, with B any 32 x 32-byte swizzled slice of shared memory that nothing writes meanwhile; a commit issued after
+// them tracks every copy.
+template <class T>
+__device__ __forceinline__ void cp_drain_operand(uint32_t acc, uint32_t tmem_a, uint32_t smem_b) {
+  constexpr uint32_t idesc = instr_desc(T::FMT, 0, 0, 128, 32);
+  const uint64_t bd = smem_desc_sw128(smem_b, 16, 1024);
+#pragma unroll
+  for (int pl = 0; pl < T::PL; ++pl)
+#pragma unroll
+    for (int s = 0; s < T::DP / T::KS; ++s) mma_ts<T::KIND>(acc, tmem_a + pl * kAColsPerPlane<T> + s * 8, bd, idesc, 0u);
+}
+
 // mma_qk with A = the whole head dimension of a tensor-memory operand copied by cp_operand_tmem, B in shared memory.
 template <class T, int NB>
 __device__ __forceinline__ void mma_qk_ts(uint32_t tmem_acc, uint32_t tmem_a, uint32_t b_base, uint32_t b_plane) {
@@ -737,6 +753,10 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
           // ring positions are released once the copies have read the pool.
           tc_fence_after();
           cp_operand_tmem<T>(tmem + C::TM_QA, sbase + C::OFF_Q, C::Q_BYTES);
+          // the copies are drained through the next score buffer (free once its previous use was read; the real
+          // score MMA overwrites it) before the pool is released
+          if (!(ok = mbar_wait(&bar_sempty[sc % NSB], ((sc / NSB) & 1) ^ 1, ctx))) break;
+          cp_drain_operand<T>(tmem + C::TM_S + (sc % NSB) * T::CH, tmem + C::TM_QA, sbase + C::OFF_Q);
           for (int s = 0; s < C::LAND; ++s, ++kc) mma_commit(&bar_kempty[kc % NK]);
         }
         for (int c = 0; c < nch && ok; c += C::PAIR) ok = issue_s();  // pass A
@@ -1266,6 +1286,11 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
           tc_fence_after();
           cp_operand_tmem<T>(tmem + C::TM_QA, sbase + C::OFF_Q, C::Q_BYTES);
           cp_operand_tmem<T>(tmem + C::TM_DOA, sbase + C::OFF_DO, C::Q_BYTES);
+          // the copies are drained through the next S buffer (free once its previous use was read; the real S MMA
+          // overwrites it) before the pool is released
+          if (!(ok = mbar_wait(&bar_sempty[sc % NSB], ((sc / NSB) & 1) ^ 1, ctx))) break;
+          cp_drain_operand<T>(tmem + C::TM_S + (sc % NSB) * T::CH, tmem + C::TM_QA, sbase + C::OFF_Q);
+          cp_drain_operand<T>(tmem + C::TM_S + (sc % NSB) * T::CH, tmem + C::TM_DOA, sbase + C::OFF_Q);
           for (int s = 0; s < C::LAND; ++s, ++kc) {
             mma_commit(&bar_kempty[kc % NKV]);
             mma_commit(&bar_vempty[kc % NKV]);
@@ -1807,6 +1832,11 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         tc_fence_after();
         cp_operand_tmem<T>(tmem + C::TM_KA, sbase + C::OFF_K, C::K_BYTES);
         cp_operand_tmem<T>(tmem + C::TM_VA, sbase + C::OFF_V, C::K_BYTES);
+        // the copies are drained through chunk 0's S^T buffer (free once its previous use was read; the real S^T
+        // MMA overwrites it) before the pool is released
+        if (!(ok = mbar_wait(&bar_sempty[g0 % NSB], ((g0 / NSB) & 1) ^ 1, ctx))) break;
+        cp_drain_operand<T>(tmem + C::TM_S + (g0 % NSB) * T::CH, tmem + C::TM_KA, sbase + C::OFF_K);
+        cp_drain_operand<T>(tmem + C::TM_S + (g0 % NSB) * T::CH, tmem + C::TM_VA, sbase + C::OFF_K);
         for (int s = q0 - C::LAND; s < q0; ++s) mma_commit(&bar_qempty[s % NQ]);
       }
       if (ok) ok = issue_s(g0);

@@ -126,6 +126,26 @@ def test_many_chunks_per_row(ops, dtype):
     _check(res, _oracle(q, k, v, dist, ang, a, b, c, do), TOL[dtype], "N=1500 %s" % dtype)
 
 
+def test_tf32_pooled_tiles_per_cta_repeat_bitwise(ops):
+    """fp32 at head dim 64 hands each tile's A operand (Q, Q/dO, K/V) from a shared-memory landing pool to tensor
+    memory and reuses the pool for the chunk rings. 384 tiles on 148 persistent CTAs (2-3 tiles each) with an odd
+    chunk count (N = 330: 11 key chunks, padded to whole pairs in the forward) exercise the hand-over between tiles:
+    repeated runs agree bitwise and match the oracle. (A pool released before its tensor-memory copies had read it
+    showed here as dK differing between runs in about one run of three.)"""
+    B, H, N, D = 16, 8, 330, 64
+    q, k, v, a, b, c, do = attn_inputs(B, H, N, D, seed=41, qscale=3.0, dtype=torch.float32)
+    lat, lon, el = stations(N, seed=42)
+    geom = ops.StationGeometry(lat, lon, el)
+    fn = lambda *x: ops.geo_attention(x[0], x[1], x[2], geom, *x[3:])  # noqa: E731
+    r1 = run_device(fn, q, k, v, a, b, c, do)
+    for _ in range(5):
+        r2 = run_device(fn, q, k, v, a, b, c, do)
+        for key in KEYS:
+            assert torch.equal(r1[key], r2[key]), key
+    dist, ang = dense_geometry(lat, lon, el)
+    _check(r1, _oracle(q, k, v, dist, ang, a, b, c, do), TOL[torch.float32], "pooled tf32 N=330")
+
+
 @pytest.mark.parametrize("D", [128, 192, 96, 160])
 def test_tf32_wide_heads(ops, D):
     """fp32 head dims above 64 (Q/K and dO/V streamed through the score MMAs in 32-wide head-dim chunks), up to the
