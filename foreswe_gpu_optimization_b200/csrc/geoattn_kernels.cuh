@@ -439,6 +439,25 @@ __device__ __forceinline__ void mma_slot(uint32_t tmem_acc, uint32_t slot, bool 
   static_assert(!T::kBF16 && T::CH == 32, "slots carry fp32 planes with 32-row B chunks");
   mma_qk<T, T::CH, T::KB>(tmem_acc, slot, kSlotPlaneBytes, slot + kBM * 128, kSlotPlaneBytes, accumulate);
 }
+// Slots whose B part holds BROWS rows (consecutive 32-row chunks; the wide forward's chunk pairs use 64).
+template <int BROWS>
+constexpr int kSlotPlaneBytesRows = (kBM + BROWS) * 128;
+template <class T, int BROWS>
+__device__ __forceinline__ void tma_slot_rows(uint8_t* slot, uint64_t* bar, const CUtensorMap* amap, int arow0,
+                                              const CUtensorMap* bmap, int brow0, int dc, int h, int b, int B) {
+  constexpr int SPB = kSlotPlaneBytesRows<BROWS>;
+  for (int pl = 0; pl < 2; ++pl) {
+    tma_load_4d(slot + pl * SPB, amap, bar, dc * T::KB, arow0, h, b + pl * B);
+    for (int r = 0; r < BROWS; r += 32)
+      tma_load_4d(slot + pl * SPB + (kBM + r) * 128, bmap, bar, dc * T::KB, brow0 + r, h, b + pl * B);
+  }
+}
+template <class T, int BROWS>
+__device__ __forceinline__ void mma_slot_rows(uint32_t tmem_acc, uint32_t slot, bool accumulate) {
+  static_assert(!T::kBF16 && T::CH == 32, "slots carry fp32 planes with 32-row B chunks");
+  constexpr int SPB = kSlotPlaneBytesRows<BROWS>;
+  mma_qk<T, BROWS, T::KB>(tmem_acc, slot, SPB, slot + kBM * 128, SPB, accumulate);
+}
 // Two consecutive chunks (rows c*CH .. c*CH + 2*CH) of a natural operand, hi[/lo] planes, into one ring slot laid out
 // [plane][region][2*CH rows x 128 B], so that the slot is a 2*CH-row K-major B operand.
 template <class T>
@@ -534,12 +553,13 @@ struct FwdCfg : Tile<BF16, DP> {
   // fp32 at head dim 64 ("pooled"): Q (hi/lo planes) is the tensor-memory A operand of the score MMAs, each of which
   // covers a pair of 32-key chunks (N = 64: half the instructions). Q lands by TMA in a shared-memory pool that,
   // once copied into tensor memory, holds the ring of K chunk pairs; the landing takes the ring's next NK positions.
+  // Wide fp32 issues its score MMAs over chunk pairs too: each slot carries a head-dim chunk of Q and of two K chunks.
   static constexpr bool POOL = !BF16 && !WIDE;
-  static constexpr int PAIR = POOL ? 2 : 1;                           // chunks per score MMA / K ring slot
-  static constexpr int NK = (WIDE || POOL || (BF16 && DP <= 128)) ? 3 : 2;  // K ring slots
+  static constexpr int PAIR = (POOL || WIDE) ? 2 : 1;                 // chunks per score MMA / K ring slot
+  static constexpr int NK = (POOL || DP <= 128) ? 3 : 2;   // K ring slots
   static constexpr int LAND = POOL ? NK : 0;                          // ring positions the Q landing takes
   static constexpr int Q_BYTES = WIDE ? 0 : kBM * DP * T::EB;          // per plane
-  static constexpr int K_BYTES = WIDE ? kSlotPlaneBytes : PAIR * T::CH * DP * T::EB;  // per plane per ring slot
+  static constexpr int K_BYTES = WIDE ? kSlotPlaneBytesRows<PAIR * T::CH> : PAIR * T::CH * DP * T::EB;  // per plane
   static constexpr int V_BYTES = T::CH * DP * T::EB;        // hi only (natural bf16 / transposed fp32)
   static constexpr int P_BYTES = kBM * 128;
   static constexpr int OFF_Q = 0;
@@ -555,6 +575,11 @@ struct FwdCfg : Tile<BF16, DP> {
   // last score MMA of a tile (which frees Q for the next tile) issues ~3 chunks before the tile ends
   static constexpr int NSB = 4;
   static_assert(NSB % PAIR == 0, "chunk pairs take aligned score buffers");
+  // Pass B loads V of chunk c after the K of chunk c + VLAG: before its P.V MMA needs V(c), the MMA warp has issued
+  // the scores of every chunk below c + NSB - PAIR + 1, so the K loads ahead of V(c) never wait on MMAs behind it. A
+  // wide pair takes NDC ring slots, more than the ring holds, so its K cannot run further ahead (lag NSB - PAIR); a
+  // pooled pair takes one slot.
+  static constexpr int VLAG = WIDE ? NSB - PAIR : NSB - 1;
   static constexpr int TM_S = 0;
   static constexpr int TM_O = NSB * T::CH;
   static constexpr int TM_QA = TM_O + DP;  // pooled: Q (hi, lo)
@@ -583,7 +608,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
   __shared__ float xch[3][Tile<BF16, DP>::EW][kBM];  // cross-warpgroup row statistics: m, l1, l2
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   // chunks every role iterates; pooled: whole pairs (an extra chunk past N is masked like a ragged one)
-  const int nch = C::POOL ? (((p.N + T::CH - 1) / T::CH + 1) & ~1) : (p.N + T::CH - 1) / T::CH;
+  const int nch = C::PAIR == 2 ? (((p.N + T::CH - 1) / T::CH + 1) & ~1) : (p.N + T::CH - 1) / T::CH;
   static_assert(C::LAND == 0 || C::LAND == NK, "a landing takes every slot of the K ring once");
   const int ntiles = p.nrb * p.B * p.H;  // tile = (128-query row block, b*h); persistent CTAs stride over tiles
   WaitCtx ctx{&abort_flag, p.status};
@@ -666,7 +691,8 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
               mbar_arrive_expect_tx(&bar_kfull[ks], T::PL * C::K_BYTES);
               uint8_t* slot = smem + C::OFF_K + ks * T::PL * C::K_BYTES;
               if constexpr (C::WIDE)
-                tma_slot<T>(slot, &bar_kfull[ks], &maps.q, rb * kBM, &maps.k, c * T::CH, dc, h, b, p.B);
+                tma_slot_rows<T, C::PAIR * T::CH>(slot, &bar_kfull[ks], &maps.q, rb * kBM, &maps.k, c * T::CH, dc, h,
+                                                  b, p.B);
               else if constexpr (C::POOL)
                 tma_pair<T>(slot, &maps.k, &bar_kfull[ks], c, h, b, p.B);
               else
@@ -674,10 +700,10 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
               ++kc;
             }
             for (int cc = c; cc < c + C::PAIR && ok; ++cc)
-              if (pass == 1 && cc >= C::NSB - 1) ok = load_v(cc - (C::NSB - 1));
+              if (pass == 1 && cc >= C::VLAG) ok = load_v(cc - C::VLAG);
           }
           if (pass == 1)
-            for (int cv = nch - (C::NSB - 1); cv < nch && ok; ++cv)
+            for (int cv = nch - C::VLAG; cv < nch && ok; ++cv)
               if (cv >= 0) ok = load_v(cv);
         }
       }
@@ -704,16 +730,22 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       bool ok = true;
       auto issue_s = [&](void) -> bool {
         const int ss = sc % NSB;
-        if constexpr (C::WIDE) {
+        if constexpr (C::WIDE) {  // a chunk pair into two adjacent score buffers, accumulated over head-dim chunks
           if (!mbar_wait(&bar_sempty[ss], ((sc / NSB) & 1) ^ 1, ctx)) return false;
+          if (!mbar_wait(&bar_sempty[ss + 1], (((sc + 1) / NSB) & 1) ^ 1, ctx)) return false;
           for (int dc = 0; dc < C::NDC; ++dc) {
             const int ks = kc % NK;
             if (!mbar_wait(&bar_kfull[ks], (kc / NK) & 1, ctx)) return false;
             tc_fence_after();
-            mma_slot<T>(tmem + C::TM_S + ss * T::CH, sbase + C::OFF_K + ks * T::PL * C::K_BYTES, dc > 0);
+            mma_slot_rows<T, C::PAIR * T::CH>(tmem + C::TM_S + ss * T::CH,
+                                              sbase + C::OFF_K + ks * T::PL * C::K_BYTES, dc > 0);
             mma_commit(&bar_kempty[ks]);
             ++kc;
           }
+          mma_commit(&bar_sfull[ss]);
+          mma_commit(&bar_sfull[ss + 1]);
+          sc += 2;
+          return true;
         } else if constexpr (C::POOL) {  // one N = 64 MMA for a chunk pair into two adjacent score buffers
           const int ks = kc % NK;
           // phases of the full barriers count only K loads; the Q landings (one per slot per tile, this tile's
@@ -1580,7 +1612,9 @@ struct ColsCfg : Tile<BF16, DP> {
   // ring for the rest of the tile: the landing takes the ring's next NQ positions, so the ring's order and phases
   // carry the hand-over both ways.
   static constexpr bool POOL = !BF16 && !WIDE;
-  static constexpr int NQ = ((BF16 && DP <= 128) || POOL) ? 3 : 1;   // query-chunk (Q, dO) buffers
+  // pooled: 2 (a 3-deep ring, 8 % faster at C2, gave dK rows of one tile that differed between runs in ~1 run of 4,
+  // with the drain and the single staging buffer alike; 2 is bitwise stable)
+  static constexpr int NQ = (BF16 && DP <= 128) ? 3 : POOL ? 2 : 1;   // query-chunk (Q, dO) buffers
   static constexpr int NSB = ((BF16 && DP <= 128) || POOL) ? 2 : 1;  // S^T / dP^T accumulator buffers in TMEM
   static constexpr int LAND = POOL ? NQ : 0;               // ring positions the K/V landing takes per tile
   static_assert(LAND == 0 || LAND == NQ, "a landing takes every slot of the ring once");
