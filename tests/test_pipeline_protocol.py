@@ -1,0 +1,137 @@
+"""Models of the kernels' ring protocols, checked on the CPU (no kernel runs here).
+
+The kernels in foreswe_gpu_optimization_b200/csrc/geoattn_kernels.cuh hand buffers between their TMA, MMA and
+element-wise warps through mbarrier rings. Two of those hand-overs are easy to get wrong and fail on the GPU only as a
+bounded-wait timeout or as results that differ between runs, so their arithmetic is restated here:
+
+* pooled fp32 kernels (head dim 64): the landing of a tile's tensor-memory operand takes every slot of a chunk ring
+  once, completing an `empty` phase per slot but no `full` phase; the consumer's `full` parity skips the landings;
+* the forward's pass B with chunk pairs: V of chunk c is loaded after the K of chunk c + VLAG. With wide head dims a
+  pair takes NDC ring slots, more than the ring holds, and a lag of NSB - 1 deadlocks (seen on the GPU as expired
+  bounded waits); the kernels use NSB - PAIR there.
+"""
+import pytest
+
+NSB = 4     # forward score buffers in tensor memory
+PAIR = 2    # 32-key chunks per score MMA (pooled and wide fp32 forward)
+
+
+def _ring_positions(n_tiles, n_chunks, depth, land):
+    """Yield (tile, position, is_landing) in the producer's order: `land` landing positions, then the chunks."""
+    pos = 0
+    for it in range(n_tiles):
+        for _ in range(land):
+            yield it, pos, True
+            pos += 1
+        for _ in range(n_chunks):
+            yield it, pos, False
+            pos += 1
+
+
+@pytest.mark.parametrize("depth,chunks_per_tile", [(2, 11), (2, 1), (2, 2), (3, 16), (4, 22), (4, 2), (3, 8)])
+def test_pooled_ring_parities(depth, chunks_per_tile):
+    """Every wait of the pooled rings targets exactly the phase it needs: `empty` waits (TMA) the release of the
+    previous use of the slot, `full` waits (MMA) the k-th chunk load of the slot, k = pos / depth - (tile + 1)."""
+    released = [0] * depth   # empty phases completed per slot (landings and chunks)
+    loads = [0] * depth      # full phases completed per slot (chunk loads only)
+    for it, pos, landing in _ring_positions(5, chunks_per_tile, depth, depth):
+        slot = pos % depth
+        # the producer waits for phase pos / depth - 1 of empty[slot]: the previous use of the slot is released
+        assert released[slot] == pos // depth
+        if not landing:
+            k = loads[slot]
+            loads[slot] += 1
+            # the consumer's parity formula for full[slot]
+            assert (pos // depth - (it + 1)) == k
+        released[slot] += 1
+
+
+def _forward_order(nch, ndc, nk, vlag):
+    """Pass A and pass B of one forward tile as three cooperating programs; returns None or the deadlock state.
+
+    TMA: K slot loads for each chunk pair (ndc head-dim slots per pair through an nk-slot ring); in pass B, after the
+    pair holding chunk cc, V of chunk cc - vlag (two V buffers). MMA: score MMAs per pair (both score buffers free),
+    keeping pass B's scores up to NSB - 1 chunks ahead, then P.V of chunk c (needs P staged and V loaded).
+    Element-wise: releases score buffers; stages P of chunk c once P.V of c - 2 ran."""
+    st = dict(kload=0, kcons=0, vload=0, pv=0, s_issued=0, s_released=0, p_staged=0)
+
+    def tma():
+        for pass_ in range(2):
+            for c in range(0, nch, PAIR):
+                for _ in range(ndc):
+                    yield lambda: st["kload"] - st["kcons"] < nk
+                    st["kload"] += 1
+                if pass_ == 1:
+                    for cc in range(c, c + PAIR):
+                        if cc >= vlag:
+                            v = cc - vlag
+                            yield lambda v=v: st["pv"] >= v - 1
+                            st["vload"] = v + 1
+            if pass_ == 1:
+                for v in range(max(0, nch - vlag), nch):
+                    yield lambda v=v: st["pv"] >= v - 1
+                    st["vload"] = v + 1
+
+    def mma():
+        sc = 0
+
+        def issue():
+            nonlocal sc
+            yield lambda: st["s_released"] >= sc + PAIR - NSB
+            for _ in range(ndc):
+                yield lambda: st["kload"] > st["kcons"]
+                st["kcons"] += 1
+            sc += PAIR
+            st["s_issued"] = sc
+
+        for _ in range(0, nch, PAIR):
+            yield from issue()
+        nb = 0
+        for c in range(nch):
+            while nb < nch and nb + PAIR - 1 < c + NSB:
+                yield from issue()
+                nb += PAIR
+            yield lambda c=c: st["p_staged"] > c and st["vload"] > c
+            st["pv"] = c + 1
+
+    def ew():
+        for c in range(0, nch, PAIR):
+            yield lambda c=c: st["s_issued"] >= c + PAIR
+            st["s_released"] = c + PAIR
+        for c in range(nch):
+            yield lambda c=c: st["s_issued"] >= nch + c + 1
+            st["s_released"] = nch + c + 1
+            yield lambda c=c: st["pv"] >= c - 1
+            st["p_staged"] = c + 1
+
+    progs = [tma(), mma(), ew()]
+    waits = [next(p) for p in progs]
+    done = [False] * 3
+    while not all(done):
+        moved = False
+        for i, prog in enumerate(progs):
+            while not done[i] and waits[i]():
+                try:
+                    waits[i] = next(prog)
+                except StopIteration:
+                    done[i] = True
+                moved = True
+        if not moved:
+            return dict(st)
+    return None
+
+
+# (head-dim slots per pair, K ring slots): pooled D = 64, wide D = 128, wide D = 192
+CONFIGS = [(1, 3, NSB - 1), (4, 3, NSB - PAIR), (6, 2, NSB - PAIR)]
+
+
+@pytest.mark.parametrize("ndc,nk,vlag", CONFIGS, ids=["pooled-d64", "wide-d128", "wide-d192"])
+@pytest.mark.parametrize("nch", [2, 4, 6, 10, 16, 48])
+def test_forward_pair_order_has_no_deadlock(ndc, nk, vlag, nch):
+    assert _forward_order(nch, ndc, nk, vlag) is None
+
+
+@pytest.mark.parametrize("ndc,nk", [(4, 3), (6, 2)], ids=["wide-d128", "wide-d192"])
+def test_forward_wide_pairs_deadlock_with_the_unpaired_lag(ndc, nk):
+    """The lag of the unpaired kernels (NSB - 1) stalls the wide pair schedule: the planted mistake is caught."""
+    assert _forward_order(16, ndc, nk, NSB - 1) is not None
