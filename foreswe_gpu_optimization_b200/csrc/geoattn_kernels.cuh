@@ -2,7 +2,8 @@
 //
 // Operator (fore_swe/custom_encoder_model.py:25-39):
 //   S = Q K^T / sqrt(d);  P1 = softmax(S);  Z = alpha*P1 + beta*Dp + gamma*Ap;  P2 = softmax(Z);  O = P2 V
-// with the geo prior Dp = 1/(1+dist_km), Ap = 1/(1+angle_deg) read from a per-call table (prior.cu).
+// with the geo prior Dp = 1/(1+dist_km), Ap = 1/(1+angle_deg) read from a table built once per station geometry
+// (prior_coords_kernel / prior_dense_kernel in geoattn.cu).
 //
 // All kernels share one CTA shape: EW element-wise warpgroups (EW = 2 for bf16, 1 for fp32; a thread of warp w owns
 // TMEM lane 32*(w%4) + lane, i.e. one row of every 128-row accumulator, and warpgroup w/4 owns every EW-th 32-column
@@ -12,6 +13,12 @@
 // 128-byte swizzle; one "region" is rows x 128 bytes (64 bf16 or 32 fp32 along the contiguous dimension). Where
 // shared memory is full the prior is read from L2 directly. bf16 outputs (O, dQ, dK, dV) leave through a swizzled
 // shared-memory tile and a TMA store; the operands of the next tile are prefetched into L2 while this one runs.
+//
+// fp32 storage (TF32 MMAs): operands come as round-to-nearest hi/lo planes and the score-shaped products take three
+// terms (hi.hi + hi.lo + lo.hi). At head dim 64 the kernels are "pooled": the 128-row A operand of the score MMAs is
+// copied into tensor memory once per tile (tcgen05.cp) and its shared-memory landing zone then holds the chunk
+// rings; the forward issues its score MMAs over pairs of 32-key chunks. Above 64 ("wide") the score operands stream
+// through slots that each hold one 32-wide head-dim chunk.
 //
 // Softmax #1 runs in log2 units: t = acc * (log2(e)/sqrt(d)) with row max m. Once the row sum l1 is known, the
 // normalised probability is one fused multiply-add and one exp2: P1 = 2^(fma(acc, log2(e)/sqrt(d), -m1)) with
