@@ -1061,7 +1061,11 @@ struct RowsCfg : Tile<BF16, DP> {
   static constexpr int LAND = POOL ? NKV : 0;  // ring positions the Q/dO landing takes per tile
   static constexpr int NPR = (BF16 && DP <= 128) ? 2 : !BF16 ? 0 : 1;  // staged prior buffers (0: L2)
   static constexpr int Q_BYTES = WIDE ? 0 : kBM * DP * T::EB;                   // per plane (Q and dO)
-  static constexpr int K_BYTES = WIDE ? kSlotPlaneBytes : T::CH * DP * T::EB;  // per plane per buffer / slot
+  // wide: the S and dP MMAs cover pairs of 32-key chunks (slots carry a head-dim chunk of Q or dO and of two K or
+  // V chunks); the K^T loads for dQ trail the slots by one pair, so the TMA never waits on a dQ MMA that needs the
+  // next pair's scores first
+  static constexpr int PAIR = WIDE ? 2 : 1;
+  static constexpr int K_BYTES = WIDE ? kSlotPlaneBytesRows<PAIR * T::CH> : T::CH * DP * T::EB;  // per plane per slot
   static constexpr int KT_BYTES = BF16 ? 0 : DP * 128;  // fp32: transposed K chunk (hi) for dQ
   static constexpr int DS_BYTES = kBM * 128;
   static constexpr int NDS = (BF16 || POOL) ? 2 : 1;  // dS / K^T buffers (ring size)
@@ -1080,7 +1084,8 @@ struct RowsCfg : Tile<BF16, DP> {
   static_assert(SMEM + 1024 <= kSmemPerBlock, "row pass: dynamic + static shared memory above the per-block limit");
   // S / dP accumulator buffers in tensor memory: 4 without the dQ accumulator, so the MMA warp runs ~3 chunks ahead
   // and frees Q / dO for the next tile early enough to hide its reload
-  static constexpr int NSB = DQ ? 2 : 4;
+  static constexpr int NSB = (DQ && !WIDE) ? 2 : 4;
+  static_assert(NSB % PAIR == 0, "chunk pairs take aligned score buffers");
   static constexpr int TM_S = 0;
   static constexpr int TM_DP = NSB * T::CH;
   static constexpr int TM_DQ = 2 * NSB * T::CH;
@@ -1117,7 +1122,8 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
   __shared__ int abort_flag;
   __shared__ double red[8][3];
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int nchunks = (p.N + T::CH - 1) / T::CH;
+  // chunks every role iterates; wide: whole pairs (an extra chunk past N is masked like a ragged one)
+  const int nch = C::PAIR == 2 ? (((p.N + T::CH - 1) / T::CH + 1) & ~1) : (p.N + T::CH - 1) / T::CH;
   const int ntiles = p.nrb * p.B * p.H;  // tile = (128-query row block, b*h); persistent CTAs stride over tiles
   WaitCtx ctx{&abort_flag, p.status};
   const bool epi_tma = DQ && C::EPI_TMA && p.out_tma;
@@ -1191,20 +1197,33 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
           prefetch_rows<T>(&maps.k, p.N, nh, nb, p.B, T::PL);
           prefetch_rows<T>(&maps.v, p.N, nh, nb, p.B, T::PL);
         }
-        for (int c = 0; c < nchunks && ok; ++c) {
-          if constexpr (C::WIDE) {  // (Q, K) head-dim chunks for S, then (dO, V) chunks for dP
+        auto load_kt = [&](int cc) -> bool {  // transposed K chunk (hi) for the dQ MMA of chunk cc
+          const int ts = tc % C::NDS;
+          if (!mbar_wait(&bar_ktempty[ts], ((tc / C::NDS) & 1) ^ 1, ctx)) return false;
+          mbar_arrive_expect_tx(&bar_ktfull[ts], C::KT_BYTES);
+          tma_tileT(smem + C::OFF_KT + ts * C::KT_BYTES, &maps.kt, &bar_ktfull[ts], cc * T::CH, h, b);
+          ++tc;
+          return true;
+        };
+        for (int c = 0; c < nch && ok; c += C::PAIR) {
+          if constexpr (C::WIDE) {  // (Q, K) head-dim chunks for S, then (dO, V) chunks for dP, two K/V chunks each
             for (int j = 0; j < 2 * C::NDC && ok; ++j) {
               const int ks = kc % NKV, dc = j % C::NDC;
               if (!(ok = mbar_wait(&bar_kempty[ks], ((kc / NKV) & 1) ^ 1, ctx))) break;
               mbar_arrive_expect_tx(&bar_kfull[ks], T::PL * C::K_BYTES);
               uint8_t* slot = smem + C::OFF_K + ks * T::PL * C::K_BYTES;
               if (j < C::NDC)
-                tma_slot<T>(slot, &bar_kfull[ks], &maps.q, rb * kBM, &maps.k, c * T::CH, dc, h, b, p.B);
+                tma_slot_rows<T, C::PAIR * T::CH>(slot, &bar_kfull[ks], &maps.q, rb * kBM, &maps.k, c * T::CH, dc, h,
+                                                  b, p.B);
               else
-                tma_slot<T>(slot, &bar_kfull[ks], &maps.dout, rb * kBM, &maps.v, c * T::CH, dc, h, b, p.B);
+                tma_slot_rows<T, C::PAIR * T::CH>(slot, &bar_kfull[ks], &maps.dout, rb * kBM, &maps.v, c * T::CH, dc,
+                                                  h, b, p.B);
               ++kc;
             }
             if (!ok) break;
+            if (sweep == 1 && c >= C::PAIR)  // K^T of the previous pair (its dQ MMAs follow this pair's scores)
+              for (int cc = c - C::PAIR; cc < c && ok; ++cc) ok = load_kt(cc);
+            continue;
           } else {
             const int ks = kc % NKV;
             if (!(ok = mbar_wait(&bar_kempty[ks], ((kc / NKV) & 1) ^ 1, ctx))) break;
@@ -1217,16 +1236,12 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
                         p.B, T::PL);
             ++kc;
           }
-          if constexpr (!BF16) {
-            if (sweep == 1) {
-              const int ts = tc % C::NDS;
-              if (!(ok = mbar_wait(&bar_ktempty[ts], ((tc / C::NDS) & 1) ^ 1, ctx))) break;
-              mbar_arrive_expect_tx(&bar_ktfull[ts], C::KT_BYTES);
-              tma_tileT(smem + C::OFF_KT + ts * C::KT_BYTES, &maps.kt, &bar_ktfull[ts], c * T::CH, h, b);
-              ++tc;
-            }
-          }
+          if constexpr (!BF16)
+            if (sweep == 1 && !(ok = load_kt(c))) break;
         }
+        if constexpr (C::WIDE)  // K^T of the last pair
+          if (sweep == 1)
+            for (int cc = nch - C::PAIR; cc < nch && ok; ++cc) ok = load_kt(cc);
       }
       }
     }
@@ -1239,7 +1254,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       const int rb = tile % p.nrb;
       if (lane == 0) {
         for (int sweep = 0; sweep < SWEEPS && ok; ++sweep) {
-          for (int c = 0; c < nchunks && ok; ++c) {
+          for (int c = 0; c < nch && ok; ++c) {
             const int ps = pc % NPR;
             if (!(ok = mbar_wait(&bar_prempty[ps], ((pc / NPR) & 1) ^ 1, ctx))) break;
             mbar_arrive_expect_tx(&bar_prfull[ps], kPriorTileBytes);
@@ -1256,20 +1271,22 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       int kc = 0, sc = 0, dc = 0, it = 0;
       bool ok = true;
       auto issue = [&](bool release_k) -> bool {
-        if constexpr (C::WIDE) {  // S then dP, each accumulated over the head-dim chunks of its slots
+        if constexpr (C::WIDE) {  // S then dP of a chunk pair, each accumulated over the head-dim chunks of its slots
           const int ss = sc % NSB;
           if (!mbar_wait(&bar_sempty[ss], ((sc / NSB) & 1) ^ 1, ctx)) return false;
+          if (!mbar_wait(&bar_sempty[ss + 1], (((sc + 1) / NSB) & 1) ^ 1, ctx)) return false;
           for (int j = 0; j < 2 * C::NDC; ++j) {
             const int ks = kc % NKV, dc = j % C::NDC;
             if (!mbar_wait(&bar_kfull[ks], (kc / NKV) & 1, ctx)) return false;
             tc_fence_after();
-            mma_slot<T>(tmem + (j < C::NDC ? C::TM_S : C::TM_DP) + ss * T::CH,
-                        sbase + C::OFF_K + ks * T::PL * C::K_BYTES, dc > 0);
+            mma_slot_rows<T, C::PAIR * T::CH>(tmem + (j < C::NDC ? C::TM_S : C::TM_DP) + ss * T::CH,
+                                              sbase + C::OFF_K + ks * T::PL * C::K_BYTES, dc > 0);
             mma_commit(&bar_kempty[ks]);
             ++kc;
           }
           mma_commit(&bar_sfull[ss]);
-          ++sc;
+          mma_commit(&bar_sfull[ss + 1]);
+          sc += 2;
           return true;
         }
         const int ks = kc % NKV, ss = sc % NSB;
@@ -1335,7 +1352,17 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
             mma_commit(&bar_vempty[kc % NKV]);
           }
         }
-        for (int c = 0; c < nchunks && ok; ++c) ok = issue(true);
+        if constexpr (C::WIDE) {  // pairs: sweep 1; sweep 2 issues the next pair's scores before this pair's dQ
+          for (int c = 0; c < nch && ok; c += C::PAIR) ok = issue(true);
+          const int kc0 = kc;
+          if (ok) ok = issue(false);
+          for (int c = 0; c < nch && ok; c += C::PAIR) {
+            if (c + C::PAIR < nch && !(ok = issue(false))) break;
+            for (int cc = c; cc < c + C::PAIR && ok; ++cc) ok = issue_dq(cc, kc0);
+          }
+          if (ok) mma_commit(&bar_dqfull);
+        } else {
+        for (int c = 0; c < nch && ok; ++c) ok = issue(true);
         if constexpr (!DQ) {
           if (ok) mma_commit(&bar_qempty);  // every S/dP MMA of this tile has been issued
           continue;
@@ -1343,19 +1370,20 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         const int kc0 = kc;  // first K use of sweep 2
         if (ok) ok = issue(false);
         // every S/dP MMA of this tile has been issued: Q and dO may take the next tile's (pooled: no separate buffer)
-        if (!C::POOL && ok && nchunks == 1) mma_commit(&bar_qempty);
-        for (int c = 0; c < nchunks && ok; ++c) {
+        if (!C::POOL && ok && nch == 1) mma_commit(&bar_qempty);
+        for (int c = 0; c < nch && ok; ++c) {
           if constexpr (NKV >= 2 || C::WIDE) {  // look ahead: S/dP of the next chunk overlap the element-wise work
-            if (c + 1 < nchunks && !(ok = issue(false))) break;
-            if (!C::POOL && c + 2 == nchunks) mma_commit(&bar_qempty);
+            if (c + 1 < nch && !(ok = issue(false))) break;
+            if (!C::POOL && c + 2 == nch) mma_commit(&bar_qempty);
             if (!(ok = issue_dq(c, kc0))) break;
           } else {                   // one K/V buffer: the next chunk's K can only arrive after this chunk's dQ
             if (!(ok = issue_dq(c, kc0))) break;
-            if (c + 1 < nchunks && !(ok = issue(false))) break;
-            if (c + 2 == nchunks) mma_commit(&bar_qempty);
+            if (c + 1 < nch && !(ok = issue(false))) break;
+            if (c + 2 == nch) mma_commit(&bar_qempty);
           }
         }
         if (ok) mma_commit(&bar_dqfull);
+        }
       }
     }
   } else if (warp < T::TMA_WARP) {
@@ -1392,7 +1420,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       c2 = cL + log2f(cst[2]);
     }
     float acc[3] = {0.f, 0.f, 0.f};  // delta2, a, b
-    for (int c = 0; c < nchunks && ok; ++c) {
+    for (int c = 0; c < nch && ok; ++c) {
       const int ss = sc % NSB, prs = pc % PRB;
       Prior32<BF16> pr;
       if constexpr (NPR == 0) load_prior32<BF16>(p.prior, p.np, row, c * T::CH, pr);  // before the waits
@@ -1487,7 +1515,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
     const float pb = acc[2];
     float gap[2] = {0.f, 0.f}, gbp[2] = {0.f, 0.f}, ggp[2] = {0.f, 0.f};  // d(alpha), d(beta), d(gamma) of the row
     if constexpr (DQ) {
-    for (int c = 0; c < nchunks && ok; ++c) {
+    for (int c = 0; c < nch && ok; ++c) {
       const int ss = sc % NSB, ds = dc % C::NDS, prs = pc % PRB;
       Prior32<BF16> pr;
       if constexpr (NPR == 0) load_prior32<BF16>(p.prior, p.np, row, c * T::CH, pr);  // before the waits
