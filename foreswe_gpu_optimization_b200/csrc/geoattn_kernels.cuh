@@ -1650,7 +1650,9 @@ struct ColsCfg : Tile<BF16, DP> {
   // pooled: 2 (a 3-deep ring, 8 % faster at C2, gave dK rows of one tile that differed between runs in ~1 run of 4,
   // with the drain and the single staging buffer alike; 2 is bitwise stable)
   static constexpr int NQ = (BF16 && DP <= 128) ? 3 : POOL ? 2 : 1;   // query-chunk (Q, dO) buffers
-  static constexpr int NSB = ((BF16 && DP <= 128) || POOL) ? 2 : 1;  // S^T / dP^T accumulator buffers in TMEM
+  // wide: two buffers let the next chunk's S^T/dP^T run while this chunk's element-wise work and dV/dK wait; its
+  // slots are then loaded before the chunk's single transposed Q/dO buffer, which frees only after the previous dV/dK
+  static constexpr int NSB = ((BF16 && DP <= 128) || POOL || WIDE) ? 2 : 1;  // S^T / dP^T buffers in TMEM
   static constexpr int LAND = POOL ? NQ : 0;               // ring positions the K/V landing takes per tile
   static_assert(LAND == 0 || LAND == NQ, "a landing takes every slot of the ring once");
   static constexpr int NR = 2;                             // row-record buffers
@@ -1789,6 +1791,20 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         const int gc = it * nchunks + c;  // chunk count over all tiles (buffer slots and phases)
         const int gq = q0 + c;            // query-chunk ring position
         const int qs = gq % NQ;
+        if constexpr (C::WIDE) {  // (K, Q) head-dim chunks for S^T, then (V, dO) chunks for dP^T
+          for (int j = 0; j < 2 * C::NDC && ok; ++j) {
+            const int ss = rc % C::NRS, dc = j % C::NDC;
+            if (!(ok = mbar_wait(&bar_rsempty[ss], ((rc / C::NRS) & 1) ^ 1, ctx))) break;
+            mbar_arrive_expect_tx(&bar_rsfull[ss], 2 * kSlotPlaneBytes);
+            uint8_t* slot = smem + C::OFF_RS + ss * 2 * kSlotPlaneBytes;
+            if (j < C::NDC)
+              tma_slot<T>(slot, &bar_rsfull[ss], &maps.k, kblk * kBM, &maps.q, c * T::CH, dc, h, b, p.B);
+            else
+              tma_slot<T>(slot, &bar_rsfull[ss], &maps.v, kblk * kBM, &maps.dout, c * T::CH, dc, h, b, p.B);
+            ++rc;
+          }
+          if (!ok) break;
+        }
         if (!(ok = mbar_wait(&bar_qempty[qs], ((gq / NQ) & 1) ^ 1, ctx))) break;
         mbar_arrive_expect_tx(&bar_qfull[qs], 2 * T::PL * C::Q_BYTES + 2 * C::QT_BYTES);
         if constexpr (!C::WIDE) {
@@ -1806,20 +1822,6 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         mbar_arrive_expect_tx(&bar_recfull[rs], C::REC_BYTES);
         bulk_load(smem + C::OFF_REC + rs * C::REC_BYTES, p.rowrec + ((size_t)bh * p.nchp + c) * 4 * T::CH,
                   C::REC_BYTES, &bar_recfull[rs]);
-        if constexpr (C::WIDE) {  // (K, Q) head-dim chunks for S^T, then (V, dO) chunks for dP^T
-          for (int j = 0; j < 2 * C::NDC && ok; ++j) {
-            const int ss = rc % C::NRS, dc = j % C::NDC;
-            if (!(ok = mbar_wait(&bar_rsempty[ss], ((rc / C::NRS) & 1) ^ 1, ctx))) break;
-            mbar_arrive_expect_tx(&bar_rsfull[ss], 2 * kSlotPlaneBytes);
-            uint8_t* slot = smem + C::OFF_RS + ss * 2 * kSlotPlaneBytes;
-            if (j < C::NDC)
-              tma_slot<T>(slot, &bar_rsfull[ss], &maps.k, kblk * kBM, &maps.q, c * T::CH, dc, h, b, p.B);
-            else
-              tma_slot<T>(slot, &bar_rsfull[ss], &maps.v, kblk * kBM, &maps.dout, c * T::CH, dc, h, b, p.B);
-            ++rc;
-          }
-          if (!ok) break;
-        }
         // the dS stores trail the loads by LAG chunks, so a store's wait for its tile never holds back the loads
         // the MMAs need next (LAG < NQ keeps the dependency chain acyclic)
         if constexpr (SDS)
