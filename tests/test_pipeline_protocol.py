@@ -1,14 +1,16 @@
 """Models of the kernels' ring protocols, checked on the CPU (no kernel runs here).
 
 The kernels in foreswe_gpu_optimization_b200/csrc/geoattn_kernels.cuh hand buffers between their TMA, MMA and
-element-wise warps through mbarrier rings. Two of those hand-overs are easy to get wrong and fail on the GPU only as a
-bounded-wait timeout or as results that differ between runs, so their arithmetic is restated here:
+element-wise warps through mbarrier rings. Some of those hand-overs are easy to get wrong and fail on the GPU only as
+a bounded-wait timeout or as results that differ between runs, so their arithmetic is restated here:
 
 * pooled fp32 kernels (head dim 64): the landing of a tile's tensor-memory operand takes every slot of a chunk ring
   once, completing an `empty` phase per slot but no `full` phase; the consumer's `full` parity skips the landings;
 * the forward's pass B with chunk pairs: V of chunk c is loaded after the K of chunk c + VLAG. With wide head dims a
   pair takes NDC ring slots, more than the ring holds, and a lag of NSB - 1 deadlocks (seen on the GPU as expired
-  bounded waits); the kernels use NSB - PAIR there.
+  bounded waits); the kernels use NSB - PAIR there;
+* the wide row pass's sweep 2 with chunk pairs: the transposed K chunks for dQ trail the slots by one pair;
+* the wide key pass with two score buffers: a chunk's slots are loaded before its single transposed Q/dO buffer.
 """
 import pytest
 
@@ -135,3 +137,157 @@ def test_forward_pair_order_has_no_deadlock(ndc, nk, vlag, nch):
 def test_forward_wide_pairs_deadlock_with_the_unpaired_lag(ndc, nk):
     """The lag of the unpaired kernels (NSB - 1) stalls the wide pair schedule: the planted mistake is caught."""
     assert _forward_order(16, ndc, nk, NSB - 1) is not None
+
+
+def _key_pass_wide_order(n, ndc, nrs, nsb, slots_first):
+    """Wide fp32 key pass, one tile: TMA loads per query chunk its 2*ndc head-dim slots (nrs-slot ring) and its
+    transposed Q/dO chunk (one buffer, free once the previous chunk's dV/dK ran); the MMA issues S^T/dP^T of chunk
+    c + 1 before dV/dK of chunk c when it has two score buffers; the element-wise warps release the scores and stage
+    P2^T/dS^T (one buffer). Returns None or the deadlock state."""
+    st = dict(sl=0, sc=0, s_iss=0, s_rel=0, staged=0, dvdk=0, qt=0)
+
+    def tma():
+        for c in range(n):
+            def slots():
+                for _ in range(2 * ndc):
+                    yield lambda: st["sl"] - st["sc"] < nrs
+                    st["sl"] += 1
+
+            def qt(c=c):
+                yield lambda: st["dvdk"] >= c
+                st["qt"] = c + 1
+
+            first, second = (slots, qt) if slots_first else (qt, slots)
+            yield from first()
+            yield from second()
+
+    def mma():
+        def issue(c):
+            yield lambda: st["s_rel"] >= c + 1 - nsb
+            for _ in range(2 * ndc):
+                yield lambda: st["sl"] > st["sc"]
+                st["sc"] += 1
+            st["s_iss"] = c + 1
+
+        yield from issue(0)
+        for c in range(n):
+            if nsb == 2 and c + 1 < n:
+                yield from issue(c + 1)
+            yield lambda c=c: st["staged"] > c and st["qt"] > c
+            st["dvdk"] = c + 1
+            if nsb == 1 and c + 1 < n:
+                yield from issue(c + 1)
+
+    def ew():
+        for c in range(n):
+            yield lambda c=c: st["s_iss"] > c
+            st["s_rel"] = c + 1
+            yield lambda c=c: st["dvdk"] >= c
+            st["staged"] = c + 1
+
+    progs = [tma(), mma(), ew()]
+    waits = [next(p) for p in progs]
+    done = [False] * 3
+    while not all(done):
+        moved = False
+        for i, prog in enumerate(progs):
+            while not done[i] and waits[i]():
+                try:
+                    waits[i] = next(prog)
+                except StopIteration:
+                    done[i] = True
+                moved = True
+        if not moved:
+            return dict(st)
+    return None
+
+
+@pytest.mark.parametrize("ndc", [4, 6], ids=["d128", "d192"])
+@pytest.mark.parametrize("n", [1, 2, 3, 16, 47])
+def test_key_pass_wide_order(ndc, n):
+    """Two score buffers need the slots before the single transposed Q/dO buffer (the kernels' order); with that
+    buffer first the look-ahead deadlocks as soon as a tile has two chunks (the planted order is caught)."""
+    assert _key_pass_wide_order(n, ndc, 3, 2, slots_first=True) is None
+    if n >= 2:
+        assert _key_pass_wide_order(n, ndc, 3, 2, slots_first=False) is not None
+
+
+def _rows_wide_pair_order(nch, ndc, nkv, kt_lag_pairs, nds=1):
+    """Wide fp32 row pass, one tile: two sweeps of chunk-pair S/dP MMAs (2*ndc head-dim slots per pair through an
+    nkv-slot ring, four score buffers); sweep 2 issues the next pair's scores before this pair's dQ MMAs, which need
+    the staged dS and the transposed K chunk (nds buffers, each free once the previous use's dQ ran). The TMA loads
+    the K^T chunks of a pair `kt_lag_pairs` pairs after its slots. Returns None or the deadlock state."""
+    st = dict(kload=0, kcons=0, s_iss=0, s_rel=0, staged=0, dq=0, kt=0)
+
+    def tma():
+        for sweep in range(2):
+            for c in range(0, nch, PAIR):
+                for _ in range(2 * ndc):
+                    yield lambda: st["kload"] - st["kcons"] < nkv
+                    st["kload"] += 1
+                if sweep == 1 and c >= PAIR * kt_lag_pairs:
+                    for cc in range(c - PAIR * kt_lag_pairs, c - PAIR * kt_lag_pairs + PAIR):
+                        yield lambda cc=cc: st["dq"] >= cc - nds + 1
+                        st["kt"] = cc + 1
+            if sweep == 1:
+                for cc in range(max(0, nch - PAIR * kt_lag_pairs), nch):
+                    yield lambda cc=cc: st["dq"] >= cc - nds + 1
+                    st["kt"] = cc + 1
+
+    def mma():
+        sc = 0
+
+        def issue():
+            nonlocal sc
+            yield lambda: st["s_rel"] >= sc + PAIR - NSB
+            for _ in range(2 * ndc):
+                yield lambda: st["kload"] > st["kcons"]
+                st["kcons"] += 1
+            sc += PAIR
+            st["s_iss"] = sc
+
+        for _ in range(0, nch, PAIR):
+            yield from issue()
+        yield from issue()
+        for c in range(0, nch, PAIR):
+            if c + PAIR < nch:
+                yield from issue()
+            for cc in range(c, c + PAIR):
+                yield lambda cc=cc: st["staged"] > cc and st["kt"] > cc
+                st["dq"] = cc + 1
+
+    def ew():
+        for c in range(nch):
+            yield lambda c=c: st["s_iss"] > c
+            st["s_rel"] = c + 1
+        for c in range(nch):
+            yield lambda c=c: st["s_iss"] > nch + c
+            st["s_rel"] = nch + c + 1
+            yield lambda c=c: st["dq"] >= c - nds + 1
+            st["staged"] = c + 1
+
+    progs = [tma(), mma(), ew()]
+    waits = [next(p) for p in progs]
+    done = [False] * 3
+    while not all(done):
+        moved = False
+        for i, prog in enumerate(progs):
+            while not done[i] and waits[i]():
+                try:
+                    waits[i] = next(prog)
+                except StopIteration:
+                    done[i] = True
+                moved = True
+        if not moved:
+            return dict(st)
+    return None
+
+
+@pytest.mark.parametrize("ndc", [4, 6], ids=["d128", "d192"])
+@pytest.mark.parametrize("nch", [2, 4, 6, 16, 48])
+def test_rows_wide_pair_order(ndc, nch):
+    """The K^T loads trail the slots by one pair (the kernels' order); loaded with their own pair, a dQ MMA that must
+    follow the next pair's scores holds the single K^T buffer and the pipeline stops (the planted order is caught)."""
+    assert _rows_wide_pair_order(nch, ndc, 3, kt_lag_pairs=1) is None
+    if nch >= 4:
+        assert _rows_wide_pair_order(nch, ndc, 3, kt_lag_pairs=0) is not None
