@@ -1653,6 +1653,11 @@ struct ColsCfg : Tile<BF16, DP> {
   // wide: two buffers let the next chunk's S^T/dP^T run while this chunk's element-wise work and dV/dK wait; its
   // slots are then loaded before the chunk's single transposed Q/dO buffer, which frees only after the previous dV/dK
   static constexpr int NSB = ((BF16 && DP <= 128) || POOL || WIDE) ? 2 : 1;  // S^T / dP^T buffers in TMEM
+  // wide: the S^T/dP^T MMAs cover pairs of 32-query chunks (the slots carry a head-dim chunk of K or V and of two Q or
+  // dO chunks) into both score buffers; the next pair issues after the first chunk's dV/dK, and a pair's odd chunk
+  // loads its transposed Q/dO after the next pair's slots
+  static constexpr int PAIR = WIDE ? 2 : 1;
+  static constexpr int SLOT_PLANE = kSlotPlaneBytesRows<PAIR * T::CH>;
   static constexpr int LAND = POOL ? NQ : 0;               // ring positions the K/V landing takes per tile
   static_assert(LAND == 0 || LAND == NQ, "a landing takes every slot of the ring once");
   static constexpr int NR = 2;                             // row-record buffers
@@ -1664,7 +1669,7 @@ struct ColsCfg : Tile<BF16, DP> {
   static constexpr int ST_BYTES = kBM * 128;                // P2^T or dS^T tile
   static constexpr int REC_BYTES = 4 * T::CH * 4;           // row records of one query chunk: m1, c2, delta1, delta2
   static constexpr int OFF_RS = 0;
-  static constexpr int OFF_K = OFF_RS + NRS * 2 * kSlotPlaneBytes;
+  static constexpr int OFF_K = OFF_RS + NRS * 2 * SLOT_PLANE;
   static constexpr int OFF_V = OFF_K + T::PL * K_BYTES;
   static constexpr int KV_END = OFF_V + T::PL * K_BYTES;
   static constexpr int OFF_Q = POOL ? OFF_K : KV_END;
@@ -1710,7 +1715,8 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
   __shared__ int abort_flag;
   __shared__ double redc[8][2];
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int nchunks = (p.N + T::CH - 1) / T::CH;
+  // chunks every role iterates; wide: whole pairs (an extra chunk past N has +inf row records: P1 = P2 = dS = 0)
+  const int nch = C::PAIR == 2 ? (((p.N + T::CH - 1) / T::CH + 1) & ~1) : (p.N + T::CH - 1) / T::CH;
   const int ntiles = p.nrb * p.B * p.H;  // tile = (128-key block, b*h); persistent CTAs stride over tiles
   WaitCtx ctx{&abort_flag, p.status};
   const bool epi_tma = C::EPI_TMA && p.out_tma;
@@ -1769,7 +1775,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         mbar_arrive(&bar_tempty[ts]);
         return true;
       };
-      const int q0 = it * (nchunks + C::LAND) + C::LAND;  // query-chunk ring position of chunk 0
+      const int q0 = it * (nch + C::LAND) + C::LAND;  // query-chunk ring position of chunk 0
       if constexpr (C::POOL) {  // K and V into the pool once its ring positions are free (the previous tile's MMAs ran)
         for (int s = q0 - C::LAND; s < q0 && ok; ++s) ok = mbar_wait(&bar_qempty[s % NQ], ((s / NQ) & 1) ^ 1, ctx);
         if (!ok) break;
@@ -1787,23 +1793,48 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         prefetch_tile<T>(&maps.k, nrow, nh, nb, p.B, T::PL);
         prefetch_tile<T>(&maps.v, nrow, nh, nb, p.B, T::PL);
       }
-      for (int c = 0; c < nchunks; ++c) {
-        const int gc = it * nchunks + c;  // chunk count over all tiles (buffer slots and phases)
+      // wide: the slots of the pair starting at chunk c, (K, Q) head-dim chunks for S^T then (V, dO) for dP^T
+      auto load_slots = [&](int c) -> bool {
+        if constexpr (!C::WIDE) {
+          (void)c;
+          return true;
+        } else {
+        for (int j = 0; j < 2 * C::NDC; ++j) {
+          const int ss = rc % C::NRS, dc = j % C::NDC;
+          if (!mbar_wait(&bar_rsempty[ss], ((rc / C::NRS) & 1) ^ 1, ctx)) return false;
+          mbar_arrive_expect_tx(&bar_rsfull[ss], 2 * C::SLOT_PLANE);
+          uint8_t* slot = smem + C::OFF_RS + ss * 2 * C::SLOT_PLANE;
+          if (j < C::NDC)
+            tma_slot_rows<T, C::PAIR * T::CH>(slot, &bar_rsfull[ss], &maps.k, kblk * kBM, &maps.q, c * T::CH, dc, h,
+                                              b, p.B);
+          else
+            tma_slot_rows<T, C::PAIR * T::CH>(slot, &bar_rsfull[ss], &maps.v, kblk * kBM, &maps.dout, c * T::CH, dc,
+                                              h, b, p.B);
+          ++rc;
+        }
+        return true;
+        }
+      };
+      for (int c = 0; c < nch; ++c) {
+        const int gc = it * nch + c;  // chunk count over all tiles (buffer slots and phases)
         const int gq = q0 + c;            // query-chunk ring position
         const int qs = gq % NQ;
-        if constexpr (C::WIDE) {  // (K, Q) head-dim chunks for S^T, then (V, dO) chunks for dP^T
-          for (int j = 0; j < 2 * C::NDC && ok; ++j) {
-            const int ss = rc % C::NRS, dc = j % C::NDC;
-            if (!(ok = mbar_wait(&bar_rsempty[ss], ((rc / C::NRS) & 1) ^ 1, ctx))) break;
-            mbar_arrive_expect_tx(&bar_rsfull[ss], 2 * kSlotPlaneBytes);
-            uint8_t* slot = smem + C::OFF_RS + ss * 2 * kSlotPlaneBytes;
-            if (j < C::NDC)
-              tma_slot<T>(slot, &bar_rsfull[ss], &maps.k, kblk * kBM, &maps.q, c * T::CH, dc, h, b, p.B);
-            else
-              tma_slot<T>(slot, &bar_rsfull[ss], &maps.v, kblk * kBM, &maps.dout, c * T::CH, dc, h, b, p.B);
-            ++rc;
-          }
-          if (!ok) break;
+        const int rs = gc % NR;  // the chunk's row records, on their own ring
+        auto load_records = [&]() -> bool {
+          if (!mbar_wait(&bar_recempty[rs], ((gc / NR) & 1) ^ 1, ctx)) return false;
+          mbar_arrive_expect_tx(&bar_recfull[rs], C::REC_BYTES);
+          bulk_load(smem + C::OFF_REC + rs * C::REC_BYTES, p.rowrec + ((size_t)bh * p.nchp + c) * 4 * T::CH,
+                    C::REC_BYTES, &bar_recfull[rs]);
+          return true;
+        };
+        // wide: the chunk's records first (the element-wise warps read them before they free the chunk's score
+        // buffer, which the next pair's MMA waits for), then a pair's slots before the previous pair's odd chunk
+        // (before chunk 0 for the first pair), so the transposed Q/dO of each chunk, which waits for the dV/dK before
+        // it, never holds back scores the MMA warp issues before that dV/dK
+        if constexpr (C::WIDE) {
+          if (!(ok = load_records())) break;
+          const int pc = (c == 0) ? 0 : ((c & 1) ? c + 1 : -1);  // first chunk of the pair whose slots load here
+          if (pc >= 0 && pc < nch && !(ok = load_slots(pc))) break;
         }
         if (!(ok = mbar_wait(&bar_qempty[qs], ((gq / NQ) & 1) ^ 1, ctx))) break;
         mbar_arrive_expect_tx(&bar_qfull[qs], 2 * T::PL * C::Q_BYTES + 2 * C::QT_BYTES);
@@ -1817,19 +1848,16 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
           tma_tileT(smem + C::OFF_QT + qs * C::QT_BYTES, &maps.qt, &bar_qfull[qs], c * T::CH, h, b);
           tma_tileT(smem + C::OFF_DOT + qs * C::QT_BYTES, &maps.dot, &bar_qfull[qs], c * T::CH, h, b);
         }
-        const int rs = gc % NR;  // the chunk's row records, on their own ring
-        if (!(ok = mbar_wait(&bar_recempty[rs], ((gc / NR) & 1) ^ 1, ctx))) break;
-        mbar_arrive_expect_tx(&bar_recfull[rs], C::REC_BYTES);
-        bulk_load(smem + C::OFF_REC + rs * C::REC_BYTES, p.rowrec + ((size_t)bh * p.nchp + c) * 4 * T::CH,
-                  C::REC_BYTES, &bar_recfull[rs]);
+        if constexpr (!C::WIDE)
+          if (!(ok = load_records())) break;
         // the dS stores trail the loads by LAG chunks, so a store's wait for its tile never holds back the loads
         // the MMAs need next (LAG < NQ keeps the dependency chain acyclic)
         if constexpr (SDS)
           if (c >= SLAG && !(ok = store_ds(gc - SLAG, c - SLAG))) break;
       }
       if constexpr (SDS)
-        for (int c2 = nchunks - SLAG < 0 ? 0 : nchunks - SLAG; c2 < nchunks && ok; ++c2)
-          ok = store_ds(it * nchunks + c2, c2);
+        for (int c2 = nch - SLAG < 0 ? 0 : nch - SLAG; c2 < nch && ok; ++c2)
+          ok = store_ds(it * nch + c2, c2);
       }
     }
   } else if (warp == T::PR_WARP) {
@@ -1840,8 +1868,8 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         int it = 0;
         for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++it) {
           const int kblk = tile % p.nrb;
-          for (int c = 0; c < nchunks && ok; ++c) {
-            const int gc = it * nchunks + c, ps = gc % NPR;
+          for (int c = 0; c < nch && ok; ++c) {
+            const int gc = it * nch + c, ps = gc % NPR;
             if (!(ok = mbar_wait(&bar_prempty[ps], ((gc / NPR) & 1) ^ 1, ctx))) break;
             mbar_arrive_expect_tx(&bar_prfull[ps], kPriorTileBytes);
             tma_prior(smem + C::OFF_PR + ps * kPriorTileBytes, &maps.prior, &bar_prfull[ps], kblk * kBM, c);
@@ -1855,19 +1883,21 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       int it = 0, rc = 0;
       int qoff = 0;  // query-chunk ring position minus chunk count (the pooled K/V landings take ring positions)
       auto issue_s = [&](int gc) -> bool {
-        if constexpr (C::WIDE) {
-          const int ss = gc % NSB;
-          if (!mbar_wait(&bar_sempty[ss], ((gc / NSB) & 1) ^ 1, ctx)) return false;
+        if constexpr (C::WIDE) {  // the pair (gc, gc + 1) into both score buffers
+          static_assert(NSB == C::PAIR, "a pair takes every score buffer");
+          if (!mbar_wait(&bar_sempty[0], ((gc / NSB) & 1) ^ 1, ctx)) return false;
+          if (!mbar_wait(&bar_sempty[1], (((gc + 1) / NSB) & 1) ^ 1, ctx)) return false;
           for (int j = 0; j < 2 * C::NDC; ++j) {
             const int rs = rc % C::NRS, dc = j % C::NDC;
             if (!mbar_wait(&bar_rsfull[rs], (rc / C::NRS) & 1, ctx)) return false;
             tc_fence_after();
-            mma_slot<T>(tmem + (j < C::NDC ? C::TM_S : C::TM_DP) + ss * T::CH,
-                        sbase + C::OFF_RS + rs * 2 * kSlotPlaneBytes, dc > 0);
+            mma_slot_rows<T, C::PAIR * T::CH>(tmem + (j < C::NDC ? C::TM_S : C::TM_DP),
+                                              sbase + C::OFF_RS + rs * 2 * C::SLOT_PLANE, dc > 0);
             mma_commit(&bar_rsempty[rs]);
             ++rc;
           }
-          mma_commit(&bar_sfull[ss]);
+          mma_commit(&bar_sfull[0]);
+          mma_commit(&bar_sfull[1]);
           return true;
         }
         const int gq = gc + qoff, qs = gq % NQ, ss = gc % NSB;
@@ -1892,7 +1922,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         return true;
       };
       for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++it) {
-      const int g0 = it * nchunks, q0 = it * (nchunks + C::LAND) + C::LAND;
+      const int g0 = it * nch, q0 = it * (nch + C::LAND) + C::LAND;
       qoff = q0 - g0;
       if constexpr (!C::WIDE)
         if (!(ok = mbar_wait(&bar_kvfull, it & 1, ctx))) break;
@@ -1912,12 +1942,12 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       }
       if (ok) ok = issue_s(g0);
       // every S^T/dP^T MMA of this tile has been issued: the K/V buffers may take the next tile's blocks
-      if (!C::POOL && ok && nchunks == 1) mma_commit(&bar_kvempty);
-      for (int c = 0; c < nchunks && ok; ++c) {
+      if (!C::POOL && ok && nch == 1) mma_commit(&bar_kvempty);
+      for (int c = 0; c < nch && ok; ++c) {
         const int gc = g0 + c;
-        if (NSB == 2 && c + 1 < nchunks) {
+        if (!C::WIDE && NSB == 2 && c + 1 < nch) {
           if (!(ok = issue_s(gc + 1))) break;
-          if (!C::POOL && c + 2 == nchunks) mma_commit(&bar_kvempty);
+          if (!C::POOL && c + 2 == nch) mma_commit(&bar_kvempty);
         }
         const int gq = gc + qoff, qs = gq % NQ, ts = gc % NST;
         if (!(ok = mbar_wait(&bar_tfull[ts], (gc / NST) & 1, ctx))) break;
@@ -1936,9 +1966,10 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         mma_pv<T>(tmem + C::TM_DK, sbase + C::OFF_DS + ts * C::ST_BYTES, qb, c > 0);
         mma_commit(&bar_tempty[ts]);
         mma_commit(&bar_qempty[qs]);
-        if (NSB == 1 && c + 1 < nchunks) {
+        if (C::WIDE && (c & 1) == 0 && c + 2 < nch && !(ok = issue_s(gc + 2))) break;  // the next pair
+        if (NSB == 1 && c + 1 < nch) {
           if (!(ok = issue_s(gc + 1))) break;
-          if (c + 2 == nchunks) mma_commit(&bar_kvempty);
+          if (c + 2 == nch) mma_commit(&bar_kvempty);
         }
       }
       if (ok) mma_commit(&bar_done);
@@ -1963,8 +1994,8 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       ew_sync(T::EWT);
     }
     float gbp[2] = {0.f, 0.f}, ggp[2] = {0.f, 0.f};  // with SDS: this key's d(beta), d(gamma) partials
-    for (int c = 0; c < nchunks; ++c) {
-      const int gc = it * nchunks + c;
+    for (int c = 0; c < nch; ++c) {
+      const int gc = it * nch + c;
       const int ss = gc % NSB, rs = gc % NR, ts = gc % NST;
       if (!ok) continue;
       Prior32<BF16> pr;
@@ -2059,8 +2090,8 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
     if (ok) ok = warp_wait(&bar_done, it & 1, ctx);
     // with SDS the staging tiles are also read by the dS stores: wait for the last ones before the epilogue
     if constexpr (SDS) {
-      for (int k = 0; k < NST && k < nchunks && ok; ++k) {
-        const int g = it * nchunks + nchunks - 1 - k;
+      for (int k = 0; k < NST && k < nch && ok; ++k) {
+        const int g = it * nch + nch - 1 - k;
         ok = warp_wait(&bar_tempty[g % NST], (g / NST) & 1, ctx);
       }
     }
