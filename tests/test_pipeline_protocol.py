@@ -10,7 +10,7 @@ a bounded-wait timeout or as results that differ between runs, so their arithmet
   pair takes NDC ring slots, more than the ring holds, and a lag of NSB - 1 deadlocks (seen on the GPU as expired
   bounded waits); the kernels use NSB - PAIR there;
 * the wide row pass's sweep 2 with chunk pairs: the transposed K chunks for dQ trail the slots by one pair;
-* the wide key pass with two score buffers: a chunk's slots are loaded before its single transposed Q/dO buffer.
+* the wide key pass with query-chunk pairs: a chunk's records load before the next pair's slots.
 """
 import pytest
 
@@ -139,49 +139,55 @@ def test_forward_wide_pairs_deadlock_with_the_unpaired_lag(ndc, nk):
     assert _forward_order(16, ndc, nk, NSB - 1) is not None
 
 
-def _key_pass_wide_order(n, ndc, nrs, nsb, slots_first):
-    """Wide fp32 key pass, one tile: TMA loads per query chunk its 2*ndc head-dim slots (nrs-slot ring) and its
-    transposed Q/dO chunk (one buffer, free once the previous chunk's dV/dK ran); the MMA issues S^T/dP^T of chunk
-    c + 1 before dV/dK of chunk c when it has two score buffers; the element-wise warps release the scores and stage
-    P2^T/dS^T (one buffer). Returns None or the deadlock state."""
-    st = dict(sl=0, sc=0, s_iss=0, s_rel=0, staged=0, dvdk=0, qt=0)
+def _key_pass_wide_order(n, ndc, nrs, records_first):
+    """Wide fp32 key pass, one tile, query chunks in pairs: per chunk the TMA loads its row records (two buffers),
+    before chunk 0 and each odd chunk the slots of the next pair (2*ndc head-dim slots through an nrs-slot ring), then
+    the chunk's transposed Q/dO (one buffer, free once the previous chunk's dV/dK ran). The MMA issues a pair into both
+    score buffers, the next pair after the first chunk's dV/dK. The element-wise warps need a chunk's scores and its
+    records before they free its score buffer, and stage P2^T/dS^T (one buffer). Returns None or the deadlock state."""
+    st = dict(sl=0, sc=0, s_iss=0, s_rel=0, staged=0, dvdk=0, qt=0, rec=0, rec_read=0)
 
     def tma():
+        def slots():
+            for _ in range(2 * ndc):
+                yield lambda: st["sl"] - st["sc"] < nrs
+                st["sl"] += 1
+
         for c in range(n):
-            def slots():
-                for _ in range(2 * ndc):
-                    yield lambda: st["sl"] - st["sc"] < nrs
-                    st["sl"] += 1
+            def records(c=c):
+                yield lambda: st["rec_read"] >= c - 1
+                st["rec"] = c + 1
 
-            def qt(c=c):
-                yield lambda: st["dvdk"] >= c
-                st["qt"] = c + 1
-
-            first, second = (slots, qt) if slots_first else (qt, slots)
-            yield from first()
-            yield from second()
+            if records_first:
+                yield from records()
+            first = 0 if c == 0 else (c + 1 if c % 2 else -1)
+            if 0 <= first < n:
+                yield from slots()
+            yield lambda c=c: st["dvdk"] >= c
+            st["qt"] = c + 1
+            if not records_first:
+                yield from records()
 
     def mma():
-        def issue(c):
-            yield lambda: st["s_rel"] >= c + 1 - nsb
+        def issue(j):
+            yield lambda: st["s_rel"] >= 2 * j
             for _ in range(2 * ndc):
                 yield lambda: st["sl"] > st["sc"]
                 st["sc"] += 1
-            st["s_iss"] = c + 1
+            st["s_iss"] = 2 * j + 2
 
         yield from issue(0)
         for c in range(n):
-            if nsb == 2 and c + 1 < n:
-                yield from issue(c + 1)
             yield lambda c=c: st["staged"] > c and st["qt"] > c
             st["dvdk"] = c + 1
-            if nsb == 1 and c + 1 < n:
-                yield from issue(c + 1)
+            if c % 2 == 0 and c + 2 < n:
+                yield from issue(c // 2 + 1)
 
     def ew():
         for c in range(n):
-            yield lambda c=c: st["s_iss"] > c
+            yield lambda c=c: st["s_iss"] > c and st["rec"] > c
             st["s_rel"] = c + 1
+            st["rec_read"] = c + 1
             yield lambda c=c: st["dvdk"] >= c
             st["staged"] = c + 1
 
@@ -203,13 +209,14 @@ def _key_pass_wide_order(n, ndc, nrs, nsb, slots_first):
 
 
 @pytest.mark.parametrize("ndc", [4, 6], ids=["d128", "d192"])
-@pytest.mark.parametrize("n", [1, 2, 3, 16, 47])
+@pytest.mark.parametrize("n", [2, 4, 10, 48])
 def test_key_pass_wide_order(ndc, n):
-    """Two score buffers need the slots before the single transposed Q/dO buffer (the kernels' order); with that
-    buffer first the look-ahead deadlocks as soon as a tile has two chunks (the planted order is caught)."""
-    assert _key_pass_wide_order(n, ndc, 3, 2, slots_first=True) is None
-    if n >= 2:
-        assert _key_pass_wide_order(n, ndc, 3, 2, slots_first=False) is not None
+    """Records before the slots (the kernels' order); loaded after the transposed Q/dO instead, the element-wise warps
+    cannot free the odd chunk's scores while the TMA waits for the next pair's slots to drain, and the pipeline stops
+    as soon as a tile has two pairs (it did on the GPU; the planted order is caught)."""
+    assert _key_pass_wide_order(n, ndc, 3, records_first=True) is None
+    if n >= 4:
+        assert _key_pass_wide_order(n, ndc, 3, records_first=False) is not None
 
 
 def _rows_wide_pair_order(nch, ndc, nkv, kt_lag_pairs, nds=1):
