@@ -1650,12 +1650,12 @@ struct ColsCfg : Tile<BF16, DP> {
   // pooled: 2 (a 3-deep ring, 8 % faster at C2, gave dK rows of one tile that differed between runs in ~1 run of 4,
   // with the drain and the single staging buffer alike; 2 is bitwise stable)
   static constexpr int NQ = (BF16 && DP <= 128) ? 3 : POOL ? 2 : 1;   // query-chunk (Q, dO) buffers
-  // wide: two buffers let the next chunk's S^T/dP^T run while this chunk's element-wise work and dV/dK wait; its
-  // slots are then loaded before the chunk's single transposed Q/dO buffer, which frees only after the previous dV/dK
+  // wide: the two buffers hold one pair of query chunks (below)
   static constexpr int NSB = ((BF16 && DP <= 128) || POOL || WIDE) ? 2 : 1;  // S^T / dP^T buffers in TMEM
   // wide: the S^T/dP^T MMAs cover pairs of 32-query chunks (the slots carry a head-dim chunk of K or V and of two Q or
-  // dO chunks) into both score buffers; the next pair issues after the first chunk's dV/dK, and a pair's odd chunk
-  // loads its transposed Q/dO after the next pair's slots
+  // dO chunks) into both score buffers; the next pair issues after the first chunk's dV/dK, and each chunk's row
+  // records load before the next pair's slots (the element-wise warps read a chunk's records before they free its
+  // scores, so records queued behind slots that wait for those scores would stop the pipeline)
   static constexpr int PAIR = WIDE ? 2 : 1;
   static constexpr int SLOT_PLANE = kSlotPlaneBytesRows<PAIR * T::CH>;
   static constexpr int LAND = POOL ? NQ : 0;               // ring positions the K/V landing takes per tile
