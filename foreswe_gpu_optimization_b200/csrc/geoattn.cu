@@ -192,8 +192,9 @@ struct Dims {
   int nabg;
 };
 
-// Every data pointer handed to a kernel must be device (or managed) memory: a host pointer would be dereferenced
-// by the GPU. Checked on the host before any launch.
+// Every data pointer handed to a kernel must be memory of the current device (or managed memory): the kernels run
+// on the current device, which would dereference a host pointer or another device's memory. Checked on the host
+// before any launch.
 bool dev_ptr(const void* p) {
   if (!p) return false;
   cudaPointerAttributes a;
@@ -201,7 +202,9 @@ bool dev_ptr(const void* p) {
     cudaGetLastError();  // clear the sticky-free error of an unregistered host pointer
     return false;
   }
-  return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
+  if (a.type == cudaMemoryTypeManaged) return true;
+  int cur = -1;
+  return a.type == cudaMemoryTypeDevice && cudaGetDevice(&cur) == cudaSuccess && a.device == cur;
 }
 
 int check_shape(const GeoAttnShape* s, Dims& d) {
@@ -447,7 +450,8 @@ int geoattn_version(void) { return GEOATTN_VERSION; }
 const char* geoattn_error_string(int code) {
   switch (code) {
     case GEOATTN_OK: return "ok";
-    case GEOATTN_ERR_INVALID: return "invalid argument (null pointer, non-positive size or unknown enum)";
+    case GEOATTN_ERR_INVALID:
+      return "invalid argument (null, host or other-device pointer, non-positive size or unknown enum)";
     case GEOATTN_ERR_UNSUPPORTED: return "unsupported shape/dtype (head_dim <= 192)";
     case GEOATTN_ERR_ALIGNMENT: return "tensor not TMA-compatible (head dim must be contiguous, base and strides 16-byte aligned)";
     case GEOATTN_ERR_TMA: return "TMA descriptor encoding failed";

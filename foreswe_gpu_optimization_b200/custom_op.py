@@ -68,7 +68,8 @@ def geo_attention_op(q, k, v, prior, alpha, beta, gamma):
     if beta.numel() != n or gamma.numel() != n or n not in (1, H):
         raise ValueError("alpha, beta, gamma must all have 1 or H entries")
     per_head = int(n == H and H > 1)
-    abg = torch.cat([alpha.reshape(-1), beta.reshape(-1), gamma.reshape(-1)]).to(torch.float32)
+    abg = torch.cat([alpha.reshape(-1), beta.reshape(-1), gamma.reshape(-1)]).to(device=q.device,
+                                                                                 dtype=torch.float32)
     o, _ = geoattn_fwd(q, k, v, prior, abg, per_head)
     return o
 

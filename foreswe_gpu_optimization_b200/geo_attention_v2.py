@@ -106,6 +106,13 @@ def _abg(alpha, beta, gamma, H, device):
     return abg.contiguous(), per_head
 
 
+def _same_device(q, **others):
+    """Every tensor a launch reads or writes lives on q's device (the kernels dereference them there)."""
+    for name, t in others.items():
+        if t.device != q.device:
+            raise ValueError("%s lives on %s, q on %s" % (name, t.device, q.device))
+
+
 def _shape(q, per_head):
     B, H, N, D = q.shape
     return _lib.Shape(B, H, N, D, _lib.DTYPE_BF16 if q.dtype == torch.bfloat16 else _lib.DTYPE_FP32, per_head)
@@ -119,10 +126,14 @@ def _forward(q, k, v, prior, abg, per_head):
         raise TypeError("q, k, v must all be bf16 or all be fp32")
     if not q.is_cuda:
         raise RuntimeError("geo attention runs on CUDA tensors only (no CPU path)")
-    if prior.device != q.device:
-        raise ValueError("the geo prior lives on %s, q on %s" % (prior.device, q.device))
+    _same_device(q, k=k, v=v, prior=prior, abg=abg)
     if q.numel() == 0:  # an empty batch, head or station set: nothing to launch
         return torch.empty_like(q), torch.empty(0, dtype=torch.float32, device=q.device)
+    with torch.cuda.device(q.device):  # the library launches on the current device's stream
+        return _forward_launch(q, k, v, prior, abg, per_head)
+
+
+def _forward_launch(q, k, v, prior, abg, per_head):
     q, k, v = _tma_ready(q), _tma_ready(k), _tma_ready(v)
     sh = _shape(q, per_head)
     L = _lib.lib()
@@ -148,6 +159,13 @@ def _backward(q, k, v, o, do, prior, abg, stats, per_head):
     if q.numel() == 0:  # empty input: empty gradients, and the bias-parameter gradients are empty sums
         return (torch.empty_like(q), torch.empty_like(k), torch.empty_like(v),
                 torch.zeros(3 * (H if per_head else 1), dtype=torch.float32, device=q.device))
+    _same_device(q, k=k, v=v, o=o, do=do, prior=prior, abg=abg, stats=stats)
+    with torch.cuda.device(q.device):
+        return _backward_launch(q, k, v, o, do, prior, abg, stats, per_head)
+
+
+def _backward_launch(q, k, v, o, do, prior, abg, stats, per_head):
+    H = q.shape[1]
     q, k, v = _tma_ready(q), _tma_ready(k), _tma_ready(v)
     do = _tma_ready(do.to(q.dtype))
     sh = _shape(q, per_head)
@@ -180,7 +198,7 @@ class FusedGeoAttentionV2(torch.autograd.Function):
         o, stats = _forward(q, k, v, prior, abg, per_head)
         ctx.save_for_backward(q, k, v, o, prior, abg, stats)
         ctx.per_head = per_head
-        ctx.abg_meta = [(t.shape, t.dtype) for t in (alpha, beta, gamma)]
+        ctx.abg_meta = [(t.shape, t.dtype, t.device) for t in (alpha, beta, gamma)]
         return o
 
     @staticmethod
@@ -189,8 +207,8 @@ class FusedGeoAttentionV2(torch.autograd.Function):
         dq, dk, dv, dabg = _backward(q, k, v, o, do, prior, abg, stats, ctx.per_head)
         nabg = q.shape[1] if ctx.per_head else 1
         grads = []
-        for i, (shape, dtype) in enumerate(ctx.abg_meta):
-            grads.append(dabg[i * nabg:(i + 1) * nabg].reshape(shape).to(dtype))
+        for i, (shape, dtype, device) in enumerate(ctx.abg_meta):  # each gradient on its parameter's device
+            grads.append(dabg[i * nabg:(i + 1) * nabg].reshape(shape).to(device=device, dtype=dtype))
         return dq, dk, dv, None, grads[0], grads[1], grads[2]
 
 

@@ -28,14 +28,19 @@ def _stream():
 def prior_from_dense(dist, ang, dtype):
     """Prior table from dense [N, N] distance (km) / angle (deg) matrices, the reference's call signature."""
     n = dist.shape[-1]
+    if dist.shape != (n, n) or ang.shape != (n, n):
+        raise ValueError("dist and ang must be [N, N], got %s and %s" % (tuple(dist.shape), tuple(ang.shape)))
+    if not dist.is_cuda or ang.device != dist.device:
+        raise ValueError("dist and ang must be on one CUDA device, got %s and %s" % (dist.device, ang.device))
     dist = dist.detach().float().contiguous()
     ang = ang.detach().float().contiguous()
     sh = _shape(n, dtype)
     L = _lib.lib()
-    prior = torch.empty(L.geoattn_prior_bytes(ctypes.byref(sh)), dtype=torch.uint8, device=dist.device)
-    _lib.check(L.geoattn_prior_from_dense(ctypes.byref(sh), ctypes.c_void_p(dist.data_ptr()), n,
-                                          ctypes.c_void_p(ang.data_ptr()), n, ctypes.c_void_p(prior.data_ptr()),
-                                          _stream()))
+    with torch.cuda.device(dist.device):  # the library launches on the current device's stream
+        prior = torch.empty(L.geoattn_prior_bytes(ctypes.byref(sh)), dtype=torch.uint8, device=dist.device)
+        _lib.check(L.geoattn_prior_from_dense(ctypes.byref(sh), ctypes.c_void_p(dist.data_ptr()), n,
+                                              ctypes.c_void_p(ang.data_ptr()), n, ctypes.c_void_p(prior.data_ptr()),
+                                              _stream()))
     return prior
 
 
@@ -67,11 +72,12 @@ class StationGeometry:
         if key not in self._prior:
             sh = _shape(self.n, key)
             L = _lib.lib()
-            t = torch.empty(L.geoattn_prior_bytes(ctypes.byref(sh)), dtype=torch.uint8, device=self.device)
-            _lib.check(L.geoattn_prior_from_coords(ctypes.byref(sh), ctypes.c_void_p(self.lat.data_ptr()),
-                                                   ctypes.c_void_p(self.lon.data_ptr()),
-                                                   ctypes.c_void_p(self.elev_ft.data_ptr()),
-                                                   ctypes.c_void_p(t.data_ptr()), None, None, _stream()))
+            with torch.cuda.device(self.device):
+                t = torch.empty(L.geoattn_prior_bytes(ctypes.byref(sh)), dtype=torch.uint8, device=self.device)
+                _lib.check(L.geoattn_prior_from_coords(ctypes.byref(sh), ctypes.c_void_p(self.lat.data_ptr()),
+                                                       ctypes.c_void_p(self.lon.data_ptr()),
+                                                       ctypes.c_void_p(self.elev_ft.data_ptr()),
+                                                       ctypes.c_void_p(t.data_ptr()), None, None, _stream()))
             self._prior[key] = t
         return self._prior[key]
 
@@ -81,8 +87,9 @@ class StationGeometry:
         sh = _shape(self.n, torch.float32)
         dist = torch.empty(self.n, self.n, dtype=torch.float32, device=self.device)
         ang = torch.empty_like(dist)
-        _lib.check(_lib.lib().geoattn_prior_from_coords(
-            ctypes.byref(sh), ctypes.c_void_p(self.lat.data_ptr()), ctypes.c_void_p(self.lon.data_ptr()),
-            ctypes.c_void_p(self.elev_ft.data_ptr()), None, ctypes.c_void_p(dist.data_ptr()),
-            ctypes.c_void_p(ang.data_ptr()), _stream()))
+        with torch.cuda.device(self.device):
+            _lib.check(_lib.lib().geoattn_prior_from_coords(
+                ctypes.byref(sh), ctypes.c_void_p(self.lat.data_ptr()), ctypes.c_void_p(self.lon.data_ptr()),
+                ctypes.c_void_p(self.elev_ft.data_ptr()), None, ctypes.c_void_p(dist.data_ptr()),
+                ctypes.c_void_p(ang.data_ptr()), _stream()))
         return dist, ang

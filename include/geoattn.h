@@ -10,7 +10,8 @@
  * A Python (ctypes) binding of every entry point below lives in
  * foreswe_gpu_optimization_b200/_lib.py; INTEGRATION.md shows it.
  *
- * Conventions: all data pointers are device pointers; tensors are [B, H, N, D] with element strides; the
+ * Conventions: all data pointers are memory of the current device (cudaGetDevice) or managed memory, and
+ * `stream` belongs to that device; tensors are [B, H, N, D] with element strides; the
  * library never allocates or frees device memory (callers pass outputs and workspaces sized by the *_bytes
  * functions); every call is asynchronous on `stream` (a cudaStream_t, NULL = legacy default stream), performs no
  * host synchronisation and is safe to capture in a CUDA graph. Every entry point returns a GEOATTN_* status code.
@@ -28,7 +29,7 @@ extern "C" {
 
 enum {
   GEOATTN_OK = 0,
-  GEOATTN_ERR_INVALID = 1,     /* null or non-device pointer, non-positive size, bad enum */
+  GEOATTN_ERR_INVALID = 1,     /* null, host or other-device pointer, non-positive size, bad enum */
   GEOATTN_ERR_UNSUPPORTED = 2, /* head_dim / dtype combination without a kernel */
   GEOATTN_ERR_ALIGNMENT = 3,   /* tensor base or stride not 16-byte aligned, or head dim not contiguous */
   GEOATTN_ERR_TMA = 4,         /* TMA descriptor encoding failed */

@@ -50,3 +50,19 @@ def test_patch_model_validates_before_patching():
     assert "scaled_dot_product_attention" not in m.encoder_layers[0].self_attn.__dict__
     g.patch_model(m, precision="bf16")
     assert callable(m.encoder_layers[0].self_attn.__dict__["scaled_dot_product_attention"])
+
+
+def test_dense_prior_arguments_checked_before_any_launch():
+    """dist / ang must be [N, N] on one CUDA device (the reference's kernels read them with two strides)."""
+    with pytest.raises(ValueError, match=r"\[N, N\]"):
+        g.prior_from_dense(torch.zeros(1, 8, 8), torch.zeros(1, 8, 8), torch.float32)
+    with pytest.raises(ValueError, match="CUDA"):
+        g.prior_from_dense(torch.zeros(8, 8), torch.zeros(8, 8), torch.float32)
+
+
+def test_tensors_on_other_devices_rejected():
+    """Every tensor a launch reads or writes must live on q's device; the check names the first one that does not."""
+    q = torch.zeros(1, 1, 4, 8)
+    gv2._same_device(q, k=torch.zeros(1, 1, 4, 8), abg=torch.zeros(3))
+    with pytest.raises(ValueError, match="abg lives on meta"):
+        gv2._same_device(q, k=torch.zeros(1, 1, 4, 8), abg=torch.zeros(3, device="meta"))

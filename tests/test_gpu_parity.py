@@ -378,3 +378,32 @@ def test_status_word_clean_and_errors_raise(ops):
                        ctypes.c_void_p(o.data_ptr()), _lib.c_ll4(*o.stride()), ctypes.c_void_p(stats.data_ptr()),
                        ctypes.c_void_p(ws.data_ptr()))
     assert L.geoattn_fwd(ctypes.byref(bad), None) == 1
+
+
+def test_inputs_on_another_device_rejected(ops):
+    """k on the host while q is on the GPU raises before any launch (the kernels would dereference it on q's
+    device)."""
+    q = torch.randn(1, 2, 64, 64, device="cuda")
+    d = torch.zeros(64, 64, device="cuda")
+    a = torch.ones(1, device="cuda")
+    with pytest.raises(ValueError, match="k lives on cpu"):
+        ops.fused_geo_attention_v2(q, q.cpu(), q, d, d, a, a, a)
+
+
+def test_host_bias_parameters_get_host_gradients(ops):
+    """alpha, beta, gamma kept on the host (q, k, v on the GPU) get their gradients on the host, equal to the
+    gradients of the same parameters on the GPU."""
+    B, H, N, D = 1, 2, 96, 64
+    q, k, v, a, b, c, do = attn_inputs(B, H, N, D, seed=21, per_head=True)
+    dist, ang = dense_geometry(*stations(N, 22))
+    dist, ang = dist.cuda(), ang.cuda()
+    grads = {}
+    for where in ("cpu", "cuda"):
+        x = [t.cuda().requires_grad_(True) for t in (q, k, v)]
+        p = [t.to(where).requires_grad_(True) for t in (a, b, c)]
+        o = ops.fused_geo_attention_v2(*x, dist, ang, *p)
+        o.backward(do.cuda())
+        assert all(t.grad.device.type == where for t in p)
+        grads[where] = [t.grad.cpu() for t in p]
+    for g_host, g_dev in zip(grads["cpu"], grads["cuda"]):
+        assert torch.equal(g_host, g_dev)
