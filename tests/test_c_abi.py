@@ -32,9 +32,11 @@ def test_every_declared_symbol_is_exported(L):
 
 def test_version_and_error_strings(L):
     assert L.geoattn_version() == 2
-    for code in range(7):
-        assert L.geoattn_error_string(code)
-    assert b"unknown" in L.geoattn_error_string(99)
+    unknown = L.geoattn_error_string(99)
+    assert b"unknown" in unknown
+    msgs = [L.geoattn_error_string(code) for code in range(8)]  # GEOATTN_OK .. GEOATTN_ERR_SCRATCH
+    assert all(msgs) and unknown not in msgs and len(set(msgs)) == 8
+    assert b"other-device" in msgs[1]
 
 
 def test_size_queries_without_gpu(L):
