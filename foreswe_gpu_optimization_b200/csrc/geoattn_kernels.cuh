@@ -430,23 +430,9 @@ __device__ __forceinline__ void tma_tile(uint8_t* dst, const CUtensorMap* map, u
       tma_load_4d(dst + (size_t)(pl * T::NKB + kb) * nrows * 128, map, bar, kb * T::KB, row0, h, b + pl * B);
 }
 // fp32 head dims above 64 ("wide"): the score-shaped products stream their operands through a ring of slots, each
-// holding one 32-wide head-dim chunk dc of a 128-row A tile and of a CH-row B chunk, hi and lo planes:
-// [plane 0: A (128 x 128 B) | B (CH x 128 B)][plane 1: A | B]. The MMA accumulates the chunks' products.
-constexpr int kSlotPlaneBytes = (kBM + 32) * 128;
-template <class T>
-__device__ __forceinline__ void tma_slot(uint8_t* slot, uint64_t* bar, const CUtensorMap* amap, int arow0,
-                                         const CUtensorMap* bmap, int brow0, int dc, int h, int b, int B) {
-  for (int pl = 0; pl < 2; ++pl) {
-    tma_load_4d(slot + pl * kSlotPlaneBytes, amap, bar, dc * T::KB, arow0, h, b + pl * B);
-    tma_load_4d(slot + pl * kSlotPlaneBytes + kBM * 128, bmap, bar, dc * T::KB, brow0, h, b + pl * B);
-  }
-}
-template <class T>
-__device__ __forceinline__ void mma_slot(uint32_t tmem_acc, uint32_t slot, bool accumulate) {
-  static_assert(!T::kBF16 && T::CH == 32, "slots carry fp32 planes with 32-row B chunks");
-  mma_qk<T, T::CH, T::KB>(tmem_acc, slot, kSlotPlaneBytes, slot + kBM * 128, kSlotPlaneBytes, accumulate);
-}
-// Slots whose B part holds BROWS rows (consecutive 32-row chunks; the wide forward's chunk pairs use 64).
+// holding one 32-wide head-dim chunk dc of a 128-row A tile and of a BROWS-row B part (BROWS / 32 consecutive 32-row
+// chunks: the wide kernels issue their score MMAs over chunk pairs, BROWS = 64), hi and lo planes:
+// [plane 0: A (128 x 128 B) | B (BROWS x 128 B)][plane 1: A | B]. The MMA accumulates the head-dim chunks' products.
 template <int BROWS>
 constexpr int kSlotPlaneBytesRows = (kBM + BROWS) * 128;
 template <class T, int BROWS>
