@@ -16,7 +16,7 @@ DTYPE_BF16, DTYPE_FP32 = 0, 1
 EXPORTED = ("geoattn_version", "geoattn_error_string", "geoattn_prior_bytes", "geoattn_prior_from_dense",
             "geoattn_prior_from_coords", "geoattn_stats_bytes", "geoattn_fwd_workspace_bytes",
             "geoattn_bwd_workspace_bytes", "geoattn_fwd", "geoattn_bwd", "geoattn_bwd_noalloc",
-            "geoattn_read_status")
+            "geoattn_read_status", "geoattn_wait_selftest")
 
 c_ll4 = ctypes.c_longlong * 4
 
@@ -84,6 +84,8 @@ def lib():
         L.geoattn_bwd_noalloc.argtypes = [ctypes.POINTER(BwdArgs), ctypes.c_void_p]
         L.geoattn_read_status.restype = ctypes.c_int
         L.geoattn_read_status.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int), ctypes.c_void_p]
+        L.geoattn_wait_selftest.restype = ctypes.c_int
+        L.geoattn_wait_selftest.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
         if L.geoattn_version() != ABI_VERSION:  # argument structs of another layout: refuse before any call
             raise RuntimeError("%s has ABI version %d, this binding expects %d; rebuild it"
                                % (LIB_PATH, L.geoattn_version(), ABI_VERSION))

@@ -179,6 +179,21 @@ __global__ void finalize_abg_kernel(const double* __restrict__ part, int B, int 
 }
 
 // ---------------------------------------------------------------------------------------------------------------
+// Self-test of the bounded waits every attention kernel uses: one thread waits for the first phase of an mbarrier
+// that nothing arrives on. The wait gives up after its limit, records the timeout in the status word (first error
+// wins) and the kernel returns, leaving the context usable.
+// ---------------------------------------------------------------------------------------------------------------
+__global__ void wait_selftest_kernel(int* status) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  abort_flag = 0;
+  mbar_init(&bar, 1);
+  fence_barrier_init();
+  const WaitCtx ctx{&abort_flag, status};
+  (void)mbar_wait(&bar, 0, ctx);
+}
+
+// ---------------------------------------------------------------------------------------------------------------
 // Host helpers
 // ---------------------------------------------------------------------------------------------------------------
 namespace {
@@ -656,6 +671,14 @@ int backward(const GeoAttnBwdArgs* a, void* stream, bool with_ds) {
 extern "C" {
 
 int geoattn_bwd(const GeoAttnBwdArgs* a, void* stream) { return backward(a, stream, true); }
+
+int geoattn_wait_selftest(void* status_word, void* stream) {
+  if (!dev_ptr(status_word) || (reinterpret_cast<uintptr_t>(status_word) & 3) != 0) return GEOATTN_ERR_INVALID;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(status_word, 0, sizeof(int), st) != cudaSuccess) return GEOATTN_ERR_LAUNCH;
+  wait_selftest_kernel<<<1, 1, 0, st>>>(reinterpret_cast<int*>(status_word));
+  return cudaGetLastError() == cudaSuccess ? GEOATTN_OK : GEOATTN_ERR_LAUNCH;
+}
 
 int geoattn_read_status(const void* workspace, int* status, void* stream) {
   if (!dev_ptr(workspace) || !status) return GEOATTN_ERR_INVALID;

@@ -140,6 +140,11 @@ int geoattn_bwd_noalloc(const GeoAttnBwdArgs* args, void* stream);
  * memory misaligned and did nothing) to *status. Synchronises
  * the stream; for tests and debugging only. */
 int geoattn_read_status(const void* workspace, int* status, void* stream);
+/* Self-test of the kernels' bounded waits: launches one thread that waits on a barrier nothing completes. After the
+ * wait limit (about 2 s) the wait gives up, the kernel sets the 4-byte device word `status_word` to 1 (as a timed-out
+ * attention kernel sets its workspace's status word) and returns; the context stays usable. Asynchronous on
+ * `stream`; for tests only. */
+int geoattn_wait_selftest(void* status_word, void* stream);
 const char* geoattn_error_string(int code);
 int geoattn_version(void);
 

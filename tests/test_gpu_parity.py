@@ -407,3 +407,29 @@ def test_host_bias_parameters_get_host_gradients(ops):
         grads[where] = [t.grad.cpu() for t in p]
     for g_host, g_dev in zip(grads["cpu"], grads["cuda"]):
         assert torch.equal(g_host, g_dev)
+
+
+def test_bounded_wait_expires_into_the_status_word(ops):
+    """A wait that nothing completes gives up after its limit (about 2 s): the kernel records the timeout in the
+    status word and returns, and the context keeps working (an attention call right after matches the oracle)."""
+    import ctypes
+    import time
+    from foreswe_gpu_optimization_b200 import _lib
+    L = _lib.lib()
+    word = torch.full((4,), -1, dtype=torch.int32, device="cuda")
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    assert L.geoattn_wait_selftest(None, stream) == 1                                   # no word: rejected
+    assert L.geoattn_wait_selftest(ctypes.c_void_p(word.data_ptr() + 2), stream) == 1   # misaligned: rejected
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    _lib.check(L.geoattn_wait_selftest(ctypes.c_void_p(word.data_ptr()), stream))
+    torch.cuda.synchronize()
+    waited = time.perf_counter() - t0
+    assert word[0].item() == 1, "the expired wait records status 1"
+    assert 1.5 < waited < 60, waited
+    B, H, N, D = 1, 2, 96, 64
+    q, k, v, a, b, c, do = attn_inputs(B, H, N, D, seed=31)
+    dist, ang = dense_geometry(*stations(N, 32))
+    res = run_device(lambda *x: ops.fused_geo_attention_v2(x[0], x[1], x[2], dist.cuda(), ang.cuda(), *x[3:]),
+                     q, k, v, a, b, c, do)
+    _check(res, _oracle(q, k, v, dist, ang, a, b, c, do), TOL[torch.float32], "after an expired wait")
