@@ -433,3 +433,50 @@ def test_bounded_wait_expires_into_the_status_word(ops):
     res = run_device(lambda *x: ops.fused_geo_attention_v2(x[0], x[1], x[2], dist.cuda(), ang.cuda(), *x[3:]),
                      q, k, v, a, b, c, do)
     _check(res, _oracle(q, k, v, dist, ang, a, b, c, do), TOL[torch.float32], "after an expired wait")
+
+
+def _rel_dev(x, ref):
+    """rel-L2 of x against ref, in float64 on the device (full-size tensors stay off the host)."""
+    x, ref = x.double(), ref.double()
+    return ((x - ref).norm() / ref.norm()).item()
+
+
+def test_full_size_bf16_step_properties(ops):
+    """The benchmarked workload at full size (256 issue dates x 16 heads x 512 stations x D = 128, bf16, per-head
+    parameters, coordinate prior; ~110 tiles per persistent CTA), checked through properties that hold at any size:
+      * O is linear in V and the backward is linear in dO; doubling scales every intermediate exactly in binary
+        floating point, so O(2V) = 2 O(V) and grads(2 dO) = 2 grads(dO) (rel-L2 1e-4);
+      * P2's rows sum to one, so sum_k dV[k] = sum_q dO[q] (rel-L2 2e-3; bf16 rounding of P2 and dV, ~1e-4 expected);
+      * dS's rows sum to zero (softmax backward), so sum_k dK[k] = 0 (2e-3 of sum_k |dK[k]|; ~1e-4 expected);
+      * a repeated backward is bitwise equal (every CTA runs many tiles, so a buffer handed back too early between
+        tiles shows up here)."""
+    B, H, N, D = 256, 16, 512, 128
+    g = torch.Generator(device="cuda").manual_seed(40)
+    s = D ** -0.25
+    q, k, v = (torch.randn(B, H, N, D, device="cuda", generator=g).mul_(s).to(torch.bfloat16).requires_grad_(True)
+               for _ in range(3))
+    do = torch.randn(B, H, N, D, device="cuda", generator=g).to(torch.bfloat16)
+    a = (torch.rand(H, device="cuda", generator=g) * 0.9 + 0.1).requires_grad_(True)
+    b = (torch.randn(H, device="cuda", generator=g) * 0.5).requires_grad_(True)
+    c = (torch.randn(H, device="cuda", generator=g) * 0.5).requires_grad_(True)
+    geom = ops.StationGeometry(*stations(N, 41))
+    o = ops.geo_attention(q, k, v, geom, a, b, c)
+    assert torch.isfinite(o.float()).all()
+    with torch.no_grad():
+        o2v = ops.geo_attention(q, k, v * 2, geom, a, b, c)
+    assert _rel_dev(o2v, 2 * o.detach()) <= 1e-4
+    del o2v
+    ins = (q, k, v, a, b, c)
+    g1 = torch.autograd.grad(o, ins, do, retain_graph=True)
+    g1b = torch.autograd.grad(o, ins, do, retain_graph=True)
+    for name, x, y in zip(("dq", "dk", "dv", "dalpha", "dbeta", "dgamma"), g1, g1b):
+        assert torch.equal(x, y), name
+    del g1b
+    g2 = torch.autograd.grad(o, ins, do * 2)
+    for name, x, y in zip(("dq", "dk", "dv", "dalpha", "dbeta", "dgamma"), g1, g2):
+        assert torch.isfinite(x.float()).all(), name
+        assert _rel_dev(y, 2 * x) <= 1e-4, name
+    del g2
+    dk, dv = g1[1].double(), g1[2].double()
+    assert _rel_dev(dv.sum(dim=2), do.double().sum(dim=2)) <= 2e-3
+    assert (dk.sum(dim=2).norm() / dk.abs().sum(dim=2).norm()).item() <= 2e-3
