@@ -441,21 +441,24 @@ def _rel_dev(x, ref):
     return ((x - ref).norm() / ref.norm()).item()
 
 
-def test_full_size_bf16_step_properties(ops):
-    """The benchmarked workload at full size (256 issue dates x 16 heads x 512 stations x D = 128, bf16, per-head
-    parameters, coordinate prior; ~110 tiles per persistent CTA), checked through properties that hold at any size:
+@pytest.mark.parametrize("dtype,B,H,D", [(torch.bfloat16, 256, 16, 128), (torch.float32, 32, 8, 64)],
+                         ids=["bf16-256x16x512x128", "tf32-32x8x512x64"])
+def test_full_size_step_properties(ops, dtype, B, H, D):
+    """Full-size workloads -- the benchmarked one (256 issue dates x 16 heads x 512 stations x D = 128, bf16; ~110
+    tiles per persistent CTA) and the TF32 one (32 x 8 x 512 x 64; ~7 tiles per CTA) -- with per-head parameters
+    and the coordinate prior, checked through properties that hold at any size:
       * O is linear in V and the backward is linear in dO; doubling scales every intermediate exactly in binary
-        floating point, so O(2V) = 2 O(V) and grads(2 dO) = 2 grads(dO) (rel-L2 1e-4);
-      * P2's rows sum to one, so sum_k dV[k] = sum_q dO[q] (rel-L2 2e-3; bf16 rounding of P2 and dV, ~1e-4 expected);
+        floating point (TF32 hi/lo splits included), so O(2V) = 2 O(V) and grads(2 dO) = 2 grads(dO) (rel-L2 1e-4);
+      * P2's rows sum to one, so sum_k dV[k] = sum_q dO[q] (rel-L2 2e-3; rounding of P2 and dV, ~1e-4 expected);
       * dS's rows sum to zero (softmax backward), so sum_k dK[k] = 0 (2e-3 of sum_k |dK[k]|; ~1e-4 expected);
-      * a repeated backward is bitwise equal (every CTA runs many tiles, so a buffer handed back too early between
+      * a repeated backward is bitwise equal (every CTA runs several tiles, so a buffer handed back too early between
         tiles shows up here)."""
-    B, H, N, D = 256, 16, 512, 128
+    N = 512
     g = torch.Generator(device="cuda").manual_seed(40)
     s = D ** -0.25
-    q, k, v = (torch.randn(B, H, N, D, device="cuda", generator=g).mul_(s).to(torch.bfloat16).requires_grad_(True)
+    q, k, v = (torch.randn(B, H, N, D, device="cuda", generator=g).mul_(s).to(dtype).requires_grad_(True)
                for _ in range(3))
-    do = torch.randn(B, H, N, D, device="cuda", generator=g).to(torch.bfloat16)
+    do = torch.randn(B, H, N, D, device="cuda", generator=g).to(dtype)
     a = (torch.rand(H, device="cuda", generator=g) * 0.9 + 0.1).requires_grad_(True)
     b = (torch.randn(H, device="cuda", generator=g) * 0.5).requires_grad_(True)
     c = (torch.randn(H, device="cuda", generator=g) * 0.5).requires_grad_(True)
