@@ -58,13 +58,15 @@ def _per_head(x, H):
 
 
 def grads(q, k, v, dist, ang, alpha, beta, gamma, do, path, score_terms=3, dp_terms=None, prior_fp16=None,
-          dalpha_form=None):
+          dalpha_form=None, row_sums="tiles"):
     """Output and gradients (dict keyed like the oracle's grads) of the kernels' formulation on the CPU.
 
     path: "bf16" or "tf32". score_terms: TF32 terms of QK^T and (unless dp_terms says otherwise) dO V^T, 3 as in
     the kernels or 1 (a cheaper variant, for comparison).
     prior_fp16: store the prior as fp16 (default: the path's choice, True for bf16). dalpha_form: "a-d2b" or
-    "dz" (default: the path's choice)."""
+    "dz" (default: the path's choice). row_sums: "tiles" (the kernels: delta2 and a from the recomputed tiles) or
+    "output" (a variant without the BF16 row pass's sweep: delta2 = rowsum(dO O) from the stored output and
+    a = rowsum(dO O') with O' = (P2 P1) V accumulated by the forward, both stored in the output dtype)."""
     bf = path == "bf16"
     prior_fp16 = bf if prior_fp16 is None else prior_fp16
     dalpha_form = ("a-d2b" if bf else "dz") if dalpha_form is None else dalpha_form
@@ -99,8 +101,13 @@ def grads(q, k, v, dist, ang, alpha, beta, gamma, do, path, score_terms=3, dp_te
     # backward (P1, P2 recomputed from the row statistics)
     p2 = torch.exp2(zl - c2)
     dpm = matmul(do, v.transpose(-1, -2), dp_kind)
-    delta2 = (p2 * dpm).sum(-1, keepdim=True)
-    ra = (p2 * dpm * p1).sum(-1, keepdim=True)
+    if row_sums == "tiles":
+        delta2 = (p2 * dpm).sum(-1, keepdim=True)
+        ra = (p2 * dpm * p1).sum(-1, keepdim=True)
+    else:
+        store = _bf16 if bf else (lambda x: x)
+        delta2 = (do * store(o)).sum(-1, keepdim=True)
+        ra = (do * store(matmul(p2 * p1, v, prod_kind))).sum(-1, keepdim=True)
     rb = (p2 * p1).sum(-1, keepdim=True)
     delta1 = a * (ra - delta2 * rb)
     dz = p2 * (dpm - delta2)

@@ -7,6 +7,7 @@ second softmax, the row-record backward) with the kernels' rounding points. Agai
   and with x30 logits, at head dims 64 and 192, and the reference's 10x-eager rule in its six regimes at D = 192;
 * one TF32 term for the score-shaped products (QK^T, dO V^T) breaks the 5e-4 bound at x30 logits, and one term for
   dO V^T alone breaks it for the bias-parameter gradients; three terms hold it -- why the kernels issue three;
+* the BF16 backward's row sums (delta2, a) come from the recomputed tiles, not from the stored output;
 * storing the prior as fp16 pairs (BF16 path) leaves O, dQ, dK, dV where they were and costs d(gamma) ~3e-4;
 * d(alpha) from the explicit dZ, sum dZ (P1 - b), as the TF32 row pass computes it, is orders of magnitude closer
   than a - delta2 b where the true d(alpha) is ~0 (the reference's `uniform` regime, Q = 0).
@@ -74,6 +75,22 @@ def test_one_tf32_term_for_dO_Vt_breaks_the_bias_gradients(case):
     bias = ("dalpha", "dbeta", "dgamma")
     assert max(one[key] for key in bias) > TOL[torch.float32], one
     assert max(three[key] for key in bias) <= 0.2 * TOL[torch.float32], three
+
+
+@pytest.mark.parametrize("case", ["near_one_hot", "wide_signed", "large_alpha"])
+def test_bf16_row_sums_come_from_the_tiles(case):
+    """delta1 = alpha (a - delta2 b) is a difference of nearly equal sums in saturated rows, so a, delta2 and b must
+    come from the same bf16-rounded tiles as dZ: taken from the stored output instead (delta2 = dO . O,
+    a = dO . O'), the variant that would drop the BF16 row pass's sweep leaves dQ and dK off by several 1e-2."""
+    x = acceptance.case_inputs(case, B=1, H=2, N=100, D=192)
+    do = acceptance.grad_seed_do(x[0].shape)
+    x = [t.to(torch.bfloat16).float() if i < 3 else t for i, t in enumerate(x)]
+    do = do.to(torch.bfloat16).float()
+    ref = oga.grads(*x, do)
+    tiles = _rels(nm.grads(*x, do, path="bf16"), ref)
+    output = _rels(nm.grads(*x, do, path="bf16", row_sums="output"), ref)
+    assert max(tiles.values()) <= TOL[torch.bfloat16], tiles
+    assert min(output["dQ"], output["dK"]) > 2 * TOL[torch.bfloat16], output
 
 
 def test_fp16_prior_pairs_cost_little():
