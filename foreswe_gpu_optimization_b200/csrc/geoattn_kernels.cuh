@@ -1690,6 +1690,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
   using T = typename C::T;
   constexpr int NQ = C::NQ, NSB = C::NSB, NR = C::NR, NST = C::NST, NPR = C::NPR;
   constexpr int SLAG = NQ > 1 ? NQ - 1 : 1;  // chunks by which the dS stores trail the query-chunk loads
+  static_assert(!SDS || SLAG <= NQ + NST - 1, "dS stores lagging further would wait on loads that wait on them");
   if (smem_misaligned(p.status)) return;  // uniform over the CTA, before any barrier or allocation
   uint8_t* smem = smem_raw;
   __shared__ uint64_t bar_kvfull, bar_kvempty, bar_qfull[3], bar_qempty[3], bar_sfull[2], bar_sempty[2], bar_tfull[2],
@@ -1836,8 +1837,10 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         }
         if constexpr (!C::WIDE)
           if (!(ok = load_records())) break;
-        // the dS stores trail the loads by LAG chunks, so a store's wait for its tile never holds back the loads
-        // the MMAs need next (LAG < NQ keeps the dependency chain acyclic)
+        // the dS stores trail the loads by SLAG chunks, so a store's wait for its tile never holds back the loads
+        // the MMAs need next. The load of chunk c waits for the dV/dK of chunk c - NQ, which waits for its staging,
+        // which waits for the store of chunk c - NQ - NST; by chunk c this loop has stored chunk c - 1 - SLAG, so
+        // SLAG <= NQ + NST - 1 keeps the chain acyclic
         if constexpr (SDS)
           if (c >= SLAG && !(ok = store_ds(gc - SLAG, c - SLAG))) break;
       }

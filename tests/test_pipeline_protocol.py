@@ -10,7 +10,8 @@ a bounded-wait timeout or as results that differ between runs, so their arithmet
   pair takes NDC ring slots, more than the ring holds, and a lag of NSB - 1 deadlocks (seen on the GPU as expired
   bounded waits); the kernels use NSB - PAIR there;
 * the wide row pass's sweep 2 with chunk pairs: the transposed K chunks for dQ trail the slots by one pair;
-* the wide key pass with query-chunk pairs: a chunk's records load before the next pair's slots.
+* the wide key pass with query-chunk pairs: a chunk's records load before the next pair's slots;
+* the BF16 key pass's dS^T scratch stores trail the query-chunk loads by at most NQ + NST - 1 chunks.
 """
 import pytest
 
@@ -298,3 +299,119 @@ def test_rows_wide_pair_order(ndc, nch):
     assert _rows_wide_pair_order(nch, ndc, 3, kt_lag_pairs=1) is None
     if nch >= 4:
         assert _rows_wide_pair_order(nch, ndc, 3, kt_lag_pairs=0) is not None
+
+
+def _key_pass_bf16_order(nch, n_tiles, nq, nsb, nst, npr, slag, nr=2):
+    """The BF16 key pass with the dS^T scratch stores (geoattn_bwd_cols_kernel<true, DP, true>) over several tiles of
+    one CTA, as five cooperating programs; returns None or the deadlock state.
+
+    TMA: per tile the K/V blocks (once the previous tile's last S^T/dP^T MMAs were issued), then per chunk the Q/dO
+    tile (nq-slot ring, released by the chunk's dV/dK MMAs), its row records (nr-slot ring, released by the
+    element-wise warps) and the store of chunk c - slag's staged dS^T tile (after the element-wise warps staged it;
+    the store is the tile's second release). Prior loader: nprior-slot ring of prior tiles. MMA: S^T/dP^T of a chunk
+    (its Q/dO loaded, a score buffer free), up to nsb chunks ahead; dV/dK of a chunk (its tiles staged), which
+    releases its Q/dO slot and the staging tile; `done` after the tile's last dV/dK. Element-wise warps: per chunk
+    wait scores, prior and records, release them, wait for the staging tile (both releases of chunk - nst), stage;
+    at the tile's end wait for `done` and for the last staged tiles' stores."""
+    st = dict(kv_loaded=0, kv_released=0, q_loaded=0, q_released=0, rec_loaded=0, rec_released=0, pr_loaded=0,
+              pr_released=0, s_issued=0, s_released=0, t_staged=0, t_mma=0, t_store=0, done=0)
+
+    def tma():
+        for it in range(n_tiles):
+            yield lambda it=it: st["kv_released"] >= it
+            st["kv_loaded"] = it + 1
+            g0 = it * nch
+            for c in range(nch):
+                gc = g0 + c
+                yield lambda gc=gc: st["q_released"] >= gc + 1 - nq
+                st["q_loaded"] = gc + 1
+                yield lambda gc=gc: st["rec_released"] >= gc + 1 - nr
+                st["rec_loaded"] = gc + 1
+                if c >= slag:
+                    yield lambda g=gc - slag: st["t_staged"] >= g + 1
+                    st["t_store"] = gc - slag + 1
+            for c in range(max(0, nch - slag), nch):
+                yield lambda g=g0 + c: st["t_staged"] >= g + 1
+                st["t_store"] = g0 + c + 1
+
+    def prior():
+        for gc in range(n_tiles * nch):
+            yield lambda gc=gc: st["pr_released"] >= gc + 1 - npr
+            st["pr_loaded"] = gc + 1
+
+    def mma():
+        def issue(gc):
+            yield lambda: st["q_loaded"] >= gc + 1 and st["s_released"] >= gc + 1 - nsb
+            st["s_issued"] = gc + 1
+
+        for it in range(n_tiles):
+            g0 = it * nch
+            yield lambda it=it: st["kv_loaded"] >= it + 1
+            yield from issue(g0)
+            if nch == 1:
+                st["kv_released"] = it + 1
+            for c in range(nch):
+                gc = g0 + c
+                if nsb == 2 and c + 1 < nch:
+                    yield from issue(gc + 1)
+                    if c + 2 == nch:
+                        st["kv_released"] = it + 1
+                yield lambda gc=gc: st["t_staged"] >= gc + 1
+                st["t_mma"] = gc + 1
+                st["q_released"] = gc + 1
+                if nsb == 1 and c + 1 < nch:
+                    yield from issue(gc + 1)
+                    if c + 2 == nch:
+                        st["kv_released"] = it + 1
+            st["done"] = it + 1
+
+    def ew():
+        for it in range(n_tiles):
+            g0 = it * nch
+            for c in range(nch):
+                gc = g0 + c
+                yield lambda gc=gc: (st["s_issued"] >= gc + 1 and st["pr_loaded"] >= gc + 1
+                                     and st["rec_loaded"] >= gc + 1)
+                st["s_released"] = st["rec_released"] = st["pr_released"] = gc + 1
+                yield lambda gc=gc: st["t_mma"] >= gc + 1 - nst and st["t_store"] >= gc + 1 - nst
+                st["t_staged"] = gc + 1
+            last = g0 + nch
+            yield lambda it=it, last=last: st["done"] >= it + 1 and st["t_mma"] >= last and st["t_store"] >= last
+
+    progs = [tma(), prior(), mma(), ew()]
+    waits = [next(p) for p in progs]
+    done = [False] * len(progs)
+    while not all(done):
+        moved = False
+        for i, prog in enumerate(progs):
+            while not done[i] and waits[i]():
+                try:
+                    waits[i] = next(prog)
+                except StopIteration:
+                    done[i] = True
+                moved = True
+        if not moved:
+            return dict(st)
+    return None
+
+
+# ColsCfg<true, DP> ring depths: (NQ, NSB, NST, NPR); the stores trail by SLAG = NQ - 1 (1 when NQ = 1)
+BF16_COLS = {64: (3, 2, 2, 2), 128: (3, 2, 1, 1), 192: (1, 1, 1, 1)}
+
+
+@pytest.mark.parametrize("D", [64, 128, 192])
+@pytest.mark.parametrize("nch", [1, 2, 3, 8])
+def test_key_pass_bf16_store_lag_has_no_deadlock(D, nch):
+    nq, nsb, nst, npr = BF16_COLS[D]
+    slag = nq - 1 if nq > 1 else 1
+    assert _key_pass_bf16_order(nch, 4, nq, nsb, nst, npr, slag) is None
+
+
+@pytest.mark.parametrize("D", [64, 128, 192])
+def test_key_pass_bf16_store_lag_bound(D):
+    """The load of chunk c waits (through the dV/dK MMAs and the staging of chunk c - NQ) for the store of chunk
+    c - NQ - NST: a lag up to NQ + NST - 1 runs, one more stops the pipeline (the planted mistake is caught)."""
+    nq, nsb, nst, npr = BF16_COLS[D]
+    bound = nq + nst - 1
+    assert all(_key_pass_bf16_order(n, 4, nq, nsb, nst, npr, bound) is None for n in (1, 2, 3, 5, 8, 16))
+    assert _key_pass_bf16_order(16, 4, nq, nsb, nst, npr, bound + 1) is not None
