@@ -303,7 +303,7 @@ def test_rows_wide_pair_order(ndc, nch):
 
 def _key_pass_bf16_order(nch, n_tiles, nq, nsb, nst, npr, slag, nr=2):
     """The BF16 key pass with the dS^T scratch stores (geoattn_bwd_cols_kernel<true, DP, true>) over several tiles of
-    one CTA, as five cooperating programs; returns None or the deadlock state.
+    one CTA, as four cooperating programs; returns None or the deadlock state.
 
     TMA: per tile the K/V blocks (once the previous tile's last S^T/dP^T MMAs were issued), then per chunk the Q/dO
     tile (nq-slot ring, released by the chunk's dV/dK MMAs), its row records (nr-slot ring, released by the
