@@ -16,10 +16,16 @@ It writes tests/golden/*.npz. What each file holds and which reference code prod
                     DataLoader.getHaversineDistance / getAlgularityOfLocations (fore_swe/extended_dl_forecasting.py
                     :305-344, executed from source with ast because the module imports sentence-transformers).
 * kahan.npz         fore_swe/extended_dl_forecasting.py:20-30 pairwise_vector_angle on seeded vectors.
+* regression_ref_norms.json  the float64 reference norms of the output and of every gradient that the reference
+                    recorded for its six regimes at case_inputs' default shape (1, 4, 128, 192) with attn_check's
+                    dO (engineering_audit/optimization/fused_attention/benchmark_results/final/regression_table.csv,
+                    column ref_norm; the same for every preset and precision).
 """
 import ast
 import contextlib
+import csv
 import io
+import json
 import os
 import sys
 
@@ -65,6 +71,18 @@ def save_attn(name, inputs, do):
                         q=q.numpy(), k=k.numpy(), v=v.numpy(), dist=dist.numpy(), ang=ang.numpy(),
                         alpha=a.numpy(), beta=b.numpy(), gamma=c.numpy(), do=do.numpy(),
                         **{key: val.numpy() for key, val in r.items()})
+
+
+def save_regression_norms():
+    path = os.path.join(REF, "engineering_audit", "optimization", "fused_attention", "benchmark_results", "final",
+                        "regression_table.csv")
+    norms = {}
+    with open(path) as f:
+        for row in csv.DictReader(f):
+            seen = norms.setdefault(row["case"], {}).setdefault(row["quantity"], float(row["ref_norm"]))
+            assert seen == float(row["ref_norm"]), row  # one reference per (case, quantity)
+    with open(os.path.join(HERE, "regression_ref_norms.json"), "w") as f:
+        json.dump({"shape": [1, 4, 128, 192], "source": os.path.relpath(path, REF), "ref_norm": norms}, f, indent=1)
 
 
 def main():
@@ -116,6 +134,7 @@ def main():
     vec[1] = vec[0] * 3.0                                  # parallel pair -> exactly 0
     vec[2] = -vec[0]                                       # antiparallel pair -> pi
     np.savez_compressed(os.path.join(HERE, "kahan.npz"), vectors=vec, angle=ns["pairwise_vector_angle"](vec))
+    save_regression_norms()
     print("golden vectors written to", HERE)
 
 

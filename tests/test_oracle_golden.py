@@ -119,3 +119,24 @@ def test_eager_tf32_error_model_is_differentiable_and_lossier():
     e32, etf = acceptance.eager(inp, do, "fp32"), acceptance.eager(inp, do, "tf32")
     for k in ("output", "dQ", "dK", "dV"):
         assert acceptance.err(etf[k], ref[k])["max_abs"] > acceptance.err(e32[k], ref[k])["max_abs"]
+
+
+@pytest.mark.parametrize("case", acceptance.CASES)
+def test_oracle_reproduces_the_reference_recorded_norms(case):
+    """The reference's recorded accuracy table holds the float64 reference's norm of the output and of every
+    gradient for its six regimes at case_inputs' default shape with attn_check's dO; the oracle's draws and
+    operator reproduce them (to ~1e-15 relative; a norm that is rounding noise around a true zero, d(alpha) of the
+    `uniform` regime, only to that noise level)."""
+    import json
+    with open(os.path.join(GOLD, "regression_ref_norms.json")) as f:
+        gold = json.load(f)
+    B, H, N, D = gold["shape"]
+    x = acceptance.case_inputs(case, B=B, H=H, N=N, D=D)
+    ref = acceptance.reference(x, acceptance.grad_seed_do(x[0].shape))
+    for key in KEYS:
+        want = gold["ref_norm"][case][key]
+        got = torch.linalg.vector_norm(ref[key].double()).item()
+        if want > 1e-12:
+            assert abs(got - want) <= 1e-12 * want, (key, got, want)
+        else:
+            assert got <= 1e-15, (key, got, want)
