@@ -400,7 +400,7 @@ def test_host_bias_parameters_get_host_gradients(ops):
     grads = {}
     for where in ("cpu", "cuda"):
         x = [t.cuda().requires_grad_(True) for t in (q, k, v)]
-        p = [t.to(where).requires_grad_(True) for t in (a, b, c)]
+        p = [t.detach().to(where).requires_grad_(True) for t in (a, b, c)]  # fresh leaves on each device
         o = ops.fused_geo_attention_v2(*x, dist, ang, *p)
         o.backward(do.cuda())
         assert all(t.grad.device.type == where for t in p)
