@@ -11,7 +11,9 @@ a bounded-wait timeout or as results that differ between runs, so their arithmet
   bounded waits); the kernels use NSB - PAIR there;
 * the wide row pass's sweep 2 with chunk pairs: the transposed K chunks for dQ trail the slots by one pair;
 * the wide key pass with query-chunk pairs: a chunk's records load before the next pair's slots;
-* the BF16 key pass's dS^T scratch stores trail the query-chunk loads by at most NQ + NST - 1 chunks.
+* the BF16 key pass's dS^T scratch stores trail the query-chunk loads by at most NQ + NST - 1 chunks;
+* the BF16 forward over several tiles: pass B's V loads may lag the K loads by 1 ... NSB + NK - 1 chunks (the kernel
+  uses NSB - 1).
 """
 import pytest
 
@@ -415,3 +417,125 @@ def test_key_pass_bf16_store_lag_bound(D):
     bound = nq + nst - 1
     assert all(_key_pass_bf16_order(n, 4, nq, nsb, nst, npr, bound) is None for n in (1, 2, 3, 5, 8, 16))
     assert _key_pass_bf16_order(16, 4, nq, nsb, nst, npr, bound + 1) is not None
+
+
+def _forward_bf16_order(nch, n_tiles, nk, npr, vlag, nsb=NSB):
+    """The BF16 forward (geoattn_fwd_kernel<true, DP>) over several tiles of one CTA as four cooperating programs;
+    returns None or the deadlock state.
+
+    TMA: per tile the Q block (once the previous tile's last score MMA was issued), then K of every chunk through an
+    nk-slot ring in pass A and again in pass B, where V of chunk c - vlag follows K of chunk c (two V buffers, each
+    freed by its P.V MMA). Prior loader: pass B's prior tiles through an npr-slot ring. MMA: pass A's score MMAs
+    (K loaded, a score buffer free), then pass B keeping its scores up to nsb chunks ahead of the P.V MMAs (Q is
+    released after the tile's last score MMA), P.V of chunk c once P(c) is staged and V(c) loaded, `ofull` after the
+    last. Element-wise warps: pass A frees the score buffers (two chunks at a time); pass B per chunk waits scores and
+    prior, frees them, waits for the P buffer (P.V of c - 2 done), stages P; then waits `ofull`."""
+    st = dict(q_loaded=0, q_released=0, k_loaded=0, k_used=0, v_loaded=0, pv=0, pr_loaded=0, pr_released=0,
+              s_issued=0, s_released=0, p_staged=0, ofull=0)
+
+    def tma():
+        for it in range(n_tiles):
+            yield lambda it=it: st["q_released"] >= it
+            st["q_loaded"] = it + 1
+            vbase = it * nch
+
+            def load_v(cv):
+                yield lambda: st["pv"] >= vbase + cv - 1        # V buffer of chunk cv - 2 free
+                st["v_loaded"] = vbase + cv + 1
+
+            for pass_ in range(2):
+                for c in range(nch):
+                    yield lambda: st["k_used"] >= st["k_loaded"] + 1 - nk
+                    st["k_loaded"] += 1
+                    if pass_ == 1 and c >= vlag:
+                        yield from load_v(c - vlag)
+                if pass_ == 1:
+                    for cv in range(max(0, nch - vlag), nch):
+                        yield from load_v(cv)
+
+    def prior():
+        for g in range(n_tiles * nch):
+            yield lambda g=g: st["pr_released"] >= g + 1 - npr
+            st["pr_loaded"] = g + 1
+
+    def mma():
+        def issue():
+            yield lambda: (st["k_loaded"] >= st["k_used"] + 1 and st["s_released"] >= st["s_issued"] + 1 - nsb)
+            st["k_used"] += 1
+            st["s_issued"] += 1
+
+        for it in range(n_tiles):
+            yield lambda it=it: st["q_loaded"] >= it + 1
+            for _ in range(nch):
+                yield from issue()
+            nb = 0
+            for c in range(nch):
+                while nb < nch and nb < c + nsb:
+                    yield from issue()
+                    nb += 1
+                    if nb == nch:
+                        st["q_released"] = it + 1
+                g = it * nch + c
+                yield lambda g=g: st["p_staged"] >= g + 1 and st["v_loaded"] >= g + 1
+                st["pv"] = g + 1
+            st["ofull"] = it + 1
+
+    def ew():
+        s = 0
+        for it in range(n_tiles):
+            for c in range(0, nch, 2):
+                two = 2 if c + 1 < nch else 1
+                yield lambda s=s, two=two: st["s_issued"] >= s + two
+                s += two
+                st["s_released"] = s
+            for c in range(nch):
+                g = it * nch + c
+                yield lambda s=s, g=g: st["s_issued"] >= s + 1 and st["pr_loaded"] >= g + 1
+                s += 1
+                st["s_released"] = s
+                st["pr_released"] = g + 1
+                yield lambda g=g: st["pv"] >= g - 1
+                st["p_staged"] = g + 1
+            yield lambda it=it: st["ofull"] >= it + 1
+
+    progs = [tma(), prior(), mma(), ew()]
+    waits = [next(p) for p in progs]
+    done = [False] * len(progs)
+    while not all(done):
+        moved = False
+        for i, prog in enumerate(progs):
+            while not done[i] and waits[i]():
+                try:
+                    waits[i] = next(prog)
+                except StopIteration:
+                    done[i] = True
+                moved = True
+        if not moved:
+            return dict(st)
+    return None
+
+
+# FwdCfg<true, DP>: (NK, NPR); V loads lag the K loads by NSB - 1 chunks
+BF16_FWD = {64: (3, 2), 128: (3, 2), 192: (2, 1)}
+
+
+@pytest.mark.parametrize("D", [64, 128, 192])
+@pytest.mark.parametrize("nch", [1, 2, 3, 4, 5, 8])
+def test_forward_bf16_order_has_no_deadlock(D, nch):
+    nk, npr = BF16_FWD[D]
+    assert _forward_bf16_order(nch, 3, nk, npr, NSB - 1) is None
+
+
+@pytest.mark.parametrize("D", [64, 128, 192])
+def test_forward_bf16_v_lag_range(D):
+    """In pass B the TMA warp loads K(x) and then V(x - VLAG); V(y) waits for P.V(y - 2) (two V buffers), and P.V(c)
+    comes after the score MMAs up to chunk c + NSB - 1. Lower bound: K(c + NSB - 1) follows V(c + NSB - 2 - VLAG),
+    which waits for P.V(c + NSB - 4 - VLAG), so VLAG >= NSB - 3 = 1. Upper bound: V(c) follows K(c + VLAG), which needs
+    the ring slot of K(c + VLAG - NK), free once that chunk's score MMA is issued, so VLAG <= NSB + NK - 1. Lags in
+    that range run; 0 and NSB + NK stop (the planted mistakes are caught)."""
+    nk, npr = BF16_FWD[D]
+    sizes = (1, 2, 3, 4, 5, 8, 16)
+    for vlag in range(1, NSB + nk):
+        assert all(_forward_bf16_order(n, 3, nk, npr, vlag) is None for n in sizes), vlag
+    assert _forward_bf16_order(16, 3, nk, npr, 0) is not None
+    assert _forward_bf16_order(16, 3, nk, npr, NSB + nk) is not None
