@@ -186,28 +186,80 @@ def gpu_eager_ms(q, k, v, do, dist, ang, a, b, c, steps):
         torch.cuda.empty_cache()
 
 
+REF_SAMPLE_DATES = 32   # issue dates per step of the reference arm: a bounded sample (1/8) of the 256-date workload
+
+
+def cpu_step_sample(n_dates, threads):
+    """One step of the reference arm: fwd+bwd of the eager operator (the oracle's restatement of the reference's eager
+    PyTorch op, fp32, on the host CPU) over `n_dates` issue dates of the workload, one issue date per call as the
+    reference's training loop batches them. Returns the wall time in ms."""
+    from oracle import geo_attention as oga
+    from oracle import geometry as ogeo
+    torch.set_num_threads(threads)
+    lat, lon, el = stations(0)
+    dist, ang = (torch.from_numpy(x).float() for x in ogeo.distance_and_angularity(lat, lon, el))
+    (q, k, v, do), (a, b, c) = inputs(1, 1000, "cpu")
+    q, k, v, do = (t.float() for t in (q, k, v, do))
+    t0 = time.perf_counter()
+    for _ in range(n_dates):
+        oga.grads(q, k, v, dist, ang, a, b, c, do, dtype=torch.float32)
+    return (time.perf_counter() - t0) * 1e3
+
+
+def cpu_c1(threads, reps=10):
+    """The CPU configuration: eager FP32 fwd+bwd at B=1 issue date, H=8, N=512, D=64 (q, k, v ~ N(0,1) D^-1/4 from
+    seed 0; coordinates lat ~ U(35,49), lon ~ U(-124,-104), elevation ~ U(500,3500) m; a_h ~ U(0.1,1),
+    b_h, g_h ~ N(0, 0.5)); median ms of `reps` calls after one warm-up."""
+    from oracle import geo_attention as oga
+    from oracle import geometry as ogeo
+    torch.set_num_threads(threads)
+    b1, h1, n1, d1 = 1, 8, 512, 64
+    g = torch.Generator().manual_seed(0)
+    q, k, v = (torch.randn(b1, h1, n1, d1, generator=g) * d1 ** -0.25 for _ in range(3))
+    rng = np.random.default_rng(0)
+    lat, lon = rng.uniform(35.0, 49.0, n1), rng.uniform(-124.0, -104.0, n1)
+    el = rng.uniform(500.0, 3500.0, n1) / 0.3048
+    dist, ang = (torch.from_numpy(x).float() for x in ogeo.distance_and_angularity(lat, lon, el))
+    a = torch.rand(h1, generator=g) * 0.9 + 0.1
+    b, c = torch.randn(h1, generator=g) * 0.5, torch.randn(h1, generator=g) * 0.5
+    do = torch.randn(b1, h1, n1, d1, generator=g)
+    oga.grads(q, k, v, dist, ang, a, b, c, do, dtype=torch.float32)
+    ts = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        oga.grads(q, k, v, dist, ang, a, b, c, do, dtype=torch.float32)
+        ts.append((time.perf_counter() - t0) * 1e3)
+    fl = 12.0 * b1 * h1 * n1 * n1 * d1
+    ms = statistics.median(ts)
+    return {"ms_fwd_bwd": ms, "gflop": fl / 1e9, "tflops": fl / (ms * 1e-3) / 1e12, "cores": threads, "reps": reps,
+            "shape_bhnd": [b1, h1, n1, d1], "dtype": "fp32",
+            "what": "eager FP32 fwd+bwd of the reference operator on the host CPU (oracle's torch restatement)"}
+
+
 def run_reference(args):
+    """The reference arm: the reference's eager operator on the host CPU cores, all threads. Each of the K timed steps
+    is a bounded sample of the workload -- REF_SAMPLE_DATES issue dates fwd+bwd, timed for real -- so ms_per_step is
+    the measured time of that sample step and value the measured rate."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
     threads = os.cpu_count() or 1
     world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
-    samples = []
     for _ in range(args.warmup):
-        cpu_reference(1.0, threads)
-    for _ in range(args.steps):
-        samples.append(cpu_reference(args.cpu_seconds / max(1, args.steps), threads))
-    value = statistics.median(s[0] for s in samples)
-    reps = sum(s[1] for s in samples)
-    el = sum(s[2] for s in samples)
-    sample = "fwd+bwd of 1 issue date (H=%d, N=%d, D=%d) fp32 eager on the CPU, %d repetitions in %.1f s" % (
-        H, N, D, reps, el)
+        cpu_step_sample(1, threads)
+    ts = [cpu_step_sample(REF_SAMPLE_DATES, threads) for _ in range(args.steps)]
+    ms = statistics.mean(ts)
+    value = flops(REF_SAMPLE_DATES) / (ms * 1e-3) / 1e12
+    sample = ("each step: fwd+bwd of %d of the %d issue dates (H=%d, N=%d, D=%d), fp32 eager on the CPU, one date per "
+              "call; %d steps, %.1f s timed" % (REF_SAMPLE_DATES, B_TOTAL, H, N, D, args.steps, sum(ts) / 1e3))
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": flops(B_TOTAL) / (value * 1e12) * 1e3,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "step_is": "a bounded sample: %d issue dates of the %d-date workload" % (REF_SAMPLE_DATES, B_TOTAL),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
             "config": config(world),
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
-            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "c1_cpu": cpu_c1(threads)}
     print(json.dumps(line), flush=True)
     return 0
 
@@ -332,28 +384,24 @@ def run_c4(args):
     return 0
 
 
-def run_c5step(args):
-    """The scaling configuration's whole step: x [B/world, N, 2048] -> W_qkv -> geo-attention (16 heads x 128, the
-    kernels on strided views of the fused projection) -> W_o -> loss, forward and backward under bf16 autocast with
-    fp32 weights, and the NCCL all-reduce of dW_qkv, dW_o (67 MB fp32) and d(alpha, beta, gamma), bucketed by DDP and
-    overlapped with the backward. Prints one JSON line (ms per step, whole-step and attention TFLOP/s)."""
-    import datetime
+def measure_c5step(args, dev, rank, world, geom):
+    """The scaling configuration's whole step on this rank's shard: x [B/world, N, 2048] -> W_qkv -> geo-attention
+    (16 heads x 128, the kernels on strided views of the fused projection) -> W_o -> loss, forward and backward under
+    bf16 autocast with fp32 weights, and (N > 1) the NCCL all-reduce of dW_qkv, dW_o (67 MB fp32) and
+    d(alpha, beta, gamma), bucketed by DDP and overlapped with the backward.
+
+    Returns the max-over-ranks device times (CUDA events) of: the step as run (``ms_per_step``); the same step with
+    DDP's gradient all-reduce switched off (``compute_ms``, DDP ``no_sync``); and the all-reduce alone on a buffer of
+    the same payload (``allreduce_ms``). Every loop runs the same number of times on every rank."""
     import torch.nn as nn
     import foreswe_gpu_optimization_b200 as g
     from foreswe_gpu_optimization_b200.dp import shard
-
-    rank, world = int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
     dist_on = world > 1
     if dist_on:
         import torch.distributed as tdist
-        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
     dm = H * D
     s0, s1 = shard(B_TOTAL, world, rank)
     b = s1 - s0
-    geom = g.StationGeometry(*stations(0), device=dev)
 
     class Step(nn.Module):
         def __init__(self):
@@ -373,8 +421,10 @@ def run_c5step(args):
 
     torch.manual_seed(0)
     model = Step().to(dev)
+    nsync = None
     if dist_on:
-        model = nn.parallel.DistributedDataParallel(model, device_ids=[local], bucket_cap_mb=25)
+        model = nn.parallel.DistributedDataParallel(model, device_ids=[dev.index], bucket_cap_mb=25)
+        nsync = model.no_sync
     gen = torch.Generator(device=dev).manual_seed(100 + rank)
     x = torch.randn(b, N, dm, device=dev, generator=gen)
     target = torch.randn(b, N, dm, device=dev, generator=gen)
@@ -387,39 +437,81 @@ def run_c5step(args):
         loss.backward()
         return loss
 
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize()
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        if dist_on:
+            tdist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            r = fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / args.steps, r
+
+    ms, loss = timed(step)
+    comp_ms, ar_ms = ms, 0.0
     if dist_on:
-        tdist.barrier()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(args.steps):
-        loss = step()
-    e1.record()
-    torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / args.steps
-    if dist_on:
-        tt = torch.tensor([ms], device=dev, dtype=torch.float64)
+        def step_no_sync():
+            with nsync():
+                return step()
+        comp_ms, _ = timed(step_no_sync)
+        payload = torch.zeros(4 * dm * dm + 3 * H, device=dev)
+
+        def allreduce():
+            tdist.all_reduce(payload)
+        ar_ms, _ = timed(allreduce)
+        del payload
+        tt = torch.tensor([ms, comp_ms, ar_ms], device=dev, dtype=torch.float64)
         tdist.all_reduce(tt, op=tdist.ReduceOp.MAX)
-        ms = tt.item()
+        ms, comp_ms, ar_ms = tt.tolist()
     attn_flops = flops(B_TOTAL)
     proj_flops = 24.0 * B_TOTAL * N * dm * dm          # W_qkv and W_o: forward 8 B N dm^2, backward twice that
+    res = {"ms_per_step": ms, "tflops": (attn_flops + proj_flops) / (ms * 1e-3) / 1e12,
+           "compute_ms": comp_ms, "allreduce_ms": ar_ms,
+           "exposed_allreduce_ms": max(0.0, ms - comp_ms),
+           "allreduce_payload_mb": (4 * dm * dm + 3 * H) * 4 / 1e6,
+           "attention_tflop_per_step": attn_flops / 1e12, "projection_tflop_per_step": proj_flops / 1e12,
+           "per_gpu_batch": b, "loss": float(loss.item()),
+           "what": "x -> W_qkv -> geo-attention -> W_o -> MSE, fwd+bwd, bf16 autocast, fp32 weights; DDP all-reduce "
+                   "of dW_qkv, dW_o, d(alpha, beta, gamma) overlapped with the backward (N > 1); compute_ms = the same "
+                   "step under DDP no_sync; allreduce_ms = the payload's all-reduce alone; max over ranks"}
+    if dist_on:
+        del model
+    torch.cuda.empty_cache()
+    return res
+
+
+def run_c5step(args):
+    """The scaling configuration's whole step (``measure_c5step``) as its own JSON line (ms per step)."""
+    import datetime
+    import foreswe_gpu_optimization_b200 as g
+    rank, world = int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist_on = world > 1
+    if dist_on:
+        import torch.distributed as tdist
+        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    geom = g.StationGeometry(*stations(0), device=dev)
+    r = measure_c5step(args, dev, rank, world, geom)
     if rank == 0:
+        dm = H * D
         line = {"metric": "geo-attention scaling step (W_qkv -> geo-attn -> W_o fwd+bwd + gradient all-reduce), ms/step",
-                "value": ms, "unit": "ms/step", "higher_is_better": False, "n_gpus": world, "steps": args.steps,
-                "warmup": args.warmup, "dtype": "bf16 autocast (fp32 weights)", "data": "synthetic",
+                "value": r["ms_per_step"], "unit": "ms/step", "higher_is_better": False, "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "dtype": "bf16 autocast (fp32 weights)", "data": "synthetic",
                 "config": {"workload": "%d issue dates sharded over %d GPU(s) x %d stations, d_model %d, %d heads x %d; "
                                        "all-reduce of dW_qkv, dW_o (%.0f MB fp32) and d(alpha, beta, gamma) by DDP"
-                                       % (B_TOTAL, world, N, dm, H, D, 4 * dm * dm * 4 / 1e6), "per_gpu_batch": b},
-                "step_tflops": (attn_flops + proj_flops) / (ms * 1e-3) / 1e12,
-                "attention_tflop_per_step": attn_flops / 1e12, "projection_tflop_per_step": proj_flops / 1e12,
-                "loss": float(loss.item())}
+                                       % (B_TOTAL, world, N, dm, H, D, 4 * dm * dm * 4 / 1e6),
+                           "per_gpu_batch": r["per_gpu_batch"]},
+                "step_tflops": r["tflops"], "step": r}
         print(json.dumps(line), flush=True)
     if dist_on:
         tdist.barrier()
-        del model
         tdist.destroy_process_group()
     return 0
 
@@ -529,6 +621,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-eager", action="store_true")
+    ap.add_argument("--no-step", action="store_true", help="skip the whole-step (projections + all-reduce) key")
     ap.add_argument("--batch", type=int, default=None, help="override the global batch (small cases for profiling)")
     ap.add_argument("--only", default=None, choices=[c[0] for c in CONFIGS],
                     help="with --workload configs: run this configuration only")
@@ -635,14 +728,17 @@ def main():
         run_step()
     e1.record()
     torch.cuda.synchronize()
-    est_ms = max(e0.elapsed_time(e1) / 3, 0.05)
+    est_ms = e0.elapsed_time(e1) / 3
 
     # clocks are sampled from a busy pre-roll of ~0.3 s through the timed region and the per-kernel pass below,
-    # all the same workload, so even a short timed region has samples under load
+    # all the same workload, so even a short timed region has samples under load. Every step holds an all-reduce
+    # (N > 1), so the pre-roll length is agreed over the ranks (max of their estimates) before any rank starts it.
+    from foreswe_gpu_optimization_b200.dp import agreed_count
+    preroll = agreed_count(est_ms, 0.3, device=dev)
     clocks = ClockSampler(range(world) if world > 1 else [local])
     if rank == 0:
         clocks.start()
-    for _ in range(int(300.0 / est_ms) + 1):
+    for _ in range(preroll):
         run_step()
     if dist_on:
         tdist.barrier()
@@ -720,6 +816,9 @@ def main():
                            % E2E_SLICES}
         del hq, hk, hv, hd, pipe
 
+    # the configuration's whole step (projections and their gradient all-reduce), every rank, at every N
+    stepm = None if args.no_step else measure_c5step(args, dev, rank, world, geom)
+
     eager = None
     if not args.no_eager and rank == 0:
         dmat, amat = geom.distance_and_angularity()
@@ -734,7 +833,7 @@ def main():
         val, reps, el_s = cpu_reference(args.cpu_seconds, threads)
         cpu = {"value": val, "unit": UNIT, "cores": threads, "kind": "port",
                "sample": "fwd+bwd of 1 issue date (H=%d, N=%d, D=%d) fp32 eager on the CPU, %d repetitions in %.1f s"
-                         % (H, N, D, reps, el_s)}
+                         % (H, N, D, reps, el_s), "c1_cpu": cpu_c1(threads)}
 
     if rank == 0:
         dom = max(kt, key=kt.get)
@@ -754,7 +853,7 @@ def main():
                           + "; per-kernel times from K eager steps with library events",
                 "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": config(world),
                 "tensor_peak_frac": value / world / pk, "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
-                "gpu_eager": eager, "gpu_launches": 5 * args.steps, "clocks": clk}
+                "gpu_eager": eager, "step": stepm, "gpu_launches": 5 * args.steps, "clocks": clk}
         print(json.dumps(line), flush=True)
     if dist_on:
         tdist.barrier()

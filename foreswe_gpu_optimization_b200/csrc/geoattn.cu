@@ -668,6 +668,11 @@ int backward(const GeoAttnBwdArgs* a, void* stream, bool with_ds) {
 }  // namespace
 }  // namespace geoattn
 
+namespace geoattn {
+// Address of geoattn_bwd_noalloc's static scratch on the current device (defined with the array below).
+int noalloc_scratch(void** out);
+}  // namespace geoattn
+
 extern "C" {
 
 int geoattn_bwd(const GeoAttnBwdArgs* a, void* stream) { return backward(a, stream, true); }
@@ -681,7 +686,13 @@ int geoattn_wait_selftest(void* status_word, void* stream) {
 }
 
 int geoattn_read_status(const void* workspace, int* status, void* stream) {
-  if (!dev_ptr(workspace) || !status) return GEOATTN_ERR_INVALID;
+  if (!status) return GEOATTN_ERR_INVALID;
+  if (!workspace) {  // geoattn_bwd_noalloc's status word: the first word of the current device's static scratch
+    void* scratch = nullptr;
+    if (int rc = geoattn::noalloc_scratch(&scratch)) return rc;
+    workspace = scratch;
+  }
+  if (!dev_ptr(workspace)) return GEOATTN_ERR_INVALID;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (cudaMemcpyAsync(status, workspace, sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess)
     return GEOATTN_ERR_LAUNCH;
@@ -710,6 +721,7 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratch
 
 namespace {
 constexpr int kMaxDevices = 64;
+}  // namespace
 
 int noalloc_scratch(void** out) {
   int dev = -1;
@@ -726,7 +738,6 @@ int noalloc_scratch(void** out) {
   *out = addr[dev];
   return GEOATTN_OK;
 }
-}  // namespace
 }  // namespace geoattn
 
 extern "C" int geoattn_bwd_noalloc(const GeoAttnBwdArgs* a, void* stream) {

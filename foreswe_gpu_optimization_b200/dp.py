@@ -30,3 +30,17 @@ def allreduce_bias_grads(params, group=None):
         n = g.numel()
         g.copy_(flat[off:off + n].view_as(g))
         off += n
+
+
+def agreed_count(est_ms, seconds, group=None, device=None):
+    """The number of repetitions of a step estimated at `est_ms` that fill about `seconds`, identical on every rank.
+
+    A loop whose body holds a collective must run the same number of times on every rank, or the ranks' collectives
+    stop pairing up and the job waits until the process-group timeout. Per-rank timings differ slightly, so the
+    count is taken from the MAX of the estimates over the ranks (one all-reduce) before any rank starts the loop."""
+    est = float(est_ms)
+    if dist.is_available() and dist.is_initialized() and dist.get_world_size(group) > 1:
+        t = torch.tensor([est], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+        est = float(t.item())
+    return int(seconds * 1000.0 / max(est, 0.05)) + 1

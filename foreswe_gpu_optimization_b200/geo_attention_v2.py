@@ -257,7 +257,9 @@ def patch_model(model, preset="accurate_experimental", geometry=None, precision=
 
 
 def read_status(workspace):
-    """Device status word of a workspace tensor (0 = ok); synchronises the current stream."""
+    """Device status word of a workspace tensor (0 = ok); ``None`` reads the status word of the last
+    ``geoattn_bwd_noalloc`` call on the current device. Synchronises the current stream."""
     st = ctypes.c_int(-1)
-    _lib.check(_lib.lib().geoattn_read_status(ctypes.c_void_p(workspace.data_ptr()), ctypes.byref(st), _stream()))
+    ptr = ctypes.c_void_p(workspace.data_ptr() if workspace is not None else None)
+    _lib.check(_lib.lib().geoattn_read_status(ptr, ctypes.byref(st), _stream()))
     return st.value

@@ -7,8 +7,7 @@
  *   fused_geo_attention_v2(q, k, v, dist, ang, a, b, g)     foreswe_bench/geo_attention_v2.py:464-465
  * and the bias construction is
  *   DataLoader.getDistanceAndAngularity (+ helpers)         fore_swe/extended_dl_forecasting.py:305-352
- * A Python (ctypes) binding of every entry point below lives in
- * foreswe_gpu_optimization_b200/_lib.py; INTEGRATION.md shows it.
+ * A Python (ctypes) binding of every entry point below lives in foreswe_gpu_optimization_b200/_lib.py.
  *
  * Conventions: all data pointers are memory of the current device (cudaGetDevice) or managed memory, and
  * `stream` belongs to that device; tensors are [B, H, N, D] with element strides; the
@@ -128,17 +127,22 @@ int geoattn_bwd(const GeoAttnBwdArgs* args, void* stream);
  * and give an operator only its inputs and outputs, or code with a fixed memory plan where an allocation would
  * synchronise the device. Same arguments and results as geoattn_bwd, except that args->workspace is ignored: the
  * scratch comes from a static 16 MiB device array that the library holds on every device that loads it until the
- * process exits. Limits: BF16 only (GEOATTN_ERR_UNSUPPORTED for FP32); geoattn_bwd_workspace_bytes(shape) must be
- * <= 16 MiB (about B*H*N <= 1,000,000 rows, e.g. 64 issue dates x 16 heads x 512 stations), else
- * GEOATTN_ERR_SCRATCH before any launch. All calls share the array, so calls that overlap on the GPU race. The
- * first call on a device looks up the array's address (cudaGetSymbolAddress); make it before any stream capture.
+ * process exits. Limits: BF16 only (GEOATTN_ERR_UNSUPPORTED for FP32). The scratch it needs is
+ *   256 + align256(B*H*N_pad*16) + align256(B*H*ceil(N/128)*24) bytes,  N_pad = N rounded up to 128
+ * (row records and bias-gradient partials; it forms dQ in a second row-pass sweep and keeps no dS scratch, so this
+ * is not geoattn_bwd_workspace_bytes), and must be <= 16 MiB, else GEOATTN_ERR_SCRATCH before any launch: at
+ * N = 512 that is B*H <= 2024 (e.g. 64 issue dates x 16 heads; 128 x 16 is rejected), about 1M query rows.
+ * All calls share the array, so calls that overlap on the GPU race. The first call on a device looks up the
+ * array's address (cudaGetSymbolAddress); make it before any stream capture. A bounded wait that expires inside
+ * the call is reported through geoattn_read_status(NULL, ...) (below), not by the return code.
  * It allocates nothing (no cudaMalloc/cudaFree, no allocating library call).                                  */
 int geoattn_bwd_noalloc(const GeoAttnBwdArgs* args, void* stream);
 
 /* ---- diagnostics --------------------------------------------------------------------------------------- */
 /* Copies the device status word of a workspace (0 = ok, 1 = a bounded wait expired, 2 = a kernel found its shared
- * memory misaligned and did nothing) to *status. Synchronises
- * the stream; for tests and debugging only. */
+ * memory misaligned and did nothing) to *status. workspace = NULL reads the status word of the last
+ * geoattn_bwd_noalloc call on the current device (its static scratch). Synchronises the stream; for tests and
+ * debugging only. */
 int geoattn_read_status(const void* workspace, int* status, void* stream);
 /* Self-test of the kernels' bounded waits: launches one thread that waits on a barrier nothing completes. After the
  * wait limit (about 2 s) the wait gives up, the kernel sets the 4-byte device word `status_word` to 1 (as a timed-out

@@ -75,8 +75,9 @@ def reference(inputs, do):
 
 
 def eager(inputs, do, prec):
-    """Eager operator's own result at the given precision ("fp32" or "tf32"), evaluated on the CPU."""
-    mm = ga.tf32_matmul if prec == "tf32" else torch.matmul
+    """Eager operator's own result at the given precision ("fp32", "tf32" or "bf16": every matmul operand rounded to
+    bf16, fp32 elsewhere, as under autocast), evaluated on the CPU."""
+    mm = {"tf32": ga.tf32_matmul, "bf16": ga.bf16_matmul}.get(prec, torch.matmul)
     return ga.grads(*inputs, do, dtype=torch.float32, matmul=mm)
 
 

@@ -118,3 +118,30 @@ class _TF32MatMul(torch.autograd.Function):
 def tf32_matmul(a, b):
     """Matmul with TF32-rounded operands and a wide accumulator: the error model of eager TF32."""
     return _TF32MatMul.apply(a, b)
+
+
+def round_bf16(x):
+    """fp32 -> bf16 round-to-nearest-even, back in fp32 (a bf16 tensor-core operand under autocast)."""
+    return x.float().to(torch.bfloat16).float()
+
+
+class _BF16MatMul(torch.autograd.Function):
+    """Matmul whose forward and backward products all take bf16-rounded operands with a wide accumulator: the error
+    model of eager PyTorch under bf16 autocast (cuBLAS bf16 GEMMs, fp32 accumulation)."""
+
+    @staticmethod
+    def forward(ctx, a, b):
+        ctx.save_for_backward(a, b)
+        return (round_bf16(a).double() @ round_bf16(b).double()).to(a.dtype)
+
+    @staticmethod
+    def backward(ctx, g):
+        a, b = ctx.saved_tensors
+        ga = (round_bf16(g).double() @ round_bf16(b).double().transpose(-2, -1)).to(a.dtype)
+        gb = (round_bf16(a).double().transpose(-2, -1) @ round_bf16(g).double()).to(b.dtype)
+        return ga, gb
+
+
+def bf16_matmul(a, b):
+    """Matmul with bf16-rounded operands and a wide accumulator: the error model of eager bf16 autocast."""
+    return _BF16MatMul.apply(a, b)

@@ -2,7 +2,7 @@
 
 Run once in a container that has the reference checkout (read-only) at REF_ROOT:
 
-    python tests/golden/make_golden.py [REF_ROOT]
+    python tests/golden/make_golden.py REF_ROOT      (REF_ROOT: the reference checkout, required)
 
 It writes tests/golden/*.npz. What each file holds and which reference code produced it:
 
@@ -33,7 +33,9 @@ import numpy as np
 import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+if len(sys.argv) != 2 or not os.path.isdir(sys.argv[1]):
+    sys.exit("usage: python make_golden.py <path of the reference checkout>")
+REF = os.path.abspath(sys.argv[1])
 sys.path.insert(0, REF)
 
 from foreswe_bench.attn_check import case_inputs  # noqa: E402

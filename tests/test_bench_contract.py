@@ -35,9 +35,13 @@ def test_reference_arm_prints_one_contract_line():
     e2e = line["e2e"]
     assert e2e["value"] == line["value"] and e2e["unit"] == line["unit"]
     assert e2e["h2d_bytes_per_step"] == 0 and e2e["d2h_bytes_per_step"] == 0
-    # ms_per_step is the whole workload's time at the measured rate
-    flops = 12.0 * 256 * 16 * 512 * 512 * 128
+    # each step is a measured, bounded sample of the workload (32 of the 256 issue dates): ms_per_step is that
+    # step's measured time and value its rate, so K steps fit inside the run
+    flops = 12.0 * 32 * 16 * 512 * 512 * 128
     assert abs(line["ms_per_step"] - flops / (line["value"] * 1e12) * 1e3) <= 1e-6 * line["ms_per_step"]
+    assert "32 issue dates" in line["step_is"]
+    c1 = line["c1_cpu"]
+    assert c1["shape_bhnd"] == [1, 8, 512, 64] and c1["ms_fwd_bwd"] > 0 and c1["cores"] == cb["cores"]
 
 
 def test_reference_arm_other_ranks_exit_quietly():

@@ -483,3 +483,79 @@ def test_full_size_step_properties(ops, dtype, B, H, D):
     dk, dv = g1[1].double(), g1[2].double()
     assert _rel_dev(dv.sum(dim=2), do.double().sum(dim=2)) <= 2e-3
     assert (dk.sum(dim=2).norm() / dk.abs().sum(dim=2).norm()).item() <= 2e-3
+
+
+@pytest.mark.parametrize("path", sorted(glob.glob(os.path.join(GOLD, "attn_*.npz"))),
+                         ids=lambda p: os.path.basename(p)[5:-4])
+def test_reference_golden_vectors_bf16(ops, path):
+    """The reference-generated golden inputs through the BF16 path. The kernels see the inputs and dO rounded to
+    bf16, so they are judged against the float64 oracle on those values (the fixture's outputs pin the oracle on the
+    unrounded inputs, tests/test_oracle_golden.py): each quantity within the BF16 rel-L2 tolerance, or -- where the
+    oracle's value vanishes (uniform: Q = 0 makes the true d(alpha) zero) -- within 10x the max-abs error of eager
+    bf16 (every matmul operand rounded to bf16, as under autocast), the reference's own acceptance rule."""
+    z = np.load(path)
+    rb = lambda t: torch.from_numpy(t).float().to(torch.bfloat16)  # noqa: E731
+    q, k, v, do = (rb(z[n]) for n in ("q", "k", "v", "do"))
+    dist, ang = (torch.from_numpy(z[n]).float() for n in ("dist", "ang"))
+    a, b, c = (torch.from_numpy(z[n]).float().reshape(-1) for n in ("alpha", "beta", "gamma"))
+    res = run_device(lambda *x: ops.fused_geo_attention_v2(x[0], x[1], x[2], dist.cuda(), ang.cuda(), *x[3:]),
+                     q, k, v, a, b, c, do)
+    inp = [q.float(), k.float(), v.float(), dist, ang, a, b, c]
+    ref = acceptance.reference(inp, do.float())
+    ev = acceptance.evaluate(res, inp, do.float(), "bf16", ref=ref)
+    for key in KEYS:
+        assert torch.isfinite(res[key].float()).all(), key
+        e = rel_l2(res[key], ref[key].reshape(res[key].shape))
+        assert e <= TOL[torch.bfloat16] or ev[key]["passed"], (key, e, ev[key]["candidate"]["max_abs"],
+                                                               ev[key]["bound"])
+
+
+@pytest.mark.parametrize("qscale", [1.0, 30.0], ids=["plain", "saturated_x30"])
+def test_full_c2_tf32_every_head_against_oracle(ops, qscale):
+    """The full TF32 configuration, 32 issue dates x 8 heads x 512 stations x D = 64 (~7 tiles per persistent CTA),
+    plain and with logits x30: all 256 heads and the bias gradients against the float64 oracle (evaluated on the CPU
+    four issue dates at a time, bias gradients summed over the slices) within the TF32 tolerance."""
+    B, H, N, D = 32, 8, 512, 64
+    q, k, v, a, b, c, do = attn_inputs(B, H, N, D, seed=50, qscale=qscale, dtype=torch.float32)
+    lat, lon, el = stations(N, seed=51)
+    geom = ops.StationGeometry(lat, lon, el)
+    res = run_device(lambda *x: ops.geo_attention(x[0], x[1], x[2], geom, *x[3:]), q, k, v, a, b, c, do)
+    dist, ang = dense_geometry(lat, lon, el)
+    parts = [_oracle(q[s:s + 4], k[s:s + 4], v[s:s + 4], dist, ang, a, b, c, do[s:s + 4]) for s in range(0, B, 4)]
+    ref = {key: torch.cat([p[key] for p in parts]) for key in ("output", "dQ", "dK", "dV")}
+    for key in ("dalpha", "dbeta", "dgamma"):
+        ref[key] = sum(p[key] for p in parts)
+    _check(res, ref, TOL[torch.float32], "full C2 x%g" % qscale)
+
+
+@pytest.mark.parametrize("B,H,D", [(256, 16, 128), (384, 16, 64)], ids=["c5-256x16x512x128", "c3-384x16x512x64"])
+def test_full_size_bf16_sampled_heads_against_oracle(ops, B, H, D):
+    """The benchmarked configuration (256 issue dates x 16 heads x 512 stations x D = 128, bf16; ~110 tiles per
+    persistent CTA) and the temporal-batched one (384 x 16 x 512 x 64): one full-size fwd+bwd on the device, then
+    the output and dQ, dK, dV of sampled heads -- the first and last issue dates and one in the middle of the
+    persistent tile order, first, middle and last heads -- against the float64 oracle on the same bf16 values, within
+    the BF16 tolerance. A wrong (b, h) offset or a tile handed between CTAs wrongly shows up in these heads."""
+    N = 512
+    g = torch.Generator(device="cuda").manual_seed(60 + D)
+    s = D ** -0.25
+    q, k, v = (torch.randn(B, H, N, D, device="cuda", generator=g).mul_(s).to(torch.bfloat16) for _ in range(3))
+    do = torch.randn(B, H, N, D, device="cuda", generator=g).to(torch.bfloat16)
+    pa = torch.rand(H, device="cuda", generator=g) * 0.9 + 0.1
+    pb, pc = (torch.randn(H, device="cuda", generator=g) * 0.5 for _ in range(2))
+    lat, lon, el = stations(N, seed=61)
+    geom = ops.StationGeometry(lat, lon, el)
+    x = [t.detach().requires_grad_(True) for t in (q, k, v)]
+    o = ops.geo_attention(x[0], x[1], x[2], geom, pa, pb, pc)
+    o.backward(do)
+    torch.cuda.synchronize()
+    dist, ang = dense_geometry(lat, lon, el)
+    for bi in (0, 97, B - 1):
+        for hi in (0, 7, H - 1):
+            sl = (slice(bi, bi + 1), slice(hi, hi + 1))
+            ref = _oracle(q[sl].cpu().float(), k[sl].cpu().float(), v[sl].cpu().float(), dist, ang,
+                          pa[hi:hi + 1].cpu(), pb[hi:hi + 1].cpu(), pc[hi:hi + 1].cpu(), do[sl].cpu().float())
+            got = dict(output=o.detach()[sl], dQ=x[0].grad[sl], dK=x[1].grad[sl], dV=x[2].grad[sl])
+            for key, val in got.items():
+                assert torch.isfinite(val.float()).all(), (bi, hi, key)
+                e = rel_l2(val, ref[key])
+                assert e <= TOL[torch.bfloat16], (bi, hi, key, e)

@@ -80,3 +80,53 @@ def test_failed_rank_surfaces_as_error_on_peer():
     out = _run("fail")
     assert str(out[1]).startswith("error")
     assert str(out[0]).startswith("error")     # the peer's all-reduce ends with an error, not a hang
+
+
+def _count_worker(rank, world, port, skew, out):
+    """Each rank sizes a loop of collectives from its own (skewed) step-time estimate through `agreed_count`, then
+    runs it: every iteration is an all-reduce, as every replay of the benchmark's captured step is."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=10))
+    try:
+        from foreswe_gpu_optimization_b200.dp import agreed_count
+        est_ms = 0.775 * (1.0 + skew * rank)            # per-rank timings differ by a fraction of a percent
+        local = int(300.0 / est_ms) + 1                  # what a rank would pick on its own
+        n = agreed_count(est_ms, 0.3)
+        one = torch.ones(1)
+        issued = 0
+        for _ in range(n):
+            dist.all_reduce(one.clone())
+            issued += 1
+        counts = [torch.zeros(1, dtype=torch.int64) for _ in range(world)]
+        dist.all_gather(counts, torch.tensor([issued]))
+        out[rank] = (local, n, [int(c.item()) for c in counts])
+    except RuntimeError as e:
+        out[rank] = "error: " + str(e)[:80]
+    finally:
+        dist.destroy_process_group()
+
+
+def test_preroll_count_agreed_over_ranks_with_skewed_timings():
+    """Four CPU ranks whose own estimates would give different loop lengths issue the same number of collectives
+    once the count comes from `agreed_count` (the max estimate over the ranks)."""
+    world = 4
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as m:
+        out = m.dict()
+        port = _port()
+        procs = [ctx.Process(target=_count_worker, args=(r, world, port, 0.004, out)) for r in range(world)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(120)
+            assert p.exitcode is not None, "a rank did not exit"
+        res = dict(out)
+    assert all(isinstance(res[r], tuple) for r in range(world)), res
+    locals_ = {res[r][0] for r in range(world)}
+    assert len(locals_) > 1, "the skew must make the ranks' own counts differ, or the test shows nothing"
+    agreed = {res[r][1] for r in range(world)}
+    assert len(agreed) == 1, res
+    n = agreed.pop()
+    assert n == min(locals_)          # sized from the slowest rank's estimate
+    for r in range(world):
+        assert res[r][2] == [n] * world, res[r]

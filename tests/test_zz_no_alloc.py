@@ -3,7 +3,9 @@
 Plugin/custom-op hosts that own every device buffer (and code with a fixed memory plan) cannot hand the backward a
 workspace; geoattn_bwd_noalloc takes its scratch from a static device array inside the library instead. This test
 calls it through the C ABI twice in a row, on different inputs, and checks each result against geoattn_bwd (the
-entry point that takes a caller-allocated workspace) within the BF16 tolerance used by the other parity tests.
+entry point that takes a caller-allocated workspace) and against the float64 oracle, within the BF16 tolerance used
+by the other parity tests, at head dims 64, 128 and 192 (each a different tile configuration of the row pass's
+second sweep, which only this entry point runs in bf16).
 It lives in its own file, collected last, and passes alone in a fresh process as well as after the other tests.
 """
 import ctypes
@@ -57,22 +59,44 @@ def _backward(L, entry, sh, q, k, v, o, do, abg, prior, stats, nabg):
     return dict(dQ=dq.cpu(), dK=dk.cpu(), dV=dv.cpu(), dabg=dabg.cpu())
 
 
-def test_noalloc_backward_matches_workspace_backward_twice(L):
+def _oracle(q, k, v, lat, lon, el, a, b, c, do):
+    from helpers import dense_geometry
+    from oracle import geo_attention as oga
+    dist, ang = dense_geometry(lat, lon, el)
+    return oga.grads(*(t.cpu().double() for t in (q, k, v)), dist.double(), ang.double(), a, b, c, do.cpu().double())
+
+
+@pytest.mark.parametrize("per_head", [1, 0], ids=["per_head", "scalar"])
+@pytest.mark.parametrize("N,D", [(512, 64), (260, 64), (260, 128), (260, 192)])
+def test_noalloc_backward_matches_workspace_backward_twice(L, N, D, per_head):
+    """Two calls in a row (the static scratch keeps the previous call's contents) at every bf16 head-dim tile
+    configuration, a ragged station count and scalar or per-head parameters: each call's gradients are within the
+    BF16 tolerance of geoattn_bwd's and of the float64 oracle's, and the status word of the static scratch reads 0."""
     from foreswe_gpu_optimization_b200 import StationGeometry
-    B, H, N, D = 2, 4, 512, 64
-    lat, lon, el = stations(N, seed=31)
+    from foreswe_gpu_optimization_b200.geo_attention_v2 import read_status
+    B, H = 2, 3
+    lat, lon, el = stations(N, seed=31 + D)
     geom = StationGeometry(lat, lon, el)
     prior = geom.prior(torch.bfloat16)
-    for seed in (41, 42):   # two calls in a row; the static scratch keeps the previous call's contents
-        q, k, v, a, b, c, do = attn_inputs(B, H, N, D, seed=seed, qscale=3.0, dtype=torch.bfloat16)
+    for seed in (41, 42):
+        q, k, v, a, b, c, do = attn_inputs(B, H, N, D, seed=seed + D, qscale=3.0, per_head=bool(per_head),
+                                           dtype=torch.bfloat16)
         q, k, v, do = (t.cuda() for t in (q, k, v, do))
+        nabg = a.numel()
         abg = torch.cat([a, b, c]).cuda()
-        sh, o, stats = _forward(L, q, k, v, abg, prior, per_head=1)
-        ref = _backward(L, "geoattn_bwd", sh, q, k, v, o, do, abg, prior, stats, H)
-        got = _backward(L, "geoattn_bwd_noalloc", sh, q, k, v, o, do, abg, prior, stats, H)
+        sh, o, stats = _forward(L, q, k, v, abg, prior, per_head=per_head)
+        ref = _backward(L, "geoattn_bwd", sh, q, k, v, o, do, abg, prior, stats, nabg)
+        got = _backward(L, "geoattn_bwd_noalloc", sh, q, k, v, o, do, abg, prior, stats, nabg)
+        assert read_status(None) == 0
         for key in ref:
             assert torch.isfinite(got[key].float()).all(), key
             assert rel_l2(got[key], ref[key]) <= TOL, (seed, key, rel_l2(got[key], ref[key]))
+        gold = _oracle(q, k, v, lat, lon, el, a, b, c, do)
+        dabg = got["dabg"].view(3, nabg)
+        mine = dict(dQ=got["dQ"], dK=got["dK"], dV=got["dV"], dalpha=dabg[0], dbeta=dabg[1], dgamma=dabg[2])
+        for key, val in mine.items():
+            e = rel_l2(val, gold[key].reshape(val.shape))
+            assert e <= TOL, (seed, key, e)
 
 
 def test_noalloc_rejects_sizes_beyond_its_buffer(L):
