@@ -527,6 +527,23 @@ CONFIGS = (("c2_tf32", 32, 8, 512, 64, torch.float32, 1.0),
 REFERENCE_A100_D192 = {"triton_v2_accurate": [0.491, 1.930, 2.191], "eager_tf32": [0.332, 0.564, 0.857]}
 
 
+def reference_triton_v2():
+    """The reference's fused Triton v2 operator (foreswe_bench/geo_attention_v2.py) from its offline install in
+    baseline/_ref (baseline/install_reference.sh), with its default `accurate_experimental` preset; a string saying
+    why when it is not installed."""
+    ref = os.path.join(REPO, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref, "foreswe_bench")):
+        return "reference not installed in baseline/_ref (sh baseline/install_reference.sh <reference checkout>)"
+    if ref not in sys.path:
+        sys.path.append(ref)
+    try:
+        from foreswe_bench import geo_attention_v2 as v2
+    except Exception as exc:
+        return "import failed: %s: %s" % (type(exc).__name__, str(exc).splitlines()[0][:200])
+    v2.use_preset("accurate_experimental")
+    return v2
+
+
 def run_configs(args):
     """The other configurations of the path, one JSON line each: fwd, bwd and fwd+bwd ms of the kernels (coordinate
     prior, per-head alpha/beta/gamma, q/k/v ~ N(0,1) D^-1/4, dO ~ N(0,1)) and of eager PyTorch on the same GPU and
@@ -594,9 +611,23 @@ def run_configs(args):
 
         mine = triple(ours)
         ref = None if args.no_eager else triple(eager)
+        tri = None
+        if not args.no_triton and dtype == torch.float32:
+            v2 = reference_triton_v2()
+            if isinstance(v2, str):
+                tri = {"unavailable": v2}
+            else:
+                sc = [t[:1] for t in params]   # the Triton v2 op takes scalar alpha, beta, gamma (same work)
+                try:
+                    tri = triple(lambda: v2.fused_geo_attention_v2(x[0], x[1], x[2], dmat, amat, *sc))
+                    if tri is not None:
+                        tri["preset"] = "accurate_experimental"
+                        tri["speedup_ours_vs_triton_v2"] = tri["fwd_bwd"] / mine["fwd_bwd"]
+                except Exception as exc:   # a compile or launch error of the reference's kernel is reported
+                    tri = {"unavailable": "%s: %s" % (type(exc).__name__, str(exc).splitlines()[0][:200])}
         fl = 12.0 * b * h * n * n * d
         line = {"workload": name, "shape_bhnd": [b, h, n, d], "dtype": "bf16" if dtype == torch.bfloat16 else "fp32 (tf32)",
-                "steps": args.steps, "warmup": args.warmup, "ms": mine, "eager_ms": ref,
+                "steps": args.steps, "warmup": args.warmup, "ms": mine, "eager_ms": ref, "triton_v2_ms": tri,
                 "tflops": fl / (mine["fwd_bwd"] * 1e-3) / 1e12,
                 "speedup_vs_eager": (ref["fwd_bwd"] / mine["fwd_bwd"]) if ref else None,
                 "l2": "inputs %s L2 (q,k,v,dO = %.0f MB)" % ("larger than" if 4 * q.numel() * q.element_size() > 126e6
@@ -622,6 +653,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-eager", action="store_true")
     ap.add_argument("--no-step", action="store_true", help="skip the whole-step (projections + all-reduce) key")
+    ap.add_argument("--no-triton", action="store_true", help="configs: skip the reference's Triton v2 timing")
     ap.add_argument("--batch", type=int, default=None, help="override the global batch (small cases for profiling)")
     ap.add_argument("--only", default=None, choices=[c[0] for c in CONFIGS],
                     help="with --workload configs: run this configuration only")

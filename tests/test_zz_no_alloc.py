@@ -92,10 +92,20 @@ def test_noalloc_backward_matches_workspace_backward_twice(L, N, D, per_head):
             assert torch.isfinite(got[key].float()).all(), key
             assert rel_l2(got[key], ref[key]) <= TOL, (seed, key, rel_l2(got[key], ref[key]))
         gold = _oracle(q, k, v, lat, lon, el, a, b, c, do)
+        # a shared (scalar) parameter's gradient is a sum over the heads that can cancel (one draw here sums per-head
+        # terms of ~0.5 to -0.003): it is judged against the magnitude of the per-head terms, from the oracle with
+        # the parameter repeated per head
+        scale = {}
+        if nabg == 1:
+            ph = _oracle(q, k, v, lat, lon, el, a.repeat(H), b.repeat(H), c.repeat(H), do)
+            scale = {key: ph[key].abs().sum().item() for key in ("dalpha", "dbeta", "dgamma")}
         dabg = got["dabg"].view(3, nabg)
         mine = dict(dQ=got["dQ"], dK=got["dK"], dV=got["dV"], dalpha=dabg[0], dbeta=dabg[1], dgamma=dabg[2])
         for key, val in mine.items():
-            e = rel_l2(val, gold[key].reshape(val.shape))
+            ref_v = gold[key].reshape(val.shape)
+            e = rel_l2(val, ref_v)
+            if key in scale:
+                e = (val.double() - ref_v.double()).abs().max().item() / max(scale[key], ref_v.abs().max().item())
             assert e <= TOL, (seed, key, e)
 
 
