@@ -40,6 +40,15 @@ def flops(b):
     return 12.0 * b * H * N * N * D
 
 
+T_START = time.time()
+
+
+def phase(msg):
+    """One progress line per phase on stderr (rank-tagged), so a run that stops can be located from its log."""
+    print("[bench rank %s %.1fs] %s" % (os.environ.get("RANK", "0"), time.time() - T_START, msg), file=sys.stderr,
+          flush=True)
+
+
 def config(world):
     return {"workload": "geo-attn fwd+bwd, %d issue dates sharded over %d GPU(s), H=%d heads, N=%d stations, "
                         "D=%d, bf16, per-head alpha/beta/gamma, prior from station coordinates" % (B_TOTAL, world, H, N, D),
@@ -387,12 +396,12 @@ def run_c4(args):
 def measure_c5step(args, dev, rank, world, geom):
     """The scaling configuration's whole step on this rank's shard: x [B/world, N, 2048] -> W_qkv -> geo-attention
     (16 heads x 128, the kernels on strided views of the fused projection) -> W_o -> loss, forward and backward under
-    bf16 autocast with fp32 weights, and (N > 1) the NCCL all-reduce of dW_qkv, dW_o (67 MB fp32) and
-    d(alpha, beta, gamma), bucketed by DDP and overlapped with the backward.
+    bf16 autocast with fp32 weights, and (N > 1) one NCCL all-reduce of dW_qkv, dW_o (67 MB fp32) and
+    d(alpha, beta, gamma) after the backward.
 
-    Returns the max-over-ranks device times (CUDA events) of: the step as run (``ms_per_step``); the same step with
-    DDP's gradient all-reduce switched off (``compute_ms``, DDP ``no_sync``); and the all-reduce alone on a buffer of
-    the same payload (``allreduce_ms``). Every loop runs the same number of times on every rank."""
+    Returns the max-over-ranks device times (CUDA events) of: the step as run (``ms_per_step``); the same step without
+    the all-reduce (``compute_ms``); and the all-reduce alone (``allreduce_ms``). Every loop runs the same number of
+    times on every rank."""
     import torch.nn as nn
     import foreswe_gpu_optimization_b200 as g
     from foreswe_gpu_optimization_b200.dp import shard
@@ -421,20 +430,32 @@ def measure_c5step(args, dev, rank, world, geom):
 
     torch.manual_seed(0)
     model = Step().to(dev)
-    nsync = None
+    params = list(model.parameters())
+    # every parameter's gradient is a view of one flat fp32 buffer, all-reduced (averaged) in place in one NCCL call
+    # once the backward is done. An all-reduce overlapped with the backward (DDP's bucket hooks) competes for SMs
+    # with the persistent attention kernels, which hold every SM until they finish: its kernels then wait for SMs,
+    # and the next persistent kernel's last CTAs wait for them (measured: 1.37 ms exposed at 4 GPUs against 0.19 ms
+    # for the all-reduce alone).
+    flat = torch.zeros(sum(p.numel() for p in params), device=dev)
+    off = 0
+    for p_ in params:
+        p_.grad = flat[off:off + p_.numel()].view_as(p_)
+        off += p_.numel()
     if dist_on:
-        model = nn.parallel.DistributedDataParallel(model, device_ids=[dev.index], bucket_cap_mb=25)
-        nsync = model.no_sync
+        for p_ in params:                       # same initial weights on every rank
+            tdist.broadcast(p_.data, src=0)
     gen = torch.Generator(device=dev).manual_seed(100 + rank)
     x = torch.randn(b, N, dm, device=dev, generator=gen)
     target = torch.randn(b, N, dm, device=dev, generator=gen)
 
-    def step():
-        model.zero_grad(set_to_none=True)
+    def step(sync=True):
+        flat.zero_()
         with torch.autocast("cuda", dtype=torch.bfloat16):
             y = model(x)
         loss = torch.nn.functional.mse_loss(y.float(), target)
         loss.backward()
+        if dist_on and sync:
+            tdist.all_reduce(flat, op=tdist.ReduceOp.AVG)
         return loss
 
     def timed(fn):
@@ -455,16 +476,11 @@ def measure_c5step(args, dev, rank, world, geom):
     ms, loss = timed(step)
     comp_ms, ar_ms = ms, 0.0
     if dist_on:
-        def step_no_sync():
-            with nsync():
-                return step()
-        comp_ms, _ = timed(step_no_sync)
-        payload = torch.zeros(4 * dm * dm + 3 * H, device=dev)
+        comp_ms, _ = timed(lambda: step(sync=False))
 
         def allreduce():
-            tdist.all_reduce(payload)
+            tdist.all_reduce(flat, op=tdist.ReduceOp.AVG)
         ar_ms, _ = timed(allreduce)
-        del payload
         tt = torch.tensor([ms, comp_ms, ar_ms], device=dev, dtype=torch.float64)
         tdist.all_reduce(tt, op=tdist.ReduceOp.MAX)
         ms, comp_ms, ar_ms = tt.tolist()
@@ -473,14 +489,14 @@ def measure_c5step(args, dev, rank, world, geom):
     res = {"ms_per_step": ms, "tflops": (attn_flops + proj_flops) / (ms * 1e-3) / 1e12,
            "compute_ms": comp_ms, "allreduce_ms": ar_ms,
            "exposed_allreduce_ms": max(0.0, ms - comp_ms),
-           "allreduce_payload_mb": (4 * dm * dm + 3 * H) * 4 / 1e6,
            "attention_tflop_per_step": attn_flops / 1e12, "projection_tflop_per_step": proj_flops / 1e12,
            "per_gpu_batch": b, "loss": float(loss.item()),
-           "what": "x -> W_qkv -> geo-attention -> W_o -> MSE, fwd+bwd, bf16 autocast, fp32 weights; DDP all-reduce "
-                   "of dW_qkv, dW_o, d(alpha, beta, gamma) overlapped with the backward (N > 1); compute_ms = the same "
-                   "step under DDP no_sync; allreduce_ms = the payload's all-reduce alone; max over ranks"}
-    if dist_on:
-        del model
+           "allreduce_payload_mb": flat.numel() * 4 / 1e6,
+           "what": "x -> W_qkv -> geo-attention -> W_o -> MSE, fwd+bwd, bf16 autocast, fp32 weights; one NCCL "
+                   "all-reduce (average) of dW_qkv, dW_o, d(alpha, beta, gamma) from a flat gradient buffer after the "
+                   "backward (N > 1); compute_ms = the same step without it; allreduce_ms = that all-reduce alone; "
+                   "max over ranks"}
+    del model, flat, params
     torch.cuda.empty_cache()
     return res
 
@@ -505,7 +521,7 @@ def run_c5step(args):
                 "value": r["ms_per_step"], "unit": "ms/step", "higher_is_better": False, "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "dtype": "bf16 autocast (fp32 weights)", "data": "synthetic",
                 "config": {"workload": "%d issue dates sharded over %d GPU(s) x %d stations, d_model %d, %d heads x %d; "
-                                       "all-reduce of dW_qkv, dW_o (%.0f MB fp32) and d(alpha, beta, gamma) by DDP"
+                                       "all-reduce of dW_qkv, dW_o (%.0f MB fp32) and d(alpha, beta, gamma), one call after the backward"
                                        % (B_TOTAL, world, N, dm, H, D, 4 * dm * dm * 4 / 1e6),
                            "per_gpu_batch": r["per_gpu_batch"]},
                 "step_tflops": r["tflops"], "step": r}
@@ -712,6 +728,7 @@ def main():
         o.backward(dd)
         allreduce_bias_grads()
 
+    phase("inputs ready; warm-up")
     # warm-up
     for _ in range(args.warmup):
         step(x[0], x[1], x[2], do)
@@ -767,6 +784,7 @@ def main():
     # (N > 1), so the pre-roll length is agreed over the ranks (max of their estimates) before any rank starts it.
     from foreswe_gpu_optimization_b200.dp import agreed_count
     preroll = agreed_count(est_ms, 0.3, device=dev)
+    phase("graph=%s est %.3f ms/step, pre-roll %d steps" % (use_graph, est_ms, preroll))
     clocks = ClockSampler(range(world) if world > 1 else [local])
     if rank == 0:
         clocks.start()
@@ -784,6 +802,7 @@ def main():
     if dist_on:
         tdist.barrier()
     ms = t0.elapsed_time(t1) / args.steps
+    phase("timed region done: %.3f ms/step" % ms)
 
     # per-kernel times for the roofline: the same K steps run eagerly, with events the library records around each
     # kernel on its launching stream (one set per step)
@@ -813,6 +832,7 @@ def main():
     value = flops(B_TOTAL) / (ms * 1e-3) / 1e12
 
     # end to end through the public API: pinned host inputs copied in every step, bias gradients read back
+    phase("per-kernel pass done")
     e2e = None
     if not args.no_e2e:
         from foreswe_gpu_optimization_b200.streaming import HostBatchPipeline
@@ -849,7 +869,9 @@ def main():
         del hq, hk, hv, hd, pipe
 
     # the configuration's whole step (projections and their gradient all-reduce), every rank, at every N
+    phase("e2e done")
     stepm = None if args.no_step else measure_c5step(args, dev, rank, world, geom)
+    phase("whole step done")
 
     eager = None
     if not args.no_eager and rank == 0:
