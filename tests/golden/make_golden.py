@@ -87,6 +87,41 @@ def save_regression_norms():
         json.dump({"shape": [1, 4, 128, 192], "source": os.path.relpath(path, REF), "ref_norm": norms}, f, indent=1)
 
 
+def save_reference_mha():
+    """The reference's own MultiHeadAttention (fore_swe/custom_encoder_model.py:7-58), imported from its source file,
+    run forward and backward in float64 on seeded inputs: its parameters, inputs, output and every gradient, so a GPU
+    test can check that the patched call site reproduces the reference class's numbers."""
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("ref_custom_encoder_model",
+                                                  os.path.join(REF, "fore_swe", "custom_encoder_model.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    torch.manual_seed(2024)
+    B, N, d_model, heads = 2, 48, 64, 4
+    mha = mod.MultiHeadAttention(d_model, heads).double()
+    with torch.no_grad():                      # bias parameters in the trained model's range
+        mha.alpha.fill_(0.8)
+        mha.beta.fill_(0.3)
+        mha.gamma.fill_(-0.4)
+    g = torch.Generator().manual_seed(2025)
+    x = (torch.randn(B, N, d_model, generator=g, dtype=torch.float64) * 0.5).requires_grad_(True)
+    dist = torch.rand(N, N, generator=g, dtype=torch.float64) * 1500
+    dist = (dist + dist.T) / 2
+    dist.fill_diagonal_(0)
+    ang = torch.rand(N, N, generator=g, dtype=torch.float64) * 20
+    ang = (ang + ang.T) / 2
+    ang.fill_diagonal_(0)
+    gout = torch.randn(B, N, d_model, generator=g, dtype=torch.float64)
+    out = mha(x, x, x, dist, ang)
+    (out * gout).sum().backward()
+    arrays = {"x": x.detach().numpy(), "dist": dist.numpy(), "ang": ang.numpy(), "gout": gout.numpy(),
+              "out": out.detach().numpy(), "grad_x": x.grad.numpy(), "heads": np.array(heads)}
+    for name, prm in mha.named_parameters():
+        arrays["param." + name] = prm.detach().numpy()
+        arrays["grad." + name] = prm.grad.numpy()
+    np.savez_compressed(os.path.join(HERE, "mha_reference.npz"), **arrays)
+
+
 def main():
     torch.manual_seed(0)
     cases = [("random", 1, 2, 32, 16, 0), ("near_one_hot", 1, 2, 33, 16, 1), ("uniform", 1, 1, 16, 8, 2),
@@ -137,6 +172,7 @@ def main():
     vec[2] = -vec[0]                                       # antiparallel pair -> pi
     np.savez_compressed(os.path.join(HERE, "kahan.npz"), vectors=vec, angle=ns["pairwise_vector_angle"](vec))
     save_regression_norms()
+    save_reference_mha()
     print("golden vectors written to", HERE)
 
 

@@ -1,6 +1,9 @@
 """Shared helpers for the parity tests: seeded inputs in the configurations' distributions and error metrics."""
+import math
+
 import numpy as np
 import torch
+import torch.nn as nn
 
 from oracle import geometry as ogeo
 
@@ -52,3 +55,44 @@ def run_device(fn, q, k, v, a, b, c, do, **kw):
     torch.cuda.synchronize()
     return dict(output=o.detach().cpu(), dQ=x[0].grad.cpu(), dK=x[1].grad.cpu(), dV=x[2].grad.cpu(),
                 dalpha=x[3].grad.cpu(), dbeta=x[4].grad.cpu(), dgamma=x[5].grad.cpu())
+
+
+class MHA(nn.Module):
+    """Minimal module with the reference's attention call site (custom_encoder_model.py:7-58): W_q/W_k/W_v
+    projections, split_heads views, the attention core, combine_heads, W_o."""
+
+    def __init__(self, d_model, heads):
+        super().__init__()
+        self.d_model, self.num_heads, self.d_k = d_model, heads, d_model // heads
+        self.alpha, self.beta, self.gamma = (nn.Parameter(torch.tensor([x])) for x in (0.7, 0.4, -0.3))
+        self.W_q, self.W_k, self.W_v, self.W_o = (nn.Linear(d_model, d_model) for _ in range(4))
+
+    def scaled_dot_product_attention(self, Q, K, V, distances, angularities, mask=None):
+        s = torch.softmax(torch.matmul(Q, K.transpose(-2, -1)) / math.sqrt(self.d_k), dim=-1)
+        z = self.alpha * s + self.beta / (1 + distances) + self.gamma / (1 + angularities)
+        return torch.matmul(torch.softmax(z, dim=-1), V)
+
+    def split_heads(self, x):
+        B, N, _ = x.size()
+        return x.view(B, N, self.num_heads, self.d_k).transpose(1, 2)
+
+    def combine_heads(self, x):
+        B, _, N, _ = x.size()
+        return x.transpose(1, 2).contiguous().view(B, N, self.d_model)
+
+    def forward(self, x, distances, angularities):
+        Q, K, V = (self.split_heads(w(x)) for w in (self.W_q, self.W_k, self.W_v))
+        return self.W_o(self.combine_heads(self.scaled_dot_product_attention(Q, K, V, distances, angularities)))
+
+
+class Encoder(nn.Module):
+    def __init__(self, d_model, heads, layers):
+        super().__init__()
+        self.encoder_layers = nn.ModuleList(nn.Module() for _ in range(layers))
+        for layer in self.encoder_layers:
+            layer.self_attn = MHA(d_model, heads)
+
+    def forward(self, x, d, a):
+        for layer in self.encoder_layers:
+            x = x + layer.self_attn(x, d, a)
+        return x
