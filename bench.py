@@ -167,6 +167,21 @@ def cpu_reference(seconds, threads):
     return flops(1) * reps / el_s / 1e12, reps, el_s
 
 
+def peak_extra_memory(fn, dev):
+    """Peak device memory one fwd+bwd allocates beyond what is live before it (inputs, dO, parameters), as the
+    reference reports for its operators: MiB, from the caching allocator's peak counter."""
+    torch.cuda.synchronize(dev)
+    base = torch.cuda.memory_allocated(dev)
+    torch.cuda.reset_peak_memory_stats(dev)
+    fn()
+    torch.cuda.synchronize(dev)
+    peak = torch.cuda.max_memory_allocated(dev)
+    return {"peak_extra_mib": (peak - base) / 2 ** 20,
+            "what": "peak allocated during one fwd+bwd minus the memory live before it (q, k, v, dO, parameters, "
+                    "prior); outputs, gradients, row statistics and the backward workspace (with the bf16 dS scratch) "
+                    "included"}
+
+
 def gpu_eager_ms(q, k, v, do, dist, ang, a, b, c, steps):
     """Eager PyTorch on the same GPU and inputs (bf16 storage; the reference's op written with torch ops)."""
     def op(q, k, v):
@@ -625,8 +640,20 @@ def run_configs(args):
                 torch.cuda.empty_cache()
                 return None
 
+        def mem_of(fn):
+            def once():
+                for t in x + params:
+                    t.grad = None
+                fn().backward(do)
+            try:
+                return round(peak_extra_memory(once, dev)["peak_extra_mib"], 1)
+            except torch.OutOfMemoryError:
+                torch.cuda.empty_cache()
+                return None
+
         mine = triple(ours)
         ref = None if args.no_eager else triple(eager)
+        mem = {"ours": mem_of(ours), "eager": None if args.no_eager else mem_of(eager)}
         tri = None
         if not args.no_triton and dtype == torch.float32:
             v2 = reference_triton_v2()
@@ -639,11 +666,14 @@ def run_configs(args):
                     if tri is not None:
                         tri["preset"] = "accurate_experimental"
                         tri["speedup_ours_vs_triton_v2"] = tri["fwd_bwd"] / mine["fwd_bwd"]
+                        mem["triton_v2"] = mem_of(lambda: v2.fused_geo_attention_v2(x[0], x[1], x[2], dmat, amat,
+                                                                                    *sc))
                 except Exception as exc:   # a compile or launch error of the reference's kernel is reported
                     tri = {"unavailable": "%s: %s" % (type(exc).__name__, str(exc).splitlines()[0][:200])}
         fl = 12.0 * b * h * n * n * d
         line = {"workload": name, "shape_bhnd": [b, h, n, d], "dtype": "bf16" if dtype == torch.bfloat16 else "fp32 (tf32)",
                 "steps": args.steps, "warmup": args.warmup, "ms": mine, "eager_ms": ref, "triton_v2_ms": tri,
+                "peak_extra_mib_fwd_bwd": mem,
                 "tflops": fl / (mine["fwd_bwd"] * 1e-3) / 1e12,
                 "speedup_vs_eager": (ref["fwd_bwd"] / mine["fwd_bwd"]) if ref else None,
                 "l2": "inputs %s L2 (q,k,v,dO = %.0f MB)" % ("larger than" if 4 * q.numel() * q.element_size() > 126e6
@@ -733,6 +763,7 @@ def main():
     for _ in range(args.warmup):
         step(x[0], x[1], x[2], do)
     torch.cuda.synchronize()
+    mem = peak_extra_memory(lambda: step(x[0], x[1], x[2], do), dev)
 
     # The step (fwd + bwd and, for N > 1, the bias-gradient all-reduce) captured as one CUDA graph: the timed region
     # replays it, so host-side launch work (autograd, argument packing) does not pace the GPU at small shards.
@@ -907,7 +938,7 @@ def main():
                           + "; per-kernel times from K eager steps with library events",
                 "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": config(world),
                 "tensor_peak_frac": value / world / pk, "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
-                "gpu_eager": eager, "step": stepm, "gpu_launches": 5 * args.steps, "clocks": clk}
+                "gpu_eager": eager, "step": stepm, "memory": mem, "gpu_launches": 5 * args.steps, "clocks": clk}
         print(json.dumps(line), flush=True)
     if dist_on:
         tdist.barrier()

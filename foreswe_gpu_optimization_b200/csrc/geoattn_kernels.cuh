@@ -547,9 +547,14 @@ struct FwdCfg : Tile<BF16, DP> {
   // covers a pair of 32-key chunks (N = 64: half the instructions). Q lands by TMA in a shared-memory pool that,
   // once copied into tensor memory, holds the ring of K chunk pairs; the landing takes the ring's next NK positions.
   // Wide fp32 issues its score MMAs over chunk pairs too: each slot carries a head-dim chunk of Q and of two K chunks.
-  static constexpr bool POOL = !BF16 && !WIDE;
+  // bf16 up to head dim 128 pools too: Q takes 32 / 64 tensor-memory columns, and a score MMA over a pair of 64-key
+  // chunks (N = 128) runs at the tensor pipe's full rate, where an N = 64 MMA with both operands in shared memory
+  // takes 48 cycles for 32 cycles of work (measured back to back on the B200). Head dim 192 keeps Q in shared memory
+  // (4 score buffers + O + Q would need 544 columns).
+  static constexpr bool POOL = !WIDE && (!BF16 || DP <= 128);
   static constexpr int PAIR = (POOL || WIDE) ? 2 : 1;                 // chunks per score MMA / K ring slot
-  static constexpr int NK = (POOL || DP <= 128) ? 3 : 2;   // K ring slots
+  // pooled bf16 at head dim 128: two pair slots (64 KB; a third would take the shared memory past the limit)
+  static constexpr int NK = POOL ? ((BF16 && DP > 64) ? 2 : 3) : (DP <= 128 ? 3 : 2);   // K ring slots
   static constexpr int LAND = POOL ? NK : 0;                          // ring positions the Q landing takes
   static constexpr int Q_BYTES = WIDE ? 0 : kBM * DP * T::EB;          // per plane
   static constexpr int K_BYTES = WIDE ? kSlotPlaneBytesRows<PAIR * T::CH> : PAIR * T::CH * DP * T::EB;  // per plane
@@ -1983,6 +1988,37 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       ew_sync(T::EWT);
     }
     float gbp[2] = {0.f, 0.f}, ggp[2] = {0.f, 0.f};  // with SDS: this key's d(beta), d(gamma) partials
+    // P2 and dS of one 32-column piece from its scores S^T, dP^T, the chunk's row records and the prior; keys past N
+    // (last block only) produce rows of P2^T / dS^T that only reach dK/dV rows that are never stored, so no per-key
+    // mask is needed
+    auto piece_math = [&](const float* rec, int piece, const uint32_t (&vs)[32], const uint32_t (&ws)[32],
+                          const Prior32<BF16>& pr, float (&v)[32], float (&w)[32]) {
+#pragma unroll
+      for (int j4 = 0; j4 < 32; j4 += 4) {
+        const int q = piece * 32 + j4;
+        const float4 m4 = *reinterpret_cast<const float4*>(rec + q);
+        const float4 c4 = *reinterpret_cast<const float4*>(rec + T::CH + q);
+        const float4 d1 = *reinterpret_cast<const float4*>(rec + 2 * T::CH + q);
+        const float4 d2 = *reinterpret_cast<const float4*>(rec + 3 * T::CH + q);
+        const float mm[4] = {m4.x, m4.y, m4.z, m4.w}, cc[4] = {c4.x, c4.y, c4.z, c4.w};
+        const float e1[4] = {d1.x, d1.y, d1.z, d1.w}, e2[4] = {d2.x, d2.y, d2.z, d2.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int j = j4 + k;
+          float dpj, apj;
+          pr.get(j, dpj, apj);
+          const float p1 = ex2(fmaf(__uint_as_float(vs[j]), sc_l2, -mm[k]));
+          const float p2 = ex2(fmaf(aL, p1, fmaf(bL, dpj, fmaf(gL, apj, -cc[k]))));
+          const float dz = p2 * (__uint_as_float(ws[j]) - e2[k]);
+          v[j] = p2;
+          w[j] = p1 * fmaf(ab.a, dz, -e1[k]);
+          if constexpr (SDS) {
+            gbp[k & 1] = fmaf(dz, dpj, gbp[k & 1]);
+            ggp[k & 1] = fmaf(dz, apj, ggp[k & 1]);
+          }
+        }
+      }
+    };
     for (int c = 0; c < nch; ++c) {
       const int gc = it * nch + c;
       const int ss = gc % NSB, rs = gc % NR, ts = gc % NST;
@@ -2015,33 +2051,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         tc_fence_before();
         mbar_arrive(&bar_sempty[ss]);  // the scores are in registers: the MMA may refill the buffer
         float v[32], w[32];
-        // keys past N (last block only) produce rows of P2^T / dS^T that only reach dK/dV rows that are never
-        // stored, so no per-key mask is needed
-#pragma unroll
-        for (int j4 = 0; j4 < 32; j4 += 4) {
-          const int q = piece * 32 + j4;
-          const float4 m4 = *reinterpret_cast<const float4*>(rec + q);
-          const float4 c4 = *reinterpret_cast<const float4*>(rec + T::CH + q);
-          const float4 d1 = *reinterpret_cast<const float4*>(rec + 2 * T::CH + q);
-          const float4 d2 = *reinterpret_cast<const float4*>(rec + 3 * T::CH + q);
-          const float mm[4] = {m4.x, m4.y, m4.z, m4.w}, cc[4] = {c4.x, c4.y, c4.z, c4.w};
-          const float e1[4] = {d1.x, d1.y, d1.z, d1.w}, e2[4] = {d2.x, d2.y, d2.z, d2.w};
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const int j = j4 + k;
-            float dpj, apj;
-            pr.get(j, dpj, apj);
-            const float p1 = ex2(fmaf(__uint_as_float(vs[j]), sc_l2, -mm[k]));
-            const float p2 = ex2(fmaf(aL, p1, fmaf(bL, dpj, fmaf(gL, apj, -cc[k]))));
-            const float dz = p2 * (__uint_as_float(ws[j]) - e2[k]);
-            v[j] = p2;
-            w[j] = p1 * fmaf(ab.a, dz, -e1[k]);
-            if constexpr (SDS) {
-              gbp[k & 1] = fmaf(dz, dpj, gbp[k & 1]);
-              ggp[k & 1] = fmaf(dz, apj, ggp[k & 1]);
-            }
-          }
-        }
+        piece_math(rec, piece, vs, ws, pr, v, w);
         mbar_arrive(&bar_recempty[rs]);  // the records and the prior tile are read and used
         if constexpr (NPR > 0) mbar_arrive(&bar_prempty[gc % NPR]);
         // the staging tiles are free once the previous chunk's dV/dK MMAs have run (waited here, after the math)

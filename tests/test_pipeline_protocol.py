@@ -13,7 +13,7 @@ a bounded-wait timeout or as results that differ between runs, so their arithmet
 * the wide key pass with query-chunk pairs: a chunk's records load before the next pair's slots;
 * the BF16 key pass's dS^T scratch stores trail the query-chunk loads by at most NQ + NST - 1 chunks;
 * the BF16 forward over several tiles: pass B's V loads may lag the K loads by 1 ... NSB + NK - 1 chunks (the kernel
-  uses NSB - 1).
+  uses NSB - 1); with Q in tensor memory and K in a ring of chunk pairs (head dims up to 128) by 0 ... NSB + 2 NK - 2.
 """
 import pytest
 
@@ -539,3 +539,134 @@ def test_forward_bf16_v_lag_range(D):
         assert all(_forward_bf16_order(n, 3, nk, npr, vlag) is None for n in sizes), vlag
     assert _forward_bf16_order(16, 3, nk, npr, 0) is not None
     assert _forward_bf16_order(16, 3, nk, npr, NSB + nk) is not None
+
+
+def _forward_pooled_bf16_order(nch, n_tiles, nk, npr, vlag, nsb=NSB):
+    """The pooled BF16 forward (geoattn_fwd_kernel<true, DP <= 128>) over several tiles as four cooperating programs;
+    returns None or the deadlock state.
+
+    Q lands in the shared-memory pool that otherwise holds the ring of K chunk pairs (nk pair slots): the landing
+    takes the ring's next nk positions (each waits for the release of its previous use), the MMA warp copies Q into
+    tensor memory, drains the copies through the next score buffer (which must be free) and releases the nk
+    positions. Each score MMA covers a pair of chunks into two adjacent score buffers (both free) and releases its K
+    pair's ring position. Pass B loads V of chunk cc - vlag after the K pair holding cc (two V buffers, each freed by
+    its P.V MMA); the MMA warp keeps pass B's scores up to nsb chunks ahead of the P.V MMAs. Prior loader and
+    element-wise warps as in the unpooled model."""
+    st = dict(pos=0, released=0, q_loaded=0, pairs_loaded=0, pairs_used=0, v_loaded=0, pv=0, pr_loaded=0,
+              pr_released=0, s_issued=0, s_released=0, p_staged=0, ofull=0)
+
+    def take_position():
+        yield lambda p=st["pos"]: st["released"] >= p + 1 - nk
+        st["pos"] += 1
+
+    def tma():
+        for it in range(n_tiles):
+            for _ in range(nk):                                   # the Q landing takes every slot once
+                yield lambda p=st["pos"]: st["released"] >= p + 1 - nk
+                st["pos"] += 1
+            st["q_loaded"] = it + 1
+            vbase = it * nch
+
+            def load_v(cv):
+                yield lambda: st["pv"] >= vbase + cv - 1          # V buffer of chunk cv - 2 free
+                st["v_loaded"] = vbase + cv + 1
+
+            for pass_ in range(2):
+                for c in range(0, nch, PAIR):
+                    yield lambda p=st["pos"]: st["released"] >= p + 1 - nk
+                    st["pos"] += 1
+                    st["pairs_loaded"] += 1
+                    if pass_ == 1:
+                        for cc in range(c, c + PAIR):
+                            if cc >= vlag:
+                                yield from load_v(cc - vlag)
+                if pass_ == 1:
+                    for cv in range(max(0, nch - vlag), nch):
+                        yield from load_v(cv)
+
+    def prior():
+        for g in range(n_tiles * nch):
+            yield lambda g=g: st["pr_released"] >= g + 1 - npr
+            st["pr_loaded"] = g + 1
+
+    def mma():
+        def issue():
+            yield lambda: (st["pairs_loaded"] >= st["pairs_used"] + 1
+                           and st["s_released"] >= st["s_issued"] + PAIR - nsb)
+            st["pairs_used"] += 1
+            st["s_issued"] += PAIR
+            st["released"] += 1                                   # the pair's ring position, after its MMA
+
+        for it in range(n_tiles):
+            yield lambda it=it: st["q_loaded"] >= it + 1
+            yield lambda: st["s_released"] >= st["s_issued"] + 1 - nsb   # drain buffer free
+            st["released"] += nk                                   # the landing's positions
+            for _ in range(0, nch, PAIR):
+                yield from issue()
+            nb = 0
+            for c in range(nch):
+                while nb < nch and nb + PAIR - 1 < c + nsb:
+                    yield from issue()
+                    nb += PAIR
+                g = it * nch + c
+                yield lambda g=g: st["p_staged"] >= g + 1 and st["v_loaded"] >= g + 1
+                st["pv"] = g + 1
+            st["ofull"] = it + 1
+
+    def ew():
+        s = 0
+        for it in range(n_tiles):
+            for c in range(0, nch, 2):
+                yield lambda s=s: st["s_issued"] >= s + 2
+                s += 2
+                st["s_released"] = s
+            for c in range(nch):
+                g = it * nch + c
+                yield lambda s=s, g=g: st["s_issued"] >= s + 1 and st["pr_loaded"] >= g + 1
+                s += 1
+                st["s_released"] = s
+                st["pr_released"] = g + 1
+                yield lambda g=g: st["pv"] >= g - 1
+                st["p_staged"] = g + 1
+            yield lambda it=it: st["ofull"] >= it + 1
+
+    progs = [tma(), prior(), mma(), ew()]
+    waits = [next(p) for p in progs]
+    done = [False] * len(progs)
+    while not all(done):
+        moved = False
+        for i, prog in enumerate(progs):
+            while not done[i] and waits[i]():
+                try:
+                    waits[i] = next(prog)
+                except StopIteration:
+                    done[i] = True
+                moved = True
+        if not moved:
+            return dict(st)
+    return None
+
+
+# FwdCfg<true, DP> pooled (DP <= 128): (NK pair slots, NPR); V loads lag the K loads by NSB - 1 chunks
+BF16_POOLED_FWD = {64: (3, 2), 128: (2, 2)}
+
+
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("nch", [2, 4, 6, 8, 16])
+def test_forward_pooled_bf16_order_has_no_deadlock(D, nch):
+    nk, npr = BF16_POOLED_FWD[D]
+    assert _forward_pooled_bf16_order(nch, 3, nk, npr, NSB - 1) is None
+
+
+@pytest.mark.parametrize("D", [64, 128])
+def test_forward_pooled_bf16_v_lag_range(D):
+    """Pass B's V(c) follows the K pair holding chunk c + VLAG, whose ring slot was last used by the pair NK pairs
+    earlier and is free once that pair's score MMA is issued, i.e. once chunk c + VLAG - PAIR * NK + 1 < c + NSB is in
+    flight: VLAG <= NSB + PAIR * NK - 2. Every lag from 0 to that bound runs (the kernel uses NSB - 1); the next one
+    stops (the planted mistake is caught)."""
+    nk, npr = BF16_POOLED_FWD[D]
+    bound = NSB + PAIR * nk - 2
+    sizes = (2, 4, 8, 16)
+    for vlag in range(0, bound + 1):
+        assert all(_forward_pooled_bf16_order(n, 3, nk, npr, vlag) is None for n in sizes), vlag
+    assert _forward_pooled_bf16_order(16, 3, nk, npr, bound + 1) is not None
