@@ -700,6 +700,8 @@ def main():
     ap.add_argument("--no-eager", action="store_true")
     ap.add_argument("--no-step", action="store_true", help="skip the whole-step (projections + all-reduce) key")
     ap.add_argument("--no-triton", action="store_true", help="configs: skip the reference's Triton v2 timing")
+    ap.add_argument("--preroll-seconds", type=float, default=0.3,
+                    help="busy pre-roll before the timed region (0 for short profiling runs)")
     ap.add_argument("--batch", type=int, default=None, help="override the global batch (small cases for profiling)")
     ap.add_argument("--only", default=None, choices=[c[0] for c in CONFIGS],
                     help="with --workload configs: run this configuration only")
@@ -814,7 +816,7 @@ def main():
     # all the same workload, so even a short timed region has samples under load. Every step holds an all-reduce
     # (N > 1), so the pre-roll length is agreed over the ranks (max of their estimates) before any rank starts it.
     from foreswe_gpu_optimization_b200.dp import agreed_count
-    preroll = agreed_count(est_ms, 0.3, device=dev)
+    preroll = agreed_count(est_ms, args.preroll_seconds, device=dev) if args.preroll_seconds > 0 else 0
     phase("graph=%s est %.3f ms/step, pre-roll %d steps" % (use_graph, est_ms, preroll))
     clocks = ClockSampler(range(world) if world > 1 else [local])
     if rank == 0:
