@@ -951,7 +951,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
           uint32_t vs[32];
           float v[32];
           tmem_ld32_issue(e.lane_base + C::TM_S + ss * T::CH + piece * 32, vs);
-          if constexpr (NPR > 0) prior32_smem<BF16>(prt, e.r, piece, pr);  // overlaps the tensor-memory load
+          if constexpr (NPR > 0 && !BF16) prior32_smem<BF16>(prt, e.r, piece, pr);  // overlaps the tensor-memory load
           tmem_wait32(vs);
           tc_fence_before();
           mbar_arrive(&bar_sempty[ss]);  // the scores are in registers: the MMA may refill the buffer
@@ -962,10 +962,25 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
             float p1[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) p1[j] = ex2(fmaf(__uint_as_float(vs[j]), sc_l2, -m1));
+            // bf16 staged prior: four pairs per 16-byte shared-memory load next to their use (no 32-register copy)
+            [[maybe_unused]] uint32_t pw[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
               float dpj, apj;
-              pr.get(j, dpj, apj);
+              if constexpr (BF16 && NPR > 0) {
+                if ((j & 3) == 0) {
+                  const uint4 u = *reinterpret_cast<const uint4*>(prt + piece * (kBM * 128) + sw128(e.r, j / 4));
+                  pw[0] = u.x;
+                  pw[1] = u.y;
+                  pw[2] = u.z;
+                  pw[3] = u.w;
+                }
+                const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&pw[j & 3]));
+                dpj = f.x;
+                apj = f.y;
+              } else {
+                pr.get(j, dpj, apj);
+              }
               float ev = ex2(fmaf(aL, p1[j], fmaf(bL, dpj, fmaf(gL, apj, -cL))));
               if constexpr (decltype(masked)::value) ev = (j < nvalid) ? ev : 0.f;
               l24[j & 3] += ev;
@@ -1426,7 +1441,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         tmem_ld32_issue(e.lane_base + C::TM_S + ss * T::CH + piece * 32, vs);
         tmem_ld32_issue(e.lane_base + C::TM_DP + ss * T::CH + piece * 32, ws);
         const int nvalid = p.N - (c * T::CH + piece * 32);
-        if constexpr (NPR > 0) prior32_smem<BF16>(prt, e.r, piece, pr);
+        if constexpr (NPR > 0 && !BF16) prior32_smem<BF16>(prt, e.r, piece, pr);
         tmem_wait32(vs);
         tmem_pin32(ws);
         tc_fence_before();
@@ -1439,10 +1454,25 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
             p1[j] = ex2(fmaf(__uint_as_float(vs[j]), sc_l2, -m1));
             if constexpr (decltype(masked)::value) p1[j] = (j < nvalid) ? p1[j] : 0.f;
           }
+          // bf16 staged prior: four pairs per 16-byte shared-memory load next to their use (no 32-register copy)
+          [[maybe_unused]] uint32_t pw[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             float dpj, apj;
-            pr.get(j, dpj, apj);
+            if constexpr (BF16 && NPR > 0) {
+              if ((j & 3) == 0) {
+                const uint4 u = *reinterpret_cast<const uint4*>(prt + piece * (kBM * 128) + sw128(e.r, j / 4));
+                pw[0] = u.x;
+                pw[1] = u.y;
+                pw[2] = u.z;
+                pw[3] = u.w;
+              }
+              const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&pw[j & 3]));
+              dpj = f.x;
+              apj = f.y;
+            } else {
+              pr.get(j, dpj, apj);
+            }
             float p2 = ex2(fmaf(aL, p1[j], fmaf(bL, dpj, fmaf(gL, apj, -c2))));
             if constexpr (decltype(masked)::value) p2 = (j < nvalid) ? p2 : 0.f;
             const float wv = p2 * __uint_as_float(ws[j]);
@@ -1991,8 +2021,10 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
     // P2 and dS of one 32-column piece from its scores S^T, dP^T, the chunk's row records and the prior; keys past N
     // (last block only) produce rows of P2^T / dS^T that only reach dK/dV rows that are never stored, so no per-key
     // mask is needed
+    // (bf16, staged prior tile `prt`: each group of four pairs is read from shared memory next to its use, one
+    // 16-byte load, instead of 32 registers of pairs held across the piece)
     auto piece_math = [&](const float* rec, int piece, const uint32_t (&vs)[32], const uint32_t (&ws)[32],
-                          const Prior32<BF16>& pr, float (&v)[32], float (&w)[32]) {
+                          const Prior32<BF16>& pr, const uint8_t* prt, float (&v)[32], float (&w)[32]) {
 #pragma unroll
       for (int j4 = 0; j4 < 32; j4 += 4) {
         const int q = piece * 32 + j4;
@@ -2002,11 +2034,25 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         const float4 d2 = *reinterpret_cast<const float4*>(rec + 3 * T::CH + q);
         const float mm[4] = {m4.x, m4.y, m4.z, m4.w}, cc[4] = {c4.x, c4.y, c4.z, c4.w};
         const float e1[4] = {d1.x, d1.y, d1.z, d1.w}, e2[4] = {d2.x, d2.y, d2.z, d2.w};
+        [[maybe_unused]] uint32_t pw[4] = {0u, 0u, 0u, 0u};
+        if constexpr (BF16 && NPR > 0) {
+          const uint4 u = *reinterpret_cast<const uint4*>(prt + piece * (kBM * 128) + sw128(e.r, j4 / 4));
+          pw[0] = u.x;
+          pw[1] = u.y;
+          pw[2] = u.z;
+          pw[3] = u.w;
+        }
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
           const int j = j4 + k;
           float dpj, apj;
-          pr.get(j, dpj, apj);
+          if constexpr (BF16 && NPR > 0) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&pw[k]));
+            dpj = f.x;
+            apj = f.y;
+          } else {
+            pr.get(j, dpj, apj);
+          }
           const float p1 = ex2(fmaf(__uint_as_float(vs[j]), sc_l2, -mm[k]));
           const float p2 = ex2(fmaf(aL, p1, fmaf(bL, dpj, fmaf(gL, apj, -cc[k]))));
           const float dz = p2 * (__uint_as_float(ws[j]) - e2[k]);
@@ -2045,13 +2091,12 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         uint32_t vs[32], ws[32];
         tmem_ld32_issue(e.lane_base + C::TM_S + ss * T::CH + piece * 32, vs);
         tmem_ld32_issue(e.lane_base + C::TM_DP + ss * T::CH + piece * 32, ws);
-        if constexpr (NPR > 0) prior32_smem<BF16>(prt, e.r, piece, pr);
         tmem_wait32(vs);
         tmem_pin32(ws);
         tc_fence_before();
         mbar_arrive(&bar_sempty[ss]);  // the scores are in registers: the MMA may refill the buffer
         float v[32], w[32];
-        piece_math(rec, piece, vs, ws, pr, v, w);
+        piece_math(rec, piece, vs, ws, pr, prt, v, w);
         mbar_arrive(&bar_recempty[rs]);  // the records and the prior tile are read and used
         if constexpr (NPR > 0) mbar_arrive(&bar_prempty[gc % NPR]);
         // the staging tiles are free once the previous chunk's dV/dK MMAs have run (waited here, after the math)
