@@ -150,6 +150,39 @@ __global__ void split_tf32_kernel(const float* __restrict__ x, long long s0, lon
   for (int k = threadIdx.y; k < 32; k += 8) tr[((size_t)bh * DP + d0 + k) * NP + n0 + tx] = tile[tx][k];
 }
 
+// The same split with 16-byte accesses, for a tensor whose head dim is contiguous (stride 1) and whose other strides,
+// base address and D are multiples of 4 elements (every operand of a torch-allocated fp32 tensor with D % 4 == 0).
+// Thread t of 256 loads 4 consecutive d of one row (tile 32 rows x 32 d), writes both natural planes as float4, and
+// the transposed hi plane leaves through a [d][n] shared-memory tile as float4 along n.
+__global__ void __launch_bounds__(256) split_tf32_vec_kernel(const float* __restrict__ x, long long s0, long long s1,
+                                                             long long s2, int B, int H, int N, int D, int DP, int NP,
+                                                             float* nat, float* tr) {
+  __shared__ float tile[32][33];
+  const int bh = blockIdx.z, b = bh / H, h = bh % H;
+  const int n0 = blockIdx.x * 32, d0 = blockIdx.y * 32, t = threadIdx.x;
+  const int r = t >> 3, d = d0 + 4 * (t & 7), n = n0 + r;
+  float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (n < N && d < D) v = *reinterpret_cast<const float4*>(x + b * s0 + h * s1 + (long long)n * s2 + d);
+  const float4 hi = make_float4(round_tf32(v.x), round_tf32(v.y), round_tf32(v.z), round_tf32(v.w));
+  if (nat && n < N) {
+    const size_t o = ((size_t)bh * N + n) * DP + d;
+    const float4 lo = make_float4(round_tf32(v.x - hi.x), round_tf32(v.y - hi.y), round_tf32(v.z - hi.z),
+                                  round_tf32(v.w - hi.w));
+    *reinterpret_cast<float4*>(nat + o) = hi;
+    *reinterpret_cast<float4*>(nat + (size_t)B * H * N * DP + o) = lo;
+  }
+  if (!tr) return;
+  const int dl = d - d0;
+  tile[dl][r] = hi.x;
+  tile[dl + 1][r] = hi.y;
+  tile[dl + 2][r] = hi.z;
+  tile[dl + 3][r] = hi.w;
+  __syncthreads();
+  const int dd = t >> 3, nq = 4 * (t & 7);
+  *reinterpret_cast<float4*>(tr + ((size_t)bh * DP + d0 + dd) * NP + n0 + nq) =
+      make_float4(tile[dd][nq], tile[dd][nq + 1], tile[dd][nq + 2], tile[dd][nq + 3]);
+}
+
 // ---------------------------------------------------------------------------------------------------------------
 // d(alpha), d(beta), d(gamma): fixed-order float64 sum of the per-(b*h, row block) partials.
 // ---------------------------------------------------------------------------------------------------------------
@@ -347,9 +380,17 @@ int map_prior(CUtensorMap* m, const void* table, const Dims& d) {
 
 int split(const GeoAttnTensor& t, const Dims& d, float* nat, float* tr, cudaStream_t st) {
   if (!t.data) return GEOATTN_ERR_INVALID;
-  dim3 grid((d.np + 31) / 32, d.DP / 32, d.B * d.H), block(32, 8);
-  split_tf32_kernel<<<grid, block, 0, st>>>(reinterpret_cast<const float*>(t.data), t.stride[0], t.stride[1],
-                                            t.stride[2], t.stride[3], d.B, d.H, d.N, d.D, d.DP, d.np, nat, tr);
+  const bool vec = t.stride[3] == 1 && (reinterpret_cast<uintptr_t>(t.data) & 15) == 0 && d.D % 4 == 0 &&
+                   t.stride[0] % 4 == 0 && t.stride[1] % 4 == 0 && t.stride[2] % 4 == 0;
+  if (vec) {
+    dim3 grid((d.np + 31) / 32, d.DP / 32, d.B * d.H);
+    split_tf32_vec_kernel<<<grid, 256, 0, st>>>(reinterpret_cast<const float*>(t.data), t.stride[0], t.stride[1],
+                                                t.stride[2], d.B, d.H, d.N, d.D, d.DP, d.np, nat, tr);
+  } else {
+    dim3 grid((d.np + 31) / 32, d.DP / 32, d.B * d.H), block(32, 8);
+    split_tf32_kernel<<<grid, block, 0, st>>>(reinterpret_cast<const float*>(t.data), t.stride[0], t.stride[1],
+                                              t.stride[2], t.stride[3], d.B, d.H, d.N, d.D, d.DP, d.np, nat, tr);
+  }
   return cudaGetLastError() == cudaSuccess ? GEOATTN_OK : GEOATTN_ERR_LAUNCH;
 }
 

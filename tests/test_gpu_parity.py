@@ -53,9 +53,10 @@ def test_c2_shape_coordinate_geometry(ops, dtype, qscale):
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32], ids=["bf16", "tf32"])
-@pytest.mark.parametrize("N,D", [(1, 64), (33, 48), (100, 64), (129, 8), (200, 64), (300, 24)])
+@pytest.mark.parametrize("N,D", [(1, 64), (33, 48), (100, 64), (129, 8), (200, 64), (300, 24), (70, 30)])
 def test_ragged_shapes_dense_prior(ops, dtype, N, D):
-    """N not a multiple of the tiles, D below the 64-wide tile; reference call with dense dist/ang."""
+    """N not a multiple of the tiles, D below the 64-wide tile (D = 30: fp32 operands split element by element, the
+    others with 16-byte accesses); reference call with dense dist/ang."""
     B, H = 1, 3
     q, k, v, a, b, c, do = attn_inputs(B, H, N, D, seed=N + D, qscale=3.0, per_head=False, dtype=dtype)
     g = torch.Generator().manual_seed(N)
