@@ -230,6 +230,37 @@ def cpu_step_sample(n_dates, threads):
     return (time.perf_counter() - t0) * 1e3
 
 
+def cpu_c2_extrapolated(threads, reps=5):
+    """The TF32 configuration's shape (H=8, N=512, D=64, fp32) on the host CPU at B = 1..4 issue dates (median ms of
+    `reps` fwd+bwd each), and the least-squares line through them evaluated at its B = 32."""
+    from oracle import geo_attention as oga
+    from oracle import geometry as ogeo
+    torch.set_num_threads(threads)
+    h1, n1, d1 = 8, 512, 64
+    rng = np.random.default_rng(0)
+    lat, lon = rng.uniform(35.0, 49.0, n1), rng.uniform(-124.0, -104.0, n1)
+    el = rng.uniform(500.0, 3500.0, n1) / 0.3048
+    dist, ang = (torch.from_numpy(x).float() for x in ogeo.distance_and_angularity(lat, lon, el))
+    g = torch.Generator().manual_seed(0)
+    a = torch.rand(h1, generator=g) * 0.9 + 0.1
+    b, c = torch.randn(h1, generator=g) * 0.5, torch.randn(h1, generator=g) * 0.5
+    ms = {}
+    for bb in (1, 2, 3, 4):
+        q, k, v, do = (torch.randn(bb, h1, n1, d1, generator=g) * (d1 ** -0.25 if i < 3 else 1.0) for i in range(4))
+        oga.grads(q, k, v, dist, ang, a, b, c, do, dtype=torch.float32)
+        ts = []
+        for _ in range(reps):
+            t0 = time.perf_counter()
+            oga.grads(q, k, v, dist, ang, a, b, c, do, dtype=torch.float32)
+            ts.append((time.perf_counter() - t0) * 1e3)
+        ms[bb] = statistics.median(ts)
+    xs, ys = np.array(list(ms)), np.array(list(ms.values()))
+    slope, icpt = np.polyfit(xs, ys, 1)
+    return {"ms_fwd_bwd_by_issue_dates": ms, "ms_fwd_bwd_extrapolated_b32": float(slope * 32 + icpt),
+            "cores": threads, "shape_hnd": [h1, n1, d1], "dtype": "fp32",
+            "what": "eager FP32 fwd+bwd on the host CPU at B = 1..4, least-squares line evaluated at B = 32"}
+
+
 def cpu_c1(threads, reps=10):
     """The CPU configuration: eager FP32 fwd+bwd at B=1 issue date, H=8, N=512, D=64 (q, k, v ~ N(0,1) D^-1/4 from
     seed 0; coordinates lat ~ U(35,49), lon ~ U(-124,-104), elevation ~ U(500,3500) m; a_h ~ U(0.1,1),
@@ -283,7 +314,7 @@ def run_reference(args):
             "config": config(world),
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-            "c1_cpu": cpu_c1(threads)}
+            "c1_cpu": cpu_c1(threads), "c2_cpu": cpu_c2_extrapolated(threads)}
     print(json.dumps(line), flush=True)
     return 0
 
