@@ -240,6 +240,10 @@ struct Dims {
   int nabg;
 };
 
+// The backward keeps a dS scratch and forms dQ by a GEMM (instead of a second row-pass sweep) for bf16 at every head
+// dim and for fp32 at head dim 64, where the pooled key pass has room for the transposed dS tile.
+inline bool uses_ds(const Dims& d) { return d.bf16 || d.DP == 64; }
+
 // Every data pointer handed to a kernel must be memory of the current device (or managed memory): the kernels run
 // on the current device, which would dereference a host pointer or another device's memory. Checked on the host
 // before any launch.
@@ -305,7 +309,8 @@ struct BwdWs {
   float *qn, *kn, *vn, *don, *kt, *qt, *dot;
   void* dsT;  // bf16 dS^T scratch [B*H][N_pad keys][N_pad queries] (dS-scratch backward only)
 };
-// The BF16 backward with a caller-provided workspace keeps dS in a scratch (`with_ds`): key pass -> dQ GEMM.
+// The backward with a caller-provided workspace keeps dS in a scratch (`with_ds`; bf16, and fp32 at head dim 64):
+// key pass -> dQ GEMM.
 size_t bwd_ws(const Dims& d, uint8_t* base, BwdWs* w, bool with_ds) {
   size_t off = 0;
   auto take = [&](size_t bytes) -> uint8_t* {
@@ -327,12 +332,21 @@ size_t bwd_ws(const Dims& d, uint8_t* base, BwdWs* w, bool with_ds) {
     t.qt = reinterpret_cast<float*>(take(trn));
     t.dot = reinterpret_cast<float*>(take(trn));
   }
-  if (with_ds && d.bf16) t.dsT = take((size_t)d.B * d.H * d.np * d.np * 2);
+  // dS scratch: bf16 dS^T [b*h][key][query]; fp32 (head dim 64) dS [b*h][query][key]
+  if (with_ds && uses_ds(d)) t.dsT = take((size_t)d.B * d.H * d.np * d.np * (d.bf16 ? 2 : 4));
   if (w) *w = t;
   return off;
 }
 
 // TMA map over the bf16 dS^T scratch, viewed as 3-D (query, key, b*h); box: 64 queries x `keys` keys.
+// TMA map over the fp32 dS scratch [b*h][query][key], viewed as 3-D (key, query, b*h); box: 32 keys x `queries`.
+int map_ds_f32(CUtensorMap* m, void* base, const Dims& d, int queries) {
+  const uint64_t dims[3] = {(uint64_t)d.np, (uint64_t)d.np, (uint64_t)d.B * d.H};
+  const uint64_t str[2] = {(uint64_t)d.np * 4, (uint64_t)d.np * d.np * 4};
+  const uint32_t box[3] = {32, (uint32_t)queries, 1};
+  return make_tmap(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, base, dims, str, box) ? GEOATTN_OK : GEOATTN_ERR_TMA;
+}
+
 int map_dsT(CUtensorMap* m, void* base, const Dims& d, int keys) {
   const uint64_t dims[3] = {(uint64_t)d.np, (uint64_t)d.np, (uint64_t)d.B * d.H};
   const uint64_t str[2] = {(uint64_t)d.np * 2, (uint64_t)d.np * d.np * 2};
@@ -485,11 +499,29 @@ int run_bwd_ds(const TileMaps& rmaps, const TileMaps& cmaps, const TileMaps& qma
                   Tile<true, DP>::NTHREADS, persistent_grid(d), st, rmaps, prow);
   if (rc) return rc;
   record(ev, 1, st);
-  rc = launch(geoattn_bwd_cols_kernel<true, DP, true>, ColsCfg<true, DP>::SMEM, Tile<true, DP>::NTHREADS,
+  rc = launch(geoattn_bwd_cols_kernel<true, DP, true>, ColsCfg<true, DP, true>::SMEM, Tile<true, DP>::NTHREADS,
               persistent_grid(d), st, cmaps, pcol);
   if (rc) return rc;
   record(ev, 2, st);
   rc = launch(geoattn_bwd_dq_kernel<DP>, DqCfg<DP>::SMEM, DqCfg<DP>::NTHREADS, persistent_grid(d), st, qmaps, pdq);
+  record(ev, 3, st);
+  return rc;
+}
+
+// fp32 at head dim 64: the one-sweep row pass, the key pass storing fp32 dS [query][key], the TF32 dQ GEMM.
+int run_bwd_ds_f32(const TileMaps& rmaps, const TileMaps& cmaps, const TileMaps& qmaps, const KParams& prow,
+                   const KParams& pcol, const KParams& pdq, const Dims& d, cudaStream_t st, void* const* ev) {
+  record(ev, 0, st);
+  int rc = launch(geoattn_bwd_rows_kernel<false, 64, false>, RowsCfg<false, 64, false>::SMEM,
+                  Tile<false, 64>::NTHREADS, persistent_grid(d), st, rmaps, prow);
+  if (rc) return rc;
+  record(ev, 1, st);
+  rc = launch(geoattn_bwd_cols_kernel<false, 64, true>, ColsCfg<false, 64, true>::SMEM, Tile<false, 64>::NTHREADS,
+              persistent_grid(d), st, cmaps, pcol);
+  if (rc) return rc;
+  record(ev, 2, st);
+  rc = launch(geoattn_bwd_dq_tf32_kernel<64>, DqTf32Cfg<64>::SMEM, DqTf32Cfg<64>::NTHREADS, persistent_grid(d), st,
+              qmaps, pdq);
   record(ev, 3, st);
   return rc;
 }
@@ -635,7 +667,7 @@ int backward(const GeoAttnBwdArgs* a, void* stream, bool with_ds) {
   if ((reinterpret_cast<uintptr_t>(a->workspace) & (kAlign - 1)) != 0) return GEOATTN_ERR_ALIGNMENT;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   BwdWs ws;
-  with_ds = with_ds && d.bf16;
+  with_ds = with_ds && uses_ds(d);
   bwd_ws(d, reinterpret_cast<uint8_t*>(a->workspace), &ws, with_ds);
   if (cudaMemsetAsync(ws.status, 0, sizeof(int), st) != cudaSuccess) return GEOATTN_ERR_LAUNCH;
   TileMaps rm, cm;
@@ -682,7 +714,14 @@ int backward(const GeoAttnBwdArgs* a, void* stream, bool with_ds) {
   prow.out_tma = map_output(&rm.out0, a->dq, a->dq_stride, d) ? 1 : 0;
   pcol.out_tma =
       (map_output(&cm.out0, a->dk, a->dk_stride, d) && map_output(&cm.out1, a->dv, a->dv_stride, d)) ? 1 : 0;
-  if (with_ds) {
+  if (with_ds && !d.bf16) {
+    TileMaps qm;
+    std::memset(&qm, 0, sizeof(qm));
+    if ((rc = map_ds_f32(&cm.dsT, ws.dsT, d, 32)) || (rc = map_ds_f32(&qm.dsT, ws.dsT, d, kBM)) ||
+        (rc = map_transposed(&qm.kt, ws.kt, d)))
+      return rc;
+    rc = run_bwd_ds_f32(rm, cm, qm, prow, pcol, prow, d, st, a->events);
+  } else if (with_ds) {
     TileMaps qm;
     std::memset(&qm, 0, sizeof(qm));
     if ((rc = map_dsT(&cm.dsT, ws.dsT, d, kBM)) || (rc = map_dsT(&qm.dsT, ws.dsT, d, 64)) ||

@@ -1113,7 +1113,8 @@ __device__ __forceinline__ float* rec_ptr(const KParams& p, int bh, int row) {
 template <bool BF16, int DP, bool DQ>
 __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
     geoattn_bwd_rows_kernel(const __grid_constant__ TileMaps maps, const KParams p) {
-  static_assert(DQ || BF16, "the dS-scratch backward is bf16 only");
+  // one sweep (dS from the key pass's scratch): bf16, and fp32 at head dim 64 (the pooled layout)
+  static_assert(DQ || BF16 || (!BF16 && DP == 64), "the dS-scratch backward is bf16 or fp32 at head dim 64");
   using C = RowsCfg<BF16, DP, DQ>;
   using T = typename C::T;
   constexpr int NKV = C::NKV, NPR = C::NPR, NSB = C::NSB;
@@ -1655,7 +1656,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
 // TMA warp also stores each staged dS^T tile to the scratch (for the dQ GEMM) and the element-wise warps accumulate
 // the key block's d(beta) = sum dZ Dp and d(gamma) = sum dZ Ap.
 // ===============================================================================================================
-template <bool BF16, int DP>
+template <bool BF16, int DP, bool SDS = false>
 struct ColsCfg : Tile<BF16, DP> {
   using T = Tile<BF16, DP>;
   // fp32 beyond 64: no resident K / V blocks; (K, Q) and (V, dO) reach the S^T and dP^T MMAs in head-dim chunks
@@ -1702,8 +1703,14 @@ struct ColsCfg : Tile<BF16, DP> {
   static constexpr int OFF_DS = OFF_P2 + NST * ST_BYTES;
   static constexpr int OFF_PR = OFF_DS + NST * ST_BYTES;
   static constexpr int OFF_REC = OFF_PR + NPR * kPriorTileBytes;
-  static constexpr int SMEM = OFF_REC + NR * REC_BYTES;
+  // fp32 with a dS scratch: the TF32 dQ GEMM needs dS K-major along the keys, so each staged tile is also written
+  // transposed, [32 queries][128 keys] as four 128-byte-swizzled regions of 32 keys, for its TMA store
+  static constexpr bool DST = SDS && !BF16;
+  static constexpr int DST_BYTES = 32 * kBM * 4;
+  static constexpr int OFF_DST = (OFF_REC + NR * REC_BYTES + 1023) / 1024 * 1024;
+  static constexpr int SMEM = DST ? OFF_DST + NST * DST_BYTES : OFF_REC + NR * REC_BYTES;
   static_assert(SMEM + 1024 <= kSmemPerBlock, "key pass: dynamic + static shared memory above the per-block limit");
+  static_assert(!DST || (T::CH == 32 && T::PIECES == 1 && T::EW == 1), "transposed dS staging: one 32-query piece");
   static constexpr int TM_S = 0;
   static constexpr int TM_DP = NSB * T::CH;
   static constexpr int TM_DK = 2 * NSB * T::CH;
@@ -1720,8 +1727,8 @@ struct ColsCfg : Tile<BF16, DP> {
 template <bool BF16, int DP, bool SDS>
 __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
     geoattn_bwd_cols_kernel(const __grid_constant__ TileMaps maps, const KParams p) {
-  static_assert(!SDS || BF16, "the dS-scratch backward is bf16 only");
-  using C = ColsCfg<BF16, DP>;
+  static_assert(!SDS || BF16 || DP == 64, "the dS-scratch backward is bf16 or fp32 at head dim 64");
+  using C = ColsCfg<BF16, DP, SDS>;
   using T = typename C::T;
   constexpr int NQ = C::NQ, NSB = C::NSB, NR = C::NR, NST = C::NST, NPR = C::NPR;
   constexpr int SLAG = NQ > 1 ? NQ - 1 : 1;  // chunks by which the dS stores trail the query-chunk loads
@@ -1791,7 +1798,13 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       auto store_ds = [&](int g, int c) -> bool {
         const int ts = g % NST;
         if (!mbar_wait(&bar_tfull[ts], (g / NST) & 1, ctx)) return false;
-        tma_store_3d(&maps.dsT, smem + C::OFF_DS + ts * C::ST_BYTES, c * T::CH, kblk * kBM, bh);
+        if constexpr (C::DST) {  // fp32: the transposed tile, [queries][keys], one store per 32-key region
+          for (int rg = 0; rg < 4; ++rg)
+            tma_store_3d(&maps.dsT, smem + C::OFF_DST + ts * C::DST_BYTES + rg * (32 * 128), kblk * kBM + rg * 32,
+                         c * T::CH, bh);
+        } else {
+          tma_store_3d(&maps.dsT, smem + C::OFF_DS + ts * C::ST_BYTES, c * T::CH, kblk * kBM, bh);
+        }
         bulk_commit();
         bulk_wait_read0();
         mbar_arrive(&bar_tempty[ts]);
@@ -2103,6 +2116,13 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         if (!(ok = warp_wait(&bar_tempty[ts], ((gc / NST) & 1) ^ 1, ctx))) break;
         stage_row32<BF16>(p2reg, e.r, piece, v);
         stage_row32<BF16>(dsreg, e.r, piece, w);
+        if constexpr (C::DST) {  // dS[query][key], TF32-rounded as for the MMAs: key e.r is word e.r % 32 of region e.r / 32
+          uint8_t* treg = smem + C::OFF_DST + ts * C::DST_BYTES + (e.r >> 5) * (32 * 128);
+          const int kk = e.r & 31;
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            *reinterpret_cast<float*>(treg + sw128(j, kk >> 2) + (kk & 3) * 4) = round_tf32(w[j]);
+        }
       }
       if (!ok) continue;
       fence_proxy_async_smem();
@@ -2321,6 +2341,133 @@ __global__ void __launch_bounds__(DqCfg<DP>::NTHREADS, 1)
       }
     }
     if (epi_tma && threadIdx.x == 0) bulk_wait_read0();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, C::TMEM_COLS);
+}
+
+// ===============================================================================================================
+// dQ = dS K / sqrt(d) for fp32 storage (TF32, 1 term) at head dim 64, from the fp32 dS tiles [b*h][query][key] the key
+// pass stored (K-major along the keys: TF32 MMAs take K-major operands only) and the transposed hi plane of K
+// [b*h][d][key] (K-major along the keys). One CTA per (128-query block, b*h), persistent; per 32-key chunk four
+// M = 128, N = DP, K = 8 MMAs; the accumulator double-buffered in tensor memory. Warps: 4 epilogue, 1 TMA, 1 MMA.
+// ===============================================================================================================
+template <int DP>
+struct DqTf32Cfg {
+  using T = Tile<false, DP>;
+  static constexpr int NSTAGE = 4;
+  static constexpr int A_BYTES = kBM * 128;  // dS: 128 queries x 32 keys (one 128-byte region per row)
+  static constexpr int B_BYTES = DP * 128;   // K^T: DP rows x 32 keys
+  static constexpr int STAGE = A_BYTES + B_BYTES;
+  static constexpr int SMEM = NSTAGE * STAGE;
+  static constexpr int TMEM_COLS = pow2_cols(2 * DP);
+  static constexpr int NTHREADS = 128 + 64;
+  static constexpr int TMA_WARP = 4, MMA_WARP = 5;
+  static_assert(SMEM + 1024 <= kSmemPerBlock, "TF32 dQ GEMM: shared memory above the per-block limit");
+};
+
+template <int DP>
+__global__ void __launch_bounds__(DqTf32Cfg<DP>::NTHREADS, 1)
+    geoattn_bwd_dq_tf32_kernel(const __grid_constant__ TileMaps maps, const KParams p) {
+  using C = DqTf32Cfg<DP>;
+  constexpr int NS = C::NSTAGE;
+  if (smem_misaligned(p.status)) return;  // uniform over the CTA, before any barrier or allocation
+  uint8_t* smem = smem_raw;
+  __shared__ uint64_t bar_full[NS], bar_empty[NS], bar_accfull[2], bar_accempty[2];
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ int abort_flag;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int nchunks = (p.N + 31) / 32;  // key chunks (keys past N meet the zero-padded columns of K^T)
+  const int ntiles = p.nrb * p.B * p.H;
+  WaitCtx ctx{&abort_flag, p.status};
+
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&bar_full[i], 1);
+      mbar_init(&bar_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bar_accfull[i], 1);
+      mbar_init(&bar_accempty[i], 128);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(&tmem_base_sh, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base_sh;
+  const uint32_t sbase = smem_u32(smem);
+
+  if (warp == C::TMA_WARP) {
+    if (lane == 0) {
+      prefetch_tmap(&maps.dsT);
+      prefetch_tmap(&maps.kt);
+      int sc = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+        const int rb = tile % p.nrb, bh = tile / p.nrb, b = bh / p.H, h = bh % p.H;
+        for (int c = 0; c < nchunks && ok; ++c, ++sc) {
+          const int st = sc % NS;
+          if (!(ok = mbar_wait(&bar_empty[st], ((sc / NS) & 1) ^ 1, ctx))) break;
+          uint8_t* dst = smem + st * C::STAGE;
+          mbar_arrive_expect_tx(&bar_full[st], C::STAGE);
+          tma_load_3d(dst, &maps.dsT, &bar_full[st], c * 32, rb * kBM, bh);
+          tma_tileT(dst + C::A_BYTES, &maps.kt, &bar_full[st], c * 32, h, b);
+        }
+      }
+    }
+  } else if (warp == C::MMA_WARP) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = instr_desc(2, 0, 0, 128, DP);  // tf32, A and B K-major
+      int sc = 0, it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++it) {
+        const int ab = it & 1;
+        if (!(ok = mbar_wait(&bar_accempty[ab], ((it >> 1) & 1) ^ 1, ctx))) break;
+        tc_fence_after();
+        for (int c = 0; c < nchunks && ok; ++c, ++sc) {
+          const int st = sc % NS;
+          if (!(ok = mbar_wait(&bar_full[st], (sc / NS) & 1, ctx))) break;
+          tc_fence_after();
+          const uint32_t a = sbase + st * C::STAGE, bsrc = a + C::A_BYTES;
+#pragma unroll
+          for (int s = 0; s < 4; ++s)  // K = 8 keys (32 bytes) per MMA
+            mma_ss<Kind::kTF32>(tmem + ab * DP, smem_desc_sw128(a + s * 32, 16, 1024),
+                                smem_desc_sw128(bsrc + s * 32, 16, 1024), idesc, (c > 0 || s > 0) ? 1u : 0u);
+          mma_commit(&bar_empty[st]);
+        }
+        if (ok) mma_commit(&bar_accfull[ab]);
+      }
+    }
+  } else {
+    // ---------------- epilogue warps: thread = query row ----------------
+    const int r = (warp & 3) * 32 + lane;
+    const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+    int it = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++it) {
+      const int rb = tile % p.nrb, bh = tile / p.nrb, b = bh / p.H, h = bh % p.H;
+      const int row = rb * kBM + r, ab = it & 1;
+      if (ok) ok = warp_wait(&bar_accfull[ab], (it >> 1) & 1, ctx);
+      tc_fence_after();
+      const long long qoff = (long long)b * p.dq_str[0] + (long long)h * p.dq_str[1] + (long long)row * p.dq_str[2];
+      if (ok) {
+#pragma unroll 1
+        for (int d0 = 0; d0 < DP; d0 += 32) {
+          float v[32];
+          tmem_ld32(lane_base + ab * DP + d0, v);
+          if (row < p.N && d0 < p.D) store_row32<false>(p.dq, qoff, p.dq_str[3], d0, p.D, v, p.inv_sqrt_d);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&bar_accempty[ab]);
+    }
   }
   tc_fence_before();
   __syncthreads();

@@ -670,3 +670,100 @@ def test_forward_pooled_bf16_v_lag_range(D):
     for vlag in range(0, bound + 1):
         assert all(_forward_pooled_bf16_order(n, 3, nk, npr, vlag) is None for n in sizes), vlag
     assert _forward_pooled_bf16_order(16, 3, nk, npr, bound + 1) is not None
+
+
+def _key_pass_pooled_f32_order(nch, n_tiles, nq, nsb, nst, slag, nr=2):
+    """The pooled fp32 key pass with the dS scratch stores (geoattn_bwd_cols_kernel<false, 64, true>) over several
+    tiles of one CTA as three cooperating programs (the prior is read from L2); returns None or the deadlock state.
+
+    The K/V landing takes the query ring's next nq positions (each waits for the release of its previous use), the
+    MMA warp copies K/V into tensor memory, drains the copies through a free score buffer and releases the nq
+    positions; then per chunk the TMA warp loads Q/dO (the next ring position), the row records (nr ring) and stores
+    the transposed dS tile of chunk c - slag once staged (the staging tile's second release). The MMA warp issues
+    S^T/dP^T up to nsb chunks ahead and dV/dK per staged chunk (releasing its ring position and staging tile); the
+    element-wise warps as in the bf16 model."""
+    st = dict(pos=0, released=0, kv_loaded=0, q_loaded=0, rec_loaded=0, rec_released=0, s_issued=0, s_released=0,
+              t_staged=0, t_mma=0, t_store=0, done=0)
+
+    def tma():
+        for it in range(n_tiles):
+            for _ in range(nq):                                     # the landing takes every slot once
+                yield lambda p=st["pos"]: st["released"] >= p + 1 - nq
+                st["pos"] += 1
+            st["kv_loaded"] = it + 1
+            g0 = it * nch
+            for c in range(nch):
+                gc = g0 + c
+                yield lambda p=st["pos"]: st["released"] >= p + 1 - nq
+                st["pos"] += 1
+                st["q_loaded"] = gc + 1
+                yield lambda gc=gc: st["rec_released"] >= gc + 1 - nr
+                st["rec_loaded"] = gc + 1
+                if c >= slag:
+                    yield lambda g=gc - slag: st["t_staged"] >= g + 1
+                    st["t_store"] = gc - slag + 1
+            for c in range(max(0, nch - slag), nch):
+                yield lambda g=g0 + c: st["t_staged"] >= g + 1
+                st["t_store"] = g0 + c + 1
+
+    def mma():
+        def issue(gc):
+            yield lambda: st["q_loaded"] >= gc + 1 and st["s_released"] >= gc + 1 - nsb
+            st["s_issued"] = gc + 1
+
+        for it in range(n_tiles):
+            g0 = it * nch
+            yield lambda it=it: st["kv_loaded"] >= it + 1
+            yield lambda g0=g0: st["s_released"] >= g0 + 1 - nsb      # the drain's score buffer
+            st["released"] += nq
+            yield from issue(g0)
+            for c in range(nch):
+                gc = g0 + c
+                if nsb == 2 and c + 1 < nch:
+                    yield from issue(gc + 1)
+                yield lambda gc=gc: st["t_staged"] >= gc + 1
+                st["t_mma"] = gc + 1
+                st["released"] += 1
+            st["done"] = it + 1
+
+    def ew():
+        for it in range(n_tiles):
+            g0 = it * nch
+            for c in range(nch):
+                gc = g0 + c
+                yield lambda gc=gc: st["s_issued"] >= gc + 1 and st["rec_loaded"] >= gc + 1
+                st["s_released"] = st["rec_released"] = gc + 1
+                yield lambda gc=gc: st["t_mma"] >= gc + 1 - nst and st["t_store"] >= gc + 1 - nst
+                st["t_staged"] = gc + 1
+            last = g0 + nch
+            yield lambda it=it, last=last: st["done"] >= it + 1 and st["t_mma"] >= last and st["t_store"] >= last
+
+    progs = [tma(), mma(), ew()]
+    waits = [next(p) for p in progs]
+    done = [False] * len(progs)
+    while not all(done):
+        moved = False
+        for i, prog in enumerate(progs):
+            while not done[i] and waits[i]():
+                try:
+                    waits[i] = next(prog)
+                except StopIteration:
+                    done[i] = True
+                moved = True
+        if not moved:
+            return dict(st)
+    return None
+
+
+# ColsCfg<false, 64, true>: NQ = 2, NSB = 2, NST = 2; the stores trail by SLAG = NQ - 1
+@pytest.mark.parametrize("nch", [1, 2, 3, 8, 11, 16])
+def test_key_pass_pooled_f32_store_lag_has_no_deadlock(nch):
+    assert _key_pass_pooled_f32_order(nch, 4, 2, 2, 2, 1) is None
+
+
+def test_key_pass_pooled_f32_store_lag_bound():
+    """As in the bf16 key pass, a store lag up to NQ + NST - 1 runs and one more stops the pipeline."""
+    nq, nsb, nst = 2, 2, 2
+    bound = nq + nst - 1
+    assert all(_key_pass_pooled_f32_order(n, 4, nq, nsb, nst, bound) is None for n in (1, 2, 3, 5, 8, 11, 16))
+    assert _key_pass_pooled_f32_order(16, 4, nq, nsb, nst, bound + 1) is not None
