@@ -606,11 +606,113 @@ def reference_triton_v2():
     return v2
 
 
-def run_configs(args):
-    """The other configurations of the path, one JSON line each: fwd, bwd and fwd+bwd ms of the kernels (coordinate
-    prior, per-head alpha/beta/gamma, q/k/v ~ N(0,1) D^-1/4, dO ~ N(0,1)) and of eager PyTorch on the same GPU and
-    inputs (TF32 matmuls for fp32 storage, as the reference's eager TF32 baseline), CUDA events, after warm-up."""
+def config_line(args, name, b, h, n, d, dtype, qscale, dev, pk_bf16, pk_src, triton=True):
+    """One configuration: fwd, bwd and fwd+bwd ms of the kernels (coordinate prior, per-head alpha/beta/gamma,
+    q/k/v ~ N(0,1) D^-1/4, dO ~ N(0,1)), of eager PyTorch on the same GPU and inputs (TF32 matmuls for fp32 storage,
+    as the reference's eager TF32 baseline) and, for fp32 storage, of the reference's Triton v2 op; CUDA events,
+    after warm-up; peak extra memory of each."""
     import foreswe_gpu_optimization_b200 as g
+    gen = torch.Generator().manual_seed(11)
+    s = d ** -0.25
+    q, k, v = (torch.randn(b, h, n, d, generator=gen) * s for _ in range(3))
+    q = q * qscale
+    do = torch.randn(b, h, n, d, generator=gen)
+    q, k, v, do = (t.to(dev, dtype) for t in (q, k, v, do))
+    gp = torch.Generator().manual_seed(7)
+    params = [(torch.rand(h, generator=gp) * 0.9 + 0.1), torch.randn(h, generator=gp) * 0.5,
+              torch.randn(h, generator=gp) * 0.5]
+    params = [t.to(dev).requires_grad_(True) for t in params]
+    rng = np.random.default_rng(0)
+    geom = g.StationGeometry(rng.uniform(35.0, 49.0, n), rng.uniform(-124.0, -104.0, n),
+                             rng.uniform(500.0, 3500.0, n) / 0.3048, device=dev)
+    dmat, amat = geom.distance_and_angularity()
+    x = [t.detach().requires_grad_(True) for t in (q, k, v)]
+
+    def ours():
+        return g.geo_attention(x[0], x[1], x[2], geom, *params)
+
+    def eager():
+        s_ = torch.softmax(torch.matmul(x[0], x[1].transpose(-2, -1)) / math.sqrt(d), dim=-1)
+        z = (params[0].view(-1, 1, 1) * s_ + params[1].view(-1, 1, 1) / (1 + dmat)
+             + params[2].view(-1, 1, 1) / (1 + amat))
+        return torch.matmul(torch.softmax(z, dim=-1).to(dtype), x[2])
+
+    def timed(fn, backward):
+        def once():
+            for t in x + params:
+                t.grad = None
+            o = fn()
+            if backward:
+                o.backward(do)
+        for _ in range(args.warmup):
+            once()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            once()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / args.steps
+
+    def triple(fn):
+        try:
+            f, fb = timed(fn, False), timed(fn, True)
+            return {"fwd": f, "bwd": fb - f, "fwd_bwd": fb}
+        except torch.OutOfMemoryError:
+            torch.cuda.empty_cache()
+            return None
+
+    def mem_of(fn):
+        def once():
+            for t in x + params:
+                t.grad = None
+            fn().backward(do)
+        try:
+            return round(peak_extra_memory(once, dev)["peak_extra_mib"], 1)
+        except torch.OutOfMemoryError:
+            torch.cuda.empty_cache()
+            return None
+
+    mine = triple(ours)
+    ref = None if args.no_eager else triple(eager)
+    mem = {"ours": mem_of(ours), "eager": None if args.no_eager else mem_of(eager)}
+    tri = None
+    if triton and not args.no_triton and dtype == torch.float32:
+        v2 = reference_triton_v2()
+        if isinstance(v2, str):
+            tri = {"unavailable": v2}
+        else:
+            sc = [t[:1] for t in params]   # the Triton v2 op takes scalar alpha, beta, gamma (same work)
+            try:
+                tri = triple(lambda: v2.fused_geo_attention_v2(x[0], x[1], x[2], dmat, amat, *sc))
+                if tri is not None:
+                    tri["preset"] = "accurate_experimental"
+                    tri["speedup_ours_vs_triton_v2"] = tri["fwd_bwd"] / mine["fwd_bwd"]
+                    mem["triton_v2"] = mem_of(lambda: v2.fused_geo_attention_v2(x[0], x[1], x[2], dmat, amat,
+                                                                                *sc))
+            except Exception as exc:   # a compile or launch error of the reference's kernel is reported
+                tri = {"unavailable": "%s: %s" % (type(exc).__name__, str(exc).splitlines()[0][:200])}
+    fl = 12.0 * b * h * n * n * d
+    line = {"workload": name, "shape_bhnd": [b, h, n, d], "dtype": "bf16" if dtype == torch.bfloat16 else "fp32 (tf32)",
+            "steps": args.steps, "warmup": args.warmup, "ms": mine, "eager_ms": ref, "triton_v2_ms": tri,
+            "peak_extra_mib_fwd_bwd": mem,
+            "tflops": fl / (mine["fwd_bwd"] * 1e-3) / 1e12,
+            "speedup_vs_eager": (ref["fwd_bwd"] / mine["fwd_bwd"]) if ref else None,
+            "l2": "inputs %s L2 (q,k,v,dO = %.0f MB)" % ("larger than" if 4 * q.numel() * q.element_size() > 126e6
+                                                        else "within", 4 * q.numel() * q.element_size() / 1e6)}
+    if dtype == torch.bfloat16:
+        line["tensor_frac_of_sustained_bf16"] = line["tflops"] / pk_bf16
+        line["peak_source"] = pk_src
+    if name == "reference_shape_tf32_d192":
+        line["reference_a100_ms_fwd_bwd_fwdbwd"] = REFERENCE_A100_D192
+    del q, k, v, do, x, geom, dmat, amat
+    torch.cuda.empty_cache()
+    return line
+
+
+def run_configs(args):
+    """The other configurations of the path, one JSON line each (config_line)."""
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
     torch.cuda.set_device(dev)
     torch.backends.cuda.matmul.allow_tf32 = True
@@ -620,103 +722,7 @@ def run_configs(args):
             continue
         if args.batch:
             b = args.batch
-        gen = torch.Generator().manual_seed(11)
-        s = d ** -0.25
-        q, k, v = (torch.randn(b, h, n, d, generator=gen) * s for _ in range(3))
-        q = q * qscale
-        do = torch.randn(b, h, n, d, generator=gen)
-        q, k, v, do = (t.to(dev, dtype) for t in (q, k, v, do))
-        gp = torch.Generator().manual_seed(7)
-        params = [(torch.rand(h, generator=gp) * 0.9 + 0.1), torch.randn(h, generator=gp) * 0.5,
-                  torch.randn(h, generator=gp) * 0.5]
-        params = [t.to(dev).requires_grad_(True) for t in params]
-        rng = np.random.default_rng(0)
-        geom = g.StationGeometry(rng.uniform(35.0, 49.0, n), rng.uniform(-124.0, -104.0, n),
-                                 rng.uniform(500.0, 3500.0, n) / 0.3048, device=dev)
-        dmat, amat = geom.distance_and_angularity()
-        x = [t.detach().requires_grad_(True) for t in (q, k, v)]
-
-        def ours():
-            return g.geo_attention(x[0], x[1], x[2], geom, *params)
-
-        def eager():
-            s_ = torch.softmax(torch.matmul(x[0], x[1].transpose(-2, -1)) / math.sqrt(d), dim=-1)
-            z = (params[0].view(-1, 1, 1) * s_ + params[1].view(-1, 1, 1) / (1 + dmat)
-                 + params[2].view(-1, 1, 1) / (1 + amat))
-            return torch.matmul(torch.softmax(z, dim=-1).to(dtype), x[2])
-
-        def timed(fn, backward):
-            def once():
-                for t in x + params:
-                    t.grad = None
-                o = fn()
-                if backward:
-                    o.backward(do)
-            for _ in range(args.warmup):
-                once()
-            torch.cuda.synchronize()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            for _ in range(args.steps):
-                once()
-            e1.record()
-            torch.cuda.synchronize()
-            return e0.elapsed_time(e1) / args.steps
-
-        def triple(fn):
-            try:
-                f, fb = timed(fn, False), timed(fn, True)
-                return {"fwd": f, "bwd": fb - f, "fwd_bwd": fb}
-            except torch.OutOfMemoryError:
-                torch.cuda.empty_cache()
-                return None
-
-        def mem_of(fn):
-            def once():
-                for t in x + params:
-                    t.grad = None
-                fn().backward(do)
-            try:
-                return round(peak_extra_memory(once, dev)["peak_extra_mib"], 1)
-            except torch.OutOfMemoryError:
-                torch.cuda.empty_cache()
-                return None
-
-        mine = triple(ours)
-        ref = None if args.no_eager else triple(eager)
-        mem = {"ours": mem_of(ours), "eager": None if args.no_eager else mem_of(eager)}
-        tri = None
-        if not args.no_triton and dtype == torch.float32:
-            v2 = reference_triton_v2()
-            if isinstance(v2, str):
-                tri = {"unavailable": v2}
-            else:
-                sc = [t[:1] for t in params]   # the Triton v2 op takes scalar alpha, beta, gamma (same work)
-                try:
-                    tri = triple(lambda: v2.fused_geo_attention_v2(x[0], x[1], x[2], dmat, amat, *sc))
-                    if tri is not None:
-                        tri["preset"] = "accurate_experimental"
-                        tri["speedup_ours_vs_triton_v2"] = tri["fwd_bwd"] / mine["fwd_bwd"]
-                        mem["triton_v2"] = mem_of(lambda: v2.fused_geo_attention_v2(x[0], x[1], x[2], dmat, amat,
-                                                                                    *sc))
-                except Exception as exc:   # a compile or launch error of the reference's kernel is reported
-                    tri = {"unavailable": "%s: %s" % (type(exc).__name__, str(exc).splitlines()[0][:200])}
-        fl = 12.0 * b * h * n * n * d
-        line = {"workload": name, "shape_bhnd": [b, h, n, d], "dtype": "bf16" if dtype == torch.bfloat16 else "fp32 (tf32)",
-                "steps": args.steps, "warmup": args.warmup, "ms": mine, "eager_ms": ref, "triton_v2_ms": tri,
-                "peak_extra_mib_fwd_bwd": mem,
-                "tflops": fl / (mine["fwd_bwd"] * 1e-3) / 1e12,
-                "speedup_vs_eager": (ref["fwd_bwd"] / mine["fwd_bwd"]) if ref else None,
-                "l2": "inputs %s L2 (q,k,v,dO = %.0f MB)" % ("larger than" if 4 * q.numel() * q.element_size() > 126e6
-                                                            else "within", 4 * q.numel() * q.element_size() / 1e6)}
-        if dtype == torch.bfloat16:
-            line["tensor_frac_of_sustained_bf16"] = line["tflops"] / pk_bf16
-            line["peak_source"] = pk_src
-        if name == "reference_shape_tf32_d192":
-            line["reference_a100_ms_fwd_bwd_fwdbwd"] = REFERENCE_A100_D192
-        print(json.dumps(line), flush=True)
-        del q, k, v, do, x, geom, dmat, amat
-        torch.cuda.empty_cache()
+        print(json.dumps(config_line(args, name, b, h, n, d, dtype, qscale, dev, pk_bf16, pk_src)), flush=True)
     return 0
 
 
@@ -730,6 +736,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-eager", action="store_true")
     ap.add_argument("--no-step", action="store_true", help="skip the whole-step (projections + all-reduce) key")
+    ap.add_argument("--no-configs", action="store_true", help="skip the C2 / C3 lines of the default run")
     ap.add_argument("--no-triton", action="store_true", help="configs: skip the reference's Triton v2 timing")
     ap.add_argument("--preroll-seconds", type=float, default=0.3,
                     help="busy pre-roll before the timed region (0 for short profiling runs)")
@@ -945,6 +952,21 @@ def main():
             eager = {"ms_per_step": e_ms, "value": flops(b) / (e_ms * 1e-3) / 1e12, "unit": UNIT,
                      "what": "eager PyTorch (bf16 storage, cuBLAS + elementwise kernels) on this GPU, same shard"}
 
+    # the TF32 configuration and the temporal-batched bf16 one against eager PyTorch on this GPU (one GPU only), so
+    # the default line carries them too
+    others = None
+    if world == 1 and not args.no_configs:
+        import copy
+        a2 = copy.copy(args)
+        a2.steps, a2.warmup = 5, 3
+        tf32_was = torch.backends.cuda.matmul.allow_tf32
+        torch.backends.cuda.matmul.allow_tf32 = True
+        pk2, src2 = peaks()
+        others = [config_line(a2, *cfg, dev, pk2, src2, triton=False) for cfg in CONFIGS
+                  if cfg[0] in ("c2_tf32", "c3_bf16")]
+        torch.backends.cuda.matmul.allow_tf32 = tf32_was
+        phase("other configurations done")
+
     cpu = None
     if rank == 0 and world == 1:
         threads = os.cpu_count() or 1
@@ -971,7 +993,8 @@ def main():
                           + "; per-kernel times from K eager steps with library events",
                 "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": config(world),
                 "tensor_peak_frac": value / world / pk, "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
-                "gpu_eager": eager, "step": stepm, "memory": mem, "gpu_launches": 5 * args.steps, "clocks": clk}
+                "gpu_eager": eager, "step": stepm, "memory": mem, "other_configs": others,
+                "gpu_launches": 5 * args.steps, "clocks": clk}
         print(json.dumps(line), flush=True)
     if dist_on:
         tdist.barrier()
