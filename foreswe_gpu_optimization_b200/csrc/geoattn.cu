@@ -465,10 +465,10 @@ inline void record(void* const* ev, int i, cudaStream_t st) {
   if (ev && ev[i]) cudaEventRecord(reinterpret_cast<cudaEvent_t>(ev[i]), st);
 }
 
-template <bool BF16, int DP>
+template <bool BF16, int DP, bool ONE = false>
 int run_fwd(const TileMaps& maps, const KParams& p, const Dims& d, cudaStream_t st, void* const* ev) {
   record(ev, 0, st);
-  int rc = launch(geoattn_fwd_kernel<BF16, DP>, FwdCfg<BF16, DP>::SMEM, Tile<BF16, DP>::NTHREADS,
+  int rc = launch(geoattn_fwd_kernel<BF16, DP, ONE>, FwdCfg<BF16, DP, ONE>::SMEM, Tile<BF16, DP>::NTHREADS,
                   persistent_grid(d), st, maps, p);
   record(ev, 1, st);
   return rc;
@@ -641,8 +641,12 @@ int geoattn_fwd(const GeoAttnFwdArgs* a, void* stream) {
   p.status = ws.status;
   p.out_tma = map_output(&maps.out0, a->o, a->o_stride, d) ? 1 : 0;
   if (d.bf16) {
-    if (d.DP == 64) return run_fwd<true, 64>(maps, p, d, st, a->events);
-    if (d.DP == 128) return run_fwd<true, 128>(maps, p, d, st, a->events);
+    // up to 512 keys the bf16 forward keeps each row's 2^(t - m) in tensor memory and runs one score pass
+    const bool one = d.N <= FwdCfg<true, 128, true>::MAX_KEYS_ONE;
+    if (d.DP == 64) return one ? run_fwd<true, 64, true>(maps, p, d, st, a->events)
+                               : run_fwd<true, 64>(maps, p, d, st, a->events);
+    if (d.DP == 128) return one ? run_fwd<true, 128, true>(maps, p, d, st, a->events)
+                                : run_fwd<true, 128>(maps, p, d, st, a->events);
     return run_fwd<true, 192>(maps, p, d, st, a->events);
   }
   if (d.DP == 64) return run_fwd<false, 64>(maps, p, d, st, a->events);

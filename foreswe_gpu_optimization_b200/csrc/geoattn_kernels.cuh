@@ -532,11 +532,17 @@ __device__ __forceinline__ void store_tile(const CUtensorMap* map, const uint8_t
 
 // ===============================================================================================================
 // Forward: one CTA per (128-query row block, b*h). Pass A: row max / sum of softmax #1 over all key chunks.
-// Pass B: recompute S, form P1, Z and e = 2^((Z-c) log2 e), accumulate O += e V and l2 = sum e.
+// Pass B: recompute S (or, with a single score pass, read back the values pass A kept), form P1, Z and
+// e = 2^((Z-c) log2 e), accumulate O += e V and l2 = sum e.
 // ===============================================================================================================
-template <bool BF16, int DP>
+template <bool BF16, int DP, bool ONE = false>
 struct FwdCfg : Tile<BF16, DP> {
   using T = Tile<BF16, DP>;
+  // ONE (bf16, head dims up to 128, up to 512 keys): a single score pass. Pass A keeps, per row, each chunk pair's
+  // 2^(t - m_c) against the running max m_c as fp16 pairs in tensor memory (256 columns for 512 keys); pass B reads
+  // them back, P1 = 2^(t - m_c) 2^(m_c - m1), and issues no score MMAs. Q stays in shared memory (its tensor-memory
+  // columns hold the stored values), the score MMAs take single 64-key chunks into two buffers.
+  static_assert(!ONE || (BF16 && DP <= 128), "single score pass: bf16 up to head dim 128");
   // fp32 beyond 64: no resident Q; Q and K reach the score MMA in head-dim chunks through the K ring's slots
   static constexpr bool WIDE = !BF16 && DP > 64;
   static constexpr int NDC = WIDE ? DP / T::KB : 1;                    // head-dim chunks per score MMA
@@ -551,7 +557,7 @@ struct FwdCfg : Tile<BF16, DP> {
   // chunks (N = 128) runs at the tensor pipe's full rate, where an N = 64 MMA with both operands in shared memory
   // takes 48 cycles for 32 cycles of work (measured back to back on the B200). Head dim 192 keeps Q in shared memory
   // (4 score buffers + O + Q would need 544 columns).
-  static constexpr bool POOL = !WIDE && (!BF16 || DP <= 128);
+  static constexpr bool POOL = !ONE && !WIDE && (!BF16 || DP <= 128);
   static constexpr int PAIR = (POOL || WIDE) ? 2 : 1;                 // chunks per score MMA / K ring slot
   // pooled bf16 at head dim 128: two pair slots (64 KB; a third would take the shared memory past the limit)
   static constexpr int NK = POOL ? ((BF16 && DP > 64) ? 2 : 3) : (DP <= 128 ? 3 : 2);   // K ring slots
@@ -571,7 +577,7 @@ struct FwdCfg : Tile<BF16, DP> {
   static_assert(SMEM + 4096 <= kSmemPerBlock, "forward: dynamic + static shared memory above the per-block limit");
   // 4 score buffers in tensor memory: the MMA warp runs up to 3 chunks ahead of the element-wise warps, and the
   // last score MMA of a tile (which frees Q for the next tile) issues ~3 chunks before the tile ends
-  static constexpr int NSB = 4;
+  static constexpr int NSB = ONE ? 2 : 4;
   static_assert(NSB % PAIR == 0, "chunk pairs take aligned score buffers");
   // Pass B loads V of chunk c after the K of chunk c + VLAG: before its P.V MMA needs V(c), the MMA warp has issued
   // the scores of every chunk below c + NSB - PAIR + 1, so the K loads ahead of V(c) never wait on MMAs behind it. A
@@ -581,17 +587,19 @@ struct FwdCfg : Tile<BF16, DP> {
   static constexpr int TM_S = 0;
   static constexpr int TM_O = NSB * T::CH;
   static constexpr int TM_QA = TM_O + DP;  // pooled: Q (hi, lo)
-  static constexpr int TMEM_NEED = TM_QA + (POOL ? T::PL * kAColsPerPlane<T> : 0);
+  static constexpr int TM_E = TM_QA + (POOL ? T::PL * kAColsPerPlane<T> : 0);  // ONE: stored 2^(t - m_c)
+  static constexpr int MAX_KEYS_ONE = 512;
+  static constexpr int TMEM_NEED = TM_E + (ONE ? MAX_KEYS_ONE / 2 : 0);
   static_assert(TMEM_NEED <= 512, "forward: tensor-memory columns above 512");
   static constexpr int TMEM_COLS = pow2_cols(TMEM_NEED);
   // O leaves through the two P buffers (free once the tile's last P.V has run) when they hold the whole row block
   static constexpr bool EPI_TMA = BF16 && T::NKB * kBM * 128 <= 2 * P_BYTES;
 };
 
-template <bool BF16, int DP>
+template <bool BF16, int DP, bool ONE = false>
 __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
     geoattn_fwd_kernel(const __grid_constant__ TileMaps maps, const KParams p) {
-  using C = FwdCfg<BF16, DP>;
+  using C = FwdCfg<BF16, DP, ONE>;
   using T = typename C::T;
   constexpr int NPR = C::NPR, NK = C::NK, NSB = C::NSB;
   constexpr int PRB = NPR > 0 ? NPR : 1;  // prior-ring modulus (unused when the prior is read from L2)
@@ -682,6 +690,10 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
             ++vc;
             return true;
           };
+          if (ONE && pass == 1) {  // single score pass: pass B reads V only
+            for (int cv = 0; cv < nch && ok; ++cv) ok = load_v(cv);
+            continue;
+          }
           for (int c = 0; c < nch && ok; c += C::PAIR) {
             for (int dc = 0; dc < C::NDC && ok; ++dc) {
               const int ks = kc % NK;
@@ -790,7 +802,8 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
           for (int s = 0; s < C::LAND; ++s, ++kc) mma_commit(&bar_kempty[kc % NK]);
         }
         for (int c = 0; c < nch && ok; c += C::PAIR) ok = issue_s();  // pass A
-        int nb = 0;  // pass-B chunks whose score MMAs are issued
+        if (ONE && ok) mma_commit(&bar_qempty);  // single score pass: Q is free once pass A's MMAs have run
+        int nb = ONE ? nch : 0;  // pass-B chunks whose score MMAs are issued (none with a single score pass)
         // keeps the pass-B scores up to NSB - 1 chunks ahead; Q is released once the tile's last one is issued
         auto top_up = [&](int upto) -> bool {
           for (; nb < nch && nb + C::PAIR - 1 < upto; nb += C::PAIR) {
@@ -892,7 +905,81 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         tc_fence_before();
         mbar_arrive(&bar_sempty[g % NSB]);
       };
-      {
+      // single score pass: each pair's reference max (the values stored for it are 2^(t - mc_k)); -inf: all masked.
+      // Four scalars, set and read under warp-uniform branches (an array indexed by the pair would live in local
+      // memory).
+      static_assert(!ONE || C::MAX_KEYS_ONE / (2 * T::CH) == 4, "single score pass: four chunk pairs");
+      [[maybe_unused]] float mc0 = -INFINITY, mc1 = -INFINITY, mc2 = -INFINITY, mc3 = -INFINITY;
+      if constexpr (ONE) {
+        // as reduce_pair, and the pair's 2^(t - mref) go to tensor memory as fp16 pairs: chunk c, piece p take the
+        // 16 columns TM_E + 32 c + 16 p of this thread's lane
+        auto reduce_store = [&](uint32_t (&u0)[32], uint32_t (&u1)[32], int c, bool two) -> float {
+          float v[64];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            v[j] = __uint_as_float(u0[j]);
+            v[32 + j] = two ? __uint_as_float(u1[j]) : -INFINITY;
+          }
+          const int nv0 = p.N - (c * T::CH + piece * 32), nv1 = nv0 - T::CH;
+          if (nv1 < 32) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              v[j] = (j < nv0) ? v[j] : -INFINITY;
+              v[32 + j] = (j < nv1) ? v[32 + j] : -INFINITY;
+            }
+          }
+          float mx8[8] = {v[0], v[1], v[2], v[3], v[4], v[5], v[6], v[7]};
+#pragma unroll
+          for (int j = 8; j < 64; ++j) mx8[j & 7] = fmaxf(mx8[j & 7], v[j]);
+          const float mxa = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                                  fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+          const float mn = fmaxf(m, mxa * sc_l2);
+          const float mref = (mn == -INFINITY) ? 0.f : mn;
+          float s8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+          uint32_t h0[16], h1[16];
+#pragma unroll
+          for (int j = 0; j < 64; j += 2) {
+            const float e0 = ex2(fmaf(v[j], sc_l2, -mref)), e1 = ex2(fmaf(v[j + 1], sc_l2, -mref));
+            s8[j & 7] += e0;
+            s8[(j + 1) & 7] += e1;
+            const __half2 hh = __floats2half2_rn(e0, e1);
+            if (j < 32) h0[j / 2] = *reinterpret_cast<const uint32_t*>(&hh);
+            else h1[(j - 32) / 2] = *reinterpret_cast<const uint32_t*>(&hh);
+          }
+          l = l * ex2(m - mref) + (((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7])));
+          m = mn;
+          tmem_st16(e.lane_base + C::TM_E + c * 32 + piece * 16, h0);
+          if (two) tmem_st16(e.lane_base + C::TM_E + (c + 1) * 32 + piece * 16, h1);
+          return mn;
+        };
+        uint32_t ua[32], ub[32];
+        const int g0 = sc;
+#pragma unroll 1
+        for (int pi = 0; pi < C::MAX_KEYS_ONE / (2 * T::CH); ++pi) {
+          const int c = 2 * pi;
+          if (c < nch && ok) {
+            const bool two = c + 1 < nch;
+            ok = load_s(g0 + c, ua);
+            if (ok && two) ok = load_s(g0 + c + 1, ub);
+            if (ok) {
+              release_s(g0 + c, ua);
+              if (two) {
+                tc_fence_before();
+                mbar_arrive(&bar_sempty[(g0 + c + 1) % NSB]);
+                tmem_pin32(ub);
+              }
+              const float mr = reduce_store(ua, ub, c, two);
+              if (pi == 0) mc0 = mr;
+              else if (pi == 1) mc1 = mr;
+              else if (pi == 2) mc2 = mr;
+              else mc3 = mr;
+            }
+          }
+        }
+        tmem_wait_all();  // no load stays in flight past the loop (aborted paths included)
+        tmem_wait_st();   // the stored values are complete before pass B reads them back
+        sc += nch;
+      } else {
         // chunks in pairs: both chunks' scores are loaded, then reduced together (64 independent values per thread)
         uint32_t ua[32], ub[32];
         const int g0 = sc;
@@ -933,6 +1020,13 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       const float m1 = m + log2f(l);  // P1 = 2^(t - m1)
       const float aL = ab.a * kLog2e, bL = ab.b * kLog2e, gL = ab.g * kLog2e, cL = ab.c * kLog2e;
       float l2 = 0.f;
+      // single score pass: P1 of a stored value of pair k = value * 2^(mc_k - m1) (0 for an all-masked pair)
+      if constexpr (ONE) {
+        mc0 = ex2(mc0 - m1);
+        mc1 = ex2(mc1 - m1);
+        mc2 = ex2(mc2 - m1);
+        mc3 = ex2(mc3 - m1);
+      }
       // Pass B
       for (int c = 0; c < nch && ok; ++c) {
         const int ss = sc % NSB, ps = pc & 1, prs = prc % PRB;
@@ -941,27 +1035,51 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
           static_assert(T::PIECES == 1 && T::EW == 1, "prior read from L2 in one piece per chunk");
           load_prior32<BF16>(p.prior, p.np, row, c * T::CH, pr);
         }
-        if (!(ok = warp_wait(&bar_sfull[ss], (sc / NSB) & 1, ctx))) break;
+        // single score pass: this row's stored values of the chunk (its own tensor-memory writes, complete since
+        // pass A's wait::st), loaded before the prior wait
+        [[maybe_unused]] uint32_t ve[16];
+        if constexpr (ONE) tmem_ld16_issue(e.lane_base + C::TM_E + c * 32 + piece * 16, ve);
+        if constexpr (!ONE)
+          if (!(ok = warp_wait(&bar_sfull[ss], (sc / NSB) & 1, ctx))) break;
         if constexpr (NPR > 0)
           if (!(ok = warp_wait(&bar_prfull[prs], (prc / PRB) & 1, ctx))) break;
         tc_fence_after();
         uint8_t* preg = smem + C::OFF_P + ps * C::P_BYTES;
         const uint8_t* prt = smem + C::OFF_PR + prs * kPriorTileBytes;
         {
-          uint32_t vs[32];
+          [[maybe_unused]] uint32_t vs[32];
           float v[32];
-          tmem_ld32_issue(e.lane_base + C::TM_S + ss * T::CH + piece * 32, vs);
-          if constexpr (NPR > 0 && !BF16) prior32_smem<BF16>(prt, e.r, piece, pr);  // overlaps the tensor-memory load
-          tmem_wait32(vs);
-          tc_fence_before();
-          mbar_arrive(&bar_sempty[ss]);  // the scores are in registers: the MMA may refill the buffer
+          [[maybe_unused]] float fc = 0.f;
+          if constexpr (ONE) {
+            const int pi = c >> 1;  // warp-uniform
+            if (pi == 0) fc = mc0;
+            else if (pi == 1) fc = mc1;
+            else if (pi == 2) fc = mc2;
+            else fc = mc3;
+            tmem_wait16(ve);
+          } else {
+            tmem_ld32_issue(e.lane_base + C::TM_S + ss * T::CH + piece * 32, vs);
+            if constexpr (NPR > 0 && !BF16) prior32_smem<BF16>(prt, e.r, piece, pr);  // overlaps the TMEM load
+            tmem_wait32(vs);
+            tc_fence_before();
+            mbar_arrive(&bar_sempty[ss]);  // the scores are in registers: the MMA may refill the buffer
+          }
           const int nvalid = p.N - (c * T::CH + piece * 32);
           float l24[4] = {0.f, 0.f, 0.f, 0.f};
           // phase-ordered: 32 independent exp2 for P1, then the biased exp2 (more independent work per warp)
           auto body = [&](auto masked) {
             float p1[32];
+            if constexpr (ONE) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) p1[j] = ex2(fmaf(__uint_as_float(vs[j]), sc_l2, -m1));
+              for (int j = 0; j < 32; j += 2) {
+                const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&ve[j / 2]));
+                p1[j] = f.x * fc;
+                p1[j + 1] = f.y * fc;
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) p1[j] = ex2(fmaf(__uint_as_float(vs[j]), sc_l2, -m1));
+            }
             // bf16 staged prior: four pairs per 16-byte shared-memory load next to their use (no 32-register copy)
             [[maybe_unused]] uint32_t pw[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
@@ -998,7 +1116,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         }
         fence_proxy_async_smem();
         mbar_arrive(&bar_pfull[ps]);
-        ++sc;
+        if constexpr (!ONE) ++sc;
         ++pc;
         ++prc;
       }

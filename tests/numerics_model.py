@@ -58,7 +58,7 @@ def _per_head(x, H):
 
 
 def grads(q, k, v, dist, ang, alpha, beta, gamma, do, path, score_terms=3, dp_terms=None, prior_fp16=None,
-          dalpha_form=None, row_sums="tiles"):
+          dalpha_form=None, row_sums="tiles", fwd_p1="exact"):
     """Output and gradients (dict keyed like the oracle's grads) of the kernels' formulation on the CPU.
 
     path: "bf16" or "tf32". score_terms: TF32 terms of QK^T and (unless dp_terms says otherwise) dO V^T, 3 as in
@@ -66,7 +66,10 @@ def grads(q, k, v, dist, ang, alpha, beta, gamma, do, path, score_terms=3, dp_te
     prior_fp16: store the prior as fp16 (default: the path's choice, True for bf16). dalpha_form: "a-d2b" or
     "dz" (default: the path's choice). row_sums: "tiles" (the kernels: delta2 and a from the recomputed tiles) or
     "output" (a variant without the BF16 row pass's sweep: delta2 = rowsum(dO O) from the stored output and
-    a = rowsum(dO O') with O' = (P2 P1) V accumulated by the forward, both stored in the output dtype)."""
+    a = rowsum(dO O') with O' = (P2 P1) V accumulated by the forward, both stored in the output dtype).
+    fwd_p1: "exact" (the forward recomputes P1 = 2^(t - m1) from a second score pass) or "fp16_chunks" (a single
+    score pass: 2^(t - m_c) against the running row max m_c after each 128-key chunk, kept as fp16 until pass B
+    scales it by 2^(m_c - m1)); the backward recomputes P1 from the scores either way."""
     bf = path == "bf16"
     prior_fp16 = bf if prior_fp16 is None else prior_fp16
     dalpha_form = ("a-d2b" if bf else "dz") if dalpha_form is None else dalpha_form
@@ -93,7 +96,17 @@ def grads(q, k, v, dist, ang, alpha, beta, gamma, do, path, score_terms=3, dp_te
     m1 = m + torch.log2(l1)
     p1 = torch.exp2(t - m1)
     zl = (a * p1 + b * dp + g * ap) * LOG2E
-    e = torch.exp2(zl - c * LOG2E)
+    if fwd_p1 == "fp16_chunks":
+        p1f = torch.empty_like(t)
+        run = torch.full_like(m, -math.inf)
+        for c0 in range(0, t.shape[-1], 128):
+            blk = t[..., c0:c0 + 128]
+            run = torch.maximum(run, blk.amax(-1, keepdim=True))
+            p1f[..., c0:c0 + 128] = torch.exp2(blk - run).half().float() * torch.exp2(run - m1)
+        zl_f = (a * p1f + b * dp + g * ap) * LOG2E
+    else:
+        zl_f = zl
+    e = torch.exp2(zl_f - c * LOG2E)
     l2 = e.sum(-1, keepdim=True)
     o = matmul(e, v, prod_kind) / l2
     c2 = c * LOG2E + torch.log2(l2)

@@ -116,3 +116,31 @@ def test_dalpha_from_explicit_dz_where_it_vanishes():
         bound = ev["dalpha"]["bound"]
     assert err["dz"] <= 1e-3 * bound, (err, bound)
     assert err["dz"] * 100 <= err["a-d2b"], err
+
+
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("qscale", [1.0, 30.0], ids=["plain", "x30"])
+def test_single_score_pass_forward_with_fp16_p1(D, qscale):
+    """A BF16 forward with one score pass (2^(t - m_c) kept as fp16 per 128-key chunk, scaled in pass B) meets the
+    BF16 tolerance and moves the errors by a few per cent of the two-pass forward's; the reference's regimes too."""
+    x = _plain_inputs(D, qscale, True)
+    ref = oga.grads(*x)
+    one = _rels(nm.grads(*x, path="bf16", fwd_p1="fp16_chunks"), ref)
+    two = _rels(nm.grads(*x, path="bf16"), ref)
+    assert all(e <= TOL[torch.bfloat16] for e in one.values()), one
+    for key in KEYS:
+        assert one[key] <= 1.1 * two[key] + 1e-5, (key, one[key], two[key])
+
+
+@pytest.mark.parametrize("case", acceptance.CASES)
+def test_single_score_pass_forward_reference_regimes(case):
+    q, k, v, dist, ang, a, b, c = acceptance.case_inputs(case, B=1, H=2, N=300, D=128)
+    do = acceptance.grad_seed_do(q.shape)
+    q, k, v, do = (t.to(torch.bfloat16).float() for t in (q, k, v, do))
+    x = (q, k, v, dist, ang, a, b, c)
+    ref = oga.grads(*x, do)
+    one = _rels(nm.grads(*x, do, path="bf16", fwd_p1="fp16_chunks"), ref)
+    two = _rels(nm.grads(*x, do, path="bf16"), ref)
+    for key in KEYS:
+        assert one[key] <= 1.1 * two[key] + 1e-5, (case, key, one[key], two[key])
+
