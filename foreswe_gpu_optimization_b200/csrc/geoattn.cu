@@ -649,7 +649,9 @@ int geoattn_fwd(const GeoAttnFwdArgs* a, void* stream) {
                                 : run_fwd<true, 128>(maps, p, d, st, a->events);
     return run_fwd<true, 192>(maps, p, d, st, a->events);
   }
-  if (d.DP == 64) return run_fwd<false, 64>(maps, p, d, st, a->events);
+  if (d.DP == 64)  // single score pass up to 512 keys, as above (Q stays pooled in tensor memory)
+    return d.N <= FwdCfg<false, 64, true>::MAX_KEYS_ONE ? run_fwd<false, 64, true>(maps, p, d, st, a->events)
+                                                         : run_fwd<false, 64>(maps, p, d, st, a->events);
   if (d.DP == 128) return run_fwd<false, 128>(maps, p, d, st, a->events);
   return run_fwd<false, 192>(maps, p, d, st, a->events);
 }

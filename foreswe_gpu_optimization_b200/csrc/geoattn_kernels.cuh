@@ -538,11 +538,13 @@ __device__ __forceinline__ void store_tile(const CUtensorMap* map, const uint8_t
 template <bool BF16, int DP, bool ONE = false>
 struct FwdCfg : Tile<BF16, DP> {
   using T = Tile<BF16, DP>;
-  // ONE (bf16, head dims up to 128, up to 512 keys): a single score pass. Pass A keeps, per row, each chunk pair's
-  // 2^(t - m_c) against the running max m_c as fp16 pairs in tensor memory (256 columns for 512 keys); pass B reads
-  // them back, P1 = 2^(t - m_c) 2^(m_c - m1), and issues no score MMAs. Q stays in shared memory (its tensor-memory
-  // columns hold the stored values), the score MMAs take single 64-key chunks into two buffers.
-  static_assert(!ONE || (BF16 && DP <= 128), "single score pass: bf16 up to head dim 128");
+  // ONE (bf16 up to head dim 128, fp32 at head dim 64; up to 512 keys): a single score pass. Pass A keeps, per row,
+  // each chunk pair's 2^(t - m_c) against the running max m_c as fp16 pairs in tensor memory (256 columns for 512
+  // keys); pass B reads them back, P1 = 2^(t - m_c) 2^(m_c - m1), and issues no score MMAs. bf16: Q stays in shared
+  // memory (its tensor-memory columns hold the stored values) and the score MMAs take single 64-key chunks into two
+  // buffers; fp32: Q stays pooled in tensor memory and the score MMAs take one pair of 32-key chunks (both buffers),
+  // issued as soon as the element-wise warps have loaded the previous pair.
+  static_assert(!ONE || (BF16 && DP <= 128) || (!BF16 && DP == 64), "single score pass: bf16 <= 128 or fp32 64");
   // fp32 beyond 64: no resident Q; Q and K reach the score MMA in head-dim chunks through the K ring's slots
   static constexpr bool WIDE = !BF16 && DP > 64;
   static constexpr int NDC = WIDE ? DP / T::KB : 1;                    // head-dim chunks per score MMA
@@ -557,7 +559,7 @@ struct FwdCfg : Tile<BF16, DP> {
   // chunks (N = 128) runs at the tensor pipe's full rate, where an N = 64 MMA with both operands in shared memory
   // takes 48 cycles for 32 cycles of work (measured back to back on the B200). Head dim 192 keeps Q in shared memory
   // (4 score buffers + O + Q would need 544 columns).
-  static constexpr bool POOL = !ONE && !WIDE && (!BF16 || DP <= 128);
+  static constexpr bool POOL = !(ONE && BF16) && !WIDE && (!BF16 || DP <= 128);
   static constexpr int PAIR = (POOL || WIDE) ? 2 : 1;                 // chunks per score MMA / K ring slot
   // pooled bf16 at head dim 128: two pair slots (64 KB; a third would take the shared memory past the limit)
   static constexpr int NK = POOL ? ((BF16 && DP > 64) ? 2 : 3) : (DP <= 128 ? 3 : 2);   // K ring slots
@@ -802,7 +804,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
           for (int s = 0; s < C::LAND; ++s, ++kc) mma_commit(&bar_kempty[kc % NK]);
         }
         for (int c = 0; c < nch && ok; c += C::PAIR) ok = issue_s();  // pass A
-        if (ONE && ok) mma_commit(&bar_qempty);  // single score pass: Q is free once pass A's MMAs have run
+        if (ONE && !C::POOL && ok) mma_commit(&bar_qempty);  // single score pass: Q is free after pass A's MMAs
         int nb = ONE ? nch : 0;  // pass-B chunks whose score MMAs are issued (none with a single score pass)
         // keeps the pass-B scores up to NSB - 1 chunks ahead; Q is released once the tile's last one is issued
         auto top_up = [&](int upto) -> bool {
@@ -906,13 +908,41 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         mbar_arrive(&bar_sempty[g % NSB]);
       };
       // single score pass: each pair's reference max (the values stored for it are 2^(t - mc_k)); -inf: all masked.
-      // Four scalars, set and read under warp-uniform branches (an array indexed by the pair would live in local
-      // memory).
-      static_assert(!ONE || C::MAX_KEYS_ONE / (2 * T::CH) == 4, "single score pass: four chunk pairs");
-      [[maybe_unused]] float mc0 = -INFINITY, mc1 = -INFINITY, mc2 = -INFINITY, mc3 = -INFINITY;
+      // Up to eight scalars (4 pairs of 64-key chunks in bf16, 8 of 32-key chunks in fp32), set and read under
+      // warp-uniform branches (an array indexed by the pair would live in local memory).
+      constexpr int NPAIR = C::MAX_KEYS_ONE / (2 * T::CH);
+      static_assert(!ONE || NPAIR == 4 || NPAIR == 8, "single score pass: four or eight chunk pairs");
+      [[maybe_unused]] float mc0 = -INFINITY, mc1 = -INFINITY, mc2 = -INFINITY, mc3 = -INFINITY, mc4 = -INFINITY,
+                             mc5 = -INFINITY, mc6 = -INFINITY, mc7 = -INFINITY;
+      auto set_mc = [&](int k, float x) {
+        switch (k) {
+          case 0: mc0 = x; break;
+          case 1: mc1 = x; break;
+          case 2: mc2 = x; break;
+          case 3: mc3 = x; break;
+          case 4: mc4 = x; break;
+          case 5: mc5 = x; break;
+          case 6: mc6 = x; break;
+          default: mc7 = x; break;
+        }
+      };
+      auto get_mc = [&](int k) -> float {
+        switch (k) {
+          case 0: return mc0;
+          case 1: return mc1;
+          case 2: return mc2;
+          case 3: return mc3;
+          case 4: return mc4;
+          case 5: return mc5;
+          case 6: return mc6;
+          default: return mc7;
+        }
+      };
+      (void)set_mc;
+      (void)get_mc;
       if constexpr (ONE) {
         // as reduce_pair, and the pair's 2^(t - mref) go to tensor memory as fp16 pairs: chunk c, piece p take the
-        // 16 columns TM_E + 32 c + 16 p of this thread's lane
+        // 16 columns TM_E + c CH / 2 + 16 p of this thread's lane
         auto reduce_store = [&](uint32_t (&u0)[32], uint32_t (&u1)[32], int c, bool two) -> float {
           float v[64];
 #pragma unroll
@@ -948,14 +978,14 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
           }
           l = l * ex2(m - mref) + (((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7])));
           m = mn;
-          tmem_st16(e.lane_base + C::TM_E + c * 32 + piece * 16, h0);
-          if (two) tmem_st16(e.lane_base + C::TM_E + (c + 1) * 32 + piece * 16, h1);
+          tmem_st16(e.lane_base + C::TM_E + c * (T::CH / 2) + piece * 16, h0);
+          if (two) tmem_st16(e.lane_base + C::TM_E + (c + 1) * (T::CH / 2) + piece * 16, h1);
           return mn;
         };
         uint32_t ua[32], ub[32];
         const int g0 = sc;
 #pragma unroll 1
-        for (int pi = 0; pi < C::MAX_KEYS_ONE / (2 * T::CH); ++pi) {
+        for (int pi = 0; pi < NPAIR; ++pi) {
           const int c = 2 * pi;
           if (c < nch && ok) {
             const bool two = c + 1 < nch;
@@ -968,11 +998,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
                 mbar_arrive(&bar_sempty[(g0 + c + 1) % NSB]);
                 tmem_pin32(ub);
               }
-              const float mr = reduce_store(ua, ub, c, two);
-              if (pi == 0) mc0 = mr;
-              else if (pi == 1) mc1 = mr;
-              else if (pi == 2) mc2 = mr;
-              else mc3 = mr;
+              set_mc(pi, reduce_store(ua, ub, c, two));
             }
           }
         }
@@ -1026,6 +1052,12 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         mc1 = ex2(mc1 - m1);
         mc2 = ex2(mc2 - m1);
         mc3 = ex2(mc3 - m1);
+        if constexpr (NPAIR > 4) {
+          mc4 = ex2(mc4 - m1);
+          mc5 = ex2(mc5 - m1);
+          mc6 = ex2(mc6 - m1);
+          mc7 = ex2(mc7 - m1);
+        }
       }
       // Pass B
       for (int c = 0; c < nch && ok; ++c) {
@@ -1035,10 +1067,6 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
           static_assert(T::PIECES == 1 && T::EW == 1, "prior read from L2 in one piece per chunk");
           load_prior32<BF16>(p.prior, p.np, row, c * T::CH, pr);
         }
-        // single score pass: this row's stored values of the chunk (its own tensor-memory writes, complete since
-        // pass A's wait::st), loaded before the prior wait
-        [[maybe_unused]] uint32_t ve[16];
-        if constexpr (ONE) tmem_ld16_issue(e.lane_base + C::TM_E + c * 32 + piece * 16, ve);
         if constexpr (!ONE)
           if (!(ok = warp_wait(&bar_sfull[ss], (sc / NSB) & 1, ctx))) break;
         if constexpr (NPR > 0)
@@ -1050,12 +1078,13 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
           [[maybe_unused]] uint32_t vs[32];
           float v[32];
           [[maybe_unused]] float fc = 0.f;
+          [[maybe_unused]] uint32_t ve[16];
           if constexpr (ONE) {
-            const int pi = c >> 1;  // warp-uniform
-            if (pi == 0) fc = mc0;
-            else if (pi == 1) fc = mc1;
-            else if (pi == 2) fc = mc2;
-            else fc = mc3;
+            // this row's stored values of the chunk (its own tensor-memory writes, complete since pass A's
+            // wait::st)
+            fc = get_mc(c >> 1);  // c is warp-uniform
+            tmem_ld16_issue(e.lane_base + C::TM_E + c * (T::CH / 2) + piece * 16, ve);
+            if constexpr (NPR > 0 && !BF16) prior32_smem<BF16>(prt, e.r, piece, pr);  // overlaps the TMEM load
             tmem_wait16(ve);
           } else {
             tmem_ld32_issue(e.lane_base + C::TM_S + ss * T::CH + piece * 32, vs);

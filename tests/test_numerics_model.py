@@ -144,3 +144,25 @@ def test_single_score_pass_forward_reference_regimes(case):
     for key in KEYS:
         assert one[key] <= 1.1 * two[key] + 1e-5, (case, key, one[key], two[key])
 
+
+@pytest.mark.parametrize("qscale", [1.0, 30.0], ids=["plain", "x30"])
+def test_single_score_pass_forward_tf32_d64(qscale):
+    """The TF32 forward at head dim 64 keeps the same fp16 values: within the TF32 tolerance and within 10 % of the
+    two-pass forward's error (its P enters P.V as a TF32 operand, 11 bits like fp16)."""
+    x = _plain_inputs(64, qscale, False)
+    ref = oga.grads(*x)
+    one = _rels(nm.grads(*x, path="tf32", fwd_p1="fp16_chunks"), ref)
+    two = _rels(nm.grads(*x, path="tf32"), ref)
+    assert all(e <= TOL[torch.float32] for e in one.values()), one
+    for key in KEYS:
+        assert one[key] <= 1.1 * two[key] + 1e-6, (key, one[key], two[key])
+
+
+@pytest.mark.parametrize("case", acceptance.CASES)
+def test_single_score_pass_forward_tf32_reference_rule(case):
+    """The reference's 10x-eager rule (foreswe_bench/attn_check.py:68-81) at head dim 64 with the fp16 values."""
+    x = acceptance.case_inputs(case, B=1, H=2, N=100, D=64)
+    do = acceptance.grad_seed_do(x[0].shape)
+    ev = acceptance.evaluate(nm.grads(*x, do, path="tf32", fwd_p1="fp16_chunks"), x, do, "tf32")
+    assert all(r["passed"] for r in ev.values()), {key: r["ratio_to_eager"] for key, r in ev.items()}
+
