@@ -240,9 +240,13 @@ struct Dims {
   int nabg;
 };
 
-// The backward keeps a dS scratch and forms dQ by a GEMM (instead of a second row-pass sweep) for bf16 at every head
-// dim and for fp32 at head dim 64, where the pooled key pass has room for the transposed dS tile.
-inline bool uses_ds(const Dims& d) { return d.bf16 || d.DP == 64; }
+// The backward keeps a dS scratch and forms dQ by a GEMM (instead of a second row-pass sweep): bf16 stores dS^T
+// and reads it MN-major; fp32 at head dim 64 stores dS [query][key] (the pooled key pass has room for the transposed
+// tile); fp32 above 64 stores dS^T and its dQ GEMM transposes each tile in shared memory (TF32 operands are K-major).
+inline bool uses_ds(const Dims&) { return true; }
+
+// Row records per query row (m1, c2, delta1, delta2; fp32 above head dim 64 also b, for the key pass's d(alpha)).
+inline int nrec(const Dims& d) { return (!d.bf16 && d.DP > 64) ? 5 : 4; }
 
 // Every data pointer handed to a kernel must be memory of the current device (or managed memory): the kernels run
 // on the current device, which would dereference a host pointer or another device's memory. Checked on the host
@@ -320,7 +324,7 @@ size_t bwd_ws(const Dims& d, uint8_t* base, BwdWs* w, bool with_ds) {
   };
   BwdWs t{};
   t.status = reinterpret_cast<int*>(take(sizeof(int)));
-  t.rowrec = reinterpret_cast<float*>(take((size_t)d.B * d.H * d.np * 4 * 4));  // [B*H][np/CH][4][CH]
+  t.rowrec = reinterpret_cast<float*>(take((size_t)d.B * d.H * d.np * nrec(d) * 4));  // [B*H][np/CH][NREC][CH]
   t.part = reinterpret_cast<double*>(take((size_t)d.B * d.H * d.nrb * 3 * 8));
   if (!d.bf16) {
     const size_t nat = (size_t)2 * d.B * d.H * d.N * d.DP * 4, trn = (size_t)d.B * d.H * d.DP * d.np * 4;
@@ -332,14 +336,15 @@ size_t bwd_ws(const Dims& d, uint8_t* base, BwdWs* w, bool with_ds) {
     t.qt = reinterpret_cast<float*>(take(trn));
     t.dot = reinterpret_cast<float*>(take(trn));
   }
-  // dS scratch: bf16 dS^T [b*h][key][query]; fp32 (head dim 64) dS [b*h][query][key]
+  // dS scratch: bf16 dS^T [b*h][key][query]; fp32 at head dim 64 dS [b*h][query][key]; fp32 above dS^T
   if (with_ds && uses_ds(d)) t.dsT = take((size_t)d.B * d.H * d.np * d.np * (d.bf16 ? 2 : 4));
   if (w) *w = t;
   return off;
 }
 
 // TMA map over the bf16 dS^T scratch, viewed as 3-D (query, key, b*h); box: 64 queries x `keys` keys.
-// TMA map over the fp32 dS scratch [b*h][query][key], viewed as 3-D (key, query, b*h); box: 32 keys x `queries`.
+// TMA map over an fp32 dS scratch, [b*h][query][key] (head dim 64) or [b*h][key][query] (above), viewed as 3-D
+// (inner, outer, b*h); box: 32 inner x `queries` outer.
 int map_ds_f32(CUtensorMap* m, void* base, const Dims& d, int queries) {
   const uint64_t dims[3] = {(uint64_t)d.np, (uint64_t)d.np, (uint64_t)d.B * d.H};
   const uint64_t str[2] = {(uint64_t)d.np * 4, (uint64_t)d.np * d.np * 4};
@@ -504,6 +509,26 @@ int run_bwd_ds(const TileMaps& rmaps, const TileMaps& cmaps, const TileMaps& qma
   if (rc) return rc;
   record(ev, 2, st);
   rc = launch(geoattn_bwd_dq_kernel<DP>, DqCfg<DP>::SMEM, DqCfg<DP>::NTHREADS, persistent_grid(d), st, qmaps, pdq);
+  record(ev, 3, st);
+  return rc;
+}
+
+// fp32 above head dim 64: the wide row pass without its second sweep (records with b), the wide key pass storing the
+// fp32 dS^T tiles (and summing d(alpha), d(beta), d(gamma)), the transposing TF32 dQ GEMM.
+template <int DP>
+int run_bwd_ds_wide(const TileMaps& rmaps, const TileMaps& cmaps, const TileMaps& qmaps, const KParams& prow,
+                    const KParams& pcol, const KParams& pdq, const Dims& d, cudaStream_t st, void* const* ev) {
+  record(ev, 0, st);
+  int rc = launch(geoattn_bwd_rows_kernel<false, DP, false>, RowsCfg<false, DP, false>::SMEM,
+                  Tile<false, DP>::NTHREADS, persistent_grid(d), st, rmaps, prow);
+  if (rc) return rc;
+  record(ev, 1, st);
+  rc = launch(geoattn_bwd_cols_kernel<false, DP, true>, ColsCfg<false, DP, true>::SMEM, Tile<false, DP>::NTHREADS,
+              persistent_grid(d), st, cmaps, pcol);
+  if (rc) return rc;
+  record(ev, 2, st);
+  rc = launch(geoattn_bwd_dq_tf32t_kernel<DP>, DqTf32tCfg<DP>::SMEM, DqTf32tCfg<DP>::NTHREADS, persistent_grid(d),
+              st, qmaps, pdq);
   record(ev, 3, st);
   return rc;
 }
@@ -720,7 +745,15 @@ int backward(const GeoAttnBwdArgs* a, void* stream, bool with_ds) {
   prow.out_tma = map_output(&rm.out0, a->dq, a->dq_stride, d) ? 1 : 0;
   pcol.out_tma =
       (map_output(&cm.out0, a->dk, a->dk_stride, d) && map_output(&cm.out1, a->dv, a->dv_stride, d)) ? 1 : 0;
-  if (with_ds && !d.bf16) {
+  if (with_ds && !d.bf16 && d.DP > 64) {
+    TileMaps qm;
+    std::memset(&qm, 0, sizeof(qm));
+    if ((rc = map_ds_f32(&cm.dsT, ws.dsT, d, kBM)) || (rc = map_ds_f32(&qm.dsT, ws.dsT, d, 32)) ||
+        (rc = map_transposed(&qm.kt, ws.kt, d)))
+      return rc;
+    rc = d.DP == 128 ? run_bwd_ds_wide<128>(rm, cm, qm, prow, pcol, prow, d, st, a->events)
+                     : run_bwd_ds_wide<192>(rm, cm, qm, prow, pcol, prow, d, st, a->events);
+  } else if (with_ds && !d.bf16) {
     TileMaps qm;
     std::memset(&qm, 0, sizeof(qm));
     if ((rc = map_ds_f32(&cm.dsT, ws.dsT, d, 32)) || (rc = map_ds_f32(&qm.dsT, ws.dsT, d, kBM)) ||

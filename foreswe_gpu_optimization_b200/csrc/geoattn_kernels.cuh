@@ -75,7 +75,7 @@ struct KParams {
   void* dv;
   long long dv_str[4];
   float* stats;         // forward -> backward: [3][B*H*N] = m (log2 units), l1, l2
-  float* rowrec;        // backward row records [B*H][nchp][4][CH] = m1, c2, delta1, delta2 per row (chunk-blocked)
+  float* rowrec;        // backward row records [B*H][nchp][NREC][CH] = m1, c2, delta1, delta2[, b] (chunk-blocked)
   int nchp;             // record chunks per b*h = np / CH
   double* part;         // [B*H*nrb][3] partial d(alpha), d(beta), d(gamma)
   int* status;          // device status word (0 = ok)
@@ -287,6 +287,9 @@ struct Tile {
   static constexpr uint32_t FMT = BF16 ? 1 : 2;
   static constexpr int EW = BF16 ? 2 : 1;   // element-wise warpgroups
   static constexpr int EWT = 128 * EW;      // element-wise threads
+  // row records per query row: m1, c2, delta1, delta2; fp32 above head dim 64 also b = sum P2 P1, for the key pass's
+  // d(alpha) = sum dZ (P1 - b)
+  static constexpr int NREC = (!BF16 && DP_ > 64) ? 5 : 4;
   static constexpr int NTHREADS = EWT + 96;
   static constexpr int TMA_WARP = 4 * EW;
   static constexpr int MMA_WARP = 4 * EW + 1;
@@ -1254,14 +1257,14 @@ struct RowsCfg : Tile<BF16, DP> {
 // Row record of `row` (chunk-blocked so that the key pass can fetch one query chunk's records in one bulk copy).
 template <class T>
 __device__ __forceinline__ float* rec_ptr(const KParams& p, int bh, int row) {
-  return p.rowrec + ((size_t)bh * p.nchp + row / T::CH) * 4 * T::CH + row % T::CH;
+  return p.rowrec + ((size_t)bh * p.nchp + row / T::CH) * T::NREC * T::CH + row % T::CH;
 }
 
 template <bool BF16, int DP, bool DQ>
 __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
     geoattn_bwd_rows_kernel(const __grid_constant__ TileMaps maps, const KParams p) {
   // one sweep (dS from the key pass's scratch): bf16, and fp32 at head dim 64 (the pooled layout)
-  static_assert(DQ || BF16 || (!BF16 && DP == 64), "the dS-scratch backward is bf16 or fp32 at head dim 64");
+  // without DQ: the dS-scratch backward (bf16; fp32 at head dim 64; fp32 above 64 with the transposing dQ GEMM)
   using C = RowsCfg<BF16, DP, DQ>;
   using T = typename C::T;
   constexpr int NKV = C::NKV, NPR = C::NPR, NSB = C::NSB;
@@ -1508,6 +1511,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         }
         if constexpr (C::WIDE) {  // pairs: sweep 1; sweep 2 issues the next pair's scores before this pair's dQ
           for (int c = 0; c < nch && ok; c += C::PAIR) ok = issue(true);
+          if constexpr (!DQ) continue;  // no resident Q / dO to release
           const int kc0 = kc;
           if (ok) ok = issue(false);
           for (int c = 0; c < nch && ok; c += C::PAIR) {
@@ -1676,6 +1680,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       rec[T::CH] = c2;
       rec[2 * T::CH] = valid ? delta1 : 0.f;
       rec[3 * T::CH] = valid ? delta2 : 0.f;
+      if constexpr (T::NREC > 4) rec[4 * T::CH] = valid ? acc[2] : 0.f;  // b
     }
     // Sweep 2. d(alpha) of the row is summed again here from the explicit dZ, as sum dZ (P1 - b) with b = sum P2 P1:
     // sum dZ is 0 in exact arithmetic, but the recomputed P2 sum to 1 + eps (fp32 rounding of c2, exp2), which
@@ -1764,7 +1769,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         for (int w = 0; w < 4 * T::EW; ++w)
           for (int k = 0; k < 3; ++k) s3[k] += red[w][k];
         double* out = p.part + ((size_t)bh * p.nrb + rb) * 3;
-        out[0] = s3[0];
+        if constexpr (DQ || !C::WIDE) out[0] = s3[0];  // wide without dQ: the key pass sums d(alpha)
         if constexpr (DQ) {
           out[1] = s3[1];
           out[2] = s3[2];
@@ -1836,7 +1841,7 @@ struct ColsCfg : Tile<BF16, DP> {
   static constexpr int Q_BYTES = WIDE ? 0 : T::CH * DP * T::EB;  // per plane per buffer (Q and dO chunks)
   static constexpr int QT_BYTES = BF16 ? 0 : DP * 128;      // fp32: transposed Q / dO chunk (hi)
   static constexpr int ST_BYTES = kBM * 128;                // P2^T or dS^T tile
-  static constexpr int REC_BYTES = 4 * T::CH * 4;           // row records of one query chunk: m1, c2, delta1, delta2
+  static constexpr int REC_BYTES = T::NREC * T::CH * 4;     // row records of one query chunk: m1, c2, delta1, delta2[, b]
   static constexpr int OFF_RS = 0;
   static constexpr int OFF_K = OFF_RS + NRS * 2 * SLOT_PLANE;
   static constexpr int OFF_V = OFF_K + T::PL * K_BYTES;
@@ -1852,7 +1857,7 @@ struct ColsCfg : Tile<BF16, DP> {
   static constexpr int OFF_REC = OFF_PR + NPR * kPriorTileBytes;
   // fp32 with a dS scratch: the TF32 dQ GEMM needs dS K-major along the keys, so each staged tile is also written
   // transposed, [32 queries][128 keys] as four 128-byte-swizzled regions of 32 keys, for its TMA store
-  static constexpr bool DST = SDS && !BF16;
+  static constexpr bool DST = SDS && !BF16 && !WIDE;
   static constexpr int DST_BYTES = 32 * kBM * 4;
   static constexpr int OFF_DST = (OFF_REC + NR * REC_BYTES + 1023) / 1024 * 1024;
   static constexpr int SMEM = DST ? OFF_DST + NST * DST_BYTES : OFF_REC + NR * REC_BYTES;
@@ -1874,7 +1879,6 @@ struct ColsCfg : Tile<BF16, DP> {
 template <bool BF16, int DP, bool SDS>
 __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
     geoattn_bwd_cols_kernel(const __grid_constant__ TileMaps maps, const KParams p) {
-  static_assert(!SDS || BF16 || DP == 64, "the dS-scratch backward is bf16 or fp32 at head dim 64");
   using C = ColsCfg<BF16, DP, SDS>;
   using T = typename C::T;
   constexpr int NQ = C::NQ, NSB = C::NSB, NR = C::NR, NST = C::NST, NPR = C::NPR;
@@ -1889,7 +1893,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
                 "ring deeper than its barrier array");
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_flag;
-  __shared__ double redc[8][2];
+  __shared__ double redc[8][3];
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   // chunks every role iterates; wide: whole pairs (an extra chunk past N has +inf row records: P1 = P2 = dS = 0)
   const int nch = C::PAIR == 2 ? (((p.N + T::CH - 1) / T::CH + 1) & ~1) : (p.N + T::CH - 1) / T::CH;
@@ -1949,7 +1953,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
           for (int rg = 0; rg < 4; ++rg)
             tma_store_3d(&maps.dsT, smem + C::OFF_DST + ts * C::DST_BYTES + rg * (32 * 128), kblk * kBM + rg * 32,
                          c * T::CH, bh);
-        } else {
+        } else {  // the staged dS^T tile itself, [keys][queries] (bf16; wide fp32: 32 queries, TF32-rounded)
           tma_store_3d(&maps.dsT, smem + C::OFF_DS + ts * C::ST_BYTES, c * T::CH, kblk * kBM, bh);
         }
         bulk_commit();
@@ -2005,7 +2009,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         auto load_records = [&]() -> bool {
           if (!mbar_wait(&bar_recempty[rs], ((gc / NR) & 1) ^ 1, ctx)) return false;
           mbar_arrive_expect_tx(&bar_recfull[rs], C::REC_BYTES);
-          bulk_load(smem + C::OFF_REC + rs * C::REC_BYTES, p.rowrec + ((size_t)bh * p.nchp + c) * 4 * T::CH,
+          bulk_load(smem + C::OFF_REC + rs * C::REC_BYTES, p.rowrec + ((size_t)bh * p.nchp + c) * T::NREC * T::CH,
                     C::REC_BYTES, &bar_recfull[rs]);
           return true;
         };
@@ -2178,6 +2182,10 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       ew_sync(T::EWT);
     }
     float gbp[2] = {0.f, 0.f}, ggp[2] = {0.f, 0.f};  // with SDS: this key's d(beta), d(gamma) partials
+    // wide fp32 with SDS: this key's d(alpha) partial, sum dZ (P1 - b) with the row's b = sum P2 P1 (the row pass has
+    // no second sweep to sum it there; the - b term cancels the bias of sum dZ, which the recomputed P2 leave at
+    // -eps delta2 instead of 0)
+    float gap[2] = {0.f, 0.f};
     // P2 and dS of one 32-column piece from its scores S^T, dP^T, the chunk's row records and the prior; keys past N
     // (last block only) produce rows of P2^T / dS^T that only reach dK/dV rows that are never stored, so no per-key
     // mask is needed
@@ -2194,6 +2202,14 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
         const float4 d2 = *reinterpret_cast<const float4*>(rec + 3 * T::CH + q);
         const float mm[4] = {m4.x, m4.y, m4.z, m4.w}, cc[4] = {c4.x, c4.y, c4.z, c4.w};
         const float e1[4] = {d1.x, d1.y, d1.z, d1.w}, e2[4] = {d2.x, d2.y, d2.z, d2.w};
+        [[maybe_unused]] float bb[4] = {0.f, 0.f, 0.f, 0.f};
+        if constexpr (SDS && C::WIDE) {
+          const float4 b4 = *reinterpret_cast<const float4*>(rec + 4 * T::CH + q);
+          bb[0] = b4.x;
+          bb[1] = b4.y;
+          bb[2] = b4.z;
+          bb[3] = b4.w;
+        }
         [[maybe_unused]] uint32_t pw[4] = {0u, 0u, 0u, 0u};
         if constexpr (BF16 && NPR > 0) {
           const uint4 u = *reinterpret_cast<const uint4*>(prt + piece * (kBM * 128) + sw128(e.r, j4 / 4));
@@ -2222,6 +2238,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
             gbp[k & 1] = fmaf(dz, dpj, gbp[k & 1]);
             ggp[k & 1] = fmaf(dz, apj, ggp[k & 1]);
           }
+          if constexpr (SDS && C::WIDE) gap[k & 1] = fmaf(dz, p1 - bb[k], gap[k & 1]);
         }
       }
     };
@@ -2275,27 +2292,29 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
       fence_proxy_async_smem();
       mbar_arrive(&bar_tfull[ts]);
     }
-    if constexpr (SDS) {  // block partials of d(beta), d(gamma) (keys past N excluded)
+    if constexpr (SDS) {  // block partials of d(beta), d(gamma) (keys past N excluded); wide: d(alpha) too
       double gb = kvalid ? (double)(gbp[0] + gbp[1]) : 0.0, gg = kvalid ? (double)(ggp[0] + ggp[1]) : 0.0;
+      double ga = (C::WIDE && kvalid) ? (double)(gap[0] + gap[1]) : 0.0;
 #pragma unroll
       for (int off = 16; off > 0; off >>= 1) {
         gb += __shfl_down_sync(0xffffffffu, gb, off);
         gg += __shfl_down_sync(0xffffffffu, gg, off);
+        ga += __shfl_down_sync(0xffffffffu, ga, off);
       }
       if (lane == 0) {
         redc[warp][0] = gb;
         redc[warp][1] = gg;
+        redc[warp][2] = ga;
       }
       ew_sync(T::EWT);
       if (threadIdx.x == 0) {
-        double s2[2] = {0.0, 0.0};
-        for (int w = 0; w < 4 * T::EW; ++w) {
-          s2[0] += redc[w][0];
-          s2[1] += redc[w][1];
-        }
+        double s3[3] = {0.0, 0.0, 0.0};
+        for (int w = 0; w < 4 * T::EW; ++w)
+          for (int k = 0; k < 3; ++k) s3[k] += redc[w][k];
         double* out = p.part + ((size_t)bh * p.nrb + kblk) * 3;
-        out[1] = s2[0];
-        out[2] = s2[1];
+        if constexpr (C::WIDE) out[0] = s3[2];
+        out[1] = s3[0];
+        out[2] = s3[1];
       }
     }
     if (ok) ok = warp_wait(&bar_done, it & 1, ctx);
@@ -2601,6 +2620,160 @@ __global__ void __launch_bounds__(DqTf32Cfg<DP>::NTHREADS, 1)
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++it) {
       const int rb = tile % p.nrb, bh = tile / p.nrb, b = bh / p.H, h = bh % p.H;
       const int row = rb * kBM + r, ab = it & 1;
+      if (ok) ok = warp_wait(&bar_accfull[ab], (it >> 1) & 1, ctx);
+      tc_fence_after();
+      const long long qoff = (long long)b * p.dq_str[0] + (long long)h * p.dq_str[1] + (long long)row * p.dq_str[2];
+      if (ok) {
+#pragma unroll 1
+        for (int d0 = 0; d0 < DP; d0 += 32) {
+          float v[32];
+          tmem_ld32(lane_base + ab * DP + d0, v);
+          if (row < p.N && d0 < p.D) store_row32<false>(p.dq, qoff, p.dq_str[3], d0, p.D, v, p.inv_sqrt_d);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&bar_accempty[ab]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, C::TMEM_COLS);
+}
+
+// ===============================================================================================================
+// dQ = dS K / sqrt(d) for fp32 storage (TF32, 1 term) above head dim 64, from the fp32 dS^T tiles [b*h][key][query]
+// the wide key pass stored (its staged A operand of dK, queries contiguous). TF32 MMAs take K-major operands only, so
+// the four element-wise warps transpose each 32-key x 128-query tile in shared memory into the K-major A operand
+// [query][key] (thread = query row: 32 reads down one column of the landed tile, 8 swizzled 16-byte writes) before the
+// MMA reads it; B is the transposed hi plane of K [b*h][d][key]. One CTA per (128-query block, b*h), persistent; per
+// 32-key chunk four M = 128, N = DP, K = 8 MMAs; the accumulator double-buffered in tensor memory; the same warps
+// store dQ (row stores). Warps: 4 transposing / epilogue, 1 TMA, 1 MMA.
+// ===============================================================================================================
+template <int DP>
+struct DqTf32tCfg {
+  using T = Tile<false, DP>;
+  static constexpr int NSTAGE = 3;
+  static constexpr int RAW_BYTES = 4 * 32 * 128;  // the landed dS^T tile: four 32-query boxes of 32 keys x 128 B
+  static constexpr int A_BYTES = kBM * 128;       // dS K-major: 128 queries x 32 keys
+  static constexpr int B_BYTES = DP * 128;        // K^T: DP rows x 32 keys
+  static constexpr int STAGE = RAW_BYTES + A_BYTES + B_BYTES;
+  static constexpr int SMEM = NSTAGE * STAGE;
+  static constexpr int TMEM_COLS = pow2_cols(2 * DP);
+  static constexpr int NTHREADS = 128 + 64;
+  static constexpr int TMA_WARP = 4, MMA_WARP = 5;
+  static_assert(SMEM + 1024 <= kSmemPerBlock, "transposing TF32 dQ GEMM: shared memory above the per-block limit");
+  static_assert(2 * DP <= 512, "transposing TF32 dQ GEMM: two accumulators in tensor memory");
+};
+
+template <int DP>
+__global__ void __launch_bounds__(DqTf32tCfg<DP>::NTHREADS, 1)
+    geoattn_bwd_dq_tf32t_kernel(const __grid_constant__ TileMaps maps, const KParams p) {
+  using C = DqTf32tCfg<DP>;
+  constexpr int NS = C::NSTAGE;
+  if (smem_misaligned(p.status)) return;  // uniform over the CTA, before any barrier or allocation
+  uint8_t* smem = smem_raw;
+  __shared__ uint64_t bar_full[NS], bar_afull[NS], bar_empty[NS], bar_accfull[2], bar_accempty[2];
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ int abort_flag;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int nchunks = (p.N + 31) / 32;  // key chunks (keys past N meet zero dS rows and zero-padded K^T columns)
+  const int ntiles = p.nrb * p.B * p.H;
+  WaitCtx ctx{&abort_flag, p.status};
+
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&bar_full[i], 1);
+      mbar_init(&bar_afull[i], 128);
+      mbar_init(&bar_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bar_accfull[i], 1);
+      mbar_init(&bar_accempty[i], 128);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(&tmem_base_sh, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base_sh;
+  const uint32_t sbase = smem_u32(smem);
+
+  if (warp == C::TMA_WARP) {
+    if (lane == 0) {
+      prefetch_tmap(&maps.dsT);
+      prefetch_tmap(&maps.kt);
+      int sc = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+        const int rb = tile % p.nrb, bh = tile / p.nrb, b = bh / p.H, h = bh % p.H;
+        for (int c = 0; c < nchunks && ok; ++c, ++sc) {
+          const int st = sc % NS;
+          if (!(ok = mbar_wait(&bar_empty[st], ((sc / NS) & 1) ^ 1, ctx))) break;
+          uint8_t* dst = smem + st * C::STAGE;
+          mbar_arrive_expect_tx(&bar_full[st], C::RAW_BYTES + C::B_BYTES);
+          for (int j = 0; j < 4; ++j)
+            tma_load_3d(dst + j * (32 * 128), &maps.dsT, &bar_full[st], rb * kBM + j * 32, c * 32, bh);
+          tma_tileT(dst + C::RAW_BYTES + C::A_BYTES, &maps.kt, &bar_full[st], c * 32, h, b);
+        }
+      }
+    }
+  } else if (warp == C::MMA_WARP) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = instr_desc(2, 0, 0, 128, DP);  // tf32, A and B K-major
+      int sc = 0, it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++it) {
+        const int ab = it & 1;
+        if (!(ok = mbar_wait(&bar_accempty[ab], ((it >> 1) & 1) ^ 1, ctx))) break;
+        tc_fence_after();
+        for (int c = 0; c < nchunks && ok; ++c, ++sc) {
+          const int st = sc % NS;
+          if (!(ok = mbar_wait(&bar_afull[st], (sc / NS) & 1, ctx))) break;
+          tc_fence_after();
+          const uint32_t a = sbase + st * C::STAGE + C::RAW_BYTES, bsrc = a + C::A_BYTES;
+#pragma unroll
+          for (int s = 0; s < 4; ++s)  // K = 8 keys (32 bytes) per MMA
+            mma_ss<Kind::kTF32>(tmem + ab * DP, smem_desc_sw128(a + s * 32, 16, 1024),
+                                smem_desc_sw128(bsrc + s * 32, 16, 1024), idesc, (c > 0 || s > 0) ? 1u : 0u);
+          mma_commit(&bar_empty[st]);
+        }
+        if (ok) mma_commit(&bar_accfull[ab]);
+      }
+    }
+  } else {
+    // ---------------- transposing / epilogue warps: thread = query row ----------------
+    const int r = (warp & 3) * 32 + lane;
+    const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+    int sc = 0, it = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++it) {
+      const int rb = tile % p.nrb, bh = tile / p.nrb, b = bh / p.H, h = bh % p.H;
+      const int row = rb * kBM + r, ab = it & 1;
+      for (int c = 0; c < nchunks; ++c, ++sc) {
+        const int st = sc % NS;
+        if (ok) ok = warp_wait(&bar_full[st], (sc / NS) & 1, ctx);
+        // the landed tile (box j = queries 32 j .. 32 j + 31): key k of query r at row k of box r / 32, word r % 32
+        const uint8_t* raw = smem + st * C::STAGE + (r >> 5) * (32 * 128);
+        uint8_t* arow = smem + st * C::STAGE + C::RAW_BYTES;
+        if (ok) {
+#pragma unroll
+          for (int k4 = 0; k4 < 8; ++k4) {
+            float4 v;
+            v.x = *reinterpret_cast<const float*>(raw + sw128(4 * k4, (r & 31) >> 2) + (r & 3) * 4);
+            v.y = *reinterpret_cast<const float*>(raw + sw128(4 * k4 + 1, (r & 31) >> 2) + (r & 3) * 4);
+            v.z = *reinterpret_cast<const float*>(raw + sw128(4 * k4 + 2, (r & 31) >> 2) + (r & 3) * 4);
+            v.w = *reinterpret_cast<const float*>(raw + sw128(4 * k4 + 3, (r & 31) >> 2) + (r & 3) * 4);
+            *reinterpret_cast<float4*>(arow + sw128(r, k4)) = v;
+          }
+        }
+        fence_proxy_async_smem();  // the generic writes above become visible to the MMA's reads
+        mbar_arrive(&bar_afull[st]);
+      }
       if (ok) ok = warp_wait(&bar_accfull[ab], (it >> 1) & 1, ctx);
       tc_fence_after();
       const long long qoff = (long long)b * p.dq_str[0] + (long long)h * p.dq_str[1] + (long long)row * p.dq_str[2];

@@ -51,15 +51,15 @@ def test_size_queries_without_gpu(L):
     assert L.geoattn_fwd_workspace_bytes(ctypes.byref(fp)) == 256 + 2 * (2 * 16 * 128 * 4) + 128 * 128 * 4
     for dtype in (_lib.DTYPE_FP32, _lib.DTYPE_BF16):  # head_dim above 192 has no kernel
         assert L.geoattn_fwd_workspace_bytes(ctypes.byref(_lib.Shape(1, 1, 16, 200, dtype, 0))) == 0
-    # fp32 backward (N = 16: N_pad 128, one row block): status word, row records, partials, hi/lo planes of q, k, v, dO,
-    # transposed hi planes of k, q, dO, each rounded up to 256 bytes; at head_dim <= 64 also the fp32 dS scratch
-    # (N_pad^2 per b*h) for the dQ GEMM, above 64 none (dQ from the row pass's second sweep)
+    # fp32 backward (N = 16: N_pad 128, one row block): status word, row records (4 floats per row; 5 above head dim
+    # 64, where b = sum P2 P1 joins them), partials, hi/lo planes of q, k, v, dO, transposed hi planes of k, q, dO,
+    # each rounded up to 256 bytes, and the fp32 dS scratch (N_pad^2 per b*h) for the dQ GEMM
     f64 = _lib.Shape(1, 1, 16, 64, _lib.DTYPE_FP32, 0)
     assert L.geoattn_bwd_workspace_bytes(ctypes.byref(f64)) == (256 + 128 * 16 + 256 + 4 * (2 * 16 * 64 * 4)
                                                                 + 3 * (64 * 128 * 4) + 128 * 128 * 4)
     f128 = _lib.Shape(1, 1, 16, 128, _lib.DTYPE_FP32, 0)
-    assert L.geoattn_bwd_workspace_bytes(ctypes.byref(f128)) == (256 + 128 * 16 + 256 + 4 * (2 * 16 * 128 * 4)
-                                                                 + 3 * (128 * 128 * 4))
+    assert L.geoattn_bwd_workspace_bytes(ctypes.byref(f128)) == (256 + 128 * 20 + 256 + 4 * (2 * 16 * 128 * 4)
+                                                                 + 3 * (128 * 128 * 4) + 128 * 128 * 4)
 
 
 def test_invalid_arguments_rejected_before_any_launch(L):

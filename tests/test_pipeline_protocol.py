@@ -142,13 +142,16 @@ def test_forward_wide_pairs_deadlock_with_the_unpaired_lag(ndc, nk):
     assert _forward_order(16, ndc, nk, NSB - 1) is not None
 
 
-def _key_pass_wide_order(n, ndc, nrs, records_first):
+def _key_pass_wide_order(n, ndc, nrs, records_first, slag=None):
     """Wide fp32 key pass, one tile, query chunks in pairs: per chunk the TMA loads its row records (two buffers),
     before chunk 0 and each odd chunk the slots of the next pair (2*ndc head-dim slots through an nrs-slot ring), then
     the chunk's transposed Q/dO (one buffer, free once the previous chunk's dV/dK ran). The MMA issues a pair into both
     score buffers, the next pair after the first chunk's dV/dK. The element-wise warps need a chunk's scores and its
-    records before they free its score buffer, and stage P2^T/dS^T (one buffer). Returns None or the deadlock state."""
-    st = dict(sl=0, sc=0, s_iss=0, s_rel=0, staged=0, dvdk=0, qt=0, rec=0, rec_read=0)
+    records before they free its score buffer, and stage P2^T/dS^T (one buffer). With `slag` (the dS-scratch backward)
+    the TMA also stores the staged dS^T tile of chunk c - slag after chunk c's transposed Q/dO, and the staging buffer
+    is free for the next chunk only once both its dV/dK MMAs and its store have read it. Returns None or the deadlock
+    state."""
+    st = dict(sl=0, sc=0, s_iss=0, s_rel=0, staged=0, dvdk=0, qt=0, rec=0, rec_read=0, stored=0)
 
     def tma():
         def slots():
@@ -170,6 +173,13 @@ def _key_pass_wide_order(n, ndc, nrs, records_first):
             st["qt"] = c + 1
             if not records_first:
                 yield from records()
+            if slag is not None and c >= slag:
+                yield lambda g=c - slag: st["staged"] > g
+                st["stored"] = c - slag + 1
+        if slag is not None:
+            for g in range(max(0, n - slag), n):
+                yield lambda g=g: st["staged"] > g
+                st["stored"] = g + 1
 
     def mma():
         def issue(j):
@@ -191,7 +201,7 @@ def _key_pass_wide_order(n, ndc, nrs, records_first):
             yield lambda c=c: st["s_iss"] > c and st["rec"] > c
             st["s_rel"] = c + 1
             st["rec_read"] = c + 1
-            yield lambda c=c: st["dvdk"] >= c
+            yield lambda c=c: st["dvdk"] >= c and (slag is None or st["stored"] >= c)
             st["staged"] = c + 1
 
     progs = [tma(), mma(), ew()]
@@ -220,6 +230,16 @@ def test_key_pass_wide_order(ndc, n):
     assert _key_pass_wide_order(n, ndc, 3, records_first=True) is None
     if n >= 4:
         assert _key_pass_wide_order(n, ndc, 3, records_first=False) is not None
+
+
+@pytest.mark.parametrize("ndc", [4, 6], ids=["d128", "d192"])
+@pytest.mark.parametrize("n", [1, 2, 3, 4, 10, 48])
+def test_key_pass_wide_store_lag(ndc, n):
+    """ColsCfg<false, DP > 64, true>: one query-chunk buffer and one staging buffer (NQ = NST = 1), the dS^T stores
+    trailing by one chunk (SLAG = 1 = NQ + NST - 1); a store two chunks behind waits on a staging that waits on it."""
+    assert _key_pass_wide_order(n, ndc, 3, records_first=True, slag=1) is None
+    if n >= 3:
+        assert _key_pass_wide_order(n, ndc, 3, records_first=True, slag=2) is not None
 
 
 def _rows_wide_pair_order(nch, ndc, nkv, kt_lag_pairs, nds=1):
