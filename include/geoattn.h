@@ -119,8 +119,8 @@ typedef struct {
 /* dQ, dK, dV and the bias-parameter gradients; replaces FusedGeoAttentionV2.backward
  * (geo_attention_v2.py:428-461). Deterministic: no atomics, fixed reduction order. BF16: the workspace holds a
  * bf16 dS scratch of B*H*N_pad^2 elements (N_pad = N rounded up to 128), which the key pass writes and a dQ GEMM
- * reads; FP32 with head_dim <= 64: the same with an fp32 scratch and a TF32 dQ GEMM; FP32 above 64: dQ comes from a
- * second sweep of the row pass. */
+ * reads; FP32: the same with an fp32 scratch of B*H*N_pad^2 elements and a TF32 dQ GEMM (above head_dim 64 the GEMM
+ * transposes each dS tile in shared memory). */
 int geoattn_bwd(const GeoAttnBwdArgs* args, void* stream);
 
 /* Allocation-free backward (no counterpart in the reference, which always allocates through PyTorch).
