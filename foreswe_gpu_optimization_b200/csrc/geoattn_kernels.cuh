@@ -2652,7 +2652,7 @@ __global__ void __launch_bounds__(DqTf32Cfg<DP>::NTHREADS, 1)
 template <int DP>
 struct DqTf32tCfg {
   using T = Tile<false, DP>;
-  static constexpr int NSTAGE = 3;
+  static constexpr int NSTAGE = 4;
   static constexpr int RAW_BYTES = 4 * 32 * 128;  // the landed dS^T tile: four 32-query boxes of 32 keys x 128 B
   static constexpr int A_BYTES = kBM * 128;       // dS K-major: 128 queries x 32 keys
   static constexpr int B_BYTES = DP * 128;        // K^T: DP rows x 32 keys
