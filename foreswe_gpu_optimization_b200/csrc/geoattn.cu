@@ -776,9 +776,8 @@ int backward(const GeoAttnBwdArgs* a, void* stream, bool with_ds) {
     else if (d.DP == 128) rc = run_bwd<true, 128>(rm, cm, prow, pcol, d, st, a->events);
     else rc = run_bwd<true, 192>(rm, cm, prow, pcol, d, st, a->events);
   } else {
-    if (d.DP == 64) rc = run_bwd<false, 64>(rm, cm, prow, pcol, d, st, a->events);
-    else if (d.DP == 128) rc = run_bwd<false, 128>(rm, cm, prow, pcol, d, st, a->events);
-    else rc = run_bwd<false, 192>(rm, cm, prow, pcol, d, st, a->events);
+    // fp32 always keeps the dS scratch (geoattn_bwd); the allocation-free entry rejects fp32 before this point
+    rc = GEOATTN_ERR_UNSUPPORTED;
   }
   if (rc) return rc;
   finalize_abg_kernel<<<dim3(3, d.nabg), 256, 0, st>>>(ws.part, d.B, d.H, d.nrb, a->shape.per_head, a->dabg);
