@@ -440,10 +440,11 @@ template <int BROWS>
 constexpr int kSlotPlaneBytesRows = (kBM + BROWS) * 128;
 template <class T, int BROWS>
 __device__ __forceinline__ void tma_slot_rows(uint8_t* slot, uint64_t* bar, const CUtensorMap* amap, int arow0,
-                                              const CUtensorMap* bmap, int brow0, int dc, int h, int b, int B) {
+                                              const CUtensorMap* bmap, int brow0, int dc, int h, int b, int B,
+                                              bool a_hi = true) {
   constexpr int SPB = kSlotPlaneBytesRows<BROWS>;
   for (int pl = 0; pl < 2; ++pl) {
-    tma_load_4d(slot + pl * SPB, amap, bar, dc * T::KB, arow0, h, b + pl * B);
+    if (pl > 0 || a_hi) tma_load_4d(slot + pl * SPB, amap, bar, dc * T::KB, arow0, h, b + pl * B);
     for (int r = 0; r < BROWS; r += 32)
       tma_load_4d(slot + pl * SPB + (kBM + r) * 128, bmap, bar, dc * T::KB, brow0 + r, h, b + pl * B);
   }
@@ -453,6 +454,36 @@ __device__ __forceinline__ void mma_slot_rows(uint32_t tmem_acc, uint32_t slot, 
   static_assert(!T::kBF16 && T::CH == 32, "slots carry fp32 planes with 32-row B chunks");
   constexpr int SPB = kSlotPlaneBytesRows<BROWS>;
   mma_qk<T, BROWS, T::KB>(tmem_acc, slot, SPB, slot + kBM * 128, SPB, accumulate);
+}
+// The same product with the A operand's hi plane resident in tensor memory (columns tmem_ah: the 32 fp32 of this
+// head-dim chunk, lane = row): (hi,hi) and (hi,lo) read A from tensor memory, (lo,hi) the lo plane from the slot, so
+// the slot needs no hi plane of A.
+template <class T, int BROWS>
+__device__ __forceinline__ void mma_slot_rows_ah(uint32_t tmem_acc, uint32_t slot, uint32_t tmem_ah, bool accumulate) {
+  static_assert(!T::kBF16 && T::CH == 32 && T::NTERM == 3, "slots carry fp32 planes with 32-row B chunks");
+  constexpr int SPB = kSlotPlaneBytesRows<BROWS>;
+  constexpr uint32_t idesc = instr_desc(T::FMT, 0, 0, 128, BROWS);
+  const uint32_t b0 = slot + kBM * 128;
+  int first = accumulate ? 0 : 1;
+#pragma unroll
+  for (int term = 0; term < 3; ++term) {
+#pragma unroll
+    for (int s = 0; s < T::KB / T::KS; ++s) {  // K = 8 elements (32 bytes, 8 columns) per MMA
+      const uint64_t bd = smem_desc_sw128(b0 + (term == 1 ? SPB : 0) + s * 32, 16, 1024);
+      if (term < 2)
+        mma_ts<T::KIND>(tmem_acc, tmem_ah + s * 8, bd, idesc, first ? 0u : 1u);
+      else
+        mma_ss<T::KIND>(tmem_acc, smem_desc_sw128(slot + SPB + s * 32, 16, 1024), bd, idesc, 1u);
+      first = 0;
+    }
+  }
+}
+// Copies the hi plane of a slot's 128-row A chunk (one head-dim chunk, 128 rows x 128 B) into tensor memory as an A
+// operand (columns tmem_ah .. tmem_ah + 31). Every MMA that read those columns before must have completed.
+template <class T>
+__device__ __forceinline__ void cp_slot_a_hi(uint32_t tmem_ah, uint32_t slot) {
+#pragma unroll
+  for (int s = 0; s < T::KB / T::KS; ++s) tmem_cp_128x256b(tmem_ah + s * 8, smem_desc_sw128(slot + s * 32, 16, 1024));
 }
 // Two consecutive chunks (rows c*CH .. c*CH + 2*CH) of a natural operand, hi[/lo] planes, into one ring slot laid out
 // [plane][region][2*CH rows x 128 B], so that the slot is a 2*CH-row K-major B operand.
@@ -594,7 +625,10 @@ struct FwdCfg : Tile<BF16, DP> {
   static constexpr int TM_QA = TM_O + DP;  // pooled: Q (hi, lo)
   static constexpr int TM_E = TM_QA + (POOL ? T::PL * kAColsPerPlane<T> : 0);  // ONE: stored 2^(t - m_c)
   static constexpr int MAX_KEYS_ONE = 512;
-  static constexpr int TMEM_NEED = TM_E + (ONE ? MAX_KEYS_ONE / 2 : 0);
+  // wide: Q's hi plane in tensor memory (DP columns), copied from the tile's first slots, so that later slots carry
+  // only Q's lo plane (a third fewer streamed bytes)
+  static constexpr int TM_QH = TM_E + (ONE ? MAX_KEYS_ONE / 2 : 0);
+  static constexpr int TMEM_NEED = TM_QH + (WIDE ? DP : 0);
   static_assert(TMEM_NEED <= 512, "forward: tensor-memory columns above 512");
   static constexpr int TMEM_COLS = pow2_cols(TMEM_NEED);
   // O leaves through the two P buffers (free once the tile's last P.V has run) when they hold the whole row block
@@ -700,14 +734,16 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
             continue;
           }
           for (int c = 0; c < nch && ok; c += C::PAIR) {
+            // wide: Q's hi plane only in the tile's first slots (the MMA warp keeps it in tensor memory)
+            [[maybe_unused]] const bool qh = pass == 0 && c == 0;
             for (int dc = 0; dc < C::NDC && ok; ++dc) {
               const int ks = kc % NK;
               if (!(ok = mbar_wait(&bar_kempty[ks], ((kc / NK) & 1) ^ 1, ctx))) break;
-              mbar_arrive_expect_tx(&bar_kfull[ks], T::PL * C::K_BYTES);
+              mbar_arrive_expect_tx(&bar_kfull[ks], T::PL * C::K_BYTES - ((C::WIDE && !qh) ? kBM * 128 : 0));
               uint8_t* slot = smem + C::OFF_K + ks * T::PL * C::K_BYTES;
               if constexpr (C::WIDE)
                 tma_slot_rows<T, C::PAIR * T::CH>(slot, &bar_kfull[ks], &maps.q, rb * kBM, &maps.k, c * T::CH, dc, h,
-                                                  b, p.B);
+                                                  b, p.B, qh);
               else if constexpr (C::POOL)
                 tma_pair<T>(slot, &maps.k, &bar_kfull[ks], c, h, b, p.B);
               else
@@ -743,7 +779,7 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
     if (lane == 0) {
       int kc = 0, sc = 0, pc = 0, it = 0;
       bool ok = true;
-      auto issue_s = [&](void) -> bool {
+      auto issue_s = [&](bool land = false) -> bool {
         const int ss = sc % NSB;
         if constexpr (C::WIDE) {  // a chunk pair into two adjacent score buffers, accumulated over head-dim chunks
           if (!mbar_wait(&bar_sempty[ss], ((sc / NSB) & 1) ^ 1, ctx)) return false;
@@ -752,8 +788,11 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
             const int ks = kc % NK;
             if (!mbar_wait(&bar_kfull[ks], (kc / NK) & 1, ctx)) return false;
             tc_fence_after();
-            mma_slot_rows<T, C::PAIR * T::CH>(tmem + C::TM_S + ss * T::CH,
-                                              sbase + C::OFF_K + ks * T::PL * C::K_BYTES, dc > 0);
+            const uint32_t slot = sbase + C::OFF_K + ks * T::PL * C::K_BYTES, qh = tmem + C::TM_QH + dc * T::KB;
+            // the tile's first pair: Q's hi chunk into tensor memory (the MMAs below read it, after the copy, and
+            // the slot is released once they have completed)
+            if (land) cp_slot_a_hi<T>(qh, slot);
+            mma_slot_rows_ah<T, C::PAIR * T::CH>(tmem + C::TM_S + ss * T::CH, slot, qh, dc > 0);
             mma_commit(&bar_kempty[ks]);
             ++kc;
           }
@@ -806,7 +845,11 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
           cp_drain_operand<T>(tmem + C::TM_S + (sc % NSB) * T::CH, tmem + C::TM_QA, sbase + C::OFF_Q);
           for (int s = 0; s < C::LAND; ++s, ++kc) mma_commit(&bar_kempty[kc % NK]);
         }
-        for (int c = 0; c < nch && ok; c += C::PAIR) ok = issue_s();  // pass A
+        // wide: Q's hi plane of this tile replaces the previous tile's in tensor memory once every MMA that read it
+        // (the previous tile's score MMAs, before its last P.V) has completed
+        if constexpr (C::WIDE)
+          if (it > 0 && !(ok = mbar_wait(&bar_ofull, (it - 1) & 1, ctx))) break;
+        for (int c = 0; c < nch && ok; c += C::PAIR) ok = issue_s(c == 0);  // pass A
         if (ONE && !C::POOL && ok) mma_commit(&bar_qempty);  // single score pass: Q is free after pass A's MMAs
         int nb = ONE ? nch : 0;  // pass-B chunks whose score MMAs are issued (none with a single score pass)
         // keeps the pass-B scores up to NSB - 1 chunks ahead; Q is released once the tile's last one is issued
