@@ -529,6 +529,38 @@ def test_full_c2_tf32_every_head_against_oracle(ops, qscale):
     _check(res, ref, TOL[torch.float32], "full C2 x%g" % qscale)
 
 
+@pytest.mark.parametrize("qscale", [1.0, 30.0], ids=["plain", "saturated_x30"])
+def test_full_size_tf32_d192_sampled_heads_against_oracle(ops, qscale):
+    """The production head dim in TF32 at 32 issue dates x 16 heads x 512 stations (13.8 tiles per persistent CTA in
+    every kernel; the dS-scratch backward with the transposing dQ GEMM and d(alpha) from the key pass): sampled heads
+    -- first, middle and last issue dates and heads -- against the float64 oracle within the TF32 tolerance."""
+    B, H, N, D = 32, 16, 512, 192
+    g = torch.Generator(device="cuda").manual_seed(71)
+    s = D ** -0.25
+    q = torch.randn(B, H, N, D, device="cuda", generator=g).mul_(s * qscale)
+    k, v = (torch.randn(B, H, N, D, device="cuda", generator=g).mul_(s) for _ in range(2))
+    do = torch.randn(B, H, N, D, device="cuda", generator=g)
+    pa = torch.rand(H, device="cuda", generator=g) * 0.9 + 0.1
+    pb, pc = (torch.randn(H, device="cuda", generator=g) * 0.5 for _ in range(2))
+    lat, lon, el = stations(N, seed=72)
+    geom = ops.StationGeometry(lat, lon, el)
+    x = [t.detach().requires_grad_(True) for t in (q, k, v)]
+    o = ops.geo_attention(x[0], x[1], x[2], geom, pa, pb, pc)
+    o.backward(do)
+    torch.cuda.synchronize()
+    dist, ang = dense_geometry(lat, lon, el)
+    for bi in (0, 13, B - 1):
+        for hi in (0, 9, H - 1):
+            sl = (slice(bi, bi + 1), slice(hi, hi + 1))
+            ref = _oracle(q[sl].cpu(), k[sl].cpu(), v[sl].cpu(), dist, ang, pa[hi:hi + 1].cpu(), pb[hi:hi + 1].cpu(),
+                          pc[hi:hi + 1].cpu(), do[sl].cpu())
+            got = dict(output=o.detach()[sl], dQ=x[0].grad[sl], dK=x[1].grad[sl], dV=x[2].grad[sl])
+            for key, val in got.items():
+                assert torch.isfinite(val).all(), (bi, hi, key)
+                e = rel_l2(val, ref[key])
+                assert e <= TOL[torch.float32], (bi, hi, key, e)
+
+
 @pytest.mark.parametrize("B,H,D", [(256, 16, 128), (384, 16, 64)], ids=["c5-256x16x512x128", "c3-384x16x512x64"])
 def test_full_size_bf16_sampled_heads_against_oracle(ops, B, H, D):
     """The benchmarked configuration (256 issue dates x 16 heads x 512 stations x D = 128, bf16; ~110 tiles per
