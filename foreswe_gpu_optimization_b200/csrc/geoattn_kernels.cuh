@@ -1847,9 +1847,10 @@ __global__ void __launch_bounds__(Tile<BF16, DP>::NTHREADS, 1)
 // ===============================================================================================================
 // Backward key pass: one CTA per (128-key block, b*h); keys on TMEM lanes. For each chunk of CH queries:
 //   S^T = K Q^T, dP^T = V dO^T; P1, P2, dZ, dS from the row records; dV += P2^T dO, dK += dS^T Q.
-// The chunk's row records arrive by bulk copy together with its Q / dO tiles. With SDS (bf16 with a dS scratch) the
-// TMA warp also stores each staged dS^T tile to the scratch (for the dQ GEMM) and the element-wise warps accumulate
-// the key block's d(beta) = sum dZ Dp and d(gamma) = sum dZ Ap.
+// The chunk's row records arrive by bulk copy together with its Q / dO tiles. With SDS (the dS-scratch backward) the
+// TMA warp also stores each staged dS^T tile to the scratch (for the dQ GEMM; fp32 at head dim 64 stores it
+// transposed) and the element-wise warps accumulate the key block's d(beta) = sum dZ Dp and d(gamma) = sum dZ Ap
+// (fp32 above head dim 64 also d(alpha) = sum dZ (P1 - b)).
 // ===============================================================================================================
 template <bool BF16, int DP, bool SDS = false>
 struct ColsCfg : Tile<BF16, DP> {
@@ -1898,8 +1899,9 @@ struct ColsCfg : Tile<BF16, DP> {
   static constexpr int OFF_DS = OFF_P2 + NST * ST_BYTES;
   static constexpr int OFF_PR = OFF_DS + NST * ST_BYTES;
   static constexpr int OFF_REC = OFF_PR + NPR * kPriorTileBytes;
-  // fp32 with a dS scratch: the TF32 dQ GEMM needs dS K-major along the keys, so each staged tile is also written
-  // transposed, [32 queries][128 keys] as four 128-byte-swizzled regions of 32 keys, for its TMA store
+  // fp32 at head dim 64 with a dS scratch: the TF32 dQ GEMM needs dS K-major along the keys, so each staged tile is
+  // also written transposed, [32 queries][128 keys] as four 128-byte-swizzled regions of 32 keys, for its TMA store
+  // (above 64 there is no shared memory for it: the tile is stored as staged and the dQ GEMM transposes it)
   static constexpr bool DST = SDS && !BF16 && !WIDE;
   static constexpr int DST_BYTES = 32 * kBM * 4;
   static constexpr int OFF_DST = (OFF_REC + NR * REC_BYTES + 1023) / 1024 * 1024;
