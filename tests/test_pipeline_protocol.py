@@ -13,7 +13,9 @@ a bounded-wait timeout or as results that differ between runs, so their arithmet
 * the wide key pass with query-chunk pairs: a chunk's records load before the next pair's slots;
 * the BF16 key pass's dS^T scratch stores trail the query-chunk loads by at most NQ + NST - 1 chunks;
 * the BF16 forward over several tiles: pass B's V loads may lag the K loads by 1 ... NSB + NK - 1 chunks (the kernel
-  uses NSB - 1); with Q in tensor memory and K in a ring of chunk pairs (head dims up to 128) by 0 ... NSB + 2 NK - 2.
+  uses NSB - 1); with Q in tensor memory and K in a ring of chunk pairs (head dims up to 128) by 0 ... NSB + 2 NK - 2;
+* the forwards with a single score pass (bf16, and fp32 at head dim 64 with its Q landing in the K ring);
+* the wide key pass's dS^T stores (fp32 above head dim 64), trailing the loads by one chunk.
 """
 import pytest
 
@@ -787,3 +789,111 @@ def test_key_pass_pooled_f32_store_lag_bound():
     bound = nq + nst - 1
     assert all(_key_pass_pooled_f32_order(n, 4, nq, nsb, nst, bound) is None for n in (1, 2, 3, 5, 8, 11, 16))
     assert _key_pass_pooled_f32_order(16, 4, nq, nsb, nst, bound + 1) is not None
+
+
+def _forward_one_order(nch, n_tiles, nk, unit, pooled, nsb, npr):
+    """The forward with a single score pass (geoattn_fwd_kernel<BF16, DP, true>) over several tiles as four
+    cooperating programs; returns None or the deadlock state.
+
+    Pass A only issues score MMAs: the TMA warp loads the K ring (nk slots; a slot holds `unit` chunks: one 64-key
+    chunk in bf16, a pair of 32-key chunks in the pooled fp32 kernel), the MMA warp issues one score MMA per slot into
+    `unit` of the nsb score buffers and releases the slot; the element-wise warps load two chunks' scores, release
+    both buffers and keep the values in tensor memory. Pass B issues no score MMA: the TMA warp loads V per chunk (two
+    buffers, each freed by its P.V MMA), the prior loader stages each chunk's prior tile (npr buffers), the
+    element-wise warps stage P once the P.V two chunks back has run, and the MMA warp issues P.V per chunk. Q: bf16
+    reloads it once the tile's last score MMA is issued; the pooled kernel lands it in the ring (nk positions,
+    released after the copies and their drain through a free score buffer), possibly while the previous tile's pass B
+    still runs."""
+    st = dict(pos=0, released=0, q_loaded=0, q_released=0, k_loaded=0, k_used=0, v_loaded=0, pv=0, pr_loaded=0,
+              pr_released=0, s_issued=0, s_released=0, p_staged=0, ofull=0)
+
+    def tma():
+        for it in range(n_tiles):
+            if pooled:
+                for _ in range(nk):
+                    yield lambda p=st["pos"]: st["released"] >= p + 1 - nk
+                    st["pos"] += 1
+            else:
+                yield lambda it=it: st["q_released"] >= it
+            st["q_loaded"] = it + 1
+            for _ in range(0, nch, unit):
+                yield lambda p=st["pos"]: st["released"] >= p + 1 - nk
+                st["pos"] += 1
+                st["k_loaded"] += 1
+            for c in range(nch):
+                g = it * nch + c
+                yield lambda g=g: st["pv"] >= g - 1
+                st["v_loaded"] = g + 1
+
+    def prior():
+        for g in range(n_tiles * nch):
+            yield lambda g=g: st["pr_released"] >= g + 1 - npr
+            st["pr_loaded"] = g + 1
+
+    def mma():
+        for it in range(n_tiles):
+            yield lambda it=it: st["q_loaded"] >= it + 1
+            if pooled:
+                yield lambda: st["s_released"] >= st["s_issued"] + 1 - nsb   # the drain's buffer
+                st["released"] += nk
+            for _ in range(0, nch, unit):
+                yield lambda: (st["k_loaded"] >= st["k_used"] + 1
+                               and st["s_released"] >= st["s_issued"] + unit - nsb)
+                st["k_used"] += 1
+                st["s_issued"] += unit
+                st["released"] += 1
+            if not pooled:
+                st["q_released"] = it + 1
+            for c in range(nch):
+                g = it * nch + c
+                yield lambda g=g: st["p_staged"] >= g + 1 and st["v_loaded"] >= g + 1
+                st["pv"] = g + 1
+            st["ofull"] = it + 1
+
+    def ew():
+        s = 0
+        for it in range(n_tiles):
+            for c in range(0, nch, 2):
+                two = 2 if c + 1 < nch else 1
+                yield lambda s=s, two=two: st["s_issued"] >= s + two
+                s += two
+                st["s_released"] = s
+            for c in range(nch):
+                g = it * nch + c
+                yield lambda g=g: st["pr_loaded"] >= g + 1
+                yield lambda g=g: st["pv"] >= g - 1
+                st["p_staged"] = g + 1
+                st["pr_released"] = g + 1
+            yield lambda it=it: st["ofull"] >= it + 1
+
+    progs = [tma(), prior(), mma(), ew()]
+    waits = [next(p) for p in progs]
+    done = [False] * len(progs)
+    while not all(done):
+        moved = False
+        for i, prog in enumerate(progs):
+            while not done[i] and waits[i]():
+                try:
+                    waits[i] = next(prog)
+                except StopIteration:
+                    done[i] = True
+                moved = True
+        if not moved:
+            return dict(st)
+    return None
+
+
+@pytest.mark.parametrize("nch", [1, 2, 3, 5, 8])
+def test_forward_one_bf16_order(nch):
+    """FwdCfg<true, DP <= 128, true>: Q in shared memory, 3-deep ring of 64-key K chunks, two score buffers, two
+    staged prior tiles; up to 8 chunks (512 keys), several tiles."""
+    assert _forward_one_order(nch, 3, 3, 1, False, 2, 2) is None
+
+
+@pytest.mark.parametrize("nch", [2, 4, 8, 16])
+def test_forward_one_pooled_tf32_order(nch):
+    """FwdCfg<false, 64, true>: Q pooled in tensor memory (its landing takes the 3-slot ring of K chunk pairs, even
+    while the previous tile's pass B runs), one pair of 32-key score buffers; with a single score buffer a pair's MMA
+    could never issue (the planted configuration stops)."""
+    assert _forward_one_order(nch, 3, 3, 2, True, 2, 2) is None
+    assert _forward_one_order(nch, 3, 3, 2, True, 1, 2) is not None
